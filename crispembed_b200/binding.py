@@ -1,0 +1,249 @@
+"""ctypes binding of libcrispembed.so (include/crispembed.h, include/ceb_ops.h).
+
+``CrispEmbed`` mirrors the reference's Python class (python/crispembed/_binding.py:
+``CrispEmbed(model_path, n_threads).encode(texts)``) for the embedding entry
+points this library implements, plus ``encode_ids`` for token-id input.  The
+operator-level wrappers (``MoELayer``, ``matmul``, ``pool_l2``) take torch CUDA
+tensors purely as device buffers.
+
+There is no CPU fallback: if the CUDA library is missing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import List, Optional, Sequence, Union
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libcrispembed.so")
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K = 0, 1, 8, 12
+ACT_F32, ACT_BF16, ACT_F16 = 0, 1, 2
+
+_lib = None
+
+
+class CrispEmbedError(RuntimeError):
+    pass
+
+
+class _Hparams(ctypes.Structure):
+    _fields_ = [
+        ("n_vocab", ctypes.c_int32), ("n_max_tokens", ctypes.c_int32), ("n_embd", ctypes.c_int32),
+        ("n_head", ctypes.c_int32), ("n_layer", ctypes.c_int32), ("n_intermediate", ctypes.c_int32),
+        ("n_output", ctypes.c_int32), ("layer_norm_eps", ctypes.c_float), ("n_experts", ctypes.c_int32),
+        ("n_experts_per_tok", ctypes.c_int32),
+    ]
+
+
+def load_library(path: Optional[str] = None):
+    """Load (never build) the shared library; raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = path or os.environ.get("CRISPEMBED_LIB") or LIB_PATH
+    if not os.path.exists(path):
+        raise CrispEmbedError(f"{path} not found: build it with `python -m crispembed_b200.build`")
+    L = ctypes.CDLL(path)
+    vp, cp, ip, fp = ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_float)
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    sig = {
+        "crispembed_init": ([cp, ctypes.c_int], vp),
+        "crispembed_free": ([vp], None),
+        "crispembed_set_dim": ([vp, ctypes.c_int], None),
+        "crispembed_set_prefix": ([vp, cp], None),
+        "crispembed_get_prefix": ([vp], cp),
+        "crispembed_set_gpu_backend": ([cp], None),
+        "crispembed_get_hparams": ([vp], ctypes.POINTER(_Hparams)),
+        "crispembed_encode": ([vp, cp, ip], fp),
+        "crispembed_encode_batch": ([vp, ctypes.POINTER(cp), ctypes.c_int, ip], fp),
+        "crispembed_encode_ids_batch": ([vp, i32p, i32p, ctypes.c_int, ip], fp),
+        "crispembed_encode_ids_device": ([vp, vp, i32p, ctypes.c_int, vp, ip, vp], ctypes.c_int),
+        "crispembed_stream": ([vp], vp),
+        "crispembed_has_sparse": ([vp], ctypes.c_int),
+        "crispembed_has_colbert": ([vp], ctypes.c_int),
+        "crispembed_is_reranker": ([vp], ctypes.c_int),
+        "ceb_moe_layer_create": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp,
+                                  ctypes.c_int, vp, vp, vp], vp),
+        "ceb_moe_layer_free": ([vp], None),
+        "ceb_moe_workspace_size": ([vp, ctypes.c_int], ctypes.c_size_t),
+        "ceb_moe_ffn": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp, ctypes.c_size_t, vp],
+                        ctypes.c_int),
+        "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_matmul": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
+                        ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_last_error": ([], cp),
+        "ceb_sync_check": ([vp], ctypes.c_int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    m = load_library().ceb_last_error()
+    return m.decode() if m else ""
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise CrispEmbedError(f"{what} failed ({rc}): {last_error()}")
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return int(stream)
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+class CrispEmbed:
+    """Text/ids -> L2-normalised embeddings through libcrispembed.so."""
+
+    def __init__(self, model_path: str, n_threads: int = 4, lib_path: Optional[str] = None):
+        self._lib = load_library(lib_path)
+        self._ctx = self._lib.crispembed_init(model_path.encode(), n_threads)
+        if not self._ctx:
+            raise CrispEmbedError(f"Failed to load model: {model_path}: {last_error()}")
+
+    def close(self):
+        if getattr(self, "_ctx", None):
+            self._lib.crispembed_free(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def hparams(self) -> _Hparams:
+        return self._lib.crispembed_get_hparams(self._ctx).contents
+
+    @property
+    def dim(self) -> int:
+        h = self.hparams
+        return h.n_output if h.n_output > 0 else h.n_embd
+
+    def set_prefix(self, prefix: Optional[str]):
+        self._lib.crispembed_set_prefix(self._ctx, (prefix or "").encode())
+
+    def set_dim(self, dim: int):
+        self._lib.crispembed_set_dim(self._ctx, int(dim))
+
+    def encode(self, texts: Union[str, List[str]], matryoshka_dim: Optional[int] = None) -> np.ndarray:
+        if matryoshka_dim is not None:
+            self.set_dim(matryoshka_dim)
+        single = isinstance(texts, str)
+        if single:
+            texts = [texts]
+        try:
+            dim = ctypes.c_int(0)
+            if len(texts) == 1:
+                ptr = self._lib.crispembed_encode(self._ctx, texts[0].encode(), ctypes.byref(dim))
+            else:
+                arr = (ctypes.c_char_p * len(texts))(*(t.encode() for t in texts))
+                ptr = self._lib.crispembed_encode_batch(self._ctx, arr, len(texts), ctypes.byref(dim))
+            if not ptr:
+                raise CrispEmbedError(f"encoding failed: {last_error()}")
+            out = np.ctypeslib.as_array(ptr, shape=(len(texts) * dim.value,)).copy().reshape(len(texts), dim.value)
+            return out[0] if single else out
+        finally:
+            if matryoshka_dim is not None:
+                self.set_dim(0)
+
+    def encode_ids(self, ids: np.ndarray, lens: Sequence[int]) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        lens = np.ascontiguousarray(lens, dtype=np.int32)
+        dim = ctypes.c_int(0)
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        ptr = self._lib.crispembed_encode_ids_batch(self._ctx, ids.ctypes.data_as(i32p), lens.ctypes.data_as(i32p),
+                                                    len(lens), ctypes.byref(dim))
+        if not ptr:
+            raise CrispEmbedError(f"encode_ids failed: {last_error()}")
+        return np.ctypeslib.as_array(ptr, shape=(len(lens) * dim.value,)).copy().reshape(len(lens), dim.value)
+
+    def encode_ids_device(self, d_ids, lens: np.ndarray, d_out, stream=None) -> int:
+        """d_ids: int32 CUDA tensor, d_out: float32 CUDA tensor [n_seqs, dim]."""
+        lens = np.ascontiguousarray(lens, dtype=np.int32)
+        dim = ctypes.c_int(0)
+        rc = self._lib.crispembed_encode_ids_device(self._ctx, d_ids.data_ptr(),
+                                                    lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(lens),
+                                                    d_out.data_ptr(), ctypes.byref(dim), _stream_ptr(stream))
+        _check(rc, "encode_ids_device")
+        return dim.value
+
+
+class MoELayer:
+    """One MoE feed-forward block on the device (ceb_moe_layer_create / ceb_moe_ffn)."""
+
+    def __init__(self, d: int, n_experts: int, top_k: int, ffn: int, router_type: int, router_raw: np.ndarray,
+                 expert_type: int, fc1_raw: np.ndarray, fc2_raw: np.ndarray, bias: Optional[np.ndarray] = None):
+        self._lib = load_library()
+        self.d, self.n_experts, self.top_k, self.ffn = d, n_experts, top_k, ffn
+        keep = [np.ascontiguousarray(router_raw), np.ascontiguousarray(fc1_raw), np.ascontiguousarray(fc2_raw)]
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._h = self._lib.ceb_moe_layer_create(d, n_experts, top_k, ffn, router_type, keep[0].ctypes.data,
+                                                 expert_type, keep[1].ctypes.data, keep[2].ctypes.data,
+                                                 None if b is None else b.ctypes.data)
+        if not self._h:
+            raise CrispEmbedError(f"ceb_moe_layer_create failed: {last_error()}")
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.ceb_moe_layer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def workspace_size(self, n_tokens: int) -> int:
+        return int(self._lib.ceb_moe_workspace_size(self._h, n_tokens))
+
+    def forward(self, x, y, workspace, ids=None, weights=None, counts=None, logits=None, stream=None):
+        import torch
+        act = {torch.float32: ACT_F32, torch.bfloat16: ACT_BF16, torch.float16: ACT_F16}[x.dtype]
+        rc = self._lib.ceb_moe_ffn(self._h, x.data_ptr(), act, x.shape[0], y.data_ptr(), _ptr(ids), _ptr(weights),
+                                   _ptr(counts), _ptr(logits), workspace.data_ptr(), workspace.numel(),
+                                   _stream_ptr(stream))
+        _check(rc, "ceb_moe_ffn")
+
+
+def matmul(w_type: int, w_raw: np.ndarray, n_out: int, k: int, x, bias=None, gelu=False, out_f16=False, stream=None):
+    import torch
+    lib = load_library()
+    out = torch.empty((x.shape[0], n_out), dtype=torch.float16 if out_f16 else torch.float32, device=x.device)
+    w_raw = np.ascontiguousarray(w_raw)
+    rc = lib.ceb_matmul(w_type, w_raw.ctypes.data, n_out, k, x.data_ptr(), x.shape[0], _ptr(bias), int(gelu),
+                        int(out_f16), out.data_ptr(), _stream_ptr(stream))
+    _check(rc, "ceb_matmul")
+    return out
+
+
+def pool_l2(hidden, cu_seqlens, out_dim: Optional[int] = None, stream=None):
+    import torch
+    lib = load_library()
+    n = cu_seqlens.numel() - 1
+    d = hidden.shape[1]
+    od = out_dim or d
+    out = torch.empty((n, od), dtype=torch.float32, device=hidden.device)
+    _check(lib.ceb_pool_l2(hidden.data_ptr(), cu_seqlens.data_ptr(), n, d, od, out.data_ptr(), _stream_ptr(stream)),
+           "ceb_pool_l2")
+    return out
+
+
+def sync_check(stream=None):
+    _check(load_library().ceb_sync_check(_stream_ptr(stream)), "device check")

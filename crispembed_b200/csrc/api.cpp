@@ -1,0 +1,524 @@
+// api.cpp -- the extern "C" entry points of include/crispembed.h and
+// include/ceb_ops.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cctype>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#define CRISPEMBED_BUILD 1
+#include "../../include/ceb_ops.h"
+#include "../../include/crispembed.h"
+#include "ceb_encoder_internal.h"
+
+static_assert(sizeof(crispembed_hparams) == sizeof(ceb_hparams_c), "hparams layout");
+
+struct crispembed_context {
+    ceb_model model;
+    ceb_workspace ws;
+    cudaStream_t stream = nullptr;
+    int device = 0;
+    int* d_err = nullptr;
+    int n_threads = 1;
+    std::string prefix;
+    int matryoshka_dim = 0;
+    std::vector<float> last_output;
+    // WordPiece tokenizer (tokenizer.ggml.type == 0)
+    int tok_type = 0;
+    int cls_id = 101, sep_id = 102, unk_id = 100, pad_id = 0;
+    bool lower = true;
+    std::unordered_map<std::string, int> vocab;
+    // pinned staging for host-buffer calls
+    int32_t* h_ids = nullptr;
+    int32_t* h_cu = nullptr;
+    float* h_out = nullptr;
+    size_t h_ids_cap = 0, h_cu_cap = 0, h_out_cap = 0;
+};
+
+namespace {
+
+int resolve_threads(int n) {
+    if (n > 0) return n;
+    unsigned hc = std::thread::hardware_concurrency();
+    return (int)std::min(4u, hc ? hc : 1u);
+}
+
+int out_dim_of(const crispembed_context* ctx) {
+    const int dim = ctx->model.hp.n_output > 0 ? ctx->model.hp.n_output : ctx->model.hp.n_embd;
+    return (ctx->matryoshka_dim > 0 && ctx->matryoshka_dim < dim) ? ctx->matryoshka_dim : dim;
+}
+
+template <typename T>
+int grow_pinned(T** p, size_t* cap, size_t n) {
+    if (n <= *cap) return 0;
+    if (*p) cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    if (cudaMallocHost((void**)p, n * sizeof(T)) != cudaSuccess) return ceb_set_error(4, "pinned host allocation failed");
+    *cap = n;
+    return 0;
+}
+
+// Checks the device error word written by bounded waits / index checks.
+int check_device(crispembed_context* ctx, cudaStream_t st) {
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "stream synchronize", __FILE__, __LINE__);
+    int h = 0;
+    e = cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "error word read", __FILE__, __LINE__);
+    if (h) {
+        cudaMemset(ctx->d_err, 0, sizeof(int));
+        return ceb_set_error(5, "device-side check failed (code 0x%x)", h);
+    }
+    return 0;
+}
+
+// Runs the encoder on device ids; cu_host [n_seqs+1] row offsets.
+int run_device(crispembed_context* ctx, const int32_t* d_ids, const int32_t* h_lens, int n_seqs, float* d_out,
+               cudaStream_t st) {
+    if (n_seqs <= 0) return ceb_set_error(1, "no sequences");
+    int rc = grow_pinned(&ctx->h_cu, &ctx->h_cu_cap, (size_t)n_seqs + 1);
+    if (rc) return rc;
+    int64_t M = 0;
+    int max_len = 0;
+    ctx->h_cu[0] = 0;
+    for (int i = 0; i < n_seqs; ++i) {
+        const int n = h_lens[i];
+        if (n <= 0 || n > ctx->model.hp.n_max_tokens)
+            return ceb_set_error(1, "sequence %d has %d tokens (allowed 1..%d)", i, n, ctx->model.hp.n_max_tokens);
+        M += n;
+        max_len = std::max(max_len, n);
+        ctx->h_cu[i + 1] = (int32_t)M;
+    }
+    if (M > (1 << 30)) return ceb_set_error(1, "too many tokens");
+    if ((rc = ceb_workspace_reserve(&ctx->ws, ctx->model, (int)M, n_seqs))) return rc;
+    cudaError_t e = cudaMemcpyAsync(ctx->ws.cu, ctx->h_cu, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "cu_seqlens upload", __FILE__, __LINE__);
+    return ceb_encoder_forward(ctx->model, ctx->ws, d_ids, ctx->ws.cu, n_seqs, (int)M, max_len, d_out,
+                               out_dim_of(ctx), ctx->d_err, st);
+}
+
+const float* encode_ids_host(crispembed_context* ctx, const int32_t* ids, const int32_t* lens, int n_seqs,
+                             int* out_n_dim) {
+    if (!ctx || !ids || !lens || n_seqs <= 0) return nullptr;
+    int64_t M = 0;
+    for (int i = 0; i < n_seqs; ++i) M += std::max(lens[i], 0);
+    const int dim = out_dim_of(ctx);
+    if (grow_pinned(&ctx->h_ids, &ctx->h_ids_cap, (size_t)std::max<int64_t>(M, 1)) ||
+        grow_pinned(&ctx->h_out, &ctx->h_out_cap, (size_t)n_seqs * dim))
+        return nullptr;
+    // the workspace must exist before the id upload targets it
+    int max_len = 0;
+    for (int i = 0; i < n_seqs; ++i) max_len = std::max(max_len, lens[i]);
+    if (max_len <= 0 || max_len > ctx->model.hp.n_max_tokens) {
+        ceb_set_error(1, "sequence lengths must lie in 1..%d", ctx->model.hp.n_max_tokens);
+        return nullptr;
+    }
+    if (ceb_workspace_reserve(&ctx->ws, ctx->model, (int)M, n_seqs)) return nullptr;
+    memcpy(ctx->h_ids, ids, (size_t)M * 4);
+    cudaStream_t st = ctx->stream;
+    if (cudaMemcpyAsync(ctx->ws.ids, ctx->h_ids, (size_t)M * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        ceb_set_error(3, "id upload failed");
+        return nullptr;
+    }
+    if (run_device(ctx, ctx->ws.ids, lens, n_seqs, ctx->ws.out, st)) return nullptr;
+    if (cudaMemcpyAsync(ctx->h_out, ctx->ws.out, (size_t)n_seqs * dim * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+        ceb_set_error(3, "embedding download failed");
+        return nullptr;
+    }
+    if (check_device(ctx, st)) return nullptr;
+    ctx->last_output.assign(ctx->h_out, ctx->h_out + (size_t)n_seqs * dim);
+    if (out_n_dim) *out_n_dim = dim;
+    return ctx->last_output.data();
+}
+
+// ---- WordPiece (BERT basic tokenizer + greedy longest-match-first) ----------
+bool is_punct(unsigned char c) {
+    return (c >= 33 && c <= 47) || (c >= 58 && c <= 64) || (c >= 91 && c <= 96) || (c >= 123 && c <= 126);
+}
+
+std::vector<int32_t> wordpiece(const crispembed_context* ctx, const std::string& text) {
+    std::vector<std::string> words;
+    std::string cur;
+    for (unsigned char c : text) {
+        if (std::isspace(c)) {
+            if (!cur.empty()) words.push_back(cur), cur.clear();
+        } else if (c < 128 && is_punct(c)) {
+            if (!cur.empty()) words.push_back(cur), cur.clear();
+            words.push_back(std::string(1, (char)c));
+        } else {
+            cur.push_back(ctx->lower && c < 128 ? (char)std::tolower(c) : (char)c);
+        }
+    }
+    if (!cur.empty()) words.push_back(cur);
+    std::vector<int32_t> ids;
+    ids.push_back(ctx->cls_id);
+    const size_t limit = (size_t)std::max(2, ctx->model.hp.n_max_tokens) - 1;
+    for (const auto& w : words) {
+        if (ids.size() >= limit) break;
+        if (w.size() > 100) {
+            ids.push_back(ctx->unk_id);
+            continue;
+        }
+        std::vector<int32_t> pieces;
+        size_t start = 0;
+        bool bad = false;
+        while (start < w.size()) {
+            size_t end = w.size();
+            int found = -1;
+            while (start < end) {
+                std::string sub = w.substr(start, end - start);
+                if (start > 0) sub = "##" + sub;
+                auto it = ctx->vocab.find(sub);
+                if (it != ctx->vocab.end()) {
+                    found = it->second;
+                    break;
+                }
+                --end;
+            }
+            if (found < 0) {
+                bad = true;
+                break;
+            }
+            pieces.push_back(found);
+            start = end;
+        }
+        if (bad) ids.push_back(ctx->unk_id);
+        else
+            for (int32_t p : pieces) {
+                if (ids.size() >= limit) break;
+                ids.push_back(p);
+            }
+    }
+    ids.push_back(ctx->sep_id);
+    return ids;
+}
+
+const float* encode_texts(crispembed_context* ctx, const char** texts, int n, int* out_n_dim) {
+    if (ctx->tok_type != 0) {
+        ceb_set_error(1, "tokenizer type %d is not implemented by this build (WordPiece only); "
+                         "use crispembed_encode_ids_batch",
+                      ctx->tok_type);
+        return nullptr;
+    }
+    std::vector<int32_t> ids, lens;
+    for (int i = 0; i < n; ++i) {
+        std::string s = ctx->prefix + (texts[i] ? texts[i] : "");
+        std::vector<int32_t> t = wordpiece(ctx, s);
+        lens.push_back((int32_t)t.size());
+        ids.insert(ids.end(), t.begin(), t.end());
+    }
+    return encode_ids_host(ctx, ids.data(), lens.data(), n, out_n_dim);
+}
+
+std::string g_str;  // backing store for the registry helpers
+
+}  // namespace
+
+// =========================================================== crispembed.h ===
+extern "C" crispembed_context* crispembed_init(const char* model_path, int n_threads) {
+    if (!model_path) return nullptr;
+    auto* ctx = new crispembed_context;
+    ctx->n_threads = resolve_threads(n_threads);
+    if (cudaGetDevice(&ctx->device) != cudaSuccess || cudaFree(nullptr) != cudaSuccess) {
+        ceb_set_error(3, "no CUDA device available");
+        delete ctx;
+        return nullptr;
+    }
+    std::string err;
+    std::vector<std::string> vocab;
+    if (ceb_model_load(&ctx->model, model_path, &err, &vocab, &ctx->tok_type, &ctx->cls_id, &ctx->sep_id, &ctx->unk_id,
+                       &ctx->pad_id)) {
+        delete ctx;
+        return nullptr;
+    }
+    ctx->vocab.reserve(vocab.size());
+    for (size_t i = 0; i < vocab.size(); ++i) ctx->vocab.emplace(vocab[i], (int)i);
+    for (const auto& t : vocab)
+        if (t.size() == 1 && t[0] >= 'A' && t[0] <= 'Z') {
+            ctx->lower = false;
+            break;
+        }
+    if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) {
+        ceb_set_error(3, "context setup failed");
+        crispembed_free(ctx);
+        return nullptr;
+    }
+    int moe = 0;
+    for (const auto& Ly : ctx->model.layers) moe += Ly.moe;
+    fprintf(stderr, "crispembed-b200: loaded %d layers (%d MoE, %d experts top-%d), %d dims, %d vocab, %.1f MB weights\n",
+            ctx->model.hp.n_layer, moe, ctx->model.hp.n_experts, ctx->model.hp.n_experts_per_tok,
+            ctx->model.hp.n_embd, ctx->model.hp.n_vocab, ctx->model.weight_bytes / 1e6);
+    return ctx;
+}
+
+extern "C" void crispembed_set_gpu_backend(const char* name) {
+    if (name && name[0] && strcasecmp(name, "cuda") != 0)
+        fprintf(stderr, "crispembed-b200: backend '%s' not available, using CUDA\n", name);
+}
+
+extern "C" void crispembed_set_dim(crispembed_context* ctx, int dim) {
+    if (ctx) ctx->matryoshka_dim = dim;
+}
+
+extern "C" void crispembed_set_prefix(crispembed_context* ctx, const char* prefix) {
+    if (ctx) ctx->prefix = prefix ? prefix : "";
+}
+
+extern "C" const char* crispembed_get_prefix(const crispembed_context* ctx) { return ctx ? ctx->prefix.c_str() : ""; }
+
+extern "C" const crispembed_hparams* crispembed_get_hparams(const crispembed_context* ctx) {
+    return ctx ? reinterpret_cast<const crispembed_hparams*>(&ctx->model.hp) : nullptr;
+}
+
+extern "C" const float* crispembed_encode(crispembed_context* ctx, const char* text, int* out_n_dim) {
+    if (!ctx || !text) return nullptr;
+    const char* t[1] = {text};
+    return encode_texts(ctx, t, 1, out_n_dim);
+}
+
+extern "C" const float* crispembed_encode_batch(crispembed_context* ctx, const char** texts, int n_texts,
+                                                int* out_n_dim) {
+    if (!ctx || !texts || n_texts <= 0) return nullptr;
+    return encode_texts(ctx, texts, n_texts, out_n_dim);
+}
+
+extern "C" const float* crispembed_encode_ids_batch(crispembed_context* ctx, const int32_t* h_ids,
+                                                    const int32_t* h_lens, int n_seqs, int* out_n_dim) {
+    return encode_ids_host(ctx, h_ids, h_lens, n_seqs, out_n_dim);
+}
+
+extern "C" int crispembed_encode_ids_device(crispembed_context* ctx, const int32_t* d_ids, const int32_t* h_lens,
+                                            int n_seqs, float* d_out, int* out_n_dim, void* stream) {
+    if (!ctx || !d_ids || !h_lens || !d_out) return ceb_set_error(1, "null argument");
+    if (out_n_dim) *out_n_dim = out_dim_of(ctx);
+    return run_device(ctx, d_ids, h_lens, n_seqs, d_out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" void* crispembed_stream(crispembed_context* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+extern "C" void crispembed_free(crispembed_context* ctx) {
+    if (!ctx) return;
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    ceb_workspace_free(&ctx->ws);
+    ceb_model_free(&ctx->model);
+    if (ctx->d_err) cudaFree(ctx->d_err);
+    if (ctx->h_ids) cudaFreeHost(ctx->h_ids);
+    if (ctx->h_cu) cudaFreeHost(ctx->h_cu);
+    if (ctx->h_out) cudaFreeHost(ctx->h_out);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+extern "C" int crispembed_has_sparse(const crispembed_context*) { return 0; }
+extern "C" int crispembed_has_colbert(const crispembed_context*) { return 0; }
+extern "C" int crispembed_is_reranker(const crispembed_context*) { return 0; }
+extern "C" int crispembed_encode_sparse(crispembed_context*, const char*, const int32_t**, const float**) { return 0; }
+extern "C" const float* crispembed_encode_multivec(crispembed_context*, const char*, int* out_n_tokens, int* out_dim) {
+    if (out_n_tokens) *out_n_tokens = 0;
+    if (out_dim) *out_dim = 0;
+    return nullptr;
+}
+extern "C" float crispembed_rerank(crispembed_context*, const char*, const char*) {
+    ceb_set_error(1, "this model has no reranker head");
+    return NAN;
+}
+extern "C" float crispembed_colbert_score(const float* q, int n_query, const float* dv, int n_doc, int dim) {
+    float score = 0.0f;
+    for (int qi = 0; qi < n_query; qi++) {
+        float best = -1e30f;
+        for (int di = 0; di < n_doc; di++) {
+            float dot = 0.0f;
+            for (int k = 0; k < dim; k++) dot += q[(size_t)qi * dim + k] * dv[(size_t)di * dim + k];
+            best = std::max(best, dot);
+        }
+        score += best;
+    }
+    return score;
+}
+
+extern "C" const char* crispembed_cache_dir(void) {
+    const char* h = getenv("CRISPEMBED_CACHE_DIR");
+    g_str = h ? h : "";
+    return g_str.c_str();
+}
+extern "C" const char* crispembed_resolve_model(const char* arg, int) {
+    g_str = arg ? arg : "";
+    return g_str.c_str();
+}
+extern "C" const char* crispembed_query_prefix(const char*) { return nullptr; }
+extern "C" const char* crispembed_passage_prefix(const char*) { return nullptr; }
+extern "C" const char* crispembed_ctx_query_prefix(const crispembed_context*) { return nullptr; }
+extern "C" const char* crispembed_ctx_passage_prefix(const crispembed_context*) { return nullptr; }
+extern "C" int crispembed_n_models(void) { return 0; }
+extern "C" const char* crispembed_model_name(int) { return ""; }
+extern "C" const char* crispembed_model_desc(int) { return ""; }
+extern "C" const char* crispembed_model_filename(int) { return ""; }
+extern "C" const char* crispembed_model_size(int) { return ""; }
+extern "C" const char* crispembed_model_license(int) { return ""; }
+extern "C" const char* crispembed_model_card_url(int) { return ""; }
+
+// ============================================================= ceb_ops.h ===
+struct ceb_moe_layer {
+    ceb_moe_weights w;
+    std::vector<void*> allocs;
+};
+
+extern "C" ceb_moe_layer* ceb_moe_layer_create(int d, int n_experts, int top_k, int ffn, int router_type,
+                                               const void* h_router, int expert_type, const void* h_fc1,
+                                               const void* h_fc2, const float* h_bias) {
+    if (d <= 0 || n_experts <= 0 || n_experts > 32 || top_k <= 0 || top_k > 4 || top_k > n_experts || ffn <= 0 ||
+        !h_router || !h_fc1 || !h_fc2) {
+        ceb_set_error(1, "moe_layer_create: bad arguments");
+        return nullptr;
+    }
+    if (router_type != CEB_TYPE_F32 && router_type != CEB_TYPE_Q8_0) {
+        ceb_set_error(1, "moe_layer_create: router type %d unsupported (F32 or Q8_0)", router_type);
+        return nullptr;
+    }
+    if (d % 128 || ffn % 128 || (expert_type == CEB_TYPE_Q4_K && (d % 256 || ffn % 256))) {
+        ceb_set_error(2, "moe_layer_create: d=%d ffn=%d must be multiples of 128 (256 for Q4_K)", d, ffn);
+        return nullptr;
+    }
+    auto* L = new ceb_moe_layer;
+    L->w.d = d;
+    L->w.n_experts = n_experts;
+    L->w.top_k = top_k;
+    L->w.ffn = ffn;
+    L->w.router_type = router_type;
+    const int64_t rrb = router_type == CEB_TYPE_F32 ? (int64_t)d * 4 : (int64_t)d / 32 * 34;
+    const size_t rbytes = (size_t)(rrb * n_experts);
+    void* p = nullptr;
+    int rc = 0;
+    if (cudaMalloc(&p, rbytes) != cudaSuccess) rc = ceb_set_error(4, "out of device memory");
+    else {
+        L->allocs.push_back(p);
+        L->w.router = static_cast<uint8_t*>(p);
+        if (cudaMemcpy(p, h_router, rbytes, cudaMemcpyHostToDevice) != cudaSuccess) rc = ceb_set_error(3, "upload");
+    }
+    if (!rc) rc = ceb_repack_weights(&L->w.fc1, expert_type, h_fc1, n_experts, ffn, d, nullptr);
+    if (!rc) rc = ceb_repack_weights(&L->w.fc2, expert_type, h_fc2, n_experts, d, ffn, nullptr);
+    if (!rc && h_bias) {
+        if (cudaMalloc(&p, (size_t)d * 4) != cudaSuccess) rc = ceb_set_error(4, "out of device memory");
+        else {
+            L->allocs.push_back(p);
+            L->w.bias = static_cast<float*>(p);
+            if (cudaMemcpy(p, h_bias, (size_t)d * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                rc = ceb_set_error(3, "upload");
+        }
+    }
+    if (rc) {
+        ceb_moe_layer_free(L);
+        return nullptr;
+    }
+    return L;
+}
+
+extern "C" void ceb_moe_layer_free(ceb_moe_layer* L) {
+    if (!L) return;
+    ceb_wplane_free(&L->w.fc1);
+    ceb_wplane_free(&L->w.fc2);
+    for (void* p : L->allocs) cudaFree(p);
+    delete L;
+}
+
+extern "C" size_t ceb_moe_workspace_size(const ceb_moe_layer* L, int max_tokens) {
+    if (!L || max_tokens <= 0) return 0;
+    return ceb_moe_ws_layout(max_tokens, L->w.d, L->w.n_experts, L->w.top_k, L->w.ffn, nullptr, nullptr);
+}
+
+namespace {
+int* g_op_err = nullptr;  // device error word for operator-level calls
+std::mutex g_op_mu;
+int* op_err_word() {
+    std::lock_guard<std::mutex> lk(g_op_mu);
+    if (!g_op_err) {
+        if (cudaMalloc(&g_op_err, sizeof(int)) != cudaSuccess) return nullptr;
+        cudaMemset(g_op_err, 0, sizeof(int));
+    }
+    return g_op_err;
+}
+}  // namespace
+
+extern "C" int ceb_moe_ffn(const ceb_moe_layer* L, const void* d_x, int x_dtype, int n_tokens, float* d_y,
+                           int32_t* d_ids, float* d_weights, int32_t* d_expert_counts, float* d_logits,
+                           void* d_workspace, size_t workspace_bytes, void* stream) {
+    if (!L || !d_x || !d_y || n_tokens < 0 || (n_tokens > 0 && !d_workspace))
+        return ceb_set_error(1, "moe_ffn: bad arguments");
+    if (x_dtype != CEB_ACT_F32 && x_dtype != CEB_ACT_BF16 && x_dtype != CEB_ACT_F16)
+        return ceb_set_error(1, "moe_ffn: x_dtype %d unsupported", x_dtype);
+    if (n_tokens == 0) return 0;
+    const size_t need = ceb_moe_workspace_size(L, n_tokens);
+    if (workspace_bytes < need)
+        return ceb_set_error(1, "moe_ffn: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    if (reinterpret_cast<uintptr_t>(d_workspace) & 255) return ceb_set_error(1, "moe_ffn: workspace not 256-B aligned");
+    int* err = op_err_word();
+    if (!err) return ceb_set_error(4, "out of device memory");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ceb_moe_ws ws;
+    ceb_moe_ws_layout(n_tokens, L->w.d, L->w.n_experts, L->w.top_k, L->w.ffn, &ws, static_cast<uint8_t*>(d_workspace));
+    int rc = ceb_moe_run(L->w, d_x, x_dtype, n_tokens, d_y, ws, d_expert_counts, d_logits, err, st);
+    if (rc) return rc;
+    const size_t S = (size_t)n_tokens * L->w.top_k;
+    if (d_ids && cudaMemcpyAsync(d_ids, ws.ids, S * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return ceb_set_error(3, "ids copy");
+    if (d_weights && cudaMemcpyAsync(d_weights, ws.wts, S * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return ceb_set_error(3, "weights copy");
+    return 0;
+}
+
+extern "C" int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int n_seqs, int d, int out_dim,
+                           float* d_out, void* stream) {
+    if (!d_hidden || !d_cu_seqlens || !d_out || n_seqs < 0 || d <= 0) return ceb_set_error(1, "pool_l2: bad arguments");
+    return ceb_pool_l2_launch(d_hidden, d_cu_seqlens, n_seqs, d, out_dim, d_out, static_cast<cudaStream_t>(stream), 0);
+}
+
+extern "C" int ceb_matmul(int w_type, const void* h_w, int n_out, int k, const void* d_x, int m, const float* d_bias,
+                          int gelu, int out_f16, void* d_out, void* stream) {
+    if (!h_w || !d_x || !d_out || m < 0) return ceb_set_error(1, "matmul: bad arguments");
+    int* err = op_err_word();
+    if (!err) return ceb_set_error(4, "out of device memory");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ceb_wplane w;
+    int rc = ceb_repack_weights(&w, w_type, h_w, 1, n_out, k, st);
+    if (rc) return rc;
+    ceb_gemm_args a;
+    a.m_rows = m;
+    a.out = d_out;
+    a.ldo = n_out;
+    a.epi = (out_f16 ? CEB_EPI_F16_OUT : 0) | (gelu ? CEB_EPI_GELU : 0) | (d_bias ? CEB_EPI_BIAS : 0);
+    a.bias = d_bias;
+    a.err = err;
+    rc = ceb_gemm_launch(w, d_x, m, a, st);
+    cudaError_t e = cudaStreamSynchronize(st);
+    ceb_wplane_free(&w);
+    if (rc) return rc;
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "matmul", __FILE__, __LINE__);
+    return 0;
+}
+
+extern "C" const char* ceb_last_error(void) { return ceb_last_error_message(); }
+
+extern "C" int ceb_sync_check(void* stream) {
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "stream synchronize", __FILE__, __LINE__);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "pending error", __FILE__, __LINE__);
+    int* err = op_err_word();
+    if (!err) return 0;
+    int h = 0;
+    if (cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return ceb_set_error(3, "error word");
+    if (h) {
+        cudaMemset(err, 0, sizeof(int));
+        return ceb_set_error(5, "device-side check failed (code 0x%x)", h);
+    }
+    return 0;
+}

@@ -1,0 +1,76 @@
+// ceb_encoder_internal.h -- NomicBERT-MoE encoder model state and forward pass.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "ceb_internal.h"
+#include "ceb_moe_internal.h"
+
+// row-wise / attention kernel launchers (encoder_kernels.cu)
+int ceb_embed_ln(const int32_t* ids, const int32_t* cu, int n_seqs, int M, int d, int n_vocab, const float* tok,
+                 const float* pos, int n_pos, int pos_offset, const float* type0, const float* gamma,
+                 const float* beta, float eps, float* out32, __half* out16, int* err, cudaStream_t st);
+int ceb_add_ln(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
+               float* out32, __half* out16, cudaStream_t st);
+int ceb_moe_combine_ln(const float* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
+                       const float* cur, int M, int d, const float* gamma, const float* beta, float eps, float* out32,
+                       __half* out16, cudaStream_t st);
+int ceb_attention(const __half* qkv, const int32_t* cu, int n_seqs, int max_len, int d, int n_head, __half* out,
+                  cudaStream_t st);
+int ceb_pool_l2_launch(const float* hidden, const int32_t* cu, int n_seqs, int d, int out_dim, float* out,
+                       cudaStream_t st, int mode = 0);
+
+struct ceb_layer {
+    ceb_wplane qkv, o, fc1, fc2;
+    float *qkv_b = nullptr, *o_b = nullptr, *fc1_b = nullptr, *fc2_b = nullptr;
+    float *ln1_w = nullptr, *ln1_b = nullptr, *ln2_w = nullptr, *ln2_b = nullptr;
+    bool moe = false;
+    ceb_moe_weights moew;
+};
+
+struct ceb_hparams_c {  // mirrors crispembed_hparams (include/crispembed.h)
+    int32_t n_vocab, n_max_tokens, n_embd, n_head, n_layer, n_intermediate, n_output;
+    float layer_norm_eps;
+    int32_t n_experts, n_experts_per_tok;
+};
+
+struct ceb_model {
+    ceb_hparams_c hp{};
+    int pool_method = 0;   // 0 mean, 1 cls, 2 last
+    int pos_offset = 0;
+    int n_pos = 0;
+    float* tok = nullptr;  // [n_vocab x d] f32
+    float* pos = nullptr;  // [n_pos x d] f32 or null
+    float* type0 = nullptr;  // row 0 of the token-type table or null
+    float *embd_ln_w = nullptr, *embd_ln_b = nullptr;
+    std::vector<ceb_layer> layers;
+    std::vector<void*> allocs;  // every device buffer owned by the model
+    size_t weight_bytes = 0;
+};
+
+struct ceb_workspace {
+    int cap_tokens = 0;
+    int cap_seqs = 0;
+    void* base = nullptr;
+    size_t bytes = 0;
+    float *x32 = nullptr, *c32 = nullptr, *t32 = nullptr;
+    __half *x16 = nullptr, *c16 = nullptr, *qkv16 = nullptr, *a16 = nullptr, *h16 = nullptr;
+    ceb_moe_ws moe;
+    int32_t* ids = nullptr;    // [cap_tokens]
+    int32_t* cu = nullptr;     // [cap_seqs + 1]
+    float* out = nullptr;      // [cap_seqs x d]
+};
+
+int ceb_model_load(ceb_model* m, const std::string& path, std::string* vocab_err,
+                   std::vector<std::string>* vocab_out, int* tok_type, int* cls_id, int* sep_id, int* unk_id,
+                   int* pad_id);
+void ceb_model_free(ceb_model* m);
+int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int seqs);
+void ceb_workspace_free(ceb_workspace* ws);
+// Full forward pass on device-resident ids; writes [n_seqs x out_dim] pooled, L2-normalised rows.
+int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_ids, const int32_t* d_cu, int n_seqs,
+                        int n_tokens, int max_len, float* d_out, int out_dim, int* d_err, cudaStream_t st);

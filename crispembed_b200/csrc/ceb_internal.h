@@ -1,0 +1,67 @@
+// ceb_internal.h -- host-side declarations shared by the .cu/.cpp files of the
+// library.  Nothing here is part of the public C ABI (see include/*.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+// ggml tensor types used on the path (values are ggml's enum)
+enum { CEB_GGML_F32 = 0, CEB_GGML_F16 = 1, CEB_GGML_Q8_0 = 8, CEB_GGML_Q4_K = 12 };
+
+// Device weight-plane formats consumed by the grouped GEMM.
+enum ceb_wformat : int {
+    CEB_W_F16 = 0,   // fp16 [G][N][K]
+    CEB_W_Q8_0 = 1,  // int8 [G][N][K] + fp16 scale [G][N][K/32]
+    CEB_W_Q4_K = 2,  // nibbles [G][N][K/2] (ggml in-chunk order) + float2 (d*sc, dmin*m) [G][N][K/32]
+};
+
+// A repacked weight matrix set: n_groups matrices of [n_out x k] (experts, or 1 for dense).
+struct ceb_wplane {
+    int format = CEB_W_F16;
+    int n_groups = 0, n_out = 0, k = 0;
+    uint8_t* q = nullptr;  // quant plane (device)
+    uint8_t* s = nullptr;  // scale plane (device), null for F16
+    int64_t q_row_bytes = 0, s_row_bytes = 0;
+    size_t q_bytes = 0, s_bytes = 0;
+};
+
+// Epilogue flags of the grouped GEMM
+enum : int {
+    CEB_EPI_F16_OUT = 1,  // store fp16 (else fp32)
+    CEB_EPI_BIAS = 2,     // add bias[n] (bias pointer per group: bias + g*bias_group_stride)
+    CEB_EPI_GELU = 4,     // erf-GELU after bias
+};
+
+struct ceb_gemm_args {
+    const int* offsets = nullptr;  // device [n_groups+1] activation-row ranges per group; null = dense
+    int m_rows = 0;                // dense: activation rows; grouped: capacity of the activation buffer
+    void* out = nullptr;
+    int ldo = 0;                   // output row stride (elements)
+    int epi = 0;
+    const float* bias = nullptr;
+    int64_t bias_group_stride = 0;
+    int* err = nullptr;            // device error word
+};
+
+// status / errors
+int ceb_set_error(int code, const char* fmt, ...);
+int ceb_set_cuda_error(cudaError_t e, const char* what, const char* file, int line);
+const char* ceb_last_error_message();
+
+// tensor maps
+int ceb_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                         uint32_t box_inner, uint32_t box_rows);
+
+// kernels (launchers return 0 or an error code)
+int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows_capacity, const ceb_gemm_args& a,
+                    cudaStream_t stream, int max_ctas = 0);
+int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int n_groups, int n_out, int k,
+                       cudaStream_t stream);
+void ceb_wplane_free(ceb_wplane* w);
+
+int ceb_num_sms();

@@ -1,0 +1,40 @@
+// ceb_moe_internal.h -- MoE layer state shared between moe.cu, the encoder and the C ABI.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "ceb_internal.h"
+
+// activation element types (same values as include/ceb_ops.h)
+#ifndef CEB_ACT_F32
+#define CEB_ACT_F32 0
+#define CEB_ACT_BF16 1
+#define CEB_ACT_F16 2
+#endif
+
+// Device-resident weights of one MoE feed-forward block.
+struct ceb_moe_weights {
+    int d = 0, n_experts = 0, top_k = 0, ffn = 0;
+    int router_type = CEB_GGML_F32;   // CEB_GGML_F32 ([E][d] floats) or CEB_GGML_Q8_0 (raw ggml blocks)
+    uint8_t* router = nullptr;        // device
+    ceb_wplane fc1;                   // E x [ffn x d]
+    ceb_wplane fc2;                   // E x [d x ffn]
+    float* bias = nullptr;            // [d] or null
+};
+
+// Per-call scratch, carved from one caller-provided buffer.
+struct ceb_moe_ws {
+    int32_t* ids = nullptr;           // [T*K] expert of each (token, slot)
+    float* wts = nullptr;             // [T*K] gate weight
+    int32_t* block_counts = nullptr;  // [nblk*E]
+    int32_t* block_base = nullptr;    // [nblk*E]
+    int32_t* offsets = nullptr;       // [E+1] expert row ranges in the permuted matrices
+    int32_t* slot_pos = nullptr;      // [T*K] permuted row of each (token, slot)
+    __half* x_perm = nullptr;         // [T*K x d]
+    __half* h_perm = nullptr;         // [T*K x ffn]
+    float* down = nullptr;            // [T*K x d]
+};
+
+size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint8_t* base);
+int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, float* y, const ceb_moe_ws& ws,
+                int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st);

@@ -1,0 +1,457 @@
+// encoder_kernels.cu -- the row-wise and attention kernels around the MoE FFN:
+// embedding gather + LayerNorm, residual add + LayerNorm (post-LN), the MoE
+// combine fused with its residual + LayerNorm, varlen multi-head attention and
+// the mean-pool + L2 epilogue.
+//
+// Reference: build_encoder_graph (src/crispembed.cpp:1068-1135 embeddings and
+// embedding LN, :1278-1297 attention, :1316-1323 and :1423-1428 residual +
+// post-LN) and encode_tokens' pooling (:1822-1846).
+#include "ceb_encoder_internal.h"
+#include "ceb_internal.h"
+#include "common.cuh"
+
+namespace {
+
+constexpr int LN_MAXV = 8;  // float4 per lane: d <= 1024
+
+CEB_DEV float wsum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// LayerNorm of one row held as float4 registers by a warp (lane owns float4
+// i*32+lane).  ggml_norm order: mean, centred values, variance of the centred
+// values, scale = 1/sqrtf(var+eps), then *gamma, +beta as separate roundings.
+CEB_DEV void ln_row_store(float4 (&v)[LN_MAXV], int nv, int d, const float* gamma, const float* beta, float eps,
+                          float* out32, __half* out16, int lane) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i)
+        if (i < nv) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = wsum(s) / (float)d;
+    float s2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i)
+        if (i < nv) {
+            v[i].x = __fsub_rn(v[i].x, mean);
+            v[i].y = __fsub_rn(v[i].y, mean);
+            v[i].z = __fsub_rn(v[i].z, mean);
+            v[i].w = __fsub_rn(v[i].w, mean);
+            s2 += (__fmul_rn(v[i].x, v[i].x) + __fmul_rn(v[i].y, v[i].y)) +
+                  (__fmul_rn(v[i].z, v[i].z) + __fmul_rn(v[i].w, v[i].w));
+        }
+    const float var = wsum(s2) / (float)d;
+    const float scale = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i)
+        if (i < nv) {
+            const int c = (i * 32 + lane) * 4;
+            const float4 g = gamma ? *reinterpret_cast<const float4*>(gamma + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 b = beta ? *reinterpret_cast<const float4*>(beta + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 o;
+            o.x = __fadd_rn(__fmul_rn(__fmul_rn(v[i].x, scale), g.x), b.x);
+            o.y = __fadd_rn(__fmul_rn(__fmul_rn(v[i].y, scale), g.y), b.y);
+            o.z = __fadd_rn(__fmul_rn(__fmul_rn(v[i].z, scale), g.z), b.z);
+            o.w = __fadd_rn(__fmul_rn(__fmul_rn(v[i].w, scale), g.w), b.w);
+            if (out32) *reinterpret_cast<float4*>(out32 + c) = o;
+            if (out16) {
+                __half2* h = reinterpret_cast<__half2*>(out16 + c);
+                h[0] = __floats2half2_rn(o.x, o.y);
+                h[1] = __floats2half2_rn(o.z, o.w);
+            }
+        }
+}
+
+CEB_DEV float4 f4add(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+CEB_DEV int find_seq(const int32_t* cu, int n_seqs, int t) {
+    int lo = 0, hi = n_seqs - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (cu[mid] <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// x = tok[id] + pos[t - start + pos_offset] (+ type[0]); LN(embd_ln)
+__global__ void embed_ln_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int n_seqs, int M,
+                                int d, int n_vocab, const float* __restrict__ tok, const float* __restrict__ pos,
+                                int n_pos, int pos_offset, const float* __restrict__ type0,
+                                const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+                                float* __restrict__ out32, __half* __restrict__ out16, int* err) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const int t = warp;
+    int id = ids[t];
+    if (id < 0 || id >= n_vocab) {
+        if (lane == 0) atomicCAS(err, 0, (int)CEB_DEVERR_BAD_INDEX);
+        id = 0;
+    }
+    int p = 0;
+    if (pos) {
+        const int s = find_seq(cu, n_seqs, t);
+        p = t - cu[s] + pos_offset;
+        if (p < 0 || p >= n_pos) {
+            if (lane == 0) atomicCAS(err, 0, (int)CEB_DEVERR_BAD_INDEX);
+            p = 0;
+        }
+    }
+    const int nv = d / 128;
+    float4 v[LN_MAXV];
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i)
+        if (i < nv) {
+            const int c = (i * 32 + lane) * 4;
+            float4 x = __ldg(reinterpret_cast<const float4*>(tok + (size_t)id * d + c));
+            if (pos) x = f4add(x, __ldg(reinterpret_cast<const float4*>(pos + (size_t)p * d + c)));
+            if (type0) x = f4add(x, __ldg(reinterpret_cast<const float4*>(type0 + c)));
+            v[i] = x;
+        }
+    if (gamma) {
+        ln_row_store(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
+    } else {
+#pragma unroll
+        for (int i = 0; i < LN_MAXV; ++i)
+            if (i < nv) {
+                const int c = (i * 32 + lane) * 4;
+                *reinterpret_cast<float4*>(out32 + (size_t)t * d + c) = v[i];
+                __half2* h = reinterpret_cast<__half2*>(out16 + (size_t)t * d + c);
+                h[0] = __floats2half2_rn(v[i].x, v[i].y);
+                h[1] = __floats2half2_rn(v[i].z, v[i].w);
+            }
+    }
+}
+
+// out = LN(res + y)   (out32 may alias res)
+__global__ void add_ln_kernel(const float* res, const float* __restrict__ y, int M, int d,
+                              const float* __restrict__ gamma, const float* __restrict__ beta, float eps, float* out32,
+                              __half* __restrict__ out16) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= M) return;
+    const int nv = d / 128;
+    float4 v[LN_MAXV];
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i)
+        if (i < nv) {
+            const int c = (i * 32 + lane) * 4;
+            v[i] = f4add(*reinterpret_cast<const float4*>(res + (size_t)t * d + c),
+                         *reinterpret_cast<const float4*>(y + (size_t)t * d + c));
+        }
+    __syncwarp();
+    ln_row_store(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
+}
+
+// ffn = sum_j w_j * down[pos_j] (fmaf in slot order) + moe_bias; out = LN(cur + ffn)
+__global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int32_t* __restrict__ slot_pos,
+                                      const float* __restrict__ wts, int K, const float* __restrict__ moe_bias,
+                                      const float* cur, int M, int d, const float* __restrict__ gamma,
+                                      const float* __restrict__ beta, float eps, float* out32,
+                                      __half* __restrict__ out16) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= M) return;
+    const int nv = d / 128;
+    float4 acc[LN_MAXV];
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < K; ++j) {
+        const int p = slot_pos[(size_t)t * K + j];
+        const float w = wts[(size_t)t * K + j];
+#pragma unroll
+        for (int i = 0; i < LN_MAXV; ++i)
+            if (i < nv) {
+                const int c = (i * 32 + lane) * 4;
+                const float4 dv = *reinterpret_cast<const float4*>(down + (size_t)p * d + c);
+                acc[i].x = __fmaf_rn(w, dv.x, acc[i].x);
+                acc[i].y = __fmaf_rn(w, dv.y, acc[i].y);
+                acc[i].z = __fmaf_rn(w, dv.z, acc[i].z);
+                acc[i].w = __fmaf_rn(w, dv.w, acc[i].w);
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i)
+        if (i < nv) {
+            const int c = (i * 32 + lane) * 4;
+            if (moe_bias) acc[i] = f4add(acc[i], *reinterpret_cast<const float4*>(moe_bias + c));
+            acc[i] = f4add(*reinterpret_cast<const float4*>(cur + (size_t)t * d + c), acc[i]);
+        }
+    __syncwarp();
+    ln_row_store(acc, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
+}
+
+// ------------------------------------------------------------------ attention
+// One CTA = 64 queries of one (sequence, head); 4 warps x 16 query rows.
+// S = Q K^T and O = P V on mma.sync m16n8k16 (fp16 in, fp32 accumulate) with a
+// one-pass online softmax over 64-key tiles; keys beyond the sequence are masked.
+constexpr int AT_Q = 64, AT_K = 64, AT_HD = 64, AT_LD = 72;  // padded smem row (halfs)
+
+CEB_DEV void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+CEB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CEB_DEV void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+CEB_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+CEB_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+CEB_DEV void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, "
+        "%2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// load a 64-row x 64-col fp16 tile (rows beyond n_valid zero-filled)
+CEB_DEV void load_tile(__half* s, const __half* g, size_t g_ld, int n_valid, int tid) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int chunk = tid + i * 128;  // 512 chunks of 16 B
+        const int row = chunk >> 3, col = (chunk & 7) * 8;
+        const bool ok = row < n_valid;
+        const __half* src = g + (size_t)(ok ? row : 0) * g_ld + col;
+        cp_async16(smem_u32(s + row * AT_LD + col), src, ok ? 16 : 0);
+    }
+}
+
+__global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ cu,
+                                                        int d, float scale_log2, __half* __restrict__ out) {
+    __shared__ __align__(128) __half sQ[AT_Q * AT_LD];
+    __shared__ __align__(128) __half sK[2][AT_K * AT_LD];
+    __shared__ __align__(128) __half sV[2][AT_K * AT_LD];
+    const int seq = blockIdx.z, head = blockIdx.y;
+    const int start = cu[seq], len = cu[seq + 1] - start;
+    const int q0 = blockIdx.x * AT_Q;
+    if (q0 >= len) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t ld = (size_t)3 * d;
+    const __half* Qg = qkv + (size_t)(start + q0) * ld + head * AT_HD;
+    const __half* Kg = qkv + (size_t)start * ld + d + head * AT_HD;
+    const __half* Vg = qkv + (size_t)start * ld + 2 * d + head * AT_HD;
+    const int nq = min(AT_Q, len - q0);
+    const int n_kt = (len + AT_K - 1) / AT_K;
+
+    load_tile(sQ, Qg, ld, nq, tid);
+    load_tile(sK[0], Kg, ld, min(AT_K, len), tid);
+    load_tile(sV[0], Vg, ld, min(AT_K, len), tid);
+    cp_async_commit();
+
+    uint32_t qf[4][4];
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+    const int g = lane >> 2, tq = lane & 3;
+
+    for (int kt = 0; kt < n_kt; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < n_kt) {
+            const int k0n = (kt + 1) * AT_K;
+            load_tile(sK[buf ^ 1], Kg + (size_t)k0n * ld, ld, min(AT_K, len - k0n), tid);
+            load_tile(sV[buf ^ 1], Vg + (size_t)k0n * ld, ld, min(AT_K, len - k0n), tid);
+        }
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        if (kt == 0) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const int row = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                const int col = ks * 16 + 8 * (lane >> 4);
+                ldsm_x4(smem_u32(sQ + row * AT_LD + col), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+            }
+        }
+        // S = Q K^T for 64 keys: 8 n-tiles of 8 keys
+        float s[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+            for (int jp = 0; jp < 4; ++jp) {  // pairs of n-tiles
+                const int key = jp * 16 + (lane & 7) + 8 * (lane >> 4);
+                const int col = ks * 16 + 8 * ((lane >> 3) & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(smem_u32(sK[buf] + key * AT_LD + col), b0, b1, b2, b3);
+                mma16816(s[2 * jp], qf[ks], b0, b1);
+                mma16816(s[2 * jp + 1], qf[ks], b2, b3);
+            }
+        }
+        // mask + online softmax (rows g and g+8 of this warp)
+        const int kbase = kt * AT_K;
+        float mx[2] = {m_r[0], m_r[1]};
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = kbase + j * 8 + 2 * tq + (e & 1);
+                float v = s[j][e] * scale_log2;
+                if (key >= len) v = -INFINITY;
+                s[j][e] = v;
+                mx[e >> 1] = fmaxf(mx[e >> 1], v);
+            }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+        }
+        float corr[2], rs[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int r = 0; r < 2; ++r) corr[r] = exp2f(m_r[r] - mx[r]);
+        uint32_t pf[4][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float p0 = exp2f(s[j][0] - mx[0]), p1 = exp2f(s[j][1] - mx[0]);
+            float p2 = exp2f(s[j][2] - mx[1]), p3 = exp2f(s[j][3] - mx[1]);
+            rs[0] += p0 + p1;
+            rs[1] += p2 + p3;
+            const int kk = j >> 1, hi = j & 1;
+            pf[kk][hi * 2 + 0] = h2_as_u32(__floats2half2_rn(p0, p1));
+            pf[kk][hi * 2 + 1] = h2_as_u32(__floats2half2_rn(p2, p3));
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+            l_r[r] = l_r[r] * corr[r] + rs[r];
+            m_r[r] = mx[r];
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            o[i][0] *= corr[0];
+            o[i][1] *= corr[0];
+            o[i][2] *= corr[1];
+            o[i][3] *= corr[1];
+        }
+        // O += P V : k = 64 keys (4 steps of 16), n = 64 dims (8 tiles of 8)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                const int key = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                const int col = np * 16 + 8 * (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(smem_u32(sV[buf] + key * AT_LD + col), b0, b1, b2, b3);
+                mma16816(o[2 * np], a, b0, b1);
+                mma16816(o[2 * np + 1], a, b2, b3);
+            }
+        }
+        __syncthreads();
+    }
+    // normalise and store fp16
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int q = q0 + warp * 16 + g + 8 * r;
+        if (q >= len) continue;
+        const float inv = l_r[r] > 0.0f ? 1.0f / l_r[r] : 0.0f;
+        __half* dst = out + (size_t)(start + q) * d + head * AT_HD;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int col = i * 8 + 2 * tq;
+            *reinterpret_cast<__half2*>(dst + col) = __floats2half2_rn(o[i][2 * r] * inv, o[i][2 * r + 1] * inv);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ pooling
+// One CTA per sequence: mean over rows (row-parallel partial sums reduced in a
+// fixed order, so results are identical run to run), then L2 over out_dim.
+// mode 0 = mean over the sequence's rows, 1 = first row ([CLS]), 2 = last row.
+__global__ void pool_l2_kernel(const float* __restrict__ hidden, const int32_t* __restrict__ cu, int d, int out_dim,
+                               float* __restrict__ out, int mode) {
+    extern __shared__ float sp[];  // [d] pooled + [32] scratch
+    const int s = blockIdx.x;
+    const int r0 = cu[s], n = cu[s + 1] - cu[s];
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        if (mode == 0) {
+            float acc = 0.0f;
+            for (int t = 0; t < n; ++t) acc += hidden[(size_t)(r0 + t) * d + c];
+            sp[c] = n > 0 ? acc / (float)n : 0.0f;
+        } else {
+            sp[c] = n > 0 ? hidden[(size_t)(mode == 1 ? r0 : r0 + n - 1) * d + c] : 0.0f;
+        }
+    }
+    __syncthreads();
+    float part = 0.0f;
+    for (int c = threadIdx.x; c < out_dim; c += blockDim.x) part += sp[c] * sp[c];
+    part = wsum(part);
+    float* red = sp + d;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float tot = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+        red[31] = sqrtf(fmaxf(tot, 1e-12f));
+    }
+    __syncthreads();
+    const float norm = red[31];
+    for (int c = threadIdx.x; c < out_dim; c += blockDim.x) out[(size_t)s * out_dim + c] = sp[c] / norm;
+}
+
+}  // namespace
+
+int ceb_embed_ln(const int32_t* ids, const int32_t* cu, int n_seqs, int M, int d, int n_vocab, const float* tok,
+                 const float* pos, int n_pos, int pos_offset, const float* type0, const float* gamma,
+                 const float* beta, float eps, float* out32, __half* out16, int* err, cudaStream_t st) {
+    if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "embed: d=%d unsupported", d);
+    const int threads = 256, per = threads / 32;
+    embed_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(ids, cu, n_seqs, M, d, n_vocab, tok, pos, n_pos,
+                                                             pos_offset, type0, gamma, beta, eps, out32, out16, err);
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
+int ceb_add_ln(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
+               float* out32, __half* out16, cudaStream_t st) {
+    if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "add_ln: d=%d unsupported", d);
+    const int threads = 256, per = threads / 32;
+    add_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(res, y, M, d, gamma, beta, eps, out32, out16);
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
+int ceb_moe_combine_ln(const float* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
+                       const float* cur, int M, int d, const float* gamma, const float* beta, float eps, float* out32,
+                       __half* out16, cudaStream_t st) {
+    if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "combine: d=%d unsupported", d);
+    const int threads = 256, per = threads / 32;
+    moe_combine_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(down, slot_pos, wts, K, moe_bias, cur, M, d, gamma,
+                                                                   beta, eps, out32, out16);
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
+int ceb_attention(const __half* qkv, const int32_t* cu, int n_seqs, int max_len, int d, int n_head, __half* out,
+                  cudaStream_t st) {
+    if (n_head <= 0 || d % n_head || d / n_head != AT_HD)
+        return ceb_set_error(2, "attention: head_dim %d unsupported (64 only)", n_head > 0 ? d / n_head : -1);
+    if (n_seqs <= 0 || max_len <= 0) return 0;
+    const float scale_log2 = (1.0f / sqrtf((float)AT_HD)) * 1.4426950408889634f;
+    dim3 grid((max_len + AT_Q - 1) / AT_Q, n_head, n_seqs);
+    attention_kernel<<<grid, 128, 0, st>>>(qkv, cu, d, scale_log2, out);
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
+int ceb_pool_l2_launch(const float* hidden, const int32_t* cu, int n_seqs, int d, int out_dim, float* out,
+                       cudaStream_t st, int mode) {
+    if (n_seqs <= 0) return 0;
+    if (out_dim <= 0 || out_dim > d) return ceb_set_error(1, "pool: out_dim %d outside (0, %d]", out_dim, d);
+    const size_t smem = (size_t)(d + 32) * sizeof(float);
+    pool_l2_kernel<<<n_seqs, 256, smem, st>>>(hidden, cu, d, out_dim, out, mode);
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}

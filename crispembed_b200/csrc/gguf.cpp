@@ -1,0 +1,209 @@
+// gguf.cpp -- see gguf.h.  Layout: magic "GGUF", u32 version, u64 n_tensors,
+// u64 n_kv, kv pairs, tensor infos, padding to general.alignment (default 32),
+// tensor data.
+#include "gguf.h"
+
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cstring>
+
+namespace {
+enum { GT_U8, GT_I8, GT_U16, GT_I16, GT_U32, GT_I32, GT_F32, GT_BOOL, GT_STR, GT_ARR, GT_U64, GT_I64, GT_F64 };
+
+struct Cursor {
+    const uint8_t* p;
+    const uint8_t* end;
+    bool ok = true;
+    bool need(size_t n) {
+        if ((size_t)(end - p) < n) ok = false;
+        return ok;
+    }
+    template <typename T>
+    T rd() {
+        T v{};
+        if (!need(sizeof(T))) return v;
+        memcpy(&v, p, sizeof(T));
+        p += sizeof(T);
+        return v;
+    }
+    std::string str() {
+        uint64_t n = rd<uint64_t>();
+        if (!need(n)) return std::string();
+        std::string s(reinterpret_cast<const char*>(p), n);
+        p += n;
+        return s;
+    }
+};
+
+size_t scalar_size(int t) {
+    switch (t) {
+        case GT_U8: case GT_I8: case GT_BOOL: return 1;
+        case GT_U16: case GT_I16: return 2;
+        case GT_U32: case GT_I32: case GT_F32: return 4;
+        case GT_U64: case GT_I64: case GT_F64: return 8;
+    }
+    return 0;
+}
+
+double read_num(Cursor& c, int t) {
+    switch (t) {
+        case GT_U8: return c.rd<uint8_t>();
+        case GT_I8: return c.rd<int8_t>();
+        case GT_U16: return c.rd<uint16_t>();
+        case GT_I16: return c.rd<int16_t>();
+        case GT_U32: return c.rd<uint32_t>();
+        case GT_I32: return c.rd<int32_t>();
+        case GT_F32: return c.rd<float>();
+        case GT_BOOL: return c.rd<uint8_t>();
+        case GT_U64: return (double)c.rd<uint64_t>();
+        case GT_I64: return (double)c.rd<int64_t>();
+        case GT_F64: return c.rd<double>();
+    }
+    c.ok = false;
+    return 0;
+}
+
+uint64_t type_row_bytes(int type, int64_t ne0, bool* ok) {
+    switch (type) {
+        case 0: return (uint64_t)ne0 * 4;
+        case 1: return (uint64_t)ne0 * 2;
+        case 8: if (ne0 % 32) break; return (uint64_t)ne0 / 32 * 34;
+        case 12: if (ne0 % 256) break; return (uint64_t)ne0 / 256 * 144;
+        case 24: return (uint64_t)ne0;       // I8
+        case 26: return (uint64_t)ne0 * 4;   // I32
+        case 30: return (uint64_t)ne0 * 2;   // BF16
+    }
+    *ok = false;
+    return 0;
+}
+}  // namespace
+
+ceb_gguf::~ceb_gguf() {
+    if (base_) munmap(const_cast<uint8_t*>(base_), size_);
+}
+
+bool ceb_gguf::open(const std::string& path, std::string* err) {
+    int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) {
+        *err = "cannot open '" + path + "'";
+        return false;
+    }
+    struct stat st;
+    if (fstat(fd, &st) != 0 || st.st_size < 24) {
+        ::close(fd);
+        *err = "'" + path + "' is not a GGUF file";
+        return false;
+    }
+    void* m = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    ::close(fd);
+    if (m == MAP_FAILED) {
+        *err = "mmap failed for '" + path + "'";
+        return false;
+    }
+    base_ = static_cast<const uint8_t*>(m);
+    size_ = (size_t)st.st_size;
+    Cursor c{base_, base_ + size_};
+    if (memcmp(base_, "GGUF", 4) != 0) {
+        *err = "'" + path + "' has no GGUF magic";
+        return false;
+    }
+    c.p += 4;
+    const uint32_t version = c.rd<uint32_t>();
+    if (version != 2 && version != 3) {
+        *err = "unsupported GGUF version " + std::to_string(version);
+        return false;
+    }
+    const uint64_t n_tensors = c.rd<uint64_t>(), n_kv = c.rd<uint64_t>();
+    for (uint64_t i = 0; i < n_kv && c.ok; ++i) {
+        std::string key = c.str();
+        ceb_gguf_value v;
+        v.type = (int)c.rd<uint32_t>();
+        if (v.type == GT_STR) {
+            v.s = c.str();
+        } else if (v.type == GT_ARR) {
+            v.arr_type = (int)c.rd<uint32_t>();
+            const uint64_t n = c.rd<uint64_t>();
+            if (v.arr_type == GT_STR) {
+                if (n > size_) { c.ok = false; break; }
+                v.arr_str.reserve(n);
+                for (uint64_t j = 0; j < n && c.ok; ++j) v.arr_str.push_back(c.str());
+            } else {
+                const size_t es = scalar_size(v.arr_type);
+                if (!es || !c.need(n * es)) { c.ok = false; break; }
+                v.arr_num.resize(n);
+                for (uint64_t j = 0; j < n; ++j) v.arr_num[j] = read_num(c, v.arr_type);
+            }
+        } else {
+            const double x = read_num(c, v.type);
+            v.f = x;
+            v.u = (uint64_t)x;
+            v.i = (int64_t)x;
+        }
+        kv_[key] = std::move(v);
+    }
+    std::vector<ceb_gguf_tensor> infos;
+    for (uint64_t i = 0; i < n_tensors && c.ok; ++i) {
+        ceb_gguf_tensor t;
+        t.name = c.str();
+        const uint32_t nd = c.rd<uint32_t>();
+        if (nd == 0 || nd > 4) { c.ok = false; break; }
+        for (uint32_t j = 0; j < nd; ++j) t.ne.push_back((int64_t)c.rd<uint64_t>());
+        t.type = (int)c.rd<uint32_t>();
+        t.offset = c.rd<uint64_t>();
+        infos.push_back(t);
+    }
+    if (!c.ok) {
+        *err = "truncated or malformed GGUF header in '" + path + "'";
+        return false;
+    }
+    int align = 32;
+    get_u32("general.alignment", &align);
+    if (align <= 0) align = 32;
+    const uint64_t hdr = (uint64_t)(c.p - base_);
+    const uint64_t data0 = (hdr + align - 1) / align * align;
+    for (auto& t : infos) {
+        bool ok = true;
+        uint64_t rows = 1;
+        for (size_t j = 1; j < t.ne.size(); ++j) rows *= (uint64_t)t.ne[j];
+        t.nbytes = type_row_bytes(t.type, t.ne[0], &ok) * rows;
+        t.offset += data0;
+        if (!ok || t.offset + t.nbytes > size_) {
+            *err = "tensor '" + t.name + "' has an unsupported type or lies outside the file";
+            return false;
+        }
+        tensors_[t.name] = t;
+    }
+    return true;
+}
+
+const ceb_gguf_value* ceb_gguf::find(const std::string& key) const {
+    auto it = kv_.find(key);
+    return it == kv_.end() ? nullptr : &it->second;
+}
+
+bool ceb_gguf::get_u32(const std::string& key, int* v) const {
+    const ceb_gguf_value* x = find(key);
+    if (!x || x->type == GT_STR || x->type == GT_ARR) return false;
+    *v = (int)x->i;
+    return true;
+}
+
+bool ceb_gguf::get_f32(const std::string& key, float* v) const {
+    const ceb_gguf_value* x = find(key);
+    if (!x || x->type == GT_STR || x->type == GT_ARR) return false;
+    *v = (float)x->f;
+    return true;
+}
+
+std::string ceb_gguf::get_str(const std::string& key) const {
+    const ceb_gguf_value* x = find(key);
+    return (x && x->type == GT_STR) ? x->s : std::string();
+}
+
+const ceb_gguf_tensor* ceb_gguf::tensor(const std::string& name) const {
+    auto it = tensors_.find(name);
+    return it == tensors_.end() ? nullptr : &it->second;
+}

@@ -1,0 +1,260 @@
+"""Seeded synthetic NomicBERT-MoE models and inputs for the benchmark configs.
+
+There is no network in this environment, so the real nomic-embed-text-v2-moe
+checkpoint cannot be fetched.  This module writes a random-init model with the
+same architecture and the same GGUF layout as the reference converter
+(models/convert-bert-to-gguf.py, CrispEmbed-native ``enc.N.*`` names,
+``bert.*`` keys, experts stacked as numpy [E, F, d] / [E, d, F] per
+models/convert-bert-to-gguf.py:1056-1081):
+
+* token/position/type embeddings and all norms stay F32 (the converter writes
+  them with ``f32``), every linear weight uses the chosen block type (the
+  converter's ``wt``), biases stay F32;
+* linear weights and biases ~ N(0, 0.02); LayerNorm gamma ~ 1 + N(0, 0.02),
+  beta ~ N(0, 0.02), so the affine parts of every norm are exercised;
+* one ``numpy.random.default_rng(seed)`` stream, tensors drawn in file order
+  (recorded in ``general.fixture_order``).
+
+The vocabulary is a synthetic WordPiece list: ids 0-4 are [PAD] [CLS] [SEP]
+[UNK] [MASK], id i >= 5 is the 4-letter lowercase word spelling i-5 in base 26,
+so any id sequence can also be driven through the text ABI 1:1.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field, asdict
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+from . import gguf_io as G
+from .quant import quantize
+
+SPECIAL_TOKENS = ["[PAD]", "[CLS]", "[SEP]", "[UNK]", "[MASK]"]
+
+
+def vocab_word(i: int) -> str:
+    if i < len(SPECIAL_TOKENS):
+        return SPECIAL_TOKENS[i]
+    v = i - len(SPECIAL_TOKENS)
+    s = []
+    for _ in range(4):
+        s.append(chr(ord("a") + v % 26))
+        v //= 26
+    return "".join(reversed(s))
+
+
+@dataclass
+class ModelSpec:
+    n_vocab: int = 250048
+    n_ctx: int = 512
+    d: int = 768
+    n_head: int = 12
+    n_layer: int = 12
+    ffn: int = 3072          # dense FFN width
+    n_experts: int = 8
+    top_k: int = 2
+    expert_ffn: int = 3072
+    moe_every: int = 2       # MoE on layers il % moe_every == moe_every - 1 (1, 3, 5, ...)
+    type_vocab: int = 2
+    ln_eps: float = 1e-5
+    wtype: int = G.GGML_Q8_0  # linear-weight block type
+    router_wtype: Optional[int] = None  # None = same as wtype (the converter quantizes the router too)
+    moe_bias: bool = True
+    seed: int = 0
+
+    def is_moe(self, il: int) -> bool:
+        return self.n_experts > 0 and self.moe_every > 0 and il % self.moe_every == self.moe_every - 1
+
+
+def nomic_moe_spec(wtype: int = G.GGML_Q8_0) -> ModelSpec:
+    """BASELINE configs 1/2/4: shape of nomic-embed-text-v2-moe with learned positions."""
+    return ModelSpec(wtype=wtype)
+
+
+def tiny_spec(wtype: int = G.GGML_Q8_0, **kw) -> ModelSpec:
+    """Small model with the same structure, for tests that must finish in seconds."""
+    base = dict(n_vocab=1000, n_ctx=128, d=256, n_head=4, n_layer=4, ffn=512, n_experts=4, top_k=2,
+                expert_ffn=512, wtype=wtype)
+    base.update(kw)
+    return ModelSpec(**base)
+
+
+def write_model(path: str, spec: ModelSpec) -> List[str]:
+    """Write the synthetic GGUF; returns the tensor order."""
+    rng = np.random.default_rng(spec.seed)
+    w = G.GGUFWriter(path)
+    w.add_str("general.architecture", "nomic-bert-moe")
+    w.add_str("general.name", "crispembed-b200 synthetic nomic-bert-moe")
+    w.add_u32("bert.vocab_size", spec.n_vocab)
+    w.add_u32("bert.max_position_embeddings", spec.n_ctx)
+    w.add_u32("bert.hidden_size", spec.d)
+    w.add_u32("bert.num_attention_heads", spec.n_head)
+    w.add_u32("bert.num_hidden_layers", spec.n_layer)
+    w.add_u32("bert.intermediate_size", spec.ffn)
+    w.add_f32("bert.layer_norm_eps", spec.ln_eps)
+    w.add_u32("bert.pooling_method", 0)
+    if spec.n_experts > 0:
+        w.add_u32("bert.num_experts", spec.n_experts)
+        w.add_u32("bert.num_experts_per_tok", spec.top_k)
+    w.add_u32("tokenizer.ggml.type", 0)
+    w.add_str_array("tokenizer.ggml.tokens", [vocab_word(i) for i in range(spec.n_vocab)])
+    w.add_u32("tokenizer.ggml.padding_token_id", 0)
+    w.add_u32("tokenizer.ggml.cls_token_id", 1)
+    w.add_u32("tokenizer.ggml.sep_token_id", 2)
+    w.add_u32("tokenizer.ggml.unknown_token_id", 3)
+
+    order: List[str] = []
+    d, wt = spec.d, spec.wtype
+    rwt = spec.router_wtype if spec.router_wtype is not None else wt
+
+    def normal(shape, scale=0.02, loc=0.0):
+        a = rng.standard_normal(size=shape, dtype=np.float32)
+        a *= np.float32(scale)
+        if loc:
+            a += np.float32(loc)
+        return a
+
+    def add(name, np_shape, gtype, gen):
+        ne = tuple(reversed(np_shape))
+        order.append(name)
+        w.add_tensor(name, ne, gtype, lambda: quantize(gen(), gtype))
+
+    add("token_embd.weight", (spec.n_vocab, d), G.GGML_F32, lambda: normal((spec.n_vocab, d)))
+    add("position_embd.weight", (spec.n_ctx, d), G.GGML_F32, lambda: normal((spec.n_ctx, d)))
+    if spec.type_vocab > 0:
+        add("token_type_embd.weight", (spec.type_vocab, d), G.GGML_F32, lambda: normal((spec.type_vocab, d)))
+    add("embd_ln.weight", (d,), G.GGML_F32, lambda: normal((d,), loc=1.0))
+    add("embd_ln.bias", (d,), G.GGML_F32, lambda: normal((d,)))
+    for il in range(spec.n_layer):
+        p = f"enc.{il}."
+        for nm in ("q", "k", "v"):
+            add(p + f"attn.{nm}.weight", (d, d), wt, lambda: normal((d, d)))
+            add(p + f"attn.{nm}.bias", (d,), G.GGML_F32, lambda: normal((d,)))
+        add(p + "attn.o.weight", (d, d), wt, lambda: normal((d, d)))
+        add(p + "attn.o.bias", (d,), G.GGML_F32, lambda: normal((d,)))
+        add(p + "ln1.weight", (d,), G.GGML_F32, lambda: normal((d,), loc=1.0))
+        add(p + "ln1.bias", (d,), G.GGML_F32, lambda: normal((d,)))
+        if spec.is_moe(il):
+            E, Fm = spec.n_experts, spec.expert_ffn
+            add(p + "ffn.moe_gate.weight", (E, d), rwt, lambda: normal((E, d)))
+            add(p + "ffn.expert_fc1.weight", (E, Fm, d), wt, lambda: normal((E, Fm, d)))
+            add(p + "ffn.expert_fc2.weight", (E, d, Fm), wt, lambda: normal((E, d, Fm)))
+            if spec.moe_bias:
+                add(p + "ffn.moe_bias", (d,), G.GGML_F32, lambda: normal((d,)))
+        else:
+            F = spec.ffn
+            add(p + "ffn.fc1.weight", (F, d), wt, lambda: normal((F, d)))
+            add(p + "ffn.fc1.bias", (F,), G.GGML_F32, lambda: normal((F,)))
+            add(p + "ffn.fc2.weight", (d, F), wt, lambda: normal((d, F)))
+            add(p + "ffn.fc2.bias", (d,), G.GGML_F32, lambda: normal((d,)))
+        add(p + "ln2.weight", (d,), G.GGML_F32, lambda: normal((d,), loc=1.0))
+        add(p + "ln2.bias", (d,), G.GGML_F32, lambda: normal((d,)))
+    w.add_str("general.fixture_order", ",".join(order))
+    w.add_str("general.fixture_init", f"numpy default_rng({spec.seed}); N(0,0.02); LN gamma 1+N(0,0.02), beta N(0,0.02)")
+    w.write()
+    return order
+
+
+# ---------------------------------------------------------------------------
+# token-id batches (2, 4)
+# ---------------------------------------------------------------------------
+
+def ids_fixed(n_seqs: int, seq_len: int, seed: int, lo: int = 5, hi: int = 250000) -> Tuple[np.ndarray, np.ndarray]:
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(lo, hi, size=(n_seqs * seq_len,), dtype=np.int64).astype(np.int32)
+    lens = np.full((n_seqs,), seq_len, dtype=np.int32)
+    return ids, lens
+
+
+def ids_ragged(n_seqs: int, min_len: int, max_len: int, seed: int, lo: int = 5, hi: int = 250000):
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(min_len, max_len + 1, size=(n_seqs,), dtype=np.int64).astype(np.int32)
+    ids = rng.integers(lo, hi, size=(int(lens.sum()),), dtype=np.int64).astype(np.int32)
+    return ids, lens
+
+
+def config_ids(cfg: int, n_vocab: int = 250048):
+    """cfg 1: 8x128 seed 1; cfg 2: 256 seqs len U[32,512] seed 2; cfg 4: 512x512 seed 3."""
+    hi = min(250000, n_vocab)
+    if cfg == 1:
+        return ids_fixed(8, 128, seed=1, hi=hi)
+    if cfg == 2:
+        return ids_ragged(256, 32, 512, seed=2, hi=hi)
+    if cfg == 4:
+        return ids_fixed(512, 512, seed=3, hi=hi)
+    raise ValueError(cfg)
+
+
+# ---------------------------------------------------------------------------
+# isolated MoE operator inputs (BASELINE configs 3 and 5)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class MoEOpInputs:
+    d: int
+    n_experts: int
+    top_k: int
+    ffn: int
+    wtype: int
+    router_wtype: int
+    x: np.ndarray              # [T, d] float32 values exactly representable in bf16
+    router_raw: np.ndarray     # router weight blocks [E, row_bytes]
+    fc1_raw: np.ndarray        # [E, F, row_bytes(d)]
+    fc2_raw: np.ndarray        # [E, d, row_bytes(F)]
+    bias: Optional[np.ndarray]  # [d] or None
+    router_bias_logits: np.ndarray  # the logit shift b realised through x (see make_moe_op_inputs)
+    meta: Dict[str, object] = field(default_factory=dict)
+
+
+def _round_bf16(x: np.ndarray) -> np.ndarray:
+    """Round float32 to the nearest bfloat16 (ties to even) and return as float32."""
+    u = x.astype(np.float32).view(np.uint32)
+    r = ((u >> 16) & 1) + np.uint32(0x7FFF)
+    return ((u + r) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def zipf_shift(router_w: np.ndarray, top_k: int, s: float, rng: np.random.Generator, n_cal: int = 8192,
+               iters: int = 60) -> np.ndarray:
+    """Find logit offsets b so that top-k selection frequencies follow Zipf(s).
+
+    The reference router has no bias term (src/crispembed.cpp:1333), so the skew
+    is realised through the input: x = z + W^+ b gives W x = W z + b.
+    """
+    E, d = router_w.shape
+    target = 1.0 / np.arange(1, E + 1, dtype=np.float64) ** s
+    target = target / target.sum() * top_k
+    z = rng.standard_normal((n_cal, d)).astype(np.float32)
+    base = z @ router_w.T  # [n, E]
+    b = np.zeros(E, dtype=np.float64)
+    for _ in range(iters):
+        lg = base + b
+        top = np.argpartition(-lg, top_k - 1, axis=1)[:, :top_k]
+        cnt = np.bincount(top.reshape(-1), minlength=E) / n_cal
+        b += 0.5 * (np.log(target) - np.log(np.maximum(cnt, 1e-6)))
+        b -= b.mean()
+    return b.astype(np.float32)
+
+
+def make_moe_op_inputs(T: int, d: int = 768, n_experts: int = 8, top_k: int = 2, ffn: int = 3072,
+                       wtype: int = G.GGML_Q4_K, router_wtype: int = G.GGML_F32, zipf_s: Optional[float] = 1.2,
+                       seed: int = 0, with_bias: bool = False) -> MoEOpInputs:
+    rng = np.random.default_rng(seed)
+    router = (rng.standard_normal((n_experts, d), dtype=np.float32) * np.float32(0.02))
+    fc1 = (rng.standard_normal((n_experts, ffn, d), dtype=np.float32) * np.float32(0.02))
+    fc2 = (rng.standard_normal((n_experts, d, ffn), dtype=np.float32) * np.float32(0.02))
+    bias = (rng.standard_normal((d,), dtype=np.float32) * np.float32(0.02)) if with_bias else None
+    z = rng.standard_normal((T, d), dtype=np.float32)
+    if zipf_s:
+        b = zipf_shift(router, top_k, zipf_s, np.random.default_rng(seed + 1))
+        m = np.linalg.pinv(router.astype(np.float64)) @ b.astype(np.float64)
+        x = z + m.astype(np.float32)[None, :]
+    else:
+        b = np.zeros(n_experts, dtype=np.float32)
+        x = z
+    x = _round_bf16(x)
+    return MoEOpInputs(d=d, n_experts=n_experts, top_k=top_k, ffn=ffn, wtype=wtype, router_wtype=router_wtype,
+                       x=x, router_raw=quantize(router, router_wtype).view(np.uint8).reshape(n_experts, -1),
+                       fc1_raw=quantize(fc1, wtype).view(np.uint8).reshape(n_experts, ffn, -1),
+                       fc2_raw=quantize(fc2, wtype).view(np.uint8).reshape(n_experts, d, -1),
+                       bias=bias, router_bias_logits=b,
+                       meta=dict(T=T, seed=seed, zipf_s=zipf_s, init="N(0,0.02) weights, x=bf16(N(0,1)+W^+ b)"))

@@ -1,0 +1,112 @@
+/*
+ * ceb_ops.h -- operator-level C ABI of crispembed-b200 (sm_100a).
+ *
+ * These entry points expose, one by one, the device implementations of the
+ * operations CrispEmbed's NomicBERT-MoE encoder builds as ggml graph nodes, so a
+ * host that drives its own graph (or a test) can call them directly.  All
+ * pointers named d_* are device pointers, h_* host pointers; `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  Calls are
+ * asynchronous on `stream` unless stated otherwise.  Every function returns 0 on
+ * success and a nonzero status otherwise; ceb_last_error() then holds a message
+ * (also printed to stderr, the reference's error channel).
+ *
+ * Status codes: 1 bad argument / not supported, 2 unsupported shape,
+ * 3 CUDA error, 4 out of device memory, 5 device-side check failed.
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(CRISPEMBED_BUILD)
+#define CEB_API __attribute__((visibility("default")))
+#else
+#define CEB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml tensor types accepted for weights (values of ggml's enum) */
+#define CEB_TYPE_F32 0
+#define CEB_TYPE_F16 1
+#define CEB_TYPE_Q8_0 8
+#define CEB_TYPE_Q4_K 12
+
+/* activation element types */
+#define CEB_ACT_F32 0
+#define CEB_ACT_BF16 1
+#define CEB_ACT_F16 2
+
+typedef struct ceb_moe_layer ceb_moe_layer;
+
+/*
+ * Upload one MoE feed-forward block.  Host buffers hold ggml tensor bytes as a
+ * GGUF file stores them (the reference binds the same tensors in load_model,
+ * src/crispembed.cpp:838-844):
+ *   router  [n_experts rows x d]        (ffn.moe_gate.weight; F32 or Q8_0)
+ *   fc1     [n_experts][ffn rows x d]   (ffn.expert_fc1.weight; F32/F16/Q8_0/Q4_K)
+ *   fc2     [n_experts][d rows x ffn]   (ffn.expert_fc2.weight; same type as fc1)
+ *   bias    [d] floats or NULL          (ffn.moe_bias)
+ * Returns NULL on failure.  Limits: n_experts <= 32, top_k <= 4, d and ffn
+ * multiples of 128 (of 256 for Q4_K).
+ */
+CEB_API ceb_moe_layer* ceb_moe_layer_create(int d, int n_experts, int top_k, int ffn, int router_type,
+                                            const void* h_router, int expert_type, const void* h_fc1,
+                                            const void* h_fc2, const float* h_bias);
+CEB_API void ceb_moe_layer_free(ceb_moe_layer* layer);
+
+/* Bytes of device scratch ceb_moe_ffn needs for up to max_tokens tokens. */
+CEB_API size_t ceb_moe_workspace_size(const ceb_moe_layer* layer, int max_tokens);
+
+/*
+ * The MoE feed-forward block, replacing the graph branch of
+ * build_encoder_graph at src/crispembed.cpp:1327-1381:
+ *   y[t] = sum_j w[t,j] * fc2_{e_j}( gelu_erf( fc1_{e_j}( x[t] ) ) ) + bias,
+ *   (e_j, w[t,j]) = top_k(softmax(router x[t])), weights not renormalised.
+ * d_x: [n_tokens x d] activations of type x_dtype.  d_y: [n_tokens x d] floats.
+ * Optional outputs (may be NULL): d_ids / d_weights [n_tokens x top_k] (slot j =
+ * j-th largest probability), d_expert_counts [n_experts], d_logits
+ * [n_tokens x n_experts] router logits.  d_workspace: at least
+ * ceb_moe_workspace_size(layer, n_tokens) bytes, 256-byte aligned.
+ */
+CEB_API int ceb_moe_ffn(const ceb_moe_layer* layer, const void* d_x, int x_dtype, int n_tokens, float* d_y,
+                        int32_t* d_ids, float* d_weights, int32_t* d_expert_counts, float* d_logits, void* d_workspace,
+                        size_t workspace_bytes, void* stream);
+
+/*
+ * Mean pool + L2 normalise, replacing the host loops of encode_tokens
+ * (src/crispembed.cpp:1822-1846) and pool_and_norm (:2024-2045):
+ *   p = mean over the rows of each sequence; out = p / sqrt(max(sum p^2, 1e-12)).
+ * d_hidden [n_rows x d] floats; d_cu_seqlens [n_seqs+1] row offsets (int32);
+ * d_out [n_seqs x out_dim] with out_dim <= d: the first out_dim pooled values,
+ * normalised over those out_dim values (Matryoshka truncation,
+ * src/crispembed.cpp:2786-2793, when out_dim < d).
+ */
+CEB_API int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int n_seqs, int d, int out_dim,
+                        float* d_out, void* stream);
+
+/*
+ * One block-quantized matrix product on the tensor cores (the ggml_mul_mat of
+ * the encoder's dense layers): d_out[m, n] = sum_k W[n, k] * d_x[m, k] (+ bias[n]),
+ * optional erf-GELU.  h_w: GGUF bytes of W [n_out rows x k] (host); d_x: [m x k]
+ * fp16; d_out: [m x n_out], fp16 if out_f16 else float.  Synchronous (uploads W
+ * for the call).  n_out a multiple of 128, k a multiple of 64 (256 for Q4_K).
+ */
+CEB_API int ceb_matmul(int w_type, const void* h_w, int n_out, int k, const void* d_x, int m, const float* d_bias,
+                       int gelu, int out_f16, void* d_out, void* stream);
+
+/* Message of the last failing call on this thread ("" if none). */
+CEB_API const char* ceb_last_error(void);
+
+/*
+ * Synchronise `stream` and report any CUDA error or device-side check (a
+ * bounded wait that gave up, a bad group range) raised by this library's kernels
+ * since the last call.  Returns 0 when clean.
+ */
+CEB_API int ceb_sync_check(void* stream);
+
+#ifdef __cplusplus
+}
+#endif

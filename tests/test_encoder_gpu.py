@@ -1,0 +1,119 @@
+"""End-to-end embeddings through the C ABI against the ggml-faithful oracle.
+
+Bar: cosine >= 0.9999 and max-abs <= 2e-3 per embedding
+vector; repeat encodes bit-identical (reference tests/test_moe_parity.py:149-154).
+"""
+import numpy as np
+import pytest
+
+from crispembed_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+MAXABS = 2e-3
+
+
+def _check(emb, ref):
+    cos = (emb.astype(np.float64) * ref).sum(1) / (np.linalg.norm(emb, axis=1) * np.linalg.norm(ref, axis=1))
+    assert cos.min() >= COS_MIN, cos.min()
+    assert np.abs(emb - ref).max() <= MAXABS, np.abs(emb - ref).max()
+
+
+@pytest.fixture(scope="module")
+def model(cuda, tiny_model):
+    from crispembed_b200 import binding
+    m = binding.CrispEmbed(tiny_model)
+    yield m
+    m.close()
+
+
+def test_hparams(model):
+    h = model.hparams
+    assert (h.n_embd, h.n_layer, h.n_head, h.n_experts, h.n_experts_per_tok) == (256, 4, 4, 4, 2)
+    assert model.dim == 256
+
+
+def test_ids_match_oracle(model, oracle, tiny_model):
+    ids, lens = synth.ids_ragged(12, 1, 128, seed=4, hi=1000)
+    emb = model.encode_ids(ids, lens)
+    ref = oracle.encode(oracle.load_model(tiny_model), ids, lens, oracle.GGML)
+    _check(emb, ref)
+    assert np.allclose(np.linalg.norm(emb, axis=1), 1.0, atol=1e-5)
+
+
+def test_repeat_bit_identical(model):
+    ids, lens = synth.ids_ragged(5, 10, 90, seed=9, hi=1000)
+    a = model.encode_ids(ids, lens)
+    b = model.encode_ids(ids, lens)
+    assert np.array_equal(a, b)
+
+
+def test_batch_independent_of_packing(model):
+    """A sequence's embedding does not depend on what else is in the batch."""
+    ids, lens = synth.ids_ragged(6, 20, 100, seed=12, hi=1000)
+    full = model.encode_ids(ids, lens)
+    off = int(lens[:3].sum())
+    single = model.encode_ids(ids[off:off + lens[3]], lens[3:4])
+    cos = float((full[3] * single[0]).sum())
+    assert cos >= 0.99999
+
+
+def test_text_abi_matches_ids(model):
+    """Synthetic WordPiece vocab: every word maps to one id, wrapped in [CLS]/[SEP]."""
+    words = [synth.vocab_word(i) for i in (5, 6, 77, 500, 999)]
+    text = " ".join(words)
+    emb_t = model.encode(text)
+    ids = np.array([1, 5, 6, 77, 500, 999, 2], dtype=np.int32)
+    emb_i = model.encode_ids(ids, [len(ids)])[0]
+    assert np.array_equal(emb_t, emb_i)
+    batch = model.encode([text, words[0]])
+    assert batch.shape == (2, 256)
+    assert np.array_equal(batch[0], emb_t)
+
+
+def test_prefix_and_matryoshka(model, oracle):
+    w = synth.vocab_word
+    model.set_prefix(w(10) + " ")
+    a = model.encode(w(11))
+    model.set_prefix("")
+    b = model.encode(w(10) + " " + w(11))
+    assert np.array_equal(a, b)
+    full = model.encode(w(12) + " " + w(13))
+    small = model.encode(w(12) + " " + w(13), matryoshka_dim=64)
+    assert small.shape == (64,)
+    ref = full[:64] / np.linalg.norm(full[:64])
+    assert np.abs(small - ref).max() <= 1e-5
+
+
+def test_device_entry_matches_host_entry(model, cuda):
+    import torch
+    ids, lens = synth.ids_ragged(7, 3, 64, seed=21, hi=1000)
+    host = model.encode_ids(ids, lens)
+    d_ids = torch.from_numpy(ids).to(cuda)
+    out = torch.empty((len(lens), model.dim), dtype=torch.float32, device=cuda)
+    model.encode_ids_device(d_ids, lens, out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), host)
+
+
+def test_rejects_bad_input(model):
+    from crispembed_b200 import binding
+    with pytest.raises(binding.CrispEmbedError):
+        model.encode_ids(np.zeros(600, dtype=np.int32), [600])  # longer than n_max_tokens (128)
+
+
+@pytest.mark.parametrize("wtype_name", ["Q4_K", "F32"])
+def test_other_weight_types(cuda, oracle, tmp_path, wtype_name):
+    from crispembed_b200 import binding
+    from crispembed_b200.gguf_io import GGML_F32, GGML_Q4_K
+    wt = {"Q4_K": GGML_Q4_K, "F32": GGML_F32}[wtype_name]
+    spec = synth.tiny_spec(wtype=wt, router_wtype=GGML_F32)
+    path = str(tmp_path / f"tiny_{wtype_name}.gguf")
+    synth.write_model(path, spec)
+    m = binding.CrispEmbed(path)
+    ids, lens = synth.ids_ragged(5, 2, 100, seed=31, hi=1000)
+    emb = m.encode_ids(ids, lens)
+    m.close()
+    ref = oracle.encode(oracle.load_model(path), ids, lens, oracle.GGML)
+    _check(emb, ref)

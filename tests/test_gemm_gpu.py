@@ -1,0 +1,89 @@
+"""Grouped-GEMM kernel (tcgen05, weights dequantized into TMEM) against the oracle.
+
+The oracle's F16 mode rounds operands exactly as the kernel does (weights to
+fp16(dequant), activations fp16) and accumulates in double, so the remaining
+difference is fp32 accumulation order: tolerance 2e-4 of the output's max-abs.
+Reference product: ggml_mul_mat in build_encoder_graph (src/crispembed.cpp:1160-1416).
+"""
+import numpy as np
+import pytest
+
+from crispembed_b200 import quant
+from crispembed_b200.gguf_io import GGML_F16, GGML_F32, GGML_Q4_K, GGML_Q8_0
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # (w_type, n_out, k, m)
+    (GGML_Q8_0, 128, 64, 1),
+    (GGML_Q8_0, 256, 768, 5),
+    (GGML_Q8_0, 384, 768, 129),
+    (GGML_Q8_0, 768, 3072, 300),
+    (GGML_Q8_0, 128, 256, 1000),
+    (GGML_Q4_K, 256, 768, 77),
+    (GGML_Q4_K, 768, 3072, 256),
+    (GGML_F32, 256, 512, 200),
+    (GGML_F16, 128, 192, 33),
+]
+
+
+def _inputs(w_type, n_out, k, m, seed):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((n_out, k), dtype=np.float32) * 0.02).astype(np.float32)
+    raw = quant.quantize(w, w_type)
+    x = rng.standard_normal((m, k), dtype=np.float32).astype(np.float16)
+    bias = (rng.standard_normal(n_out, dtype=np.float32) * 0.02).astype(np.float32)
+    return raw, x, bias
+
+
+@pytest.mark.parametrize("w_type,n_out,k,m", CASES)
+def test_matmul_f32_out(cuda, oracle, w_type, n_out, k, m):
+    import torch
+    from crispembed_b200 import binding
+    raw, x, bias = _inputs(w_type, n_out, k, m, seed=n_out + k + m)
+    xd = torch.from_numpy(x).to(cuda)
+    out = binding.matmul(w_type, raw, n_out, k, xd).cpu().numpy()
+    ref = oracle.matmul(w_type, raw, n_out, k, x.astype(np.float32), oracle.F16)
+    tol = 2e-4 * max(1.0, float(np.abs(ref).max()))
+    assert np.abs(out - ref).max() <= tol, np.abs(out - ref).max()
+
+
+@pytest.mark.parametrize("w_type,n_out,k,m", [CASES[2], CASES[5], CASES[7]])
+def test_matmul_bias_gelu_f16_out(cuda, oracle, w_type, n_out, k, m):
+    import torch
+    from crispembed_b200 import binding
+    raw, x, bias = _inputs(w_type, n_out, k, m, seed=7 * m + 1)
+    xd = torch.from_numpy(x).to(cuda)
+    bd = torch.from_numpy(bias).to(cuda)
+    out = binding.matmul(w_type, raw, n_out, k, xd, bias=bd, gelu=True, out_f16=True).float().cpu().numpy()
+    ref = oracle.gelu_erf(oracle.matmul(w_type, raw, n_out, k, x.astype(np.float32), oracle.F16, bias=bias))
+    ref16 = ref.astype(np.float16).astype(np.float32)
+    tol = 2e-3 * max(1.0, float(np.abs(ref).max()))
+    assert np.abs(out - ref16).max() <= tol
+
+
+def test_matmul_repeatable(cuda):
+    import torch
+    from crispembed_b200 import binding
+    raw, x, _ = _inputs(GGML_Q8_0, 384, 768, 517, seed=3)
+    xd = torch.from_numpy(x).to(cuda)
+    a = binding.matmul(GGML_Q8_0, raw, 384, 768, xd).cpu().numpy()
+    b = binding.matmul(GGML_Q8_0, raw, 384, 768, xd).cpu().numpy()
+    assert np.array_equal(a, b)
+
+
+def test_matmul_zero_rows(cuda):
+    import torch
+    from crispembed_b200 import binding
+    raw, x, _ = _inputs(GGML_Q8_0, 128, 64, 1, seed=1)
+    out = binding.matmul(GGML_Q8_0, raw, 128, 64, torch.zeros((0, 64), dtype=torch.float16, device=cuda))
+    assert out.shape == (0, 128)
+
+
+def test_matmul_rejects_bad_shape(cuda):
+    import torch
+    from crispembed_b200 import binding
+    raw, x, _ = _inputs(GGML_Q8_0, 128, 64, 4, seed=1)
+    xd = torch.from_numpy(x).to(cuda)
+    with pytest.raises(binding.CrispEmbedError):
+        binding.matmul(GGML_Q8_0, quant.quantize(np.zeros((96, 64), np.float32), GGML_Q8_0), 96, 64, xd)

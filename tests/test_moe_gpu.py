@@ -1,0 +1,115 @@
+"""MoE feed-forward operator (ceb_moe_ffn) against the CPU oracle.
+
+Reference: the MoE branch of build_encoder_graph, src/crispembed.cpp:1327-1381.
+Checks, per BASELINE's bar:
+  * router logits bit-identical to the ggml-faithful oracle for Q8_0 routers
+    (x re-quantized to Q8_0, integer block dots in ggml's lane order);
+  * expert ids bit-exact wherever the k-th/(k+1)-th logit gap exceeds 1e-4;
+  * expert math within 1e-3 (of max-abs) of the oracle computed with the same
+    routing and the kernels' operand precision (F16 mode), and cos >= 0.999 per
+    token against the ggml-faithful oracle;
+  * repeat calls bit-identical (tests/test_moe_parity.py:149-154 of the reference).
+"""
+import numpy as np
+import pytest
+
+from crispembed_b200 import synth
+from crispembed_b200.gguf_io import GGML_F32, GGML_Q4_K, GGML_Q8_0
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = {
+    "q8_small": dict(T=300, d=256, n_experts=4, top_k=2, ffn=512, wtype=GGML_Q8_0, router_wtype=GGML_Q8_0,
+                     zipf_s=None, with_bias=True),
+    "c3_zipf": dict(T=512, d=768, n_experts=8, top_k=2, ffn=3072, wtype=GGML_Q4_K, router_wtype=GGML_F32,
+                    zipf_s=1.2, with_bias=False),
+    "c3_q8router": dict(T=257, d=768, n_experts=8, top_k=2, ffn=3072, wtype=GGML_Q8_0, router_wtype=GGML_Q8_0,
+                        zipf_s=1.2, with_bias=True),
+    "c5_wide": dict(T=200, d=1024, n_experts=32, top_k=4, ffn=1536, wtype=GGML_Q4_K, router_wtype=GGML_F32,
+                    zipf_s=None, with_bias=False),
+    "c5_zipf": dict(T=129, d=1024, n_experts=32, top_k=4, ffn=1536, wtype=GGML_Q4_K, router_wtype=GGML_F32,
+                    zipf_s=1.5, with_bias=False),
+    "one_token": dict(T=1, d=256, n_experts=4, top_k=2, ffn=256, wtype=GGML_Q8_0, router_wtype=GGML_Q8_0,
+                      zipf_s=None, with_bias=True),
+    "skew_empty": dict(T=33, d=256, n_experts=8, top_k=2, ffn=256, wtype=GGML_Q8_0, router_wtype=GGML_Q8_0,
+                       zipf_s=3.0, with_bias=False),
+}
+
+
+def _run(cuda, inp, x_dtype="bf16", repeat=1):
+    import torch
+    from crispembed_b200 import binding
+    layer = binding.MoELayer(inp.d, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
+                             inp.fc1_raw, inp.fc2_raw, inp.bias)
+    T = inp.x.shape[0]
+    tdt = {"bf16": torch.bfloat16, "f32": torch.float32, "f16": torch.float16}[x_dtype]
+    x = torch.from_numpy(inp.x).to(cuda).to(tdt)
+    ws = torch.empty(layer.workspace_size(T), dtype=torch.uint8, device=cuda)
+    outs = []
+    for _ in range(repeat):
+        y = torch.empty((T, inp.d), dtype=torch.float32, device=cuda)
+        ids = torch.empty((T, inp.top_k), dtype=torch.int32, device=cuda)
+        w = torch.empty((T, inp.top_k), dtype=torch.float32, device=cuda)
+        cnt = torch.empty((inp.n_experts,), dtype=torch.int32, device=cuda)
+        lg = torch.empty((T, inp.n_experts), dtype=torch.float32, device=cuda)
+        layer.forward(x, y, ws, ids=ids, weights=w, counts=cnt, logits=lg)
+        binding.sync_check()
+        outs.append(tuple(t.cpu().numpy() for t in (y, ids, w, cnt, lg)))
+    layer.close()
+    return outs
+
+
+def _kth_gap(logits, k):
+    s = np.sort(logits, axis=1)[:, ::-1]
+    return s[:, k - 1] - s[:, k] if logits.shape[1] > k else np.full(logits.shape[0], np.inf)
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_moe_matches_oracle(cuda, oracle, name):
+    cfg = dict(CONFIGS[name])
+    T = cfg.pop("T")
+    inp = synth.make_moe_op_inputs(T, seed=11, **cfg)
+    (y, ids, w, cnt, lg), = _run(cuda, inp)
+    x = inp.x
+    ry, rids, rw, rlg = oracle.moe_ffn(x, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw,
+                                       inp.wtype, inp.fc1_raw, inp.fc2_raw, inp.bias, oracle.GGML)
+    # router logits
+    if inp.router_wtype == GGML_Q8_0:
+        assert np.array_equal(lg, rlg), np.abs(lg - rlg).max()
+    else:
+        assert np.allclose(lg, rlg, rtol=1e-5, atol=1e-5)
+    # routing: bit-exact where the k-th / (k+1)-th logit gap exceeds 1e-4
+    gap = _kth_gap(rlg, inp.top_k)
+    sure = gap > 1e-4
+    assert np.array_equal(ids[sure], rids[sure])
+    assert np.allclose(w[sure], rw[sure], rtol=1e-5, atol=1e-7)
+    assert np.array_equal(cnt, np.bincount(ids.reshape(-1), minlength=inp.n_experts))
+    # expert math at kernel precision on the kernel's own routing
+    fy, _, _, _ = oracle.moe_ffn(x, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
+                                 inp.fc1_raw, inp.fc2_raw, inp.bias, oracle.F16, ids_in=ids, wts_in=w)
+    scale = max(1e-3, float(np.abs(fy).max()))
+    assert np.abs(y - fy).max() <= 1e-3 * scale, np.abs(y - fy).max() / scale
+    # against the ggml-faithful oracle (q8 activations) on tokens routed identically
+    same = np.all(ids == rids, axis=1)
+    a, b = y[same].astype(np.float64), ry[same].astype(np.float64)
+    cos = (a * b).sum(1) / np.maximum(np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1), 1e-30)
+    assert cos.min() >= 0.999, cos.min()
+
+
+def test_moe_repeat_bit_identical(cuda):
+    inp = synth.make_moe_op_inputs(700, d=768, n_experts=8, top_k=2, ffn=3072, wtype=GGML_Q8_0,
+                                   router_wtype=GGML_Q8_0, zipf_s=1.2, seed=5, with_bias=True)
+    r = _run(cuda, inp, repeat=2)
+    for a, b in zip(r[0], r[1]):
+        assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16"])
+def test_moe_input_dtypes(cuda, oracle, dtype):
+    inp = synth.make_moe_op_inputs(96, d=256, n_experts=4, top_k=2, ffn=512, wtype=GGML_Q8_0,
+                                   router_wtype=GGML_Q8_0, zipf_s=None, seed=2, with_bias=True)
+    (y, ids, w, cnt, lg), = _run(cuda, inp, x_dtype=dtype)
+    (yb, idsb, _, _, _), = _run(cuda, inp, x_dtype="bf16")
+    # x holds bf16-representable values, exactly representable in f32 and (at this range) f16
+    assert np.array_equal(ids, idsb)
+    assert np.abs(y - yb).max() <= 1e-6 * max(1.0, np.abs(yb).max())
