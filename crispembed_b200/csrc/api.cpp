@@ -483,6 +483,7 @@ extern "C" int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, i
 
 extern "C" int ceb_matmul(int w_type, const void* h_w, int n_out, int k, const void* d_x, int m, const float* d_bias,
                           int gelu, int out_f16, void* d_out, void* stream) {
+    if (m == 0) return 0;
     if (!h_w || !d_x || !d_out || m < 0) return ceb_set_error(1, "matmul: bad arguments");
     int* err = op_err_word();
     if (!err) return ceb_set_error(4, "out of device memory");
