@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""MoE-encoder throughput on B200 -- one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c3]
+
+Workloads (inputs synthetic and seeded, weights random-init
+of the nomic-embed-text-v2-moe architecture, see crispembed_b200/synth.py):
+  c2 (default)  NomicBERT-MoE encoder, Q8_0 GGUF, 256 sequences with lengths
+                U[32,512] (seed 2, 70825 tokens) per step; one step = embed,
+                12 layers (6 MoE), mean-pool + L2 of the whole batch.
+  c3            the isolated MoE FFN operator, Q4_K experts, T=65536 bf16 tokens,
+                Zipf(1.2) expert loads (seed 0).
+
+value  : tokens/s of the whole job with ids already in HBM (device entry point,
+         CUDA events on the launching stream, max over ranks).
+e2e    : same metric through the host-buffer C-ABI call (crispembed_encode_ids_batch:
+         ids copied host->device and embeddings device->host inside the timed call).
+Multi-GPU (torchrun): data-parallel replicas, every rank encodes its own copy of
+the config-2 batch (weak scaling, no collective on the data path).
+--impl reference: the CPU restatement of the reference's ggml CPU path (oracle/,
+the reference itself cannot be built here) on all host threads, bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE-encoder tokens/s/GPU (Q8_0, 1/2/4/8 B200); grouped-GEMM TC util %"
+CACHE = os.environ.get("CEB_BENCH_CACHE", "/tmp/crispembed_b200_bench")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def model_path(rank_local: int) -> str:
+    """config-2 model (Q8_0), written once per box; other local ranks wait for it."""
+    from crispembed_b200 import synth
+    os.makedirs(CACHE, exist_ok=True)
+    path = os.path.join(CACHE, "nomic_moe_q8_0_seed0.gguf")
+    if os.path.exists(path):
+        return path
+    if rank_local == 0:
+        tmp = path + f".tmp{os.getpid()}"
+        t = time.time()
+        synth.write_model(tmp, synth.nomic_moe_spec())
+        os.replace(tmp, path)
+        log(f"[bench] wrote {path} in {time.time() - t:.1f}s")
+    else:
+        t0 = time.time()
+        while not os.path.exists(path):
+            if time.time() - t0 > 600:
+                raise RuntimeError("timed out waiting for the model file")
+            time.sleep(1.0)
+    return path
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self._t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(path, ids, lens, budget_s=15.0):
+    """Oracle (CPU restatement of ggml's CPU path) on the first sequences of the batch."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = O.set_threads(os.cpu_count() or 1)
+    m = O.load_model(path)
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    done_tok, n, t0 = 0, 0, time.perf_counter()
+    while n < len(lens) and (time.perf_counter() - t0) < budget_s:
+        O.encode(m, ids[cu[n]:cu[n + 1]], lens[n:n + 1], O.GGML)
+        done_tok += int(lens[n])
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": done_tok / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"first {n} sequences ({done_tok} tokens) of the config-2 batch, one encode per sequence "
+                      f"as the reference's sequential path does, ggml-faithful mode, {dt:.1f}s"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    from crispembed_b200 import synth
+    path = model_path(0)
+    ids, lens = synth.config_ids(2)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = O.set_threads(os.cpu_count() or 1)
+    m = O.load_model(path)
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    per_step = 2  # sequences per step: bounded sample of the config-2 batch
+    times, toks = [], []
+    for s in range(args.warmup + args.steps):
+        a = (s * per_step) % len(lens)
+        b = min(a + per_step, len(lens))
+        t0 = time.perf_counter()
+        for q in range(a, b):
+            O.encode(m, ids[cu[q]:cu[q + 1]], lens[q:q + 1], O.GGML)
+        dt = time.perf_counter() - t0
+        if s >= args.warmup:
+            times.append(dt)
+            toks.append(int(lens[a:b].sum()))
+    value = sum(toks) / sum(times)
+    sample = (f"{per_step} sequences per step of the config-2 batch (lens U[32,512] seed 2), encoded one by one "
+              f"(the reference's sequential encode_tokens path), oracle ggml-faithful CPU restatement")
+    out = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8 blocks / f32",
+           "data": "synthetic", "config": {"workload": "c2 NomicBERT-MoE Q8_0 encoder (bounded CPU sample)",
+                                           "tokens_per_step": float(np.mean(toks))},
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "reference ggml cannot be built here (empty submodule); CPU restatement in oracle/ timed instead"}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def traffic_from_profile(workload):
+    p = os.path.join(ROOT, "profiles", f"gemm_traffic_{workload}.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c3"], default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+    from crispembed_b200 import binding, synth
+
+    path = model_path(local) if args.workload == "c2" else None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    if args.workload == "c3":
+        return bench_moe_op(args, rank, world, local)
+
+    ids, lens = synth.config_ids(2)
+    n_seqs, tokens = len(lens), int(lens.sum())
+    m = binding.CrispEmbed(path)
+    dim = m.dim
+    d_ids = torch.from_numpy(ids).cuda()
+    out = torch.empty((n_seqs, dim), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        m.encode_ids_device(d_ids, lens, out)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    n0 = binding.launch_count()
+    binding.profile_enable(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            m.encode_ids_device(d_ids, lens, out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = binding.launch_count() - n0
+    prof = binding.profile_read()
+    binding.profile_enable(False)
+    binding.sync_check()
+    t = ev0.elapsed_time(ev1) / 1000.0
+    if dist:
+        tt = torch.tensor([t], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+        dist.barrier()
+    value = world * tokens * args.steps / t
+
+    # end to end through the host-buffer C ABI (ids H2D and embeddings D2H inside)
+    for _ in range(2):
+        m.encode_ids(ids, lens)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        emb = m.encode_ids(ids, lens)
+    te = time.perf_counter() - t0
+    if dist:
+        tt = torch.tensor([te], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        te = float(tt.item())
+    e2e = world * tokens * args.steps / te
+    assert np.allclose(np.linalg.norm(emb, axis=1), 1.0, atol=1e-4)
+    m.close()
+
+    pk, pk_src = peaks()
+    g = prof["gemm"]
+    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
+    peak = float(pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    tr = traffic_from_profile("c2")
+    per_launch_flops = g["flops"] / max(1, g["launches"])
+    result = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * t / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 (Q8_0 weights dequantized to fp16, fp32 accumulate)",
+        "data": "synthetic (seeded ids; random-init weights of the nomic-embed-text-v2-moe architecture)",
+        "config": {"workload": f"c2: NomicBERT-MoE Q8_0 encoder, {n_seqs} seqs len U[32,512] seed 2 per rank",
+                   "tokens_per_step_per_gpu": tokens, "global_batch": n_seqs * world, "seq_len": "U[32,512]",
+                   "parallelism": f"dp{world} replicas", "l2": "inputs larger than L2 (~3 GB activations/step)"},
+        "per_gpu_tokens_per_s": value / world,
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(ids.nbytes),
+                "d2h_bytes_per_step": int(n_seqs * dim * 4)},
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "ceb_gemm_kernel (grouped tcgen05 GEMM, all linear layers)", "bound": "tensor",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{pk_src} bf16_tflops_sustained", "launches": g["launches"],
+                     "flops_per_launch": per_launch_flops, "avg_launch_ms": g["ms"] / max(1, g["launches"]),
+                     "traffic": (tr or {}).get("bytes_per_launch"),
+                     "traffic_source": (tr or {}).get("source")},
+        "breakdown_ms_per_step": {k: v["ms"] / args.steps for k, v in prof.items()},
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(path, ids, lens)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def bench_moe_op(args, rank, world, local):
+    """isolated MoE FFN operator, Q4_K experts, T=65536, Zipf 1.2."""
+    import torch
+
+    from crispembed_b200 import binding, synth
+    from crispembed_b200.gguf_io import GGML_F32, GGML_Q4_K
+    T = 65536
+    inp = synth.make_moe_op_inputs(T, d=768, n_experts=8, top_k=2, ffn=3072, wtype=GGML_Q4_K, router_wtype=GGML_F32,
+                                   zipf_s=1.2, seed=0)
+    layer = binding.MoELayer(inp.d, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
+                             inp.fc1_raw, inp.fc2_raw, inp.bias)
+    x = torch.from_numpy(inp.x).cuda().to(torch.bfloat16)
+    y = torch.empty((T, inp.d), dtype=torch.float32, device="cuda")
+    ws = torch.empty(layer.workspace_size(T), dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        layer.forward(x, y, ws)
+    torch.cuda.synchronize()
+    binding.profile_enable(True)
+    n0 = binding.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            layer.forward(x, y, ws)
+        ev1.record()
+        torch.cuda.synchronize()
+    prof = binding.profile_read()
+    binding.profile_enable(False)
+    launches = binding.launch_count() - n0
+    t = ev0.elapsed_time(ev1) / 1000.0
+    value = T * args.steps / t
+    pk, pk_src = peaks()
+    g = prof["gemm"]
+    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12
+    peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    result = {"metric": "MoE FFN operator tokens/s (Q4_K, T=65536, Zipf 1.2)", "value": value, "unit": "tokens/s",
+              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * t / args.steps,
+              "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (Q4_K dequant)",
+              "data": "synthetic", "config": {"workload": "c3 MoE op d=768 E=8 k=2 F=3072 T=65536 bf16 x"},
+              "gpu_launches": int(launches),
+              "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                           "frac": achieved / peak, "peak_source": f"{pk_src} bf16_tflops (burst)",
+                           "traffic": None},
+              "breakdown_ms_per_step": {k: v["ms"] / args.steps for k, v in prof.items()},
+              "clocks": clk.summary()}
+    layer.close()
+    print(json.dumps(result), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

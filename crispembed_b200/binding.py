@@ -74,6 +74,11 @@ def load_library(path: Optional[str] = None):
         "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_matmul": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
                         ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_launch_count": ([], ctypes.c_longlong),
+        "ceb_profile_enable": ([ctypes.c_int], None),
+        "ceb_profile_read": ([ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_double),
+                              ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), ctypes.c_int],
+                             ctypes.c_int),
         "ceb_last_error": ([], cp),
         "ceb_sync_check": ([vp], ctypes.c_int),
     }
@@ -247,3 +252,23 @@ def pool_l2(hidden, cu_seqlens, out_dim: Optional[int] = None, stream=None):
 
 def sync_check(stream=None):
     _check(load_library().ceb_sync_check(_stream_ptr(stream)), "device check")
+
+
+PROFILE_CATEGORIES = ("gemm", "attention", "routing", "rowwise")
+
+
+def launch_count() -> int:
+    return int(load_library().ceb_launch_count())
+
+
+def profile_enable(on: bool = True):
+    load_library().ceb_profile_enable(int(on))
+
+
+def profile_read() -> dict:
+    n = len(PROFILE_CATEGORIES)
+    L = (ctypes.c_longlong * n)()
+    ms, fl, by = (ctypes.c_double * n)(), (ctypes.c_double * n)(), (ctypes.c_double * n)()
+    _check(load_library().ceb_profile_read(L, ms, fl, by, n), "ceb_profile_read")
+    return {c: dict(launches=int(L[i]), ms=float(ms[i]), flops=float(fl[i]), bytes=float(by[i]))
+            for i, c in enumerate(PROFILE_CATEGORIES)}

@@ -65,3 +65,25 @@ int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int
 void ceb_wplane_free(ceb_wplane* w);
 
 int ceb_num_sms();
+
+// ---- launch accounting and optional per-category CUDA-event timing ---------
+enum ceb_prof_cat : int {
+    CEB_PROF_GEMM = 0,
+    CEB_PROF_ATTN = 1,
+    CEB_PROF_ROUTE = 2,   // router + histogram/scan + permutation
+    CEB_PROF_ROWWISE = 3, // embedding, residual+LN, combine+LN, pooling
+    CEB_PROF_NCAT = 4,
+};
+// Counts one kernel launch; when profiling is on, records a start event on `st`.
+int ceb_prof_begin(cudaStream_t st, int cat);
+// Records the stop event of the token returned by ceb_prof_begin (no-op for -1)
+// with the launch's algorithmic flops / bytes.
+void ceb_prof_end(int token, cudaStream_t st, double flops, double bytes);
+
+// Wraps one kernel launch statement with ceb_prof_begin / ceb_prof_end.
+#define CEB_LAUNCH(cat, st, flops, bytes, ...)          \
+    do {                                                \
+        const int tk__ = ceb_prof_begin((st), (cat));   \
+        __VA_ARGS__;                                    \
+        ceb_prof_end(tk__, (st), (flops), (bytes));     \
+    } while (0)

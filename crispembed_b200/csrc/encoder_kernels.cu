@@ -408,8 +408,8 @@ int ceb_embed_ln(const int32_t* ids, const int32_t* cu, int n_seqs, int M, int d
                  const float* beta, float eps, float* out32, __half* out16, int* err, cudaStream_t st) {
     if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "embed: d=%d unsupported", d);
     const int threads = 256, per = threads / 32;
-    embed_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(ids, cu, n_seqs, M, d, n_vocab, tok, pos, n_pos,
-                                                             pos_offset, type0, gamma, beta, eps, out32, out16, err);
+    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, embed_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(ids, cu, n_seqs, M, d, n_vocab, tok, pos, n_pos,
+                                                             pos_offset, type0, gamma, beta, eps, out32, out16, err));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
@@ -418,7 +418,7 @@ int ceb_add_ln(const float* res, const float* y, int M, int d, const float* gamm
                float* out32, __half* out16, cudaStream_t st) {
     if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "add_ln: d=%d unsupported", d);
     const int threads = 256, per = threads / 32;
-    add_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(res, y, M, d, gamma, beta, eps, out32, out16);
+    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, add_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(res, y, M, d, gamma, beta, eps, out32, out16));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
@@ -428,8 +428,8 @@ int ceb_moe_combine_ln(const float* down, const int32_t* slot_pos, const float* 
                        __half* out16, cudaStream_t st) {
     if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "combine: d=%d unsupported", d);
     const int threads = 256, per = threads / 32;
-    moe_combine_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(down, slot_pos, wts, K, moe_bias, cur, M, d, gamma,
-                                                                   beta, eps, out32, out16);
+    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, moe_combine_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(down, slot_pos, wts, K, moe_bias, cur, M, d, gamma,
+                                                                   beta, eps, out32, out16));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
@@ -441,7 +441,7 @@ int ceb_attention(const __half* qkv, const int32_t* cu, int n_seqs, int max_len,
     if (n_seqs <= 0 || max_len <= 0) return 0;
     const float scale_log2 = (1.0f / sqrtf((float)AT_HD)) * 1.4426950408889634f;
     dim3 grid((max_len + AT_Q - 1) / AT_Q, n_head, n_seqs);
-    attention_kernel<<<grid, 128, 0, st>>>(qkv, cu, d, scale_log2, out);
+    CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_kernel<<<grid, 128, 0, st>>>(qkv, cu, d, scale_log2, out));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
@@ -451,7 +451,7 @@ int ceb_pool_l2_launch(const float* hidden, const int32_t* cu, int n_seqs, int d
     if (n_seqs <= 0) return 0;
     if (out_dim <= 0 || out_dim > d) return ceb_set_error(1, "pool: out_dim %d outside (0, %d]", out_dim, d);
     const size_t smem = (size_t)(d + 32) * sizeof(float);
-    pool_l2_kernel<<<n_seqs, 256, smem, st>>>(hidden, cu, d, out_dim, out, mode);
+    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, pool_l2_kernel<<<n_seqs, 256, smem, st>>>(hidden, cu, d, out_dim, out, mode));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }

@@ -420,18 +420,23 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
     if ((reinterpret_cast<uintptr_t>(act_f16) & 15) != 0) return ceb_set_error(2, "gemm: activations not 16-B aligned");
     if (act_rows <= 0) return 0;
     CUtensorMap map;
-    int rc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);
-    if (rc) return rc;
+    const int mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);
+    if (mrc) return mrc;
     const int n_ftiles = w.n_out / BM;
     const int groups = a.offsets ? w.n_groups : 1;
     long long bound = (long long)n_ftiles * ((act_rows + BN - 1) / BN + groups);
     int grid = ceb_num_sms();
     if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
     if (bound < grid) grid = (int)bound;
+    const double flops = 2.0 * (double)a.m_rows * w.n_out * w.k;
+    const double bytes = (double)(w.q_bytes + w.s_bytes) + (double)a.m_rows * w.k * 2 +
+                         (double)a.m_rows * w.n_out * ((a.epi & CEB_EPI_F16_OUT) ? 2 : 4);
+    int rc = 0;
     switch (w.format) {
-        case CEB_W_Q8_0: return launch_fmt<CEB_W_Q8_0>(map, w, a, grid, stream);
-        case CEB_W_Q4_K: return launch_fmt<CEB_W_Q4_K>(map, w, a, grid, stream);
-        case CEB_W_F16: return launch_fmt<CEB_W_F16>(map, w, a, grid, stream);
+        case CEB_W_Q8_0: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q8_0>(map, w, a, grid, stream)); break;
+        case CEB_W_Q4_K: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q4_K>(map, w, a, grid, stream)); break;
+        case CEB_W_F16: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_F16>(map, w, a, grid, stream)); break;
+        default: return ceb_set_error(2, "gemm: unknown weight format %d", w.format);
     }
-    return ceb_set_error(2, "gemm: unknown weight format %d", w.format);
+    return rc;
 }

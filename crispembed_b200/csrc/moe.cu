@@ -296,30 +296,30 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, fl
     const int nblk = (T + CHUNK - 1) / CHUNK;
     const size_t route_smem = MAXE * 4 + (size_t)ROUTE_WARPS * d + (size_t)ROUTE_WARPS * (d / 32) * 2;
     if (x_dtype == CEB_ACT_F32) {
-        route_kernel<float><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>((const float*)x, T, d, E, K, mw.router_type,
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, route_kernel<float><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>((const float*)x, T, d, E, K, mw.router_type,
                                                                         mw.router, ws.ids, ws.wts, logits_out,
-                                                                        ws.block_counts);
+                                                                        ws.block_counts));
     } else if (x_dtype == CEB_ACT_BF16) {
-        route_kernel<__nv_bfloat16><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>(
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, route_kernel<__nv_bfloat16><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>(
             (const __nv_bfloat16*)x, T, d, E, K, mw.router_type, mw.router, ws.ids, ws.wts, logits_out,
-            ws.block_counts);
+            ws.block_counts));
     } else {
-        route_kernel<__half><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>((const __half*)x, T, d, E, K, mw.router_type,
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, route_kernel<__half><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>((const __half*)x, T, d, E, K, mw.router_type,
                                                                          mw.router, ws.ids, ws.wts, logits_out,
-                                                                         ws.block_counts);
+                                                                         ws.block_counts));
     }
     CEB_CUDA_OK(cudaGetLastError());
-    scan_kernel<<<1, 64, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts);
+    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scan_kernel<<<1, 64, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts));
     CEB_CUDA_OK(cudaGetLastError());
     if (x_dtype == CEB_ACT_F32)
-        scatter_kernel<float><<<nblk, 256, 0, st>>>((const float*)x, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
-                                                    ws.x_perm);
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<float><<<nblk, 256, 0, st>>>((const float*)x, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
+                                                    ws.x_perm));
     else if (x_dtype == CEB_ACT_BF16)
-        scatter_kernel<__nv_bfloat16><<<nblk, 256, 0, st>>>((const __nv_bfloat16*)x, T, d, E, K, ws.ids,
-                                                            ws.block_base, ws.slot_pos, ws.x_perm);
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__nv_bfloat16><<<nblk, 256, 0, st>>>((const __nv_bfloat16*)x, T, d, E, K, ws.ids,
+                                                            ws.block_base, ws.slot_pos, ws.x_perm));
     else
-        scatter_kernel<__half><<<nblk, 256, 0, st>>>((const __half*)x, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
-                                                     ws.x_perm);
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__half><<<nblk, 256, 0, st>>>((const __half*)x, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
+                                                     ws.x_perm));
     CEB_CUDA_OK(cudaGetLastError());
 
     const int rows = T * K;
@@ -342,7 +342,7 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, fl
     rc = ceb_gemm_launch(mw.fc2, ws.h_perm, rows, a2, st);
     if (rc) return rc;
     if (y) {
-        combine_kernel<<<T, 256, 0, st>>>(ws.down, ws.slot_pos, ws.wts, T, d, K, mw.bias, y);
+        CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, combine_kernel<<<T, 256, 0, st>>>(ws.down, ws.slot_pos, ws.wts, T, d, K, mw.bias, y));
         CEB_CUDA_OK(cudaGetLastError());
     }
     return 0;

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "ceb_internal.h"
+#include "../../include/ceb_ops.h"
 
 namespace {
 thread_local std::string g_last_error;
@@ -203,4 +204,74 @@ void ceb_wplane_free(ceb_wplane* w) {
     if (w->q) cudaFree(w->q);
     if (w->s) cudaFree(w->s);
     *w = ceb_wplane();
+}
+
+// ------------------------------------------------------------------ profiling
+namespace {
+struct ProfRec {
+    cudaEvent_t a = nullptr, b = nullptr;
+    int cat = 0;
+    double flops = 0, bytes = 0;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+long long g_launches = 0;
+std::vector<ProfRec> g_prof_recs;
+size_t g_prof_used = 0;
+}  // namespace
+
+int ceb_prof_begin(cudaStream_t st, int cat) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    ++g_launches;
+    if (!g_prof_on) return -1;
+    if (g_prof_used == g_prof_recs.size()) {
+        ProfRec r;
+        if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess) return -1;
+        g_prof_recs.push_back(r);
+    }
+    ProfRec& r = g_prof_recs[g_prof_used];
+    r.cat = cat;
+    r.flops = r.bytes = 0;
+    cudaEventRecord(r.a, st);
+    return (int)g_prof_used++;
+}
+
+void ceb_prof_end(int token, cudaStream_t st, double flops, double bytes) {
+    if (token < 0) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    ProfRec& r = g_prof_recs[(size_t)token];
+    r.flops = flops;
+    r.bytes = bytes;
+    cudaEventRecord(r.b, st);
+}
+
+extern "C" long long ceb_launch_count(void) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    return g_launches;
+}
+
+extern "C" void ceb_profile_enable(int on) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_on = on != 0;
+    g_prof_used = 0;
+}
+
+// Per category: launches, summed kernel milliseconds, algorithmic flops and bytes.
+// Synchronises on the recorded events and clears the record list.
+extern "C" int ceb_profile_read(long long* launches, double* ms, double* flops, double* bytes, int n_cat) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    for (int c = 0; c < n_cat; ++c) launches[c] = 0, ms[c] = flops[c] = bytes[c] = 0;
+    for (size_t i = 0; i < g_prof_used; ++i) {
+        ProfRec& r = g_prof_recs[i];
+        if (r.cat >= n_cat) continue;
+        float t = 0;
+        if (cudaEventSynchronize(r.b) != cudaSuccess || cudaEventElapsedTime(&t, r.a, r.b) != cudaSuccess)
+            return ceb_set_error(3, "profile event read failed");
+        launches[r.cat] += 1;
+        ms[r.cat] += t;
+        flops[r.cat] += r.flops;
+        bytes[r.cat] += r.bytes;
+    }
+    g_prof_used = 0;
+    return 0;
 }

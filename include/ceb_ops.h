@@ -97,6 +97,21 @@ CEB_API int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int 
 CEB_API int ceb_matmul(int w_type, const void* h_w, int n_out, int k, const void* d_x, int m, const float* d_bias,
                        int gelu, int out_f16, void* d_out, void* stream);
 
+/*
+ * Instrumentation (no counterpart in the reference beyond its
+ * CRISPEMBED_CRISPEMBED_BENCH wall-clock prints, src/crispembed.cpp:1707-1712).
+ * ceb_launch_count: kernels this library has launched since it was loaded.
+ * ceb_profile_enable(1): from now on record CUDA events around every launch,
+ * on the launch's own stream.  ceb_profile_read: per category (0 grouped GEMM,
+ * 1 attention, 2 routing + permutation, 3 row-wise: embedding / LayerNorm /
+ * combine / pooling) the number of launches, summed kernel milliseconds and
+ * algorithmic flops / bytes; synchronises on the recorded events and clears
+ * them.  Returns 0 on success.
+ */
+CEB_API long long ceb_launch_count(void);
+CEB_API void ceb_profile_enable(int on);
+CEB_API int ceb_profile_read(long long* launches, double* ms, double* flops, double* bytes, int n_categories);
+
 /* Message of the last failing call on this thread ("" if none). */
 CEB_API const char* ceb_last_error(void);
 
