@@ -74,6 +74,9 @@ def load_library(path: Optional[str] = None):
         "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_matmul": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
                         ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_linear_create": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int], vp),
+        "ceb_linear_forward": ([vp, vp, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_linear_free": ([vp], None),
         "ceb_launch_count": ([], ctypes.c_longlong),
         "ceb_profile_enable": ([ctypes.c_int], None),
         "ceb_profile_read": ([ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_double),
@@ -225,6 +228,38 @@ class MoELayer:
                                    _ptr(counts), _ptr(logits), workspace.data_ptr(), workspace.numel(),
                                    _stream_ptr(stream))
         _check(rc, "ceb_moe_ffn")
+
+
+class Linear:
+    """Device-resident linear layer (ceb_linear_create / ceb_linear_forward)."""
+
+    def __init__(self, w_type: int, w_raw: np.ndarray, n_out: int, k: int):
+        self._lib = load_library()
+        self.n_out, self.k = n_out, k
+        w_raw = np.ascontiguousarray(w_raw)
+        self._h = self._lib.ceb_linear_create(w_type, w_raw.ctypes.data, n_out, k)
+        if not self._h:
+            raise CrispEmbedError(f"ceb_linear_create failed: {last_error()}")
+
+    def __call__(self, x, out=None, bias=None, gelu=False, out_f16=False, stream=None):
+        import torch
+        if out is None:
+            out = torch.empty((x.shape[0], self.n_out), dtype=torch.float16 if out_f16 else torch.float32,
+                              device=x.device)
+        _check(self._lib.ceb_linear_forward(self._h, x.data_ptr(), x.shape[0], _ptr(bias), int(gelu), int(out_f16),
+                                            out.data_ptr(), _stream_ptr(stream)), "ceb_linear_forward")
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.ceb_linear_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def matmul(w_type: int, w_raw: np.ndarray, n_out: int, k: int, x, bias=None, gelu=False, out_f16=False, stream=None):

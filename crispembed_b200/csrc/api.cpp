@@ -481,6 +481,45 @@ extern "C" int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, i
     return ceb_pool_l2_launch(d_hidden, d_cu_seqlens, n_seqs, d, out_dim, d_out, static_cast<cudaStream_t>(stream), 0);
 }
 
+struct ceb_linear {
+    ceb_wplane w;
+};
+
+extern "C" ceb_linear* ceb_linear_create(int w_type, const void* h_w, int n_out, int k) {
+    if (!h_w || n_out <= 0 || k <= 0) {
+        ceb_set_error(1, "linear_create: bad arguments");
+        return nullptr;
+    }
+    auto* L = new ceb_linear;
+    if (ceb_repack_weights(&L->w, w_type, h_w, 1, n_out, k, nullptr)) {
+        delete L;
+        return nullptr;
+    }
+    return L;
+}
+
+extern "C" int ceb_linear_forward(const ceb_linear* L, const void* d_x, int m, const float* d_bias, int gelu,
+                                  int out_f16, void* d_out, void* stream) {
+    if (m == 0) return 0;
+    if (!L || !d_x || !d_out || m < 0) return ceb_set_error(1, "linear_forward: bad arguments");
+    int* err = op_err_word();
+    if (!err) return ceb_set_error(4, "out of device memory");
+    ceb_gemm_args a;
+    a.m_rows = m;
+    a.out = d_out;
+    a.ldo = L->w.n_out;
+    a.epi = (out_f16 ? CEB_EPI_F16_OUT : 0) | (gelu ? CEB_EPI_GELU : 0) | (d_bias ? CEB_EPI_BIAS : 0);
+    a.bias = d_bias;
+    a.err = err;
+    return ceb_gemm_launch(L->w, d_x, m, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" void ceb_linear_free(ceb_linear* L) {
+    if (!L) return;
+    ceb_wplane_free(&L->w);
+    delete L;
+}
+
 extern "C" int ceb_matmul(int w_type, const void* h_w, int n_out, int k, const void* d_x, int m, const float* d_bias,
                           int gelu, int out_f16, void* d_out, void* stream) {
     if (m == 0) return 0;

@@ -1,0 +1,120 @@
+"""Time one kernel of the library in isolation (CUDA events, inputs resident).
+
+    python -m crispembed_b200.kernel_bench gemm --type q8_0 --m 16384 --n 3072 --k 768 [--gelu] [--f16-out]
+    python -m crispembed_b200.kernel_bench moe --T 65536 --type q4_k --zipf 1.2
+
+Used for the roofline numbers of single kernels and as the command that ncu
+captures (small cases: a few launches, a few GB at most).  Prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import numpy as np
+
+TYPES = {"q8_0": 8, "q4_k": 12, "f16": 1, "f32": 0}
+
+
+def _peaks():
+    import os
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}, "fallback"
+
+
+def bench_gemm(a):
+    import torch
+
+    from . import binding, quant
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((a.n, a.k), dtype=np.float32) * 0.02).astype(np.float32)
+    lin = binding.Linear(TYPES[a.type], quant.quantize(w, TYPES[a.type]), a.n, a.k)
+    x = torch.randn((a.m, a.k), device="cuda", dtype=torch.float16)
+    bias = torch.randn((a.n,), device="cuda", dtype=torch.float32) * 0.02 if a.bias else None
+    out = torch.empty((a.m, a.n), device="cuda", dtype=torch.float16 if a.f16_out else torch.float32)
+    for _ in range(a.warmup):
+        lin(x, out=out, bias=bias, gelu=a.gelu, out_f16=a.f16_out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        lin(x, out=out, bias=bias, gelu=a.gelu, out_f16=a.f16_out)
+    e1.record()
+    torch.cuda.synchronize()
+    binding.sync_check()
+    ms = e0.elapsed_time(e1) / a.iters
+    flops = 2.0 * a.m * a.n * a.k
+    pk, src = _peaks()
+    tf = flops / (ms / 1e3) / 1e12
+    lin.close()
+    return {"kernel": "gemm", "type": a.type, "m": a.m, "n": a.n, "k": a.k, "gelu": a.gelu, "f16_out": a.f16_out,
+            "ms": ms, "tflops": tf, "frac_of_peak": tf / pk["bf16_tflops"], "peak_source": src}
+
+
+def bench_moe(a):
+    import torch
+
+    from . import binding, synth
+    inp = synth.make_moe_op_inputs(a.T, d=a.d, n_experts=a.E, top_k=a.topk, ffn=a.F, wtype=TYPES[a.type],
+                                   router_wtype=0, zipf_s=a.zipf or None, seed=0)
+    layer = binding.MoELayer(inp.d, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
+                             inp.fc1_raw, inp.fc2_raw, inp.bias)
+    x = torch.from_numpy(inp.x).cuda().to(torch.bfloat16)
+    y = torch.empty((a.T, a.d), dtype=torch.float32, device="cuda")
+    ws = torch.empty(layer.workspace_size(a.T), dtype=torch.uint8, device="cuda")
+    for _ in range(a.warmup):
+        layer.forward(x, y, ws)
+    torch.cuda.synchronize()
+    binding.profile_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        layer.forward(x, y, ws)
+    e1.record()
+    torch.cuda.synchronize()
+    prof = binding.profile_read()
+    binding.profile_enable(False)
+    ms = e0.elapsed_time(e1) / a.iters
+    layer.close()
+    flops = 2.0 * 2 * a.T * a.topk * a.d * a.F
+    return {"kernel": "moe_ffn", "T": a.T, "type": a.type, "E": a.E, "k": a.topk, "ms": ms,
+            "tokens_per_s": a.T / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+            "breakdown_ms": {k: v["ms"] / a.iters for k, v in prof.items()}}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="what", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--type", default="q8_0", choices=list(TYPES))
+    g.add_argument("--m", type=int, default=16384)
+    g.add_argument("--n", type=int, default=3072)
+    g.add_argument("--k", type=int, default=768)
+    g.add_argument("--gelu", action="store_true")
+    g.add_argument("--bias", action="store_true")
+    g.add_argument("--f16-out", action="store_true")
+    g.add_argument("--iters", type=int, default=20)
+    g.add_argument("--warmup", type=int, default=3)
+    m = sub.add_parser("moe")
+    m.add_argument("--T", type=int, default=65536)
+    m.add_argument("--d", type=int, default=768)
+    m.add_argument("--E", type=int, default=8)
+    m.add_argument("--topk", type=int, default=2)
+    m.add_argument("--F", type=int, default=3072)
+    m.add_argument("--type", default="q4_k", choices=list(TYPES))
+    m.add_argument("--zipf", type=float, default=1.2)
+    m.add_argument("--iters", type=int, default=10)
+    m.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    r = bench_gemm(a) if a.what == "gemm" else bench_moe(a)
+    print(json.dumps(r), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

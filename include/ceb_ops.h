@@ -88,6 +88,20 @@ CEB_API int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int 
                         float* d_out, void* stream);
 
 /*
+ * A device-resident linear layer (one ggml_mul_mat weight of the encoder,
+ * src/crispembed.cpp:1160-1416): W [n_out rows x k] given as GGUF bytes on the
+ * host, repacked once into the planes the tensor-core GEMM streams.
+ * ceb_linear_forward: d_out[m, n] = sum_k W[n, k] * d_x[m, k] (+ d_bias[n]),
+ * optional erf-GELU; d_x [m x k] fp16; d_out fp16 if out_f16 else float.
+ * Asynchronous on `stream`.  n_out a multiple of 128, k of 64 (256 for Q4_K).
+ */
+typedef struct ceb_linear ceb_linear;
+CEB_API ceb_linear* ceb_linear_create(int w_type, const void* h_w, int n_out, int k);
+CEB_API int ceb_linear_forward(const ceb_linear* lin, const void* d_x, int m, const float* d_bias, int gelu,
+                               int out_f16, void* d_out, void* stream);
+CEB_API void ceb_linear_free(ceb_linear* lin);
+
+/*
  * One block-quantized matrix product on the tensor cores (the ggml_mul_mat of
  * the encoder's dense layers): d_out[m, n] = sum_k W[n, k] * d_x[m, k] (+ bias[n]),
  * optional erf-GELU.  h_w: GGUF bytes of W [n_out rows x k] (host); d_x: [m x k]
