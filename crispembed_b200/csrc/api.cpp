@@ -465,7 +465,7 @@ extern "C" int ceb_moe_ffn(const ceb_moe_layer* L, const void* d_x, int x_dtype,
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     ceb_moe_ws ws;
     ceb_moe_ws_layout(n_tokens, L->w.d, L->w.n_experts, L->w.top_k, L->w.ffn, &ws, static_cast<uint8_t*>(d_workspace));
-    int rc = ceb_moe_run(L->w, d_x, x_dtype, n_tokens, d_y, ws, d_expert_counts, d_logits, err, st);
+    int rc = ceb_moe_run(L->w, d_x, x_dtype, nullptr, n_tokens, d_y, ws, d_expert_counts, d_logits, err, st);
     if (rc) return rc;
     const size_t S = (size_t)n_tokens * L->w.top_k;
     if (d_ids && cudaMemcpyAsync(d_ids, ws.ids, S * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)

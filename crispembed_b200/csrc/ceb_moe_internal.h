@@ -36,5 +36,8 @@ struct ceb_moe_ws {
 };
 
 size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint8_t* base);
-int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, float* y, const ceb_moe_ws& ws,
-                int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st);
+// x: router input ([T x d], x_dtype); x16: optional fp16 copy of x used for the
+// expert row gather (else x is converted on the fly).  y may be null when the
+// caller fuses the combine (the permuted expert outputs stay in ws.down).
+int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
+                const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st);

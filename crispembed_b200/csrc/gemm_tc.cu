@@ -8,18 +8,22 @@
 //     out[r, n] = epilogue( sum_k W_g[n, k] * X[r, k] )
 //
 // Operand roles ("TS" form of tcgen05.mma, A from tensor memory):
-//   A = weight tile, 128 output features x 64 k, dequantized by four warps
-//       straight from global memory (Q8_0 / Q4_K / fp16 planes) into TMEM;
-//   B = activation tile, up to 128 rows x 64 k fp16, loaded by TMA into
+//   A = weight tile, 128 output features x 64 k, dequantized by eight warps
+//       straight from global memory (Q8_0 / Q4_K / fp16 planes) into TMEM,
+//       so the weights never pass through shared memory;
+//   B = activation tile, up to BN rows x 64 k fp16, loaded by TMA into
 //       128-byte-swizzled shared memory;
-//   D = fp32 accumulator in TMEM, [128 features (lanes)] x [N rows (columns)],
+//   D = fp32 accumulator in TMEM, [128 features (lanes)] x [BN rows (columns)],
 //       double buffered so the epilogue of one tile overlaps the next tile.
+// TMEM budget (512 columns): 2 x BN accumulator columns + SA x 32 A-stage columns.
 //
-// Warp roles (384 threads, one persistent CTA per SM):
-//   warp 0       TMA producer of activation stages
-//   warp 1       TMEM owner + single-thread MMA issuer
-//   warps 4..7   dequant producers (thread i <-> weight row / TMEM lane i)
-//   warps 8..11  epilogue (thread i <-> output feature i): bias, GELU, store
+// Warp roles (640 threads, one persistent CTA per SM):
+//   warp 0        TMA producer of activation stages
+//   warp 1        TMEM owner + single-thread MMA issuer
+//   warps 4..11   dequant producers, two warpgroups taking alternate K-blocks
+//                 (thread i of a warpgroup <-> weight row / TMEM lane i)
+//   warps 12..19  epilogue, two warpgroups taking alternate 32-column chunks
+//                 (thread i <-> output feature i): bias, GELU, store
 // Tiles (group, token tile, feature tile) are distributed round-robin; the
 // group table is read from device memory, so no host synchronisation is
 // needed between routing and the expert GEMMs.
@@ -31,20 +35,18 @@
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BN = 192;               // activation rows (tokens) per tile = MMA N
 constexpr int BK = 64;
-constexpr int SB = 6;   // activation smem stages
-constexpr int SA = 4;   // TMEM A stages
+constexpr int SB = 6;                 // activation smem stages
+constexpr int SA = (512 - 2 * BN) / 32;  // TMEM A stages (4)
 constexpr int MAXG = 64;
 constexpr int B_STAGE_BYTES = BN * BK * 2;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int A_COL0 = 2 * BN;
-constexpr int NTHREADS = 384;
-// dequant prefetch depth (K-blocks in flight per thread), bounded by registers
-template <int FMT>
-struct Prefetch {
-    static constexpr int depth = FMT == CEB_W_F16 ? 2 : 4;
-};
+constexpr int DEQ_WG = 2, EPI_WG = 2;
+constexpr int DEQ_WARP0 = 4, EPI_WARP0 = DEQ_WARP0 + 4 * DEQ_WG;
+constexpr int NTHREADS = 32 * (EPI_WARP0 + 4 * EPI_WG);
+static_assert(SA >= 2 && A_COL0 + 32 * SA <= 512, "TMEM budget");
 
 constexpr int NBARS = 2 * SB + 2 * SA + 4 + 1;
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)SB * B_STAGE_BYTES + NBARS * 8 + 16 + 3 * (MAXG + 1) * 4;
@@ -120,6 +122,12 @@ struct Raw<CEB_W_F16> {
     uint4 q[8];
 };
 
+// dequant prefetch depth (K-blocks in flight per thread of one warpgroup)
+template <int FMT>
+struct Prefetch {
+    static constexpr int depth = FMT == CEB_W_F16 ? 1 : 2;
+};
+
 CEB_DEV uint4 ldg128(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
 template <int FMT>
@@ -162,7 +170,9 @@ CEB_DEV void convert<CEB_W_Q8_0>(const Raw<CEB_W_Q8_0>& r, uint32_t (&o)[32]) {
     for (int w = 0; w < 16; ++w) i8x4_to_h2x2(wd[w], w < 8 ? d0 : d1, o[2 * w], o[2 * w + 1]);
 }
 
-CEB_DEV float nib_f(uint32_t v, int byte) { return __uint_as_float(0x4B000000u | ((v >> (8 * byte)) & 0xFFu)) - 8388608.0f; }
+CEB_DEV float nib_f(uint32_t v, int byte) {
+    return __uint_as_float(0x4B000000u | ((v >> (8 * byte)) & 0xFFu)) - 8388608.0f;
+}
 
 template <>
 CEB_DEV void convert<CEB_W_Q4_K>(const Raw<CEB_W_Q4_K>& r, uint32_t (&o)[32]) {
@@ -194,6 +204,21 @@ CEB_DEV void convert<CEB_W_F16>(const Raw<CEB_W_F16>& r, uint32_t (&o)[32]) {
     }
 }
 
+// erf-GELU 0.5 x (1 + erf(x / sqrt 2)) with erf from Abramowitz & Stegun 7.1.26
+// (|error| <= 1.5e-7 on erf), far below the fp16 rounding of the output.
+CEB_DEV float gelu_as(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = __frcp_rn(fmaf(0.3275911f, z, 1.0f));
+    float p = fmaf(1.061405429f, t, -1.453152027f);
+    p = fmaf(p, t, 1.421413741f);
+    p = fmaf(p, t, -0.284496736f);
+    p = fmaf(p, t, 0.254829592f);
+    p *= t;
+    const float e = 1.0f - p * __expf(-z * z);  // erf(|x|/sqrt2)
+    const float erf_s = copysignf(e, x);
+    return 0.5f * x + 0.5f * x * erf_s;
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(NTHREADS, 1)
     ceb_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const ceb_wplane w, const ceb_gemm_args a) {
@@ -207,8 +232,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NBARS; ++i) {
             uint32_t cnt = 1;
-            if (i >= 2 * SB && i < 2 * SB + SA) cnt = 128;                        // A full: all dequant threads
-            if (i >= 2 * SB + 2 * SA + 2 && i < 2 * SB + 2 * SA + 4) cnt = 128;  // acc empty: all epilogue threads
+            if (i >= 2 * SB && i < 2 * SB + SA) cnt = 4;                                  // A full: one per dequant warp
+            if (i >= 2 * SB + 2 * SA + 2 && i < 2 * SB + 2 * SA + 4) cnt = 4 * EPI_WG;   // acc empty: epilogue warps
             mbar_init(smem_u32(&S.bars[i]), cnt);
         }
         fence_mbar_init();
@@ -268,7 +293,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t it = 0, ia = 0, lt = 0;
+            uint32_t it = 0, lt = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++lt) {
                 const TileInfo ti = decode_tile(S, G, n_ftiles, t);
@@ -279,9 +304,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 n = n < 16 ? 16 : n;
                 const uint32_t idesc = idesc_f16_f32(BM, n);
                 const uint32_t d_tmem = tmem + (uint32_t)(ab * BN);
-                for (int kb = 0; kb < nkb; ++kb, ++it, ++ia) {
-                    const int s = it % SB, sa = ia % SA;
-                    if (!mbar_wait(bar(BAR_A_FULL(sa)), (ia / SA) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA) ||
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % SB, sa = it % SA;
+                    if (!mbar_wait(bar(BAR_A_FULL(sa)), (it / SA) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA) ||
                         !mbar_wait(bar(BAR_B_FULL(s)), (it / SB) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
@@ -301,9 +326,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mma_commit(bar(BAR_DRAIN()));
             mbar_wait(bar(BAR_DRAIN()), 0, nullptr, nullptr, 0);
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= DEQ_WARP0 && warp < EPI_WARP0) {
         // ------------------------------------------------ dequant producers
-        const int r = threadIdx.x - 128;  // == 32*(warp%4) + lane : weight row / TMEM lane of this thread
+        const int wg = (warp - DEQ_WARP0) >> 2;  // this warpgroup takes items i with i % DEQ_WG == wg
+        const int r = 32 * (warp & 3) + lane;    // weight row within the tile == TMEM lane
         const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
         const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
         const int n_items = my_tiles * nkb;
@@ -314,20 +340,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const TileInfo ti = decode_tile(S, G, n_ftiles, t);
             load_raw<FMT>(w, ti.g, ti.ft * BM + r, i % nkb, dst);
         };
+        // own items: i_j = wg + j * DEQ_WG
+        const int n_mine = n_items > wg ? (n_items - 1 - wg) / DEQ_WG + 1 : 0;
 #pragma unroll
         for (int u = 0; u < PF - 1; ++u)
-            if (u < n_items) item_load(u, buf[u]);
+            if (u < n_mine) item_load(wg + u * DEQ_WG, buf[u]);
         bool ok = true;
-        for (int i0 = 0; i0 < n_items && ok; i0 += PF) {
+        for (int j0 = 0; j0 < n_mine && ok; j0 += PF) {
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
-                const int i = i0 + u;
-                if (i < n_items && ok) {
-                    if (i + PF - 1 < n_items) item_load(i + PF - 1, buf[(u + PF - 1) % PF]);
+                const int j = j0 + u;
+                if (j < n_mine && ok) {
+                    if (j + PF - 1 < n_mine) item_load(wg + (j + PF - 1) * DEQ_WG, buf[(u + PF - 1) % PF]);
+                    const int i = wg + j * DEQ_WG;
                     const int sa = i % SA;
-                    const bool got =
-                        __all_sync(0xffffffffu, mbar_wait(bar(BAR_A_EMPTY(sa)), ((i / SA) & 1) ^ 1, abort, a.err,
-                                                          CEB_DEVERR_TIMEOUT_DEQ));
+                    const bool got = __all_sync(0xffffffffu, mbar_wait(bar(BAR_A_EMPTY(sa)), ((i / SA) & 1) ^ 1,
+                                                                       abort, a.err, CEB_DEVERR_TIMEOUT_DEQ));
                     if (!got) {
                         ok = false;
                     } else {
@@ -337,15 +365,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tmem_st32(tmem + lane_addr + (uint32_t)(A_COL0 + sa * 32), o);
                         tmem_st_wait();
                         tc_fence_before();
-                        mbar_arrive(bar(BAR_A_FULL(sa)));
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(bar(BAR_A_FULL(sa)));
                     }
                 }
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= EPI_WARP0) {
         // ------------------------------------------------ epilogue
-        const int r = threadIdx.x - 256;  // output feature within the tile
+        const int wg = (warp - EPI_WARP0) >> 2;  // this warpgroup takes 32-column chunks c with c % EPI_WG == wg
+        const int r = 32 * (warp & 3) + lane;    // output feature within the tile
         const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
+        const bool f16 = (a.epi & CEB_EPI_F16_OUT) != 0, gelu = (a.epi & CEB_EPI_GELU) != 0;
         uint32_t lt = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
             const TileInfo ti = decode_tile(S, G, n_ftiles, t);
@@ -356,35 +387,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_after();
             const int n = ti.ft * BM + r;
             const float bv = (a.epi & CEB_EPI_BIAS) ? a.bias[(size_t)ti.g * a.bias_group_stride + n] : 0.0f;
-            for (int c0 = 0; c0 < ti.rows; c0 += 32) {
+            for (int c0 = 32 * wg; c0 < ti.rows; c0 += 32 * EPI_WG) {
                 uint32_t v[32];
                 tmem_ld32(tmem + lane_addr + (uint32_t)(ab * BN + c0), v);
                 tmem_ld_wait();
                 const int lim = ti.rows - c0 < 32 ? ti.rows - c0 : 32;
-                if (a.epi & CEB_EPI_F16_OUT) {
-                    __half* o = reinterpret_cast<__half*>(a.out) + (size_t)(ti.row0 + c0) * a.ldo + n;
+                float x[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if (j < lim) {
-                            float x = __uint_as_float(v[j]) + bv;
-                            if (a.epi & CEB_EPI_GELU) x = gelu_erf(x);
-                            o[(size_t)j * a.ldo] = __float2half_rn(x);
-                        }
+                for (int j = 0; j < 32; ++j) {
+                    x[j] = __uint_as_float(v[j]) + bv;
+                    if (gelu) x[j] = gelu_as(x[j]);
+                }
+                if (f16) {
+                    // lane pairs (2i, 2i+1) exchange so each lane stores a half2 of
+                    // features (2i, 2i+1): even lanes for even rows, odd lanes for odd rows
+                    const bool odd = lane & 1;
+                    __half* o = reinterpret_cast<__half*>(a.out) + (size_t)(ti.row0 + c0) * a.ldo + (n & ~1);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const float send = odd ? x[j] : x[j + 1];
+                        const float got = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const int row = odd ? j + 1 : j;
+                        const __half2 hv = odd ? __floats2half2_rn(got, x[j + 1]) : __floats2half2_rn(x[j], got);
+                        if (row < lim) *reinterpret_cast<__half2*>(o + (size_t)row * a.ldo) = hv;
                     }
                 } else {
                     float* o = reinterpret_cast<float*>(a.out) + (size_t)(ti.row0 + c0) * a.ldo + n;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if (j < lim) {
-                            float x = __uint_as_float(v[j]) + bv;
-                            if (a.epi & CEB_EPI_GELU) x = gelu_erf(x);
-                            o[(size_t)j * a.ldo] = x;
-                        }
-                    }
+                    for (int j = 0; j < 32; ++j)
+                        if (j < lim) o[(size_t)j * a.ldo] = x[j];
                 }
             }
             tc_fence_before();
-            mbar_arrive(bar(BAR_ACC_EMPTY(ab)));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(BAR_ACC_EMPTY(ab)));
         }
     }
 
@@ -418,6 +454,7 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
     if (a.offsets && (w.n_groups < 1 || w.n_groups > MAXG))
         return ceb_set_error(2, "gemm: %d groups (max %d)", w.n_groups, MAXG);
     if ((reinterpret_cast<uintptr_t>(act_f16) & 15) != 0) return ceb_set_error(2, "gemm: activations not 16-B aligned");
+    if ((a.epi & CEB_EPI_F16_OUT) && (a.ldo & 1)) return ceb_set_error(2, "gemm: fp16 output stride must be even");
     if (act_rows <= 0) return 0;
     CUtensorMap map;
     const int mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);

@@ -25,8 +25,8 @@
 
 namespace {
 
-constexpr int ROUTE_WARPS = 8;          // tokens per route CTA = ROUTE_WARPS * TOK_PER_WARP
-constexpr int TOK_PER_WARP = 32;
+constexpr int ROUTE_WARPS = 16;         // tokens per route CTA = ROUTE_WARPS * TOK_PER_WARP
+constexpr int TOK_PER_WARP = 16;
 constexpr int CHUNK = ROUTE_WARPS * TOK_PER_WARP;  // tokens per histogram block (256)
 constexpr int MAXE = 64;
 constexpr int MAXD = 4096;
@@ -55,25 +55,42 @@ CEB_DEV float warp_sum(float v) {
 // Router.  Q8_0 router weights reproduce ggml's CPU arithmetic bit for bit:
 // the token row is re-quantized to Q8_0 (amax/127 scale stored as fp16,
 // multiplier 127/amax, round half to even), each 32-block contributes eight
-// 4-product integer partial sums scaled by d_w*d_x with one FMA per lane and
-// block, and the eight lanes are summed as ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)).
-// F32 router weights use a plain fp32 dot.
+// 4-product integer partial sums (dp4a) scaled by d_w*d_x with one FMA per lane
+// and block, and the eight lanes are summed as ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)).
+// The Q8_0 weights are staged once per CTA in shared memory (quants padded by
+// 32 B per expert row so the four experts of a pass hit distinct banks).
+// F32 router weights use a plain fp32 dot read through the L1 cache.
+// One warp per token, ROUTE_WARPS warps per CTA, CHUNK tokens per CTA.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(ROUTE_WARPS * 32)
     route_kernel(const T* __restrict__ x, int T_tokens, int d, int E, int K, int rtype, const uint8_t* __restrict__ rw,
                  int32_t* __restrict__ ids, float* __restrict__ wts, float* __restrict__ logits_out,
                  int32_t* __restrict__ block_counts) {
-    extern __shared__ uint8_t sm[];
-    int* s_cnt = reinterpret_cast<int*>(sm);                                   // [E]
-    int8_t* s_q = reinterpret_cast<int8_t*>(sm + MAXE * 4);                    // [warps][d]
-    __half* s_d = reinterpret_cast<__half*>(sm + MAXE * 4 + ROUTE_WARPS * d);  // [warps][d/32]
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int nb = d / 32;
+    const int wpitch = d + 32;
+    int* s_cnt = reinterpret_cast<int*>(sm);                                            // [MAXE]
+    float* s_wd = reinterpret_cast<float*>(sm + MAXE * 4);                              // [E][nb]
+    float* s_xd = s_wd + (size_t)E * nb;                                                // [warps][nb]
+    int8_t* s_wq = reinterpret_cast<int8_t*>(s_xd + (size_t)ROUTE_WARPS * nb);         // [E][wpitch]
+    int8_t* s_xq = s_wq + (size_t)E * wpitch;                                           // [warps][d]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < E; i += blockDim.x) s_cnt[i] = 0;
+    if (rtype == CEB_GGML_Q8_0) {
+        // stage weights: block (e, b) -> scale s_wd[e][b], quants s_wq[e][b*32 .. +31]
+        for (int i = threadIdx.x; i < E * nb; i += blockDim.x) {
+            const uint8_t* blk = rw + (size_t)i * 34;
+            const int e = i / nb, b = i - e * nb;
+            s_wd[i] = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+            int8_t* dst = s_wq + (size_t)e * wpitch + b * 32;
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) dst[j] = (int8_t)blk[2 + j];
+        }
+    }
     __syncthreads();
-    const int nb = d / 32;
-    int8_t* q = s_q + warp * d;
-    __half* qd = s_d + warp * nb;
+    int8_t* q = s_xq + (size_t)warp * d;
+    float* qd = s_xd + (size_t)warp * nb;
 
     for (int tt = 0; tt < TOK_PER_WARP; ++tt) {
         const int t = blockIdx.x * CHUNK + warp * TOK_PER_WARP + tt;
@@ -86,24 +103,21 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32)
                 const float amax = warp_max(fabsf(v));
                 const float id = amax != 0.0f ? 127.0f / amax : 0.0f;
                 q[b * 32 + lane] = (int8_t)__float2int_rn(v * id);
-                if (lane == 0) qd[b] = __float2half_rn(amax / 127.0f);
+                if (lane == 0) qd[b] = __half2float(__float2half_rn(amax / 127.0f));
             }
             __syncwarp();
             // lane = (expert-in-pass, partial-lane): 4 experts x 8 lanes per pass
-            const int rb = nb * 34;
             for (int e0 = 0; e0 < E; e0 += 4) {
                 const int e = e0 + (lane >> 3), l = lane & 7;
                 float acc = 0.0f;
                 if (e < E) {
-                    const uint8_t* wr = rw + (size_t)e * rb;
+                    const int8_t* wq = s_wq + (size_t)e * wpitch + 4 * l;
+                    const float* wd = s_wd + (size_t)e * nb;
+                    const int8_t* xq = q + 4 * l;
                     for (int b = 0; b < nb; ++b) {
-                        const uint8_t* blk = wr + b * 34;
-                        const float dw = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
-                        const float dd = __fmul_rn(dw, __half2float(qd[b]));
-                        const int8_t* qw = reinterpret_cast<const int8_t*>(blk + 2) + 4 * l;
-                        const int8_t* qa = q + b * 32 + 4 * l;
-                        const int s = qw[0] * qa[0] + qw[1] * qa[1] + qw[2] * qa[2] + qw[3] * qa[3];
-                        acc = __fmaf_rn(dd, (float)s, acc);
+                        const int s = __dp4a(*reinterpret_cast<const int*>(wq + b * 32),
+                                             *reinterpret_cast<const int*>(xq + b * 32), 0);
+                        acc = __fmaf_rn(__fmul_rn(wd[b], qd[b]), (float)s, acc);
                     }
                 }
                 // ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)) within each group of 8 lanes
@@ -193,9 +207,9 @@ __global__ void scan_kernel(const int32_t* __restrict__ block_counts, int nblk, 
 // matrix consumed by fc1.
 template <typename T>
 __global__ void __launch_bounds__(256)
-    scatter_kernel(const T* __restrict__ x, int T_tokens, int d, int E, int K, const int32_t* __restrict__ ids,
-                   const int32_t* __restrict__ block_base, int32_t* __restrict__ slot_pos,
-                   __half* __restrict__ x_perm) {
+    scatter_kernel(const T* __restrict__ x, const __half* __restrict__ x16, int T_tokens, int d, int E, int K,
+                   const int32_t* __restrict__ ids, const int32_t* __restrict__ block_base,
+                   int32_t* __restrict__ slot_pos, __half* __restrict__ x_perm) {
     __shared__ int running[MAXE];
     __shared__ int s_pos[CHUNK * 4];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -229,15 +243,22 @@ __global__ void __launch_bounds__(256)
         }
     }
     __syncthreads();
-    // gather rows: one warp per slot, fp16 out, 8 values per lane step
+    // gather rows: one warp per slot.  With an fp16 copy of x available the rows
+    // move as 16-byte vectors; otherwise they are converted on the fly.
     for (int s = warp; s < n_slots; s += blockDim.x / 32) {
         const int pos = s_pos[s];
         if (pos < 0) continue;
-        const T* src = x + (size_t)(t0 + s / K) * d;
         __half* dst = x_perm + (size_t)pos * d;
-        for (int c = lane * 2; c < d; c += 64) {
-            const float a = ld_act<T>(src, c), b = ld_act<T>(src, c + 1);
-            *reinterpret_cast<__half2*>(dst + c) = __floats2half2_rn(a, b);
+        if (x16) {
+            const uint4* src = reinterpret_cast<const uint4*>(x16 + (size_t)(t0 + s / K) * d);
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+            for (int c = lane; c < d / 8; c += 32) d4[c] = __ldg(src + c);
+        } else {
+            const T* src = x + (size_t)(t0 + s / K) * d;
+            for (int c = lane * 2; c < d; c += 64) {
+                const float a = ld_act<T>(src, c), b = ld_act<T>(src, c + 1);
+                *reinterpret_cast<__half2*>(dst + c) = __floats2half2_rn(a, b);
+            }
         }
     }
 }
@@ -287,14 +308,22 @@ size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint
     return off;
 }
 
-int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, float* y, const ceb_moe_ws& ws,
-                int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st) {
+int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
+                const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st) {
     const int d = mw.d, E = mw.n_experts, K = mw.top_k, F = mw.ffn;
     if (T <= 0) return 0;
     if (E > 32 || E < 1 || K < 1 || K > E || K > 4 || d % 64 || d > MAXD || F % 128 || d % 128)
         return ceb_set_error(2, "moe: unsupported shape d=%d E=%d K=%d F=%d", d, E, K, F);
     const int nblk = (T + CHUNK - 1) / CHUNK;
-    const size_t route_smem = MAXE * 4 + (size_t)ROUTE_WARPS * d + (size_t)ROUTE_WARPS * (d / 32) * 2;
+    const size_t route_smem = MAXE * 4 + (size_t)(E + ROUTE_WARPS) * (d / 32) * 4 + (size_t)E * (d + 32) +
+                              (size_t)ROUTE_WARPS * d;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(route_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+        cudaFuncSetAttribute(route_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+        cudaFuncSetAttribute(route_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+        attr = true;
+    }
     if (x_dtype == CEB_ACT_F32) {
         CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, route_kernel<float><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>((const float*)x, T, d, E, K, mw.router_type,
                                                                         mw.router, ws.ids, ws.wts, logits_out,
@@ -312,13 +341,13 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, fl
     CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scan_kernel<<<1, 64, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts));
     CEB_CUDA_OK(cudaGetLastError());
     if (x_dtype == CEB_ACT_F32)
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<float><<<nblk, 256, 0, st>>>((const float*)x, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<float><<<nblk, 256, 0, st>>>((const float*)x, x16, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
                                                     ws.x_perm));
     else if (x_dtype == CEB_ACT_BF16)
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__nv_bfloat16><<<nblk, 256, 0, st>>>((const __nv_bfloat16*)x, T, d, E, K, ws.ids,
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__nv_bfloat16><<<nblk, 256, 0, st>>>((const __nv_bfloat16*)x, x16, T, d, E, K, ws.ids,
                                                             ws.block_base, ws.slot_pos, ws.x_perm));
     else
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__half><<<nblk, 256, 0, st>>>((const __half*)x, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__half><<<nblk, 256, 0, st>>>((const __half*)x, x16, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
                                                      ws.x_perm));
     CEB_CUDA_OK(cudaGetLastError());
 
