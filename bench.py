@@ -91,7 +91,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                          "-lms", "50", "-i", str(self.idx)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -220,6 +220,7 @@ def main():
 
         import torch.distributed as dist
     from crispembed_b200 import binding, synth
+    from crispembed_b200.dist import max_over_ranks
 
     path = model_path(local) if args.workload == "c2" else None
     if world > 1:
@@ -254,10 +255,8 @@ def main():
     binding.profile_enable(False)
     binding.sync_check()
     t = ev0.elapsed_time(ev1) / 1000.0
+    t = max_over_ranks(t, "cuda")
     if dist:
-        tt = torch.tensor([t], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t = float(tt.item())
         dist.barrier()
     value = world * tokens * args.steps / t
 
@@ -270,10 +269,7 @@ def main():
     for _ in range(args.steps):
         emb = m.encode_ids(ids, lens)
     te = time.perf_counter() - t0
-    if dist:
-        tt = torch.tensor([te], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        te = float(tt.item())
+    te = max_over_ranks(te, "cuda")
     e2e = world * tokens * args.steps / te
     assert np.allclose(np.linalg.norm(emb, axis=1), 1.0, atol=1e-4)
     m.close()
