@@ -71,6 +71,7 @@ def load_library(path: Optional[str] = None):
         "ceb_moe_workspace_size": ([vp, ctypes.c_int], ctypes.c_size_t),
         "ceb_moe_ffn": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp, ctypes.c_size_t, vp],
                         ctypes.c_int),
+        "ceb_moe_ffn_static": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_matmul": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
                         ctypes.c_int, vp, vp], ctypes.c_int),
@@ -217,6 +218,13 @@ class MoELayer:
             self.close()
         except Exception:
             pass
+
+    def forward_static(self, x, y, stream=None):
+        """ceb_moe_ffn_static: the library's own fixed scratch, no device allocation."""
+        import torch
+        act = {torch.float32: ACT_F32, torch.bfloat16: ACT_BF16, torch.float16: ACT_F16}[x.dtype]
+        _check(self._lib.ceb_moe_ffn_static(self._h, x.data_ptr(), act, x.shape[0], y.data_ptr(), _stream_ptr(stream)),
+               "ceb_moe_ffn_static")
 
     def workspace_size(self, n_tokens: int) -> int:
         return int(self._lib.ceb_moe_workspace_size(self._h, n_tokens))

@@ -20,6 +20,8 @@
 
 static_assert(sizeof(crispembed_hparams) == sizeof(ceb_hparams_c), "hparams layout");
 
+int ceb_moe_static_take_error();  // moe_static.cu
+
 struct crispembed_context {
     ceb_model model;
     ceb_workspace ws;
@@ -367,11 +369,6 @@ extern "C" const char* crispembed_model_license(int) { return ""; }
 extern "C" const char* crispembed_model_card_url(int) { return ""; }
 
 // ============================================================= ceb_ops.h ===
-struct ceb_moe_layer {
-    ceb_moe_weights w;
-    std::vector<void*> allocs;
-};
-
 extern "C" ceb_moe_layer* ceb_moe_layer_create(int d, int n_experts, int top_k, int ffn, int router_type,
                                                const void* h_router, int expert_type, const void* h_fc1,
                                                const void* h_fc2, const float* h_bias) {
@@ -552,6 +549,8 @@ extern "C" int ceb_sync_check(void* stream) {
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "stream synchronize", __FILE__, __LINE__);
     e = cudaGetLastError();
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "pending error", __FILE__, __LINE__);
+    const int hs = ceb_moe_static_take_error();
+    if (hs) return ceb_set_error(5, "device-side check failed in ceb_moe_ffn_static (code 0x%x)", hs);
     int* err = op_err_word();
     if (!err) return 0;
     int h = 0;

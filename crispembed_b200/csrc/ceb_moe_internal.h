@@ -3,6 +3,8 @@
 
 #include <cuda_fp16.h>
 
+#include <vector>
+
 #include "ceb_internal.h"
 
 // activation element types (same values as include/ceb_ops.h)
@@ -41,3 +43,9 @@ size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint
 // caller fuses the combine (the permuted expert outputs stay in ws.down).
 int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
                 const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st);
+
+// Handle behind the ceb_moe_layer* of include/ceb_ops.h.
+struct ceb_moe_layer {
+    ceb_moe_weights w;
+    std::vector<void*> allocs;  // router / bias buffers owned by the handle
+};

@@ -76,6 +76,31 @@ CEB_API int ceb_moe_ffn(const ceb_moe_layer* layer, const void* d_x, int x_dtype
                         size_t workspace_bytes, void* stream);
 
 /*
+ * ceb_moe_ffn without any device allocation (no counterpart in the reference).
+ *
+ * For callers that must not allocate device memory once running -- a host whose
+ * GPU memory belongs to another allocator, a plugin handed only a stream, or a
+ * latency-critical path that cannot take the device-wide synchronisation of
+ * cudaMalloc/cudaFree.  The scratch is a fixed CEB_MOE_STATIC_SCRATCH_BYTES
+ * array inside this library, held on every GPU that loads it until the process
+ * exits; the call itself allocates nothing (with instrumentation off, the
+ * default).  Computes what ceb_moe_ffn computes (y only).
+ *
+ * Limits and rules:
+ *  - n_tokens is limited by the scratch: ceb_moe_workspace_size(layer, n_tokens)
+ *    must not exceed CEB_MOE_STATIC_SCRATCH_BYTES (about 3000 tokens for d=768,
+ *    ffn=3072, top-2); larger batches are rejected with status 1 -- split them.
+ *  - The first call on a device looks the scratch up on that device; make that
+ *    first call before any stream capture.
+ *  - All calls on a device share the one scratch, which keeps the previous
+ *    call's contents: calls that overlap on the GPU (other streams, other host
+ *    threads) race and corrupt each other.  Serialise them.
+ */
+#define CEB_MOE_STATIC_SCRATCH_BYTES (64u << 20)
+CEB_API int ceb_moe_ffn_static(const ceb_moe_layer* layer, const void* d_x, int x_dtype, int n_tokens, float* d_y,
+                               void* stream);
+
+/*
  * Mean pool + L2 normalise, replacing the host loops of encode_tokens
  * (src/crispembed.cpp:1822-1846) and pool_and_norm (:2024-2045):
  *   p = mean over the rows of each sequence; out = p / sqrt(max(sum p^2, 1e-12)).
