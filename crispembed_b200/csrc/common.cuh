@@ -83,6 +83,24 @@ CEB_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int
         "l"(map), "r"(bar), "r"(x), "r"(y)
         : "memory");
 }
+// shared -> global tiled store, completion tracked by the issuing thread's bulk groups
+CEB_DEV void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+CEB_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N committed bulk groups still read their shared-memory source
+template <int N>
+CEB_DEV void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+CEB_DEV void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA, tcgen05)
+CEB_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 CEB_DEV void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

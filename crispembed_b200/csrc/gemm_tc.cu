@@ -7,23 +7,26 @@
 //
 //     out[r, n] = epilogue( sum_k W_g[n, k] * X[r, k] )
 //
-// Operand roles ("TS" form of tcgen05.mma, A from tensor memory):
-//   A = weight tile, 128 output features x 64 k, dequantized by eight warps
-//       straight from global memory (Q8_0 / Q4_K / fp16 planes) into TMEM,
-//       so the weights never pass through shared memory;
-//   B = activation tile, up to BN rows x 64 k fp16, loaded by TMA into
-//       128-byte-swizzled shared memory;
-//   D = fp32 accumulator in TMEM, [128 features (lanes)] x [BN rows (columns)],
-//       double buffered so the epilogue of one tile overlaps the next tile.
-// TMEM budget (512 columns): 2 x BN accumulator columns + SA x 32 A-stage columns.
+// Operands (tcgen05.mma kind::f16, both from shared memory, 128-byte swizzle):
+//   A = weight tile, 128 output features x 64 k, dequantized by eight warps from
+//       the Q8_0 / Q4_K / fp16 planes in global memory and written to shared
+//       memory in the MMA's swizzled K-major layout;
+//   B = activation tile, up to 256 rows x 64 k fp16, loaded by TMA;
+//   D = fp32 accumulator in TMEM, [128 features (lanes)] x [256 rows (columns)],
+//       double buffered (all 512 TMEM columns) so the epilogue of one tile
+//       overlaps the next tile.  An M=128,K=16 MMA costs the same time for any
+//       N <= 256, hence the full-width 256-row tile.
 //
 // Warp roles (640 threads, one persistent CTA per SM):
 //   warp 0        TMA producer of activation stages
 //   warp 1        TMEM owner + single-thread MMA issuer
 //   warps 4..11   dequant producers, two warpgroups taking alternate K-blocks
-//                 (thread i of a warpgroup <-> weight row / TMEM lane i)
-//   warps 12..19  epilogue, two warpgroups taking alternate 32-column chunks
-//                 (thread i <-> output feature i): bias, GELU, store
+//                 (thread i of a warpgroup <-> weight row i of the tile)
+//   warps 12..19  epilogue, two warpgroups taking alternate 32-row chunks
+//                 (thread i <-> output feature i): bias, GELU, then each warp
+//                 stages its 32x32 block in shared memory for one TMA store
+//                 (rows past a group's end are stored directly instead, so a
+//                 tile never writes into the next expert's rows)
 // Tiles (group, token tile, feature tile) are distributed round-robin; the
 // group table is read from device memory, so no host synchronisation is
 // needed between routing and the expert GEMMs.
@@ -35,21 +38,24 @@
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 192;               // activation rows (tokens) per tile = MMA N
+constexpr int BN = 256;               // activation rows (tokens) per tile = max MMA N
 constexpr int BK = 64;
-constexpr int SB = 6;                 // activation smem stages
-constexpr int SA = (512 - 2 * BN) / 32;  // TMEM A stages (4)
+constexpr int S = 3;                  // pipeline stages (A + B tiles)
 constexpr int MAXG = 64;
-constexpr int B_STAGE_BYTES = BN * BK * 2;
-constexpr uint32_t TMEM_COLS = 512;
-constexpr int A_COL0 = 2 * BN;
+constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KB, written by the dequant warps
+constexpr int B_STAGE_BYTES = BN * BK * 2;   // 32 KB, written by TMA
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr uint32_t TMEM_COLS = 512;          // two BN-column fp32 accumulators
 constexpr int DEQ_WG = 2, EPI_WG = 2;
 constexpr int DEQ_WARP0 = 4, EPI_WARP0 = DEQ_WARP0 + 4 * DEQ_WG;
 constexpr int NTHREADS = 32 * (EPI_WARP0 + 4 * EPI_WG);
-static_assert(SA >= 2 && A_COL0 + 32 * SA <= 512, "TMEM budget");
+constexpr int STAGING_SLOT = 32 * 32 * 4;    // one 32x32 fp32 output block per slot
+constexpr int STAGING_BYTES = 4 * EPI_WG * 2 * STAGING_SLOT;  // two slots per epilogue warp
+static_assert(2 * BN <= (int)TMEM_COLS, "TMEM budget");
 
-constexpr int NBARS = 2 * SB + 2 * SA + 4 + 1;
-constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)SB * B_STAGE_BYTES + NBARS * 8 + 16 + 3 * (MAXG + 1) * 4;
+constexpr int NBARS = 2 * S + 4 + 1;
+constexpr size_t SMEM_BYTES =
+    1024 /*align slack*/ + (size_t)S * STAGE_BYTES + STAGING_BYTES + NBARS * 8 + 16 + 3 * (MAXG + 1) * 4;
 
 struct Shared {
     uint64_t* bars;
@@ -58,14 +64,17 @@ struct Shared {
     int* g_tile;
     int* g_row;
     int* g_cnt;
-    uint8_t* b_stages;
+    uint8_t* stages;   // stage s: A at s*STAGE_BYTES, B right after
+    uint8_t* staging;  // epilogue output blocks
 };
 
 CEB_DEV Shared carve(uint8_t* raw) {
     Shared s;
     uintptr_t p = (reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023);
-    s.b_stages = reinterpret_cast<uint8_t*>(p);
-    p += (size_t)SB * B_STAGE_BYTES;
+    s.stages = reinterpret_cast<uint8_t*>(p);
+    p += (size_t)S * STAGE_BYTES;
+    s.staging = reinterpret_cast<uint8_t*>(p);
+    p += STAGING_BYTES;
     s.bars = reinterpret_cast<uint64_t*>(p);
     p += NBARS * 8;
     s.tmem_slot = reinterpret_cast<uint32_t*>(p);
@@ -78,28 +87,26 @@ CEB_DEV Shared carve(uint8_t* raw) {
 }
 
 // barrier indices
-CEB_DEV int BAR_B_FULL(int s) { return s; }
-CEB_DEV int BAR_B_EMPTY(int s) { return SB + s; }
-CEB_DEV int BAR_A_FULL(int s) { return 2 * SB + s; }
-CEB_DEV int BAR_A_EMPTY(int s) { return 2 * SB + SA + s; }
-CEB_DEV int BAR_ACC_FULL(int b) { return 2 * SB + 2 * SA + b; }
-CEB_DEV int BAR_ACC_EMPTY(int b) { return 2 * SB + 2 * SA + 2 + b; }
-CEB_DEV int BAR_DRAIN() { return 2 * SB + 2 * SA + 4; }
+CEB_DEV int BAR_FULL(int s) { return s; }       // TMA bytes + one arrive per dequant warp
+CEB_DEV int BAR_EMPTY(int s) { return S + s; }  // MMA commit
+CEB_DEV int BAR_ACC_FULL(int b) { return 2 * S + b; }
+CEB_DEV int BAR_ACC_EMPTY(int b) { return 2 * S + 2 + b; }
+CEB_DEV int BAR_DRAIN() { return 2 * S + 4; }
 
 struct TileInfo {
     int g, ft, row0, rows;
 };
 
-CEB_DEV TileInfo decode_tile(const Shared& S, int G, int n_ftiles, int t) {
+CEB_DEV TileInfo decode_tile(const Shared& S_, int G, int n_ftiles, int t) {
     int g = 0;
-    while (g + 1 < G && t >= S.g_tile[g + 1]) ++g;
-    int local = t - S.g_tile[g];
+    while (g + 1 < G && t >= S_.g_tile[g + 1]) ++g;
+    int local = t - S_.g_tile[g];
     TileInfo ti;
     ti.g = g;
     ti.ft = local % n_ftiles;
     int tt = local / n_ftiles;
-    ti.row0 = S.g_row[g] + tt * BN;
-    int rem = S.g_cnt[g] - tt * BN;
+    ti.row0 = S_.g_row[g] + tt * BN;
+    int rem = S_.g_cnt[g] - tt * BN;
     ti.rows = rem < BN ? rem : BN;
     return ti;
 }
@@ -205,25 +212,42 @@ CEB_DEV void convert<CEB_W_F16>(const Raw<CEB_W_F16>& r, uint32_t (&o)[32]) {
 }
 
 // erf-GELU 0.5 x (1 + erf(x / sqrt 2)) with erf from Abramowitz & Stegun 7.1.26
-// (|error| <= 1.5e-7 on erf), far below the fp16 rounding of the output.
+// (|error| <= 1.5e-7 on erf), far below the fp16/fp32 rounding of the output:
+//   z = |x|/sqrt2, t = 1/(1 + p z), erf(z) = 1 - t(a1 + t(a2 + t(a3 + t(a4 + t a5)))) exp(-z^2).
+// The reciprocal and the exponential use the MUFU approximations (rel. error ~2^-22),
+// exp(-z^2) as 2^(-(z sqrt(log2 e))^2) with the scaling folded into one constant.
+CEB_DEV float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+CEB_DEV float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
 CEB_DEV float gelu_as(float x) {
-    const float z = fabsf(x) * 0.70710678118654752f;
-    const float t = __frcp_rn(fmaf(0.3275911f, z, 1.0f));
+    constexpr float kZ = 0.70710678118654752f;             // 1/sqrt(2)
+    constexpr float kE = 0.84932180028801904f;             // sqrt(log2 e) / sqrt(2)
+    const float ax = fabsf(x);
+    const float t = rcp_approx(fmaf(0.3275911f * kZ, ax, 1.0f));
     float p = fmaf(1.061405429f, t, -1.453152027f);
     p = fmaf(p, t, 1.421413741f);
     p = fmaf(p, t, -0.284496736f);
     p = fmaf(p, t, 0.254829592f);
-    p *= t;
-    const float e = 1.0f - p * __expf(-z * z);  // erf(|x|/sqrt2)
-    const float erf_s = copysignf(e, x);
-    return 0.5f * x + 0.5f * x * erf_s;
+    const float u = ax * kE;
+    const float e = ex2_approx(-u * u);                     // exp(-x^2/2)
+    const float erf_abs = fmaf(-p * t, e, 1.0f);            // erf(|x|/sqrt2)
+    const float h = 0.5f * x;
+    return fmaf(fabsf(h), erf_abs, h);                      // 0.5x + 0.5|x| erf(|x|/sqrt2)
 }
 
 template <int FMT>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    ceb_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const ceb_wplane w, const ceb_gemm_args a) {
+    ceb_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap omap,
+                    const ceb_wplane w, const ceb_gemm_args a) {
     extern __shared__ uint8_t smem_raw[];
-    const Shared S = carve(smem_raw);
+    const Shared SH = carve(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.offsets ? w.n_groups : 1;
     const int n_ftiles = w.n_out / BM;
@@ -232,12 +256,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NBARS; ++i) {
             uint32_t cnt = 1;
-            if (i >= 2 * SB && i < 2 * SB + SA) cnt = 4;                                  // A full: one per dequant warp
-            if (i >= 2 * SB + 2 * SA + 2 && i < 2 * SB + 2 * SA + 4) cnt = 4 * EPI_WG;   // acc empty: epilogue warps
-            mbar_init(smem_u32(&S.bars[i]), cnt);
+            if (i < S) cnt = 1 + 4;                                     // stage full: TMA + 4 dequant warps
+            if (i >= 2 * S + 2 && i < 2 * S + 4) cnt = 4 * EPI_WG;      // acc empty: epilogue warps
+            mbar_init(smem_u32(&SH.bars[i]), cnt);
         }
         fence_mbar_init();
-        *S.abort = 0;
+        *SH.abort = 0;
         int tiles = 0;
         for (int g = 0; g < G; ++g) {
             int r0 = a.offsets ? a.offsets[g] : 0;
@@ -246,48 +270,51 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (a.err) atomicCAS(a.err, 0, (int)CEB_DEVERR_BAD_GROUP);
                 r0 = r1 = 0;
             }
-            S.g_tile[g] = tiles;
-            S.g_row[g] = r0;
-            S.g_cnt[g] = r1 - r0;
+            SH.g_tile[g] = tiles;
+            SH.g_row[g] = r0;
+            SH.g_cnt[g] = r1 - r0;
             tiles += ((r1 - r0 + BN - 1) / BN) * n_ftiles;
         }
-        S.g_tile[G] = tiles;
+        SH.g_tile[G] = tiles;
     }
-    if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap);
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmap);
+        tma_prefetch_desc(&omap);
+    }
     if (warp == 1) {
-        tmem_alloc(smem_u32(S.tmem_slot), TMEM_COLS);
+        tmem_alloc(smem_u32(SH.tmem_slot), TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *S.tmem_slot;
-    const int total = S.g_tile[G];
-    volatile int* abort = S.abort;
-    auto bar = [&](int i) { return smem_u32(&S.bars[i]); };
+    const uint32_t tmem = *SH.tmem_slot;
+    const int total = SH.g_tile[G];
+    volatile int* abort = SH.abort;
+    auto bar = [&](int i) { return smem_u32(&SH.bars[i]); };
+    auto a_stage = [&](int s) { return SH.stages + (size_t)s * STAGE_BYTES; };
+    auto b_stage = [&](int s) { return SH.stages + (size_t)s * STAGE_BYTES + A_STAGE_BYTES; };
 
     if (warp == 0) {
-        // ------------------------------------------------ TMA producer
+        // ------------------------------------------------ TMA producer (activation tiles)
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                const TileInfo ti = decode_tile(S, G, n_ftiles, t);
+                const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % SB;
-                    if (!mbar_wait(bar(BAR_B_EMPTY(s)), ((it / SB) & 1) ^ 1, abort, a.err, CEB_DEVERR_TIMEOUT_TMA)) {
+                    const int s = it % S;
+                    if (!mbar_wait(bar(BAR_EMPTY(s)), ((it / S) & 1) ^ 1, abort, a.err, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(bar(BAR_B_FULL(s)), B_STAGE_BYTES);
-                    tma_load_2d(smem_u32(S.b_stages + (size_t)s * B_STAGE_BYTES), &tmap, bar(BAR_B_FULL(s)), kb * BK,
-                                ti.row0);
+                    mbar_arrive_expect_tx(bar(BAR_FULL(s)), B_STAGE_BYTES);
+                    tma_load_2d(smem_u32(b_stage(s)), &tmap, bar(BAR_FULL(s)), kb * BK, ti.row0);
                 }
             }
             if (!ok) {  // let issued copies land before the CTA can exit
-                const uint32_t n = it < SB ? it : SB;
-                for (uint32_t i = it - n; i < it; ++i)
-                    mbar_wait(bar(BAR_B_FULL(i % SB)), (i / SB) & 1, nullptr, nullptr, 0);
+                const uint32_t n = it < S ? it : S;
+                for (uint32_t i = it - n; i < it; ++i) mbar_wait(bar(BAR_FULL(i % S)), (i / S) & 1, nullptr, nullptr, 0);
             }
         }
     } else if (warp == 1) {
@@ -296,7 +323,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t it = 0, lt = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++lt) {
-                const TileInfo ti = decode_tile(S, G, n_ftiles, t);
+                const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
                 const int ab = lt & 1;
                 if (!mbar_wait(bar(BAR_ACC_EMPTY(ab)), ((lt >> 1) & 1) ^ 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA)) break;
                 tc_fence_after();
@@ -305,20 +332,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t idesc = idesc_f16_f32(BM, n);
                 const uint32_t d_tmem = tmem + (uint32_t)(ab * BN);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % SB, sa = it % SA;
-                    if (!mbar_wait(bar(BAR_A_FULL(sa)), (it / SA) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA) ||
-                        !mbar_wait(bar(BAR_B_FULL(s)), (it / SB) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA)) {
+                    const int s = it % S;
+                    if (!mbar_wait(bar(BAR_FULL(s)), (it / S) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(S.b_stages + (size_t)s * B_STAGE_BYTES));
-                    const uint32_t a_tmem = tmem + (uint32_t)(A_COL0 + sa * 32);
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(a_stage(s)));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(b_stage(s)));
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
-                        mma_f16_ts(d_tmem, a_tmem + kk * 8, bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
-                    mma_commit(bar(BAR_B_EMPTY(s)));
-                    mma_commit(bar(BAR_A_EMPTY(sa)));
+                        mma_f16_ss(d_tmem, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
+                                   (kb | kk) != 0);
+                    mma_commit(bar(BAR_EMPTY(s)));
                 }
                 if (ok) mma_commit(bar(BAR_ACC_FULL(ab)));
             }
@@ -327,20 +353,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_wait(bar(BAR_DRAIN()), 0, nullptr, nullptr, 0);
         }
     } else if (warp >= DEQ_WARP0 && warp < EPI_WARP0) {
-        // ------------------------------------------------ dequant producers
+        // ------------------------------------------------ dequant producers (weight tiles)
         const int wg = (warp - DEQ_WARP0) >> 2;  // this warpgroup takes items i with i % DEQ_WG == wg
-        const int r = 32 * (warp & 3) + lane;    // weight row within the tile == TMEM lane
-        const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
+        const int r = 32 * (warp & 3) + lane;    // weight row within the tile
         const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
         const int n_items = my_tiles * nkb;
         constexpr int PF = Prefetch<FMT>::depth;
         Raw<FMT> buf[PF];
         auto item_load = [&](int i, Raw<FMT>& dst) {
             const int t = blockIdx.x + (i / nkb) * gridDim.x;
-            const TileInfo ti = decode_tile(S, G, n_ftiles, t);
+            const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
             load_raw<FMT>(w, ti.g, ti.ft * BM + r, i % nkb, dst);
         };
-        // own items: i_j = wg + j * DEQ_WG
         const int n_mine = n_items > wg ? (n_items - 1 - wg) / DEQ_WG + 1 : 0;
 #pragma unroll
         for (int u = 0; u < PF - 1; ++u)
@@ -353,64 +377,85 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (j < n_mine && ok) {
                     if (j + PF - 1 < n_mine) item_load(wg + (j + PF - 1) * DEQ_WG, buf[(u + PF - 1) % PF]);
                     const int i = wg + j * DEQ_WG;
-                    const int sa = i % SA;
-                    const bool got = __all_sync(0xffffffffu, mbar_wait(bar(BAR_A_EMPTY(sa)), ((i / SA) & 1) ^ 1,
-                                                                       abort, a.err, CEB_DEVERR_TIMEOUT_DEQ));
+                    const int s = i % S;
+                    uint32_t o[32];
+                    convert<FMT>(buf[u], o);
+                    const bool got = __all_sync(0xffffffffu, mbar_wait(bar(BAR_EMPTY(s)), ((i / S) & 1) ^ 1, abort,
+                                                                       a.err, CEB_DEVERR_TIMEOUT_DEQ));
                     if (!got) {
                         ok = false;
                     } else {
-                        tc_fence_after();
-                        uint32_t o[32];
-                        convert<FMT>(buf[u], o);
-                        tmem_st32(tmem + lane_addr + (uint32_t)(A_COL0 + sa * 32), o);
-                        tmem_st_wait();
-                        tc_fence_before();
+                        // 128-byte swizzled K-major row: 16-byte chunk c lands at chunk c ^ (row & 7)
+                        uint8_t* row = a_stage(s) + r * 128;
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
+                                make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                        fence_proxy_async_smem();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(bar(BAR_A_FULL(sa)));
+                        if (lane == 0) mbar_arrive(bar(BAR_FULL(s)));
                     }
                 }
             }
         }
     } else if (warp >= EPI_WARP0) {
         // ------------------------------------------------ epilogue
-        const int wg = (warp - EPI_WARP0) >> 2;  // this warpgroup takes 32-column chunks c with c % EPI_WG == wg
-        const int r = 32 * (warp & 3) + lane;    // output feature within the tile
-        const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
+        const int ew = warp - EPI_WARP0;
+        const int wg = ew >> 2;                  // this warpgroup takes 32-column chunks c with c % EPI_WG == wg
+        const int q = warp & 3;                  // features 32q .. 32q+31 of the tile (TMEM lanes)
+        const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
         const bool f16 = (a.epi & CEB_EPI_F16_OUT) != 0, gelu = (a.epi & CEB_EPI_GELU) != 0;
-        uint32_t lt = 0;
+        const int esz = f16 ? 2 : 4;
+        uint8_t* slots = SH.staging + (size_t)ew * 2 * STAGING_SLOT;
+        uint32_t lt = 0, nstore = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
-            const TileInfo ti = decode_tile(S, G, n_ftiles, t);
+            const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
             const int ab = lt & 1;
             if (!__all_sync(0xffffffffu,
                             mbar_wait(bar(BAR_ACC_FULL(ab)), (lt >> 1) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_EPI)))
                 break;
             tc_fence_after();
-            const int n = ti.ft * BM + r;
+            const int n0 = ti.ft * BM + 32 * q;
+            const int n = n0 + lane;
             const float bv = (a.epi & CEB_EPI_BIAS) ? a.bias[(size_t)ti.g * a.bias_group_stride + n] : 0.0f;
             for (int c0 = 32 * wg; c0 < ti.rows; c0 += 32 * EPI_WG) {
                 uint32_t v[32];
                 tmem_ld32(tmem + lane_addr + (uint32_t)(ab * BN + c0), v);
                 tmem_ld_wait();
-                const int lim = ti.rows - c0 < 32 ? ti.rows - c0 : 32;
                 float x[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     x[j] = __uint_as_float(v[j]) + bv;
                     if (gelu) x[j] = gelu_as(x[j]);
                 }
-                if (f16) {
-                    // lane pairs (2i, 2i+1) exchange so each lane stores a half2 of
-                    // features (2i, 2i+1): even lanes for even rows, odd lanes for odd rows
-                    const bool odd = lane & 1;
-                    __half* o = reinterpret_cast<__half*>(a.out) + (size_t)(ti.row0 + c0) * a.ldo + (n & ~1);
-#pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        const float send = odd ? x[j] : x[j + 1];
-                        const float got = __shfl_xor_sync(0xffffffffu, send, 1);
-                        const int row = odd ? j + 1 : j;
-                        const __half2 hv = odd ? __floats2half2_rn(got, x[j + 1]) : __floats2half2_rn(x[j], got);
-                        if (row < lim) *reinterpret_cast<__half2*>(o + (size_t)row * a.ldo) = hv;
+                const int lim = ti.rows - c0;
+                if (lim >= 32) {
+                    // full 32-row block: stage [row][feature] in shared memory, one TMA store
+                    uint8_t* slot = slots + (nstore & 1) * STAGING_SLOT;
+                    if (nstore >= 2) {
+                        if (lane == 0) bulk_wait_read<1>();
+                        __syncwarp();
                     }
+                    if (f16) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            reinterpret_cast<__half*>(slot)[j * 32 + lane] = __float2half_rn(x[j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) reinterpret_cast<float*>(slot)[j * 32 + lane] = x[j];
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&omap, smem_u32(slot), n0, ti.row0 + c0);
+                        bulk_commit();
+                    }
+                    ++nstore;
+                } else if (f16) {
+                    __half* o = reinterpret_cast<__half*>(a.out) + (size_t)(ti.row0 + c0) * a.ldo + n;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < lim) o[(size_t)j * a.ldo] = __float2half_rn(x[j]);
                 } else {
                     float* o = reinterpret_cast<float*>(a.out) + (size_t)(ti.row0 + c0) * a.ldo + n;
 #pragma unroll
@@ -422,6 +467,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(BAR_ACC_EMPTY(ab)));
         }
+        (void)esz;
+        if (lane == 0) bulk_wait<0>();  // output stores complete before the CTA retires
     }
 
     tc_fence_before();
@@ -433,14 +480,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 template <int FMT>
-int launch_fmt(const CUtensorMap& map, const ceb_wplane& w, const ceb_gemm_args& a, int grid, cudaStream_t st) {
+int launch_fmt(const CUtensorMap& map, const CUtensorMap& omap, const ceb_wplane& w, const ceb_gemm_args& a, int grid,
+               cudaStream_t st) {
     static bool attr_set = false;
     if (!attr_set) {
         CEB_CUDA_OK(cudaFuncSetAttribute(ceb_gemm_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)SMEM_BYTES));
         attr_set = true;
     }
-    ceb_gemm_kernel<FMT><<<grid, NTHREADS, SMEM_BYTES, st>>>(map, w, a);
+    ceb_gemm_kernel<FMT><<<grid, NTHREADS, SMEM_BYTES, st>>>(map, omap, w, a);
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
@@ -456,8 +504,14 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
     if ((reinterpret_cast<uintptr_t>(act_f16) & 15) != 0) return ceb_set_error(2, "gemm: activations not 16-B aligned");
     if ((a.epi & CEB_EPI_F16_OUT) && (a.ldo & 1)) return ceb_set_error(2, "gemm: fp16 output stride must be even");
     if (act_rows <= 0) return 0;
-    CUtensorMap map;
-    const int mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);
+    CUtensorMap map, omap;
+    int mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);
+    if (mrc) return mrc;
+    const int esz = (a.epi & CEB_EPI_F16_OUT) ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(a.out) & 15) || ((size_t)a.ldo * esz) % 16 || a.ldo < w.n_out)
+        return ceb_set_error(2, "gemm: output must be 16-B aligned with a row stride >= n_out and a multiple of 16 B");
+    mrc = ceb_make_tmap_2d(&omap, a.out, esz, (uint64_t)w.n_out, (uint64_t)a.m_rows, (uint64_t)a.ldo * esz, 32, 32,
+                           false);
     if (mrc) return mrc;
     const int n_ftiles = w.n_out / BM;
     const int groups = a.offsets ? w.n_groups : 1;
@@ -470,9 +524,9 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
                          (double)a.m_rows * w.n_out * ((a.epi & CEB_EPI_F16_OUT) ? 2 : 4);
     int rc = 0;
     switch (w.format) {
-        case CEB_W_Q8_0: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q8_0>(map, w, a, grid, stream)); break;
-        case CEB_W_Q4_K: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q4_K>(map, w, a, grid, stream)); break;
-        case CEB_W_F16: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_F16>(map, w, a, grid, stream)); break;
+        case CEB_W_Q8_0: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q8_0>(map, omap, w, a, grid, stream)); break;
+        case CEB_W_Q4_K: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q4_K>(map, omap, w, a, grid, stream)); break;
+        case CEB_W_F16: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_F16>(map, omap, w, a, grid, stream)); break;
         default: return ceb_set_error(2, "gemm: unknown weight format %d", w.format);
     }
     return rc;

@@ -66,21 +66,28 @@ EncodeTiledFn encode_fn() {
 }
 }  // namespace
 
-int ceb_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
-                         uint32_t box_inner, uint32_t box_rows) {
+int ceb_make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                     uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return ceb_set_error(3, "cuTensorMapEncodeTiled unavailable");
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15))
         return ceb_set_error(2, "tensor map: base/stride not 16-byte aligned");
+    if ((box_inner * (uint32_t)elem_bytes) & 15) return ceb_set_error(2, "tensor map: box inner extent not 16-byte multiple");
     cuuint64_t dims[2] = {inner, rows};
     cuuint64_t strides[1] = {row_stride_bytes};
     cuuint32_t box[2] = {box_inner, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return ceb_set_error(3, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return 0;
+}
+
+int ceb_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                         uint32_t box_inner, uint32_t box_rows) {
+    return ceb_make_tmap_2d(map, base, 2, inner, rows, row_stride_bytes, box_inner, box_rows, true);
 }
 
 // ------------------------------------------------------------------ repack
