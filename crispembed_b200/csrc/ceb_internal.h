@@ -13,20 +13,31 @@
 // ggml tensor types used on the path (values are ggml's enum)
 enum { CEB_GGML_F32 = 0, CEB_GGML_F16 = 1, CEB_GGML_Q8_0 = 8, CEB_GGML_Q4_K = 12 };
 
-// Device weight-plane formats consumed by the grouped GEMM.
+// Device weight formats consumed by the grouped GEMM.  Weights are stored
+// tile-major: one contiguous block per (group, 128-row feature tile, 64-wide
+// k-block), blocks ordered [group][feature tile][k-block], so the GEMM streams
+// each block into shared memory with one bulk copy.  Inside a block (row r of
+// the tile, 16-byte chunks XOR-swizzled so a warp reading one chunk of 32
+// consecutive rows hits distinct shared-memory banks):
 enum ceb_wformat : int {
-    CEB_W_F16 = 0,   // fp16 [G][N][K]
-    CEB_W_Q8_0 = 1,  // int8 [G][N][K] + fp16 scale [G][N][K/32]
-    CEB_W_Q4_K = 2,  // nibbles [G][N][K/2] (ggml in-chunk order) + float2 (d*sc, dmin*m) [G][N][K/32]
+    CEB_W_F16 = 0,   // 16384 B: row r at r*128, chunk c (k 8c..8c+7) at chunk c^(r&7) -- the
+                     //          128-byte-swizzled K-major image the MMA reads directly
+    CEB_W_Q8_0 = 1,  //  8704 B: int8 quants row r at r*64, chunk c (k 16c..16c+15) at chunk c^((r>>1)&3);
+                     //          then the two fp16 block scales of each row at 8192 + 4r
+    CEB_W_Q4_K = 2,  //  6144 B: ggml nibble bytes of the 64-chunk, row r at r*32, chunk c at c^((r>>2)&1);
+                     //          then (d*sc, dmin*m) floats of the two sub-blocks of each row at 4096 + 16r
 };
+
+constexpr int ceb_wblock_bytes(int format) {
+    return format == CEB_W_F16 ? 16384 : format == CEB_W_Q8_0 ? 8704 : 6144;
+}
 
 // A repacked weight matrix set: n_groups matrices of [n_out x k] (experts, or 1 for dense).
 struct ceb_wplane {
     int format = CEB_W_F16;
     int n_groups = 0, n_out = 0, k = 0;
-    uint8_t* q = nullptr;  // quant plane (device)
-    uint8_t* s = nullptr;  // scale plane (device), null for F16
-    int64_t q_row_bytes = 0, s_row_bytes = 0;
+    uint8_t* q = nullptr;    // tile-major blocks (device)
+    int64_t blk_bytes = 0;   // bytes per (group, feature tile, k-block) block
     size_t q_bytes = 0, s_bytes = 0;
 };
 

@@ -83,6 +83,12 @@ CEB_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int
         "l"(map), "r"(bar), "r"(x), "r"(y)
         : "memory");
 }
+// contiguous global -> shared bulk copy (16-byte aligned addresses, size a multiple of 16)
+CEB_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
 // shared -> global tiled store, completion tracked by the issuing thread's bulk groups
 CEB_DEV void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),

@@ -41,6 +41,8 @@ constexpr int BM = 128;
 constexpr int BN = 256;               // activation rows (tokens) per tile = max MMA N
 constexpr int BK = 64;
 constexpr int S = 3;                  // pipeline stages (A + B tiles)
+constexpr int R = 4;                  // raw (still quantized) weight stages
+constexpr int RAW_STAGE = 8704;       // largest quantized block (Q8_0)
 constexpr int MAXG = 64;
 constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KB, written by the dequant warps
 constexpr int B_STAGE_BYTES = BN * BK * 2;   // 32 KB, written by TMA
@@ -50,12 +52,13 @@ constexpr int DEQ_WG = 2, EPI_WG = 2;
 constexpr int DEQ_WARP0 = 4, EPI_WARP0 = DEQ_WARP0 + 4 * DEQ_WG;
 constexpr int NTHREADS = 32 * (EPI_WARP0 + 4 * EPI_WG);
 constexpr int STAGING_SLOT = 32 * 32 * 4;    // one 32x32 fp32 output block per slot
-constexpr int STAGING_BYTES = 4 * EPI_WG * 2 * STAGING_SLOT;  // two slots per epilogue warp
+constexpr int STAGING_BYTES = 4 * EPI_WG * STAGING_SLOT;  // one slot per epilogue warp
 static_assert(2 * BN <= (int)TMEM_COLS, "TMEM budget");
 
-constexpr int NBARS = 2 * S + 4 + 1;
-constexpr size_t SMEM_BYTES =
-    1024 /*align slack*/ + (size_t)S * STAGE_BYTES + STAGING_BYTES + NBARS * 8 + 16 + 3 * (MAXG + 1) * 4;
+constexpr int NBARS = 2 * S + 4 + 1 + 2 * R;
+constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)S * STAGE_BYTES + (size_t)R * RAW_STAGE + STAGING_BYTES +
+                              NBARS * 8 + 16 + 3 * (MAXG + 1) * 4;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 struct Shared {
     uint64_t* bars;
@@ -65,6 +68,7 @@ struct Shared {
     int* g_row;
     int* g_cnt;
     uint8_t* stages;   // stage s: A at s*STAGE_BYTES, B right after
+    uint8_t* raw;      // raw weight stages
     uint8_t* staging;  // epilogue output blocks
 };
 
@@ -73,6 +77,8 @@ CEB_DEV Shared carve(uint8_t* raw) {
     uintptr_t p = (reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023);
     s.stages = reinterpret_cast<uint8_t*>(p);
     p += (size_t)S * STAGE_BYTES;
+    s.raw = reinterpret_cast<uint8_t*>(p);
+    p += (size_t)R * RAW_STAGE;
     s.staging = reinterpret_cast<uint8_t*>(p);
     p += STAGING_BYTES;
     s.bars = reinterpret_cast<uint64_t*>(p);
@@ -92,6 +98,8 @@ CEB_DEV int BAR_EMPTY(int s) { return S + s; }  // MMA commit
 CEB_DEV int BAR_ACC_FULL(int b) { return 2 * S + b; }
 CEB_DEV int BAR_ACC_EMPTY(int b) { return 2 * S + 2 + b; }
 CEB_DEV int BAR_DRAIN() { return 2 * S + 4; }
+CEB_DEV int BAR_RAW_FULL(int r) { return 2 * S + 5 + r; }      // bulk-copy bytes
+CEB_DEV int BAR_RAW_EMPTY(int r) { return 2 * S + 5 + R + r; } // one arrive per dequant warp
 
 struct TileInfo {
     int g, ft, row0, rows;
@@ -129,42 +137,26 @@ struct Raw<CEB_W_F16> {
     uint4 q[8];
 };
 
-// dequant prefetch depth (K-blocks in flight per thread of one warpgroup)
+// Row r's share of a raw block in shared memory (layouts in ceb_internal.h).
 template <int FMT>
-struct Prefetch {
-    static constexpr int depth = FMT == CEB_W_F16 ? 1 : 2;
-};
-
-CEB_DEV uint4 ldg128(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
-
-template <int FMT>
-CEB_DEV void load_raw(const ceb_wplane& w, int g, int row, int kb, Raw<FMT>& r);
+CEB_DEV void load_raw_smem(const uint8_t* blk, int r, Raw<FMT>& out);
 
 template <>
-CEB_DEV void load_raw<CEB_W_Q8_0>(const ceb_wplane& w, int g, int row, int kb, Raw<CEB_W_Q8_0>& r) {
-    const size_t grow = (size_t)g * w.n_out + row;
-    const uint8_t* q = w.q + grow * w.q_row_bytes + (size_t)kb * 64;
+CEB_DEV void load_raw_smem<CEB_W_Q8_0>(const uint8_t* blk, int r, Raw<CEB_W_Q8_0>& o) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) r.q[i] = ldg128(q + 16 * i);
-    r.sc = __ldg(reinterpret_cast<const uint32_t*>(w.s + grow * w.s_row_bytes + (size_t)kb * 4));
+    for (int c = 0; c < 4; ++c) o.q[c] = *reinterpret_cast<const uint4*>(blk + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+    o.sc = *reinterpret_cast<const uint32_t*>(blk + 8192 + 4 * r);
 }
 template <>
-CEB_DEV void load_raw<CEB_W_Q4_K>(const ceb_wplane& w, int g, int row, int kb, Raw<CEB_W_Q4_K>& r) {
-    const size_t grow = (size_t)g * w.n_out + row;
-    const uint8_t* q = w.q + grow * w.q_row_bytes + (size_t)kb * 32;
-    r.q[0] = ldg128(q);
-    r.q[1] = ldg128(q + 16);
-    r.s = ldg128(w.s + grow * w.s_row_bytes + (size_t)kb * 16);
-}
-template <>
-CEB_DEV void load_raw<CEB_W_F16>(const ceb_wplane& w, int g, int row, int kb, Raw<CEB_W_F16>& r) {
-    const size_t grow = (size_t)g * w.n_out + row;
-    const uint8_t* q = w.q + grow * w.q_row_bytes + (size_t)kb * 128;
+CEB_DEV void load_raw_smem<CEB_W_Q4_K>(const uint8_t* blk, int r, Raw<CEB_W_Q4_K>& o) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) r.q[i] = ldg128(q + 16 * i);
+    for (int c = 0; c < 2; ++c) o.q[c] = *reinterpret_cast<const uint4*>(blk + r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
+    o.s = *reinterpret_cast<const uint4*>(blk + 4096 + 16 * r);
 }
+template <>
+CEB_DEV void load_raw_smem<CEB_W_F16>(const uint8_t*, int, Raw<CEB_W_F16>&) {}
 
-// ---- conversion into the TMEM A layout: column c holds k = 2c (low half), 2c+1
+// ---- conversion to fp16 pairs: word c holds k = 2c (low half), 2c+1
 template <int FMT>
 CEB_DEV void convert(const Raw<FMT>& r, uint32_t (&o)[32]);
 
@@ -256,7 +248,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NBARS; ++i) {
             uint32_t cnt = 1;
-            if (i < S) cnt = 1 + 4;                                     // stage full: TMA + 4 dequant warps
+            if (i < S) cnt = FMT == CEB_W_F16 ? 1 : 1 + 4;              // stage full: TMA (+ 4 dequant warps)
+            if (i >= 2 * S + 5 + R && i < 2 * S + 5 + 2 * R) cnt = 4;  // raw empty: one dequant warpgroup
             if (i >= 2 * S + 2 && i < 2 * S + 4) cnt = 4 * EPI_WG;      // acc empty: epilogue warps
             mbar_init(smem_u32(&SH.bars[i]), cnt);
         }
@@ -294,6 +287,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto bar = [&](int i) { return smem_u32(&SH.bars[i]); };
     auto a_stage = [&](int s) { return SH.stages + (size_t)s * STAGE_BYTES; };
     auto b_stage = [&](int s) { return SH.stages + (size_t)s * STAGE_BYTES + A_STAGE_BYTES; };
+    auto wblock = [&](const TileInfo& ti, int kb) {
+        return w.q + (((size_t)ti.g * n_ftiles + ti.ft) * nkb + kb) * (size_t)w.blk_bytes;
+    };
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer (activation tiles)
@@ -308,7 +304,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(bar(BAR_FULL(s)), B_STAGE_BYTES);
+                    if (FMT == CEB_W_F16) {  // fp16 weights are stored as the swizzled A image
+                        mbar_arrive_expect_tx(bar(BAR_FULL(s)), B_STAGE_BYTES + A_STAGE_BYTES);
+                        bulk_load(smem_u32(a_stage(s)), wblock(ti, kb), A_STAGE_BYTES, bar(BAR_FULL(s)));
+                    } else {
+                        mbar_arrive_expect_tx(bar(BAR_FULL(s)), B_STAGE_BYTES);
+                    }
                     tma_load_2d(smem_u32(b_stage(s)), &tmap, bar(BAR_FULL(s)), kb * BK, ti.row0);
                 }
             }
@@ -352,50 +353,60 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mma_commit(bar(BAR_DRAIN()));
             mbar_wait(bar(BAR_DRAIN()), 0, nullptr, nullptr, 0);
         }
-    } else if (warp >= DEQ_WARP0 && warp < EPI_WARP0) {
-        // ------------------------------------------------ dequant producers (weight tiles)
-        const int wg = (warp - DEQ_WARP0) >> 2;  // this warpgroup takes items i with i % DEQ_WG == wg
-        const int r = 32 * (warp & 3) + lane;    // weight row within the tile
-        const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-        const int n_items = my_tiles * nkb;
-        constexpr int PF = Prefetch<FMT>::depth;
-        Raw<FMT> buf[PF];
-        auto item_load = [&](int i, Raw<FMT>& dst) {
-            const int t = blockIdx.x + (i / nkb) * gridDim.x;
-            const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
-            load_raw<FMT>(w, ti.g, ti.ft * BM + r, i % nkb, dst);
-        };
-        const int n_mine = n_items > wg ? (n_items - 1 - wg) / DEQ_WG + 1 : 0;
-#pragma unroll
-        for (int u = 0; u < PF - 1; ++u)
-            if (u < n_mine) item_load(wg + u * DEQ_WG, buf[u]);
-        bool ok = true;
-        for (int j0 = 0; j0 < n_mine && ok; j0 += PF) {
-#pragma unroll
-            for (int u = 0; u < PF; ++u) {
-                const int j = j0 + u;
-                if (j < n_mine && ok) {
-                    if (j + PF - 1 < n_mine) item_load(wg + (j + PF - 1) * DEQ_WG, buf[(u + PF - 1) % PF]);
-                    const int i = wg + j * DEQ_WG;
-                    const int s = i % S;
-                    uint32_t o[32];
-                    convert<FMT>(buf[u], o);
-                    const bool got = __all_sync(0xffffffffu, mbar_wait(bar(BAR_EMPTY(s)), ((i / S) & 1) ^ 1, abort,
-                                                                       a.err, CEB_DEVERR_TIMEOUT_DEQ));
-                    if (!got) {
+    } else if (warp == 2) {
+        // ------------------------------------------------ weight loader (quantized blocks -> raw stages)
+        if (FMT != CEB_W_F16 && lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int rs = it % R;
+                    if (!mbar_wait(bar(BAR_RAW_EMPTY(rs)), ((it / R) & 1) ^ 1, abort, a.err, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
-                    } else {
-                        // 128-byte swizzled K-major row: 16-byte chunk c lands at chunk c ^ (row & 7)
-                        uint8_t* row = a_stage(s) + r * 128;
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
-                                make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(bar(BAR_FULL(s)));
+                        break;
                     }
+                    mbar_arrive_expect_tx(bar(BAR_RAW_FULL(rs)), (uint32_t)w.blk_bytes);
+                    bulk_load(smem_u32(SH.raw + (size_t)rs * RAW_STAGE), wblock(ti, kb), (uint32_t)w.blk_bytes,
+                              bar(BAR_RAW_FULL(rs)));
                 }
+            }
+            if (!ok) {  // let issued copies land before the CTA can exit
+                const uint32_t n = it < R ? it : R;
+                for (uint32_t i = it - n; i < it; ++i)
+                    mbar_wait(bar(BAR_RAW_FULL(i % R)), (i / R) & 1, nullptr, nullptr, 0);
+            }
+        }
+    } else if (warp >= DEQ_WARP0 && warp < EPI_WARP0) {
+        // ------------------------------------------------ dequant (raw stage -> fp16 A stage)
+        if (FMT != CEB_W_F16) {
+            const int wg = (warp - DEQ_WARP0) >> 2;  // this warpgroup takes items i with i % DEQ_WG == wg
+            const int r = 32 * (warp & 3) + lane;    // weight row within the tile
+            const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+            const int n_items = my_tiles * nkb;
+            for (int i = wg; i < n_items; i += DEQ_WG) {
+                const int rs = i % R, s = i % S;
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(BAR_RAW_FULL(rs)), (i / R) & 1, abort, a.err,
+                                                       CEB_DEVERR_TIMEOUT_DEQ)))
+                    break;
+                Raw<FMT> raw;
+                load_raw_smem<FMT>(SH.raw + (size_t)rs * RAW_STAGE, r, raw);
+                uint32_t o[32];
+                convert<FMT>(raw, o);  // consumes the loaded values: the raw stage may be refilled now
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(BAR_RAW_EMPTY(rs)));
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(BAR_EMPTY(s)), ((i / S) & 1) ^ 1, abort, a.err,
+                                                       CEB_DEVERR_TIMEOUT_DEQ)))
+                    break;
+                // 128-byte swizzled K-major row: 16-byte chunk c lands at chunk c ^ (row & 7)
+                uint8_t* row = a_stage(s) + r * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
+                        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(BAR_FULL(s)));
             }
         }
     } else if (warp >= EPI_WARP0) {
@@ -406,7 +417,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
         const bool f16 = (a.epi & CEB_EPI_F16_OUT) != 0, gelu = (a.epi & CEB_EPI_GELU) != 0;
         const int esz = f16 ? 2 : 4;
-        uint8_t* slots = SH.staging + (size_t)ew * 2 * STAGING_SLOT;
+        uint8_t* slot = SH.staging + (size_t)ew * STAGING_SLOT;
         uint32_t lt = 0, nstore = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
             const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
@@ -431,9 +442,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int lim = ti.rows - c0;
                 if (lim >= 32) {
                     // full 32-row block: stage [row][feature] in shared memory, one TMA store
-                    uint8_t* slot = slots + (nstore & 1) * STAGING_SLOT;
-                    if (nstore >= 2) {
-                        if (lane == 0) bulk_wait_read<1>();
+                    if (nstore >= 1) {  // the previous store has finished reading the slot
+                        if (lane == 0) bulk_wait_read<0>();
                         __syncwarp();
                     }
                     if (f16) {

@@ -124,82 +124,72 @@ int64_t ceb_ggml_row_bytes(int type, int64_t k) {
     return -1;
 }
 
-// GGUF rows -> device planes.
-//   Q8_0: int8 quants [rows][k], fp16 scales [rows][k/32] (block headers split off).
-//   Q4_K: the 128 quant bytes of every super-block back to back (ggml's in-chunk
-//         nibble order kept), plus per 32-value sub-block the pair
-//         (d*sc, dmin*m) as floats, computed exactly as ggml's dequantizer does.
-//   F32/F16: fp16 plane (F32 rounded to nearest even).
+// GGUF rows -> tile-major device blocks (layout in ceb_internal.h).  Values are
+// not changed: Q8_0 keeps its int8 quants and fp16 scales, Q4_K its nibbles with
+// (d*sc, dmin*m) computed per sub-block exactly as ggml's dequantizer does, F32
+// weights are rounded to fp16 (nearest even).
 int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int n_groups, int n_out, int k,
                        cudaStream_t stream) {
-    const int64_t rows = (int64_t)n_groups * n_out;
     const int64_t rb = ceb_ggml_row_bytes(ggml_type, k);
     if (rb < 0) return ceb_set_error(2, "repack: unsupported type %d for k=%d", ggml_type, k);
+    if (n_out % 128 || k % 64)
+        return ceb_set_error(2, "repack: n_out=%d must be a multiple of 128 and k=%d of 64", n_out, k);
     const uint8_t* src = static_cast<const uint8_t*>(host_raw);
     ceb_wplane w;
     w.n_groups = n_groups;
     w.n_out = n_out;
     w.k = k;
-    std::vector<uint8_t> q, s;
-    if (ggml_type == CEB_GGML_Q8_0) {
-        w.format = CEB_W_Q8_0;
-        w.q_row_bytes = k;
-        w.s_row_bytes = (int64_t)(k / 32) * 2;
-        q.resize((size_t)(rows * w.q_row_bytes));
-        s.resize((size_t)(rows * w.s_row_bytes));
-        for (int64_t r = 0; r < rows; ++r) {
-            const uint8_t* row = src + r * rb;
-            for (int b = 0; b < k / 32; ++b) {
-                memcpy(&s[(size_t)(r * w.s_row_bytes + b * 2)], row + b * 34, 2);
-                memcpy(&q[(size_t)(r * w.q_row_bytes + b * 32)], row + b * 34 + 2, 32);
-            }
-        }
-    } else if (ggml_type == CEB_GGML_Q4_K) {
-        w.format = CEB_W_Q4_K;
-        w.q_row_bytes = k / 2;
-        w.s_row_bytes = (int64_t)(k / 32) * 8;
-        q.resize((size_t)(rows * w.q_row_bytes));
-        s.resize((size_t)(rows * w.s_row_bytes));
-        for (int64_t r = 0; r < rows; ++r) {
-            const uint8_t* row = src + r * rb;
-            float* sr = reinterpret_cast<float*>(&s[(size_t)(r * w.s_row_bytes)]);
-            for (int b = 0; b < k / 256; ++b) {
-                const uint8_t* blk = row + b * 144;
-                const float d = h2f(rd16(blk)), dmin = h2f(rd16(blk + 2));
-                for (int j = 0; j < 8; ++j) {
-                    int sc, mn;
-                    q4k_scale_min(j, blk + 4, &sc, &mn);
-                    sr[2 * (b * 8 + j)] = d * (float)sc;
-                    sr[2 * (b * 8 + j) + 1] = dmin * (float)mn;
+    w.format = ggml_type == CEB_GGML_Q8_0 ? CEB_W_Q8_0 : ggml_type == CEB_GGML_Q4_K ? CEB_W_Q4_K : CEB_W_F16;
+    w.blk_bytes = ceb_wblock_bytes(w.format);
+    const int nft = n_out / 128, nkb = k / 64;
+    std::vector<uint8_t> q((size_t)n_groups * nft * nkb * w.blk_bytes);
+    for (int g = 0; g < n_groups; ++g)
+        for (int ft = 0; ft < nft; ++ft)
+            for (int kb = 0; kb < nkb; ++kb) {
+                uint8_t* blk = &q[(((size_t)g * nft + ft) * nkb + kb) * w.blk_bytes];
+                for (int r = 0; r < 128; ++r) {
+                    const uint8_t* row = src + ((int64_t)g * n_out + (int64_t)ft * 128 + r) * rb;
+                    if (w.format == CEB_W_Q8_0) {
+                        for (int b = 0; b < 2; ++b) {  // the two 32-value blocks of this k-block
+                            const uint8_t* qb = row + (int64_t)(2 * kb + b) * 34;
+                            memcpy(blk + 8192 + 4 * r + 2 * b, qb, 2);
+                            for (int c2 = 0; c2 < 2; ++c2) {
+                                const int c = 2 * b + c2;
+                                memcpy(blk + r * 64 + ((c ^ ((r >> 1) & 3)) << 4), qb + 2 + 16 * c2, 16);
+                            }
+                        }
+                    } else if (w.format == CEB_W_Q4_K) {
+                        const uint8_t* sb = row + (int64_t)(kb / 4) * 144;  // 256-super-block
+                        const uint8_t* qs = sb + 16 + (kb % 4) * 32;        // this 64-chunk's nibble bytes
+                        for (int c = 0; c < 2; ++c) memcpy(blk + r * 32 + ((c ^ ((r >> 2) & 1)) << 4), qs + 16 * c, 16);
+                        const float d = h2f(rd16(sb)), dmin = h2f(rd16(sb + 2));
+                        float sm[4];
+                        for (int j = 0; j < 2; ++j) {
+                            int sc, mn;
+                            q4k_scale_min(2 * (kb % 4) + j, sb + 4, &sc, &mn);
+                            sm[2 * j] = d * (float)sc;
+                            sm[2 * j + 1] = dmin * (float)mn;
+                        }
+                        memcpy(blk + 4096 + 16 * r, sm, 16);
+                    } else {
+                        uint16_t h[64];
+                        if (ggml_type == CEB_GGML_F16) {
+                            memcpy(h, row + (int64_t)kb * 128, 128);
+                        } else {
+                            const float* f = reinterpret_cast<const float*>(row) + (int64_t)kb * 64;
+                            for (int i = 0; i < 64; ++i) h[i] = f2h(f[i]);
+                        }
+                        for (int c = 0; c < 8; ++c) memcpy(blk + r * 128 + ((c ^ (r & 7)) << 4), h + 8 * c, 16);
+                    }
                 }
-                memcpy(&q[(size_t)(r * w.q_row_bytes + b * 128)], blk + 16, 128);
             }
-        }
-    } else {
-        w.format = CEB_W_F16;
-        w.q_row_bytes = (int64_t)k * 2;
-        q.resize((size_t)(rows * w.q_row_bytes));
-        uint16_t* qh = reinterpret_cast<uint16_t*>(q.data());
-        if (ggml_type == CEB_GGML_F16) {
-            memcpy(q.data(), src, q.size());
-        } else {
-            const float* f = reinterpret_cast<const float*>(src);
-            for (int64_t i = 0; i < rows * k; ++i) qh[i] = f2h(f[i]);
-        }
-    }
     w.q_bytes = q.size();
-    w.s_bytes = s.size();
+    w.s_bytes = 0;
     if (cudaMalloc(&w.q, w.q_bytes) != cudaSuccess) return ceb_set_error(4, "repack: out of device memory");
-    if (w.s_bytes && cudaMalloc(&w.s, w.s_bytes) != cudaSuccess) {
-        cudaFree(w.q);
-        return ceb_set_error(4, "repack: out of device memory");
-    }
     cudaError_t e = cudaMemcpyAsync(w.q, q.data(), w.q_bytes, cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess && w.s_bytes) e = cudaMemcpyAsync(w.s, s.data(), w.s_bytes, cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);  // host vectors die at return
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);  // the host vector dies at return
     if (e != cudaSuccess) {
         cudaFree(w.q);
-        if (w.s) cudaFree(w.s);
         return ceb_set_cuda_error(e, "repack upload", __FILE__, __LINE__);
     }
     *dst = w;
@@ -209,7 +199,6 @@ int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int
 void ceb_wplane_free(ceb_wplane* w) {
     if (!w) return;
     if (w->q) cudaFree(w->q);
-    if (w->s) cudaFree(w->s);
     *w = ceb_wplane();
 }
 
