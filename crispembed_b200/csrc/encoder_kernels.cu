@@ -188,6 +188,11 @@ __global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int3
 // one-pass online softmax over 64-key tiles; keys beyond the sequence are masked.
 constexpr int AT_Q = 64, AT_K = 64, AT_HD = 64, AT_LD = 72;  // padded smem row (halfs)
 
+CEB_DEV float ex2_approx(float x) {  // MUFU 2^x (ex2(-inf) = 0)
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
 CEB_DEV void cp_async16(uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
@@ -289,32 +294,41 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
                 mma16816(s[2 * jp + 1], qf[ks], b2, b3);
             }
         }
-        // mask + online softmax (rows g and g+8 of this warp)
+        // online softmax (rows g and g+8 of this warp).  Only the sequence's last key
+        // tile holds keys past its end; the max is taken on raw scores and the
+        // softmax scale folds into one FMA ahead of the exp2.
         const int kbase = kt * AT_K;
+        if (kbase + AT_K > len) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (kbase + j * 8 + 2 * tq + (e & 1) >= len) s[j][e] = -INFINITY;
+        }
         float mx[2] = {m_r[0], m_r[1]};
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = kbase + j * 8 + 2 * tq + (e & 1);
-                float v = s[j][e] * scale_log2;
-                if (key >= len) v = -INFINITY;
-                s[j][e] = v;
-                mx[e >> 1] = fmaxf(mx[e >> 1], v);
-            }
+        for (int j = 0; j < 8; ++j) {
+            mx[0] = fmaxf(mx[0], fmaxf(s[j][0], s[j][1]));
+            mx[1] = fmaxf(mx[1], fmaxf(s[j][2], s[j][3]));
+        }
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
         }
-        float corr[2], rs[2] = {0.0f, 0.0f};
+        float corr[2], rs[2] = {0.0f, 0.0f}, nm[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) corr[r] = exp2f(m_r[r] - mx[r]);
+        for (int r = 0; r < 2; ++r) {
+            nm[r] = -mx[r] * scale_log2;
+            corr[r] = ex2_approx(fmaf(m_r[r], scale_log2, nm[r]));
+        }
         uint32_t pf[4][4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            float p0 = exp2f(s[j][0] - mx[0]), p1 = exp2f(s[j][1] - mx[0]);
-            float p2 = exp2f(s[j][2] - mx[1]), p3 = exp2f(s[j][3] - mx[1]);
+            const float p0 = ex2_approx(fmaf(s[j][0], scale_log2, nm[0]));
+            const float p1 = ex2_approx(fmaf(s[j][1], scale_log2, nm[0]));
+            const float p2 = ex2_approx(fmaf(s[j][2], scale_log2, nm[1]));
+            const float p3 = ex2_approx(fmaf(s[j][3], scale_log2, nm[1]));
             rs[0] += p0 + p1;
             rs[1] += p2 + p3;
             const int kk = j >> 1, hi = j & 1;

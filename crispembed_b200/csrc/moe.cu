@@ -16,6 +16,7 @@
 // row order is (expert, token, slot), the order ggml_mul_mat_id groups rows
 // in, so the permutation is deterministic and identical across runs.
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -26,10 +27,10 @@
 namespace {
 
 constexpr int ROUTE_WARPS = 16;         // tokens per route CTA = ROUTE_WARPS * TOK_PER_WARP
-constexpr int TOK_PER_WARP = 16;
+constexpr int TOK_PER_WARP = 4;
 constexpr int CHUNK = ROUTE_WARPS * TOK_PER_WARP;  // tokens per histogram block (256)
 constexpr int MAXE = 64;
-constexpr int MAXD = 4096;
+constexpr int MAXD = 1024;  // the router gives each lane one 32-value block
 
 template <typename T>
 CEB_DEV float ld_act(const T* p, size_t i);
@@ -39,6 +40,25 @@ template <>
 CEB_DEV float ld_act<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) { return __bfloat162float(p[i]); }
 template <>
 CEB_DEV float ld_act<__half>(const __half* p, size_t i) { return __half2float(p[i]); }
+
+template <typename T>
+CEB_DEV float4 ld_act4(const T* p, size_t i);
+template <>
+CEB_DEV float4 ld_act4<float>(const float* p, size_t i) { return *reinterpret_cast<const float4*>(p + i); }
+template <>
+CEB_DEV float4 ld_act4<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p + i);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+template <>
+CEB_DEV float4 ld_act4<__half>(const __half* p, size_t i) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p + i);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
 
 CEB_DEV float warp_max(float v) {
 #pragma unroll
@@ -98,12 +118,22 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32)
         const T* xr = x + (size_t)t * d;
         float lg_mine = -INFINITY;  // lane e < E ends up holding logit e
         if (rtype == CEB_GGML_Q8_0) {
-            for (int b = 0; b < nb; ++b) {
-                const float v = ld_act<T>(xr, (size_t)b * 32 + lane);
-                const float amax = warp_max(fabsf(v));
-                const float id = amax != 0.0f ? 127.0f / amax : 0.0f;
-                q[b * 32 + lane] = (int8_t)__float2int_rn(v * id);
-                if (lane == 0) qd[b] = __half2float(__float2half_rn(amax / 127.0f));
+            // 128 values per pass, 4 per lane (coalesced); 8 lanes hold one 32-value
+            // block, whose amax three xor-shuffles combine.  Packed quants land in
+            // consecutive shared-memory words.
+            for (int seg = 0; seg < d / 128; ++seg) {
+                const float4 v = ld_act4<T>(xr, (size_t)seg * 128 + 4 * lane);
+                float am = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+                const float id = am != 0.0f ? 127.0f / am : 0.0f;
+                const uint32_t b0 = (uint32_t)(__float2int_rn(v.x * id) & 0xFF);
+                const uint32_t b1 = (uint32_t)(__float2int_rn(v.y * id) & 0xFF);
+                const uint32_t b2 = (uint32_t)(__float2int_rn(v.z * id) & 0xFF);
+                const uint32_t b3 = (uint32_t)(__float2int_rn(v.w * id) & 0xFF);
+                reinterpret_cast<uint32_t*>(q)[seg * 32 + lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+                if ((lane & 7) == 0) qd[seg * 4 + (lane >> 3)] = __half2float(__float2half_rn(am / 127.0f));
             }
             __syncwarp();
             // lane = (expert-in-pass, partial-lane): 4 experts x 8 lanes per pass
@@ -178,14 +208,27 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32)
 }
 
 // One CTA: expert offsets (exclusive scan of the totals) and, per histogram
-// block, the first output row of each expert.
-__global__ void scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E, int32_t* __restrict__ block_base,
-                            int32_t* __restrict__ offsets, int32_t* __restrict__ expert_counts) {
-    __shared__ int tot[MAXE];
+// block, the first output row of each expert.  The per-block counts are staged
+// in shared memory first (coalesced), then each expert's thread walks them.
+constexpr int SCAN_MAX_SMEM_INTS = 48 * 1024 / 4;
+
+__global__ void __launch_bounds__(256) scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E,
+                                                   int32_t* __restrict__ block_base, int32_t* __restrict__ offsets,
+                                                   int32_t* __restrict__ expert_counts) {
+    extern __shared__ int sc[];  // [nblk*E] counts (when they fit), then [E] totals
+    const int n = nblk * E;
+    const bool staged = n <= SCAN_MAX_SMEM_INTS - MAXE;
+    int* tot = staged ? sc + n : sc;
+    if (staged)
+        for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = block_counts[i];
+    __syncthreads();
     const int e = threadIdx.x;
     if (e < E) {
         int s = 0;
-        for (int b = 0; b < nblk; ++b) s += block_counts[(size_t)b * E + e];
+        if (staged)
+            for (int b = 0; b < nblk; ++b) s += sc[b * E + e];
+        else
+            for (int b = 0; b < nblk; ++b) s += block_counts[(size_t)b * E + e];
         tot[e] = s;
         if (expert_counts) expert_counts[e] = s;
     }
@@ -197,7 +240,7 @@ __global__ void scan_kernel(const int32_t* __restrict__ block_counts, int nblk, 
         offsets[e + 1] = base + tot[e];
         for (int b = 0; b < nblk; ++b) {
             block_base[(size_t)b * E + e] = base;
-            base += block_counts[(size_t)b * E + e];
+            base += staged ? sc[b * E + e] : block_counts[(size_t)b * E + e];
         }
     }
 }
@@ -312,7 +355,7 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __h
                 const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st) {
     const int d = mw.d, E = mw.n_experts, K = mw.top_k, F = mw.ffn;
     if (T <= 0) return 0;
-    if (E > 32 || E < 1 || K < 1 || K > E || K > 4 || d % 64 || d > MAXD || F % 128 || d % 128)
+    if (E > 32 || E < 1 || K < 1 || K > E || K > 4 || d > MAXD || F % 128 || d % 128)
         return ceb_set_error(2, "moe: unsupported shape d=%d E=%d K=%d F=%d", d, E, K, F);
     const int nblk = (T + CHUNK - 1) / CHUNK;
     const size_t route_smem = MAXE * 4 + (size_t)(E + ROUTE_WARPS) * (d / 32) * 4 + (size_t)E * (d + 32) +
@@ -338,7 +381,8 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __h
                                                                          ws.block_counts));
     }
     CEB_CUDA_OK(cudaGetLastError());
-    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scan_kernel<<<1, 64, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts));
+    const size_t scan_smem = (size_t)std::min(nblk * E + MAXE, SCAN_MAX_SMEM_INTS) * sizeof(int);
+    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scan_kernel<<<1, 256, scan_smem, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts));
     CEB_CUDA_OK(cudaGetLastError());
     if (x_dtype == CEB_ACT_F32)
         CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<float><<<nblk, 256, 0, st>>>((const float*)x, x16, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,

@@ -61,10 +61,10 @@ def bench_moe(a):
 
     from . import binding, synth
     inp = synth.make_moe_op_inputs(a.T, d=a.d, n_experts=a.E, top_k=a.topk, ffn=a.F, wtype=TYPES[a.type],
-                                   router_wtype=0, zipf_s=a.zipf or None, seed=0)
+                                   router_wtype=TYPES[a.router_type], zipf_s=a.zipf or None, seed=0)
     layer = binding.MoELayer(inp.d, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
                              inp.fc1_raw, inp.fc2_raw, inp.bias)
-    x = torch.from_numpy(inp.x).cuda().to(torch.bfloat16)
+    x = torch.from_numpy(inp.x).cuda().to(torch.float32 if a.f32_input else torch.bfloat16)
     y = torch.empty((a.T, a.d), dtype=torch.float32, device="cuda")
     ws = torch.empty(layer.workspace_size(a.T), dtype=torch.uint8, device="cuda")
     for _ in range(a.warmup):
@@ -108,7 +108,9 @@ def main(argv=None):
     m.add_argument("--F", type=int, default=3072)
     m.add_argument("--type", default="q4_k", choices=list(TYPES))
     m.add_argument("--zipf", type=float, default=1.2)
+    m.add_argument("--router-type", default="f32", choices=["f32", "q8_0"])
     m.add_argument("--iters", type=int, default=10)
+    m.add_argument("--f32-input", action="store_true")
     m.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
     r = bench_gemm(a) if a.what == "gemm" else bench_moe(a)
