@@ -285,6 +285,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int total = SH.g_tile[G];
     volatile int* abort = SH.abort;
     auto bar = [&](int i) { return smem_u32(&SH.bars[i]); };
+    // bounded barrier wait; a timeout records its site as code | (barrier index + 1) << 16
+    auto wait_at = [&](int i, uint32_t parity, int code) {
+        return mbar_wait(bar(i), parity, abort, a.err, code | ((i + 1) << 16));
+    };
     auto a_stage = [&](int s) { return SH.stages + (size_t)s * STAGE_BYTES; };
     auto b_stage = [&](int s) { return SH.stages + (size_t)s * STAGE_BYTES + A_STAGE_BYTES; };
     auto wblock = [&](const TileInfo& ti, int kb) {
@@ -300,7 +304,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % S;
-                    if (!mbar_wait(bar(BAR_EMPTY(s)), ((it / S) & 1) ^ 1, abort, a.err, CEB_DEVERR_TIMEOUT_TMA)) {
+                    if (!wait_at(BAR_EMPTY(s), ((it / S) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++lt) {
                 const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
                 const int ab = lt & 1;
-                if (!mbar_wait(bar(BAR_ACC_EMPTY(ab)), ((lt >> 1) & 1) ^ 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA)) break;
+                if (!wait_at(BAR_ACC_EMPTY(ab), ((lt >> 1) & 1) ^ 1, CEB_DEVERR_TIMEOUT_MMA)) break;
                 tc_fence_after();
                 int n = (ti.rows + 15) & ~15;
                 n = n < 16 ? 16 : n;
@@ -334,7 +338,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t d_tmem = tmem + (uint32_t)(ab * BN);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % S;
-                    if (!mbar_wait(bar(BAR_FULL(s)), (it / S) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_MMA)) {
+                    if (!wait_at(BAR_FULL(s), (it / S) & 1, CEB_DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
                     }
@@ -362,7 +366,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int rs = it % R;
-                    if (!mbar_wait(bar(BAR_RAW_EMPTY(rs)), ((it / R) & 1) ^ 1, abort, a.err, CEB_DEVERR_TIMEOUT_TMA)) {
+                    if (!wait_at(BAR_RAW_EMPTY(rs), ((it / R) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
@@ -386,8 +390,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int n_items = my_tiles * nkb;
             for (int i = wg; i < n_items; i += DEQ_WG) {
                 const int rs = i % R, s = i % S;
-                if (!__all_sync(0xffffffffu, mbar_wait(bar(BAR_RAW_FULL(rs)), (i / R) & 1, abort, a.err,
-                                                       CEB_DEVERR_TIMEOUT_DEQ)))
+                if (!__all_sync(0xffffffffu, wait_at(BAR_RAW_FULL(rs), (i / R) & 1, CEB_DEVERR_TIMEOUT_DEQ)))
                     break;
                 Raw<FMT> raw;
                 load_raw_smem<FMT>(SH.raw + (size_t)rs * RAW_STAGE, r, raw);
@@ -395,8 +398,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 convert<FMT>(raw, o);  // consumes the loaded values: the raw stage may be refilled now
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(BAR_RAW_EMPTY(rs)));
-                if (!__all_sync(0xffffffffu, mbar_wait(bar(BAR_EMPTY(s)), ((i / S) & 1) ^ 1, abort, a.err,
-                                                       CEB_DEVERR_TIMEOUT_DEQ)))
+                if (!__all_sync(0xffffffffu, wait_at(BAR_EMPTY(s), ((i / S) & 1) ^ 1, CEB_DEVERR_TIMEOUT_DEQ)))
                     break;
                 // 128-byte swizzled K-major row: 16-byte chunk c lands at chunk c ^ (row & 7)
                 uint8_t* row = a_stage(s) + r * 128;
@@ -423,7 +425,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const TileInfo ti = decode_tile(SH, G, n_ftiles, t);
             const int ab = lt & 1;
             if (!__all_sync(0xffffffffu,
-                            mbar_wait(bar(BAR_ACC_FULL(ab)), (lt >> 1) & 1, abort, a.err, CEB_DEVERR_TIMEOUT_EPI)))
+                            wait_at(BAR_ACC_FULL(ab), (lt >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI)))
                 break;
             tc_fence_after();
             const int n0 = ti.ft * BM + 32 * q;
