@@ -195,6 +195,98 @@ CEB_DEV uint32_t idesc_f16_f32(int M, int N) {
            | ((uint32_t)(M >> 4) << 24);  // M
 }
 
+// ------------------------------------------------- CTA pairs (cluster of 2)
+// The pair shares one tcgen05.mma.cta_group::2 (M = 256): each CTA holds half of
+// the A rows and half of the B rows in its own shared memory and half of D (its
+// 128 lanes x N columns) in its own tensor memory.  Rank 0 issues the MMAs.
+CEB_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// all threads of both CTAs; release/acquire at cluster scope
+CEB_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// address of the same shared-memory location in CTA `rank` of the cluster
+CEB_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// arrive (release, cluster scope) on an mbarrier given by its cluster address
+CEB_DEV void mbar_arrive_cluster(uint32_t cl_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_bar) : "memory");
+}
+CEB_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait (acquire at cluster scope) for barriers that other CTAs of the pair arrive on
+CEB_DEV bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort, int* err, int code) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    long long t0 = clock64();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 255) == 0) {
+            if (abort && *abort) return false;
+            if (clock64() - t0 > CEB_WAIT_LIMIT_CYCLES) {
+                if (abort) *abort = 1;
+                if (err) atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+CEB_DEV void tmem_alloc_pair(uint32_t smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_dst), "r"(ncols)
+                 : "memory");
+}
+CEB_DEV void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+CEB_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+CEB_DEV void mma_pair_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// arrive on the mbarrier at cluster address `cl_bar` when this thread's MMAs complete
+CEB_DEV void mma_pair_commit(uint32_t cl_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cl_bar)
+                 : "memory");
+}
+// shared::cta -> shared::cluster bulk copy (16-byte aligned, size a multiple of 16)
+// whose bytes count on the mbarrier at cluster address `cl_bar` (in the
+// destination CTA).  Used as an asynchronous, non-blocking cross-CTA signal.
+CEB_DEV void bulk_copy_to_cluster(uint32_t cl_dst, uint32_t src, uint32_t bytes, uint32_t cl_bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     cl_dst),
+                 "r"(src), "r"(bytes), "r"(cl_bar)
+                 : "memory");
+}
+// 2D tile load into this CTA's shared memory whose completion bytes count on the
+// mbarrier at cluster address `cl_bar` (the pair leader's)
+CEB_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t cl_bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];" ::"r"(dst),
+        "l"(map), "r"(cl_bar), "r"(x), "r"(y)
+        : "memory");
+}
+
 // ------------------------------------------------------------------ numerics
 CEB_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
 

@@ -31,6 +31,7 @@
 // group table is read from device memory, so no host synchronisation is
 // needed between routing and the expert GEMMs.
 #include <cstdio>
+#include <cstdlib>
 
 #include "ceb_internal.h"
 #include "common.cuh"
@@ -40,8 +41,14 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 256;               // activation rows (tokens) per tile = max MMA N
 constexpr int BK = 64;
-constexpr int S = 3;                  // pipeline stages (A + B tiles)
-constexpr int R = 4;                  // raw (still quantized) weight stages
+#ifndef CEB_GEMM_S
+#define CEB_GEMM_S 3
+#endif
+#ifndef CEB_GEMM_R
+#define CEB_GEMM_R 4
+#endif
+constexpr int S = CEB_GEMM_S;         // pipeline stages (A + B tiles)
+constexpr int R = CEB_GEMM_R;         // raw (still quantized) weight stages
 constexpr int RAW_STAGE = 8704;       // largest quantized block (Q8_0)
 constexpr int MAXG = 64;
 constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KB, written by the dequant warps
@@ -51,10 +58,18 @@ constexpr uint32_t TMEM_COLS = 512;          // two BN-column fp32 accumulators
 constexpr int DEQ_WG = 2, EPI_WG = 2;
 constexpr int DEQ_WARP0 = 4, EPI_WARP0 = DEQ_WARP0 + 4 * DEQ_WG;
 constexpr int NTHREADS = 32 * (EPI_WARP0 + 4 * EPI_WG);
+#ifndef CEB_GEMM_TMA_STORE
+#define CEB_GEMM_TMA_STORE 1
+#endif
 constexpr int STAGING_SLOT = 32 * 32 * 4;    // one 32x32 fp32 output block per slot
-constexpr int STAGING_BYTES = 4 * EPI_WG * STAGING_SLOT;  // one slot per epilogue warp
+constexpr int STAGING_BYTES = CEB_GEMM_TMA_STORE ? 4 * EPI_WG * STAGING_SLOT : 0;  // one slot per epilogue warp
 static_assert(2 * BN <= (int)TMEM_COLS, "TMEM budget");
 
+// The dequant warpgroups take alternate K-blocks. Every raw stage must always be
+// consumed by the same warpgroup: with an odd ring a stage's items alternate
+// between warpgroups, one of them can wait on a phase two ahead of the barrier,
+// and the mbarrier's parity test then passes on a stale phase.
+static_assert(R % DEQ_WG == 0, "raw stages must map to one dequant warpgroup each");
 constexpr int NBARS = 2 * S + 4 + 1 + 2 * R;
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)S * STAGE_BYTES + (size_t)R * RAW_STAGE + STAGING_BYTES +
                               NBARS * 8 + 16 + 3 * (MAXG + 1) * 4;
@@ -442,7 +457,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (gelu) x[j] = gelu_as(x[j]);
                 }
                 const int lim = ti.rows - c0;
-                if (lim >= 32) {
+                if (CEB_GEMM_TMA_STORE && lim >= 32) {
                     // full 32-row block: stage [row][feature] in shared memory, one TMA store
                     if (nstore >= 1) {  // the previous store has finished reading the slot
                         if (lane == 0) bulk_wait_read<0>();
@@ -505,7 +520,473 @@ int launch_fmt(const CUtensorMap& map, const CUtensorMap& omap, const ceb_wplane
     return 0;
 }
 
+
+// ===========================================================================
+// CTA-pair kernel (cluster of 2, tcgen05.mma.cta_group::2, M = 256).
+//
+// Orientation: tokens are the MMA's M (A = activations, 128 rows per CTA, TMA),
+// features are N (B = dequantized weights, 128 rows per CTA, N = 256 per pair).
+// Each CTA's tensor memory holds D for its 128 tokens x all 256 features of the
+// pair tile, double buffered (2 x 256 columns).  Per SM and K-block this moves
+// half the shared-memory bytes of the 1-CTA kernel for the activations and
+// runs the tensor pipe at its full rate (one M=256,N=256,K=16 MMA per 128
+// cycles per pair, measured), against ~178 cycles per M=128 MMA on one SM.
+//
+// Barriers: FULL[s] lives in the leader (rank 0): the leader's TMA thread posts
+// the expected bytes of both CTAs' activation tiles, both CTAs' TMA loads count
+// their bytes on it, and the leader's 4 dequant warps arrive on it.  Rank 1's
+// dequant warps arrive on its local W_FULL[s]; a relay thread of rank 1 then
+// copies 16 bytes into the leader's shared memory with cp.async.bulk, whose
+// complete_tx lands on FULL[s] (the leader expects 2 activation tiles + 16 B).
+// The leader's MMA commits EMPTY[s] / ACC_FULL[b] to both CTAs.  ACC_EMPTY[b]
+// takes the leader's epilogue warps plus 16 relayed bytes once rank 1's
+// epilogue warps have arrived on its local ACC_FREE[b].  The cross-CTA signals
+// are asynchronous copies: a blocking cluster-scope release arrive costs ~1500
+// cycles per call, three times the MMA time of a K-block.
+namespace pair {
+constexpr int TOK = 128;                     // tokens per CTA
+constexpr int FEAT = 256;                    // features per pair tile (MMA N)
+constexpr int PS = 4;                         // A+B stages
+constexpr int PR = 4;                         // raw weight stages
+constexpr int X_BYTES = TOK * BK * 2;        // 16 KB activation tile
+constexpr int W_BYTES = 128 * BK * 2;        // 16 KB dequantized weight tile (this CTA's 128 features)
+constexpr int STAGE = X_BYTES + W_BYTES;
+constexpr int SLOT = 32 * 128;               // 32 rows x 128 B, 128-byte swizzled
+constexpr int STAGING = 4 * EPI_WG * SLOT;
+constexpr int NB = 2 * PS + 4 + 1 + 2 * PR + PS + 2;
+constexpr int SIG = 16;                      // bytes of one relayed signal
+constexpr int SIG_BYTES = (PS + 2 + 1) * SIG;  // sinks for FULL[s], ACC_EMPTY[b] + one source
+constexpr size_t SMEM = 1024 + (size_t)PS * STAGE + (size_t)PR * RAW_STAGE + STAGING + SIG_BYTES + NB * 8 + 16 +
+                        3 * (MAXG + 1) * 4;
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+static_assert(PR % DEQ_WG == 0, "raw stages must map to one dequant warpgroup each");
+static_assert((PS * STAGE + PR * RAW_STAGE) % 1024 == 0, "staging slots must stay 1024-byte aligned");
+
+CEB_DEV int B_FULL(int s) { return s; }
+CEB_DEV int B_EMPTY(int s) { return PS + s; }
+CEB_DEV int B_ACC_FULL(int b) { return 2 * PS + b; }
+CEB_DEV int B_ACC_EMPTY(int b) { return 2 * PS + 2 + b; }
+CEB_DEV int B_DRAIN() { return 2 * PS + 4; }
+CEB_DEV int B_RAW_FULL(int r) { return 2 * PS + 5 + r; }
+CEB_DEV int B_RAW_EMPTY(int r) { return 2 * PS + 5 + PR + r; }
+CEB_DEV int B_W_FULL(int s) { return 2 * PS + 5 + 2 * PR + s; }       // rank 1 only
+CEB_DEV int B_ACC_FREE(int b) { return 3 * PS + 5 + 2 * PR + b; }     // rank 1 only
+
+struct Smem {
+    uint64_t* bars;
+    uint32_t* tmem_slot;
+    int* abort;
+    int* g_tile;
+    int* g_row;
+    int* g_cnt;
+    uint8_t* stages;
+    uint8_t* raw;
+    uint8_t* staging;
+    uint8_t* sig;  // [0, PS): FULL sinks, [PS, PS+2): ACC_EMPTY sinks, PS+2: source
+};
+CEB_DEV Smem carve(uint8_t* base) {
+    Smem s;
+    uintptr_t p = (reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023);
+    s.stages = reinterpret_cast<uint8_t*>(p);
+    p += (size_t)PS * STAGE;
+    s.raw = reinterpret_cast<uint8_t*>(p);
+    p += (size_t)PR * RAW_STAGE;
+    s.staging = reinterpret_cast<uint8_t*>(p);
+    p += STAGING;
+    s.sig = reinterpret_cast<uint8_t*>(p);
+    p += SIG_BYTES;
+    s.bars = reinterpret_cast<uint64_t*>(p);
+    p += NB * 8;
+    s.tmem_slot = reinterpret_cast<uint32_t*>(p);
+    s.abort = reinterpret_cast<int*>(p + 4);
+    p += 16;
+    s.g_tile = reinterpret_cast<int*>(p);
+    s.g_row = s.g_tile + (MAXG + 1);
+    s.g_cnt = s.g_row + (MAXG + 1);
+    return s;
+}
+
+struct Tile {
+    int g, fp, row0, rows;  // group, feature-pair tile, first token of the pair tile, tokens in it (<= 256)
+};
+CEB_DEV Tile decode(const Smem& S_, int G, int n_fp, int t) {
+    int g = 0;
+    while (g + 1 < G && t >= S_.g_tile[g + 1]) ++g;
+    const int local = t - S_.g_tile[g];
+    Tile ti;
+    ti.g = g;
+    ti.fp = local % n_fp;
+    const int tt = local / n_fp;
+    ti.row0 = S_.g_row[g] + tt * 2 * TOK;
+    const int rem = S_.g_cnt[g] - tt * 2 * TOK;
+    ti.rows = rem < 2 * TOK ? rem : 2 * TOK;
+    return ti;
+}
+
+// one 32-row x 32-column fp32 accumulator block -> bias (+GELU) in place
+CEB_DEV void epi_math(float (&x)[32], const uint32_t (&v)[32], const float* bias, bool gelu) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        float4 b = bias ? __ldg(reinterpret_cast<const float4*>(bias + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[j] = __uint_as_float(v[j]) + b.x;
+        x[j + 1] = __uint_as_float(v[j + 1]) + b.y;
+        x[j + 2] = __uint_as_float(v[j + 2]) + b.z;
+        x[j + 3] = __uint_as_float(v[j + 3]) + b.w;
+    }
+    if (gelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = gelu_as(x[j]);
+    }
+}
+
+}  // namespace pair
+
+template <int FMT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
+    ceb_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap omap,
+                         const ceb_wplane w, const ceb_gemm_args a) {
+    using namespace pair;
+    extern __shared__ uint8_t smem_raw[];
+    const Smem SH = pair::carve(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int G = a.offsets ? w.n_groups : 1;
+    const int n_fp = w.n_out / FEAT;
+    const int n_ftiles = w.n_out / BM;
+    const int nkb = w.k / BK;
+    const int pair_id = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NB; ++i) {
+            uint32_t cnt = 1;
+            if (i < PS) cnt = 1 + 4;                                        // expect_tx + leader dequant warps
+            if (i >= 2 * PS + 2 && i < 2 * PS + 4) cnt = 4 * EPI_WG;        // leader epilogue warps (one with expect_tx)
+            if (i >= 2 * PS + 5 + PR && i < 2 * PS + 5 + 2 * PR) cnt = 4;   // this CTA's dequant warpgroup
+            if (i >= B_W_FULL(0) && i < B_W_FULL(0) + PS) cnt = 4;          // rank 1's dequant warpgroup
+            if (i >= B_ACC_FREE(0) && i < B_ACC_FREE(0) + 2) cnt = 4 * EPI_WG;  // rank 1's epilogue warps
+            mbar_init(smem_u32(&SH.bars[i]), cnt);
+        }
+        fence_mbar_init();
+        *SH.abort = 0;
+        *reinterpret_cast<uint4*>(SH.sig + (PS + 2) * SIG) = make_uint4(0, 0, 0, 0);  // signal source
+        fence_proxy_async_smem();
+        int tiles = 0;
+        for (int g = 0; g < G; ++g) {
+            int r0 = a.offsets ? a.offsets[g] : 0;
+            int r1 = a.offsets ? a.offsets[g + 1] : a.m_rows;
+            if (r0 < 0 || r1 < r0 || r1 > a.m_rows) {
+                if (a.err) atomicCAS(a.err, 0, (int)CEB_DEVERR_BAD_GROUP);
+                r0 = r1 = 0;
+            }
+            SH.g_tile[g] = tiles;
+            SH.g_row[g] = r0;
+            SH.g_cnt[g] = r1 - r0;
+            tiles += ((r1 - r0 + 2 * TOK - 1) / (2 * TOK)) * n_fp;
+        }
+        SH.g_tile[G] = tiles;
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&xmap);
+        tma_prefetch_desc(&omap);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(SH.tmem_slot), TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem = *SH.tmem_slot;
+    const int total = SH.g_tile[G];
+    volatile int* abort = SH.abort;
+    auto bar = [&](int i) { return smem_u32(&SH.bars[i]); };
+    auto lead_bar = [&](int i) { return mapa_shared(bar(i), 0); };
+    auto wait_at = [&](int i, uint32_t parity, int code) {
+        return mbar_wait(bar(i), parity, abort, a.err, code | ((i + 1) << 16));
+    };
+    auto wait_cl = [&](int i, uint32_t parity, int code) {
+        return mbar_wait_cluster(bar(i), parity, abort, a.err, code | ((i + 1) << 16));
+    };
+    auto x_stage = [&](int s) { return SH.stages + (size_t)s * STAGE; };
+    auto w_stage = [&](int s) { return SH.stages + (size_t)s * STAGE + X_BYTES; };
+    auto wblock = [&](const Tile& ti, int kb) {
+        const int ft = 2 * ti.fp + (int)rank;  // this CTA's 128-feature weight tile
+        return w.q + (((size_t)ti.g * n_ftiles + ft) * nkb + kb) * (size_t)w.blk_bytes;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------ activation tiles (this CTA's 128 tokens)
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = pair_id; t < total && ok; t += n_pairs) {
+                const Tile ti = pair::decode(SH, G, n_fp, t);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % PS;
+                    if (!wait_at(B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(bar(B_FULL(s)), 2 * X_BYTES + SIG);
+                    tma_load_2d_pair(smem_u32(x_stage(s)), &xmap, lead_bar(B_FULL(s)), kb * BK,
+                                     ti.row0 + TOK * (int)rank);
+                }
+            }
+            if (!ok && leader) {  // let issued copies land before the CTA can exit
+                const uint32_t n = it < PS ? it : PS;
+                for (uint32_t i = it - n; i < it; ++i)
+                    mbar_wait_cluster(bar(B_FULL(i % PS)), (i / PS) & 1, nullptr, nullptr, 0);
+            }
+        }
+    } else if (warp == 1 && !leader) {
+        // ------------------------------------------------ relay: rank 1's weight tiles ready -> leader's FULL
+        if (lane == 0) {
+            const int my_tiles = pair_id < total ? (total - 1 - pair_id) / n_pairs + 1 : 0;
+            const uint32_t n_items = (uint32_t)(my_tiles * nkb);
+            for (uint32_t it = 0; it < n_items; ++it) {
+                const int s = it % PS;
+                if (!wait_at(B_W_FULL(s), (it / PS) & 1, CEB_DEVERR_TIMEOUT_DEQ)) break;
+                bulk_copy_to_cluster(mapa_shared(smem_u32(SH.sig + s * SIG), 0), smem_u32(SH.sig + (PS + 2) * SIG),
+                                     SIG, lead_bar(B_FULL(s)));
+            }
+        }
+    } else if (warp == 3 && !leader) {
+        // ------------------------------------------------ relay: rank 1's accumulator drained -> leader's ACC_EMPTY
+        if (lane == 0) {
+            uint32_t lt = 0;
+            for (int t = pair_id; t < total; t += n_pairs, ++lt) {
+                const int ab = lt & 1;
+                if (!wait_at(B_ACC_FREE(ab), (lt >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI)) break;
+                bulk_copy_to_cluster(mapa_shared(smem_u32(SH.sig + (PS + ab) * SIG), 0),
+                                     smem_u32(SH.sig + (PS + 2) * SIG), SIG, lead_bar(B_ACC_EMPTY(ab)));
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer (leader only)
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(2 * TOK, FEAT);
+            uint32_t it = 0, lt = 0;
+            bool ok = true;
+            for (int t = pair_id; t < total && ok; t += n_pairs, ++lt) {
+                const int ab = lt & 1;
+                if (!wait_cl(B_ACC_EMPTY(ab), ((lt >> 1) & 1) ^ 1, CEB_DEVERR_TIMEOUT_MMA)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)(ab * FEAT);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % PS;
+                    if (!wait_cl(B_FULL(s), (it / PS) & 1, CEB_DEVERR_TIMEOUT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(x_stage(s)));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(w_stage(s)));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        mma_pair_f16_ss(d_tmem, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
+                                        (kb | kk) != 0);
+                    mma_pair_commit(bar(B_EMPTY(s)));
+                    mma_pair_commit(mapa_shared(bar(B_EMPTY(s)), 1));
+                }
+                if (ok) {
+                    mma_pair_commit(bar(B_ACC_FULL(ab)));
+                    mma_pair_commit(mapa_shared(bar(B_ACC_FULL(ab)), 1));
+                }
+            }
+            // every issued MMA (they write both CTAs' tensor memory) retires before TMEM is released
+            mma_pair_commit(bar(B_DRAIN()));
+            mbar_wait(bar(B_DRAIN()), 0, nullptr, nullptr, 0);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------ weight loader (this CTA's quantized blocks)
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = pair_id; t < total && ok; t += n_pairs) {
+                const Tile ti = pair::decode(SH, G, n_fp, t);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int rs = it % PR;
+                    if (!wait_at(B_RAW_EMPTY(rs), ((it / PR) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(bar(B_RAW_FULL(rs)), (uint32_t)w.blk_bytes);
+                    bulk_load(smem_u32(SH.raw + (size_t)rs * RAW_STAGE), wblock(ti, kb), (uint32_t)w.blk_bytes,
+                              bar(B_RAW_FULL(rs)));
+                }
+            }
+            if (!ok) {
+                const uint32_t n = it < PR ? it : PR;
+                for (uint32_t i = it - n; i < it; ++i)
+                    mbar_wait(bar(B_RAW_FULL(i % PR)), (i / PR) & 1, nullptr, nullptr, 0);
+            }
+        }
+    } else if (warp >= DEQ_WARP0 && warp < EPI_WARP0) {
+        // ------------------------------------------------ dequant (raw stage -> fp16 weight stage)
+        const int wg = (warp - DEQ_WARP0) >> 2;
+        const int r = 32 * (warp & 3) + lane;
+        const int my_tiles = pair_id < total ? (total - 1 - pair_id) / n_pairs + 1 : 0;
+        const int n_items = my_tiles * nkb;
+        for (int i = wg; i < n_items; i += DEQ_WG) {
+            const int rs = i % PR, s = i % PS;
+            if (!__all_sync(0xffffffffu, wait_at(B_RAW_FULL(rs), (i / PR) & 1, CEB_DEVERR_TIMEOUT_DEQ))) break;
+            Raw<FMT> raw;
+            load_raw_smem<FMT>(SH.raw + (size_t)rs * RAW_STAGE, r, raw);
+            uint32_t o[32];
+            convert<FMT>(raw, o);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_RAW_EMPTY(rs)));
+            if (!__all_sync(0xffffffffu, wait_at(B_EMPTY(s), ((i / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_DEQ))) break;
+            uint8_t* row = w_stage(s) + r * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
+                    make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(leader ? B_FULL(s) : B_W_FULL(s)));
+        }
+    } else if (warp >= EPI_WARP0) {
+        // ------------------------------------------------ epilogue (this CTA's 128 tokens)
+        const int ew = warp - EPI_WARP0;
+        const int wg = ew >> 2;                 // columns (features) 128*wg .. 128*wg+127 of the pair tile
+        const int q = warp & 3;                 // TMEM lanes (tokens) 32q .. 32q+31
+        const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+        const bool f16 = (a.epi & CEB_EPI_F16_OUT) != 0, gelu = (a.epi & CEB_EPI_GELU) != 0;
+        uint8_t* slot = SH.staging + (size_t)ew * SLOT;
+        const uint32_t slot_u32 = smem_u32(slot);
+        uint32_t lt = 0, nstore = 0;
+        for (int t = pair_id; t < total; t += n_pairs, ++lt) {
+            const Tile ti = pair::decode(SH, G, n_fp, t);
+            const int ab = lt & 1;
+            if (!__all_sync(0xffffffffu, wait_at(B_ACC_FULL(ab), (lt >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI))) break;
+            tc_fence_after();
+            const int my_rows = ti.rows - TOK * (int)rank;   // tokens of the pair tile held by this CTA
+            const int lim = my_rows - 32 * q;                 // valid rows of this warp's 32
+            const int row = ti.row0 + TOK * (int)rank + 32 * q;
+            const int f_base = ti.fp * FEAT + 128 * wg;
+            const float* bias = (a.epi & CEB_EPI_BIAS) ? a.bias + (size_t)ti.g * a.bias_group_stride : nullptr;
+            const uint32_t col0 = (uint32_t)(ab * FEAT + 128 * wg);
+            const int chunk_cols = f16 ? 64 : 32;
+            for (int c0 = 0; c0 < 128; c0 += chunk_cols) {
+                if (lim <= 0) break;
+                const bool full = lim >= 32;
+                if (full && nstore >= 1) {  // the previous store has finished reading the slot
+                    if (lane == 0) bulk_wait_read<0>();
+                    __syncwarp();
+                }
+                for (int h = 0; h < chunk_cols; h += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + lane_addr + col0 + (uint32_t)(c0 + h), v);
+                    tmem_ld_wait();
+                    float x[32];
+                    epi_math(x, v, bias ? bias + f_base + c0 + h : nullptr, gelu);
+                    if (f16) {
+                        uint32_t p[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) p[j] = h2_as_u32(__floats2half2_rn(x[2 * j], x[2 * j + 1]));
+                        if (full) {  // 64 B = chunks 4*(h/32) .. +3 of the 128-B swizzled row
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                const int cc = c + (h >> 3);
+                                *reinterpret_cast<uint4*>(slot + lane * 128 + ((cc ^ (lane & 7)) << 4)) =
+                                    make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+                            }
+                        } else if (lane < lim) {
+                            uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) +
+                                                                (size_t)(row + lane) * a.ldo + f_base + c0 + h);
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) o[c] = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+                        }
+                    } else {
+                        if (full) {
+#pragma unroll
+                            for (int c = 0; c < 8; ++c)
+                                *reinterpret_cast<float4*>(slot + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                                    make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+                        } else if (lane < lim) {
+                            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) +
+                                                                  (size_t)(row + lane) * a.ldo + f_base + c0 + h);
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) o[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+                        }
+                    }
+                }
+                if (full) {
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&omap, slot_u32, f_base + c0, row);
+                        bulk_commit();
+                    }
+                    ++nstore;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (!leader)
+                    mbar_arrive(bar(B_ACC_FREE(ab)));
+                else if (ew == 0)
+                    mbar_arrive_expect_tx(bar(B_ACC_EMPTY(ab)), SIG);  // + rank 1's relayed signal
+                else
+                    mbar_arrive(bar(B_ACC_EMPTY(ab)));
+            }
+        }
+        if (lane == 0) bulk_wait<0>();  // output stores complete before the CTA retires
+    }
+
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();  // no remote arrive or MMA can still target this CTA once it passes here
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, TMEM_COLS);
+    }
+}
+
+template <int FMT>
+int launch_pair(const CUtensorMap& xmap, const CUtensorMap& omap, const ceb_wplane& w, const ceb_gemm_args& a,
+                int max_pairs, cudaStream_t st) {
+    static int pairs_resident = -1;
+    if (pairs_resident < 0) {
+        CEB_CUDA_OK(cudaFuncSetAttribute(ceb_gemm_pair_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)pair::SMEM));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * ceb_num_sms(), 1, 1);
+        cfg.blockDim = dim3(NTHREADS, 1, 1);
+        cfg.dynamicSmemBytes = pair::SMEM;
+        int n = 0;  // cluster size comes from the kernel's __cluster_dims__
+        CEB_CUDA_OK(cudaOccupancyMaxActiveClusters(&n, ceb_gemm_pair_kernel<FMT>, &cfg));
+        pairs_resident = n > 0 ? n : 1;
+    }
+    int pairs = pairs_resident < max_pairs ? pairs_resident : max_pairs;
+    if (pairs < 1) pairs = 1;
+    ceb_gemm_pair_kernel<FMT><<<2 * pairs, NTHREADS, pair::SMEM, st>>>(xmap, omap, w, a);
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
 }  // namespace
+
+// The CTA-pair kernel takes quantized weights whose output width is a multiple of
+// 256 (every linear layer of the supported encoders); fp16 weights, narrower or
+// odd widths and unaligned bias vectors use the single-CTA kernel.  Setting
+// CEB_GEMM_SINGLE_CTA=1 in the environment forces the single-CTA kernel.
+static bool ceb_gemm_use_pairs(const ceb_wplane& w, const ceb_gemm_args& a) {
+    static const bool forced_single = [] {
+        const char* e = getenv("CEB_GEMM_SINGLE_CTA");
+        return e && e[0] == '1';
+    }();
+    if (forced_single) return false;
+    if (w.format != CEB_W_Q8_0 && w.format != CEB_W_Q4_K) return false;
+    if (w.n_out % pair::FEAT) return false;
+    if ((a.epi & CEB_EPI_BIAS) &&
+        ((reinterpret_cast<uintptr_t>(a.bias) & 15) || (a.offsets && (a.bias_group_stride & 3))))
+        return false;
+    return true;
+}
 
 int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, const ceb_gemm_args& a,
                     cudaStream_t stream, int max_ctas) {
@@ -516,24 +997,44 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
     if ((reinterpret_cast<uintptr_t>(act_f16) & 15) != 0) return ceb_set_error(2, "gemm: activations not 16-B aligned");
     if ((a.epi & CEB_EPI_F16_OUT) && (a.ldo & 1)) return ceb_set_error(2, "gemm: fp16 output stride must be even");
     if (act_rows <= 0) return 0;
-    CUtensorMap map, omap;
-    int mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);
-    if (mrc) return mrc;
     const int esz = (a.epi & CEB_EPI_F16_OUT) ? 2 : 4;
     if ((reinterpret_cast<uintptr_t>(a.out) & 15) || ((size_t)a.ldo * esz) % 16 || a.ldo < w.n_out)
         return ceb_set_error(2, "gemm: output must be 16-B aligned with a row stride >= n_out and a multiple of 16 B");
+    const int groups = a.offsets ? w.n_groups : 1;
+    const double flops = 2.0 * (double)a.m_rows * w.n_out * w.k;
+    const double bytes = (double)(w.q_bytes + w.s_bytes) + (double)a.m_rows * w.k * 2 +
+                         (double)a.m_rows * w.n_out * ((a.epi & CEB_EPI_F16_OUT) ? 2 : 4);
+    CUtensorMap map, omap;
+    int mrc = 0;
+    if (ceb_gemm_use_pairs(w, a)) {
+        // CTA-pair kernel: 128-token activation boxes, 128-byte-swizzled 32-row output boxes
+        mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, pair::TOK);
+        if (mrc) return mrc;
+        mrc = ceb_make_tmap_2d(&omap, a.out, esz, (uint64_t)w.n_out, (uint64_t)a.m_rows, (uint64_t)a.ldo * esz,
+                               esz == 2 ? 64 : 32, 32, true);
+        if (mrc) return mrc;
+        const int n_fp = w.n_out / pair::FEAT;
+        long long bound = (long long)n_fp * ((act_rows + 2 * pair::TOK - 1) / (2 * pair::TOK) + groups);
+        int max_pairs = ceb_num_sms() / 2;
+        if (max_ctas > 0 && max_ctas / 2 < max_pairs) max_pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
+        if (bound < max_pairs) max_pairs = (int)bound;
+        int rc = 0;
+        if (w.format == CEB_W_Q8_0)
+            CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q8_0>(map, omap, w, a, max_pairs, stream));
+        else
+            CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q4_K>(map, omap, w, a, max_pairs, stream));
+        return rc;
+    }
+    mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);
+    if (mrc) return mrc;
     mrc = ceb_make_tmap_2d(&omap, a.out, esz, (uint64_t)w.n_out, (uint64_t)a.m_rows, (uint64_t)a.ldo * esz, 32, 32,
                            false);
     if (mrc) return mrc;
     const int n_ftiles = w.n_out / BM;
-    const int groups = a.offsets ? w.n_groups : 1;
     long long bound = (long long)n_ftiles * ((act_rows + BN - 1) / BN + groups);
     int grid = ceb_num_sms();
     if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
     if (bound < grid) grid = (int)bound;
-    const double flops = 2.0 * (double)a.m_rows * w.n_out * w.k;
-    const double bytes = (double)(w.q_bytes + w.s_bytes) + (double)a.m_rows * w.k * 2 +
-                         (double)a.m_rows * w.n_out * ((a.epi & CEB_EPI_F16_OUT) ? 2 : 4);
     int rc = 0;
     switch (w.format) {
         case CEB_W_Q8_0: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q8_0>(map, omap, w, a, grid, stream)); break;

@@ -1,4 +1,9 @@
-"""Grouped-GEMM kernel (tcgen05, weights dequantized into TMEM) against the oracle.
+"""Grouped-GEMM kernels (tcgen05) against the oracle.
+
+Quantized weights with an output width that is a multiple of 256 run on the
+CTA-pair kernel (cta_group::2); other widths and fp16/f32 weights on the
+single-CTA kernel.  The cases below cover both, including partial token tiles
+where only the first CTA of a pair has rows (m mod 256 in 1..128).
 
 The oracle's F16 mode rounds operands exactly as the kernel does (weights to
 fp16(dequant), activations fp16) and accumulates in double, so the remaining
@@ -24,6 +29,10 @@ CASES = [
     (GGML_Q4_K, 768, 3072, 256),
     (GGML_F32, 256, 512, 200),
     (GGML_F16, 128, 192, 33),
+    (GGML_Q8_0, 768, 768, 1000),
+    (GGML_Q8_0, 512, 256, 257),
+    (GGML_Q8_0, 256, 128, 128),
+    (GGML_Q4_K, 512, 512, 383),
 ]
 
 
@@ -48,7 +57,7 @@ def test_matmul_f32_out(cuda, oracle, w_type, n_out, k, m):
     assert np.abs(out - ref).max() <= tol, np.abs(out - ref).max()
 
 
-@pytest.mark.parametrize("w_type,n_out,k,m", [CASES[2], CASES[5], CASES[7]])
+@pytest.mark.parametrize("w_type,n_out,k,m", [CASES[2], CASES[5], CASES[7], CASES[9], CASES[10], CASES[12]])
 def test_matmul_bias_gelu_f16_out(cuda, oracle, w_type, n_out, k, m):
     import torch
     from crispembed_b200 import binding
@@ -87,3 +96,34 @@ def test_matmul_rejects_bad_shape(cuda):
     xd = torch.from_numpy(x).to(cuda)
     with pytest.raises(binding.CrispEmbedError):
         binding.matmul(GGML_Q8_0, quant.quantize(np.zeros((96, 64), np.float32), GGML_Q8_0), 96, 64, xd)
+
+
+def test_pair_and_single_cta_kernels_agree(cuda, tmp_path):
+    """The single-CTA kernel (forced by CEB_GEMM_SINGLE_CTA=1 in a child process)
+    and the CTA-pair kernel give the same product up to fp32 summation order."""
+    import os
+    import subprocess
+    import sys
+
+    import torch
+    from crispembed_b200 import binding
+    raw, x, bias = _inputs(GGML_Q8_0, 768, 768, 700, seed=11)
+    xd = torch.from_numpy(x).to(cuda)
+    bd = torch.from_numpy(bias).to(cuda)
+    pair_out = binding.matmul(GGML_Q8_0, raw, 768, 768, xd, bias=bd, gelu=True, out_f16=True).float().cpu().numpy()
+    np.save(tmp_path / "raw.npy", raw)
+    np.save(tmp_path / "x.npy", x)
+    np.save(tmp_path / "bias.npy", bias)
+    code = (
+        "import numpy as np, torch, sys\n"
+        "from crispembed_b200 import binding\n"
+        f"d = {str(tmp_path)!r}\n"
+        "raw = np.load(d + '/raw.npy'); x = np.load(d + '/x.npy'); b = np.load(d + '/bias.npy')\n"
+        "o = binding.matmul(8, raw, 768, 768, torch.from_numpy(x).cuda(), bias=torch.from_numpy(b).cuda(),"
+        " gelu=True, out_f16=True).float().cpu().numpy()\n"
+        "np.save(d + '/single.npy', o)\n")
+    env = dict(os.environ, CEB_GEMM_SINGLE_CTA="1")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=root, timeout=300)
+    single = np.load(tmp_path / "single.npy")
+    assert np.abs(single - pair_out).max() <= 2e-3 * max(1.0, float(np.abs(pair_out).max()))
