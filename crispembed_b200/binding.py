@@ -73,6 +73,8 @@ def load_library(path: Optional[str] = None):
                         ctypes.c_int),
         "ceb_moe_ffn_static": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_attention_forward": ([vp, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp],
+                                  ctypes.c_int),
         "ceb_matmul": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
                         ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_linear_create": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int], vp),
@@ -290,6 +292,21 @@ def pool_l2(hidden, cu_seqlens, out_dim: Optional[int] = None, stream=None):
     out = torch.empty((n, od), dtype=torch.float32, device=hidden.device)
     _check(lib.ceb_pool_l2(hidden.data_ptr(), cu_seqlens.data_ptr(), n, d, od, out.data_ptr(), _stream_ptr(stream)),
            "ceb_pool_l2")
+    return out
+
+
+def attention(qkv, cu_seqlens, n_head: int, max_len: Optional[int] = None, stream=None):
+    """softmax(Q K^T / sqrt(64)) V per sequence and head; qkv [rows, 3d] fp16 on the device."""
+    import torch
+    lib = load_library()
+    rows, d3 = qkv.shape
+    d = d3 // 3
+    n = cu_seqlens.numel() - 1
+    if max_len is None:
+        max_len = int((cu_seqlens[1:] - cu_seqlens[:-1]).max().item()) if n else 0
+    out = torch.empty((rows, d), dtype=torch.float16, device=qkv.device)
+    _check(lib.ceb_attention_forward(qkv.data_ptr(), rows, cu_seqlens.data_ptr(), n, max_len, d, n_head,
+                                     out.data_ptr(), _stream_ptr(stream)), "ceb_attention_forward")
     return out
 
 

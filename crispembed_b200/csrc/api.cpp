@@ -478,6 +478,17 @@ extern "C" int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, i
     return ceb_pool_l2_launch(d_hidden, d_cu_seqlens, n_seqs, d, out_dim, d_out, static_cast<cudaStream_t>(stream), 0);
 }
 
+extern "C" int ceb_attention_forward(const void* d_qkv, int n_rows, const int32_t* d_cu_seqlens, int n_seqs,
+                                     int max_len, int d, int n_head, void* d_out, void* stream) {
+    if (!d_qkv || !d_cu_seqlens || !d_out || n_rows < 0 || n_seqs < 0 || max_len < 0)
+        return ceb_set_error(1, "attention: bad arguments");
+    if (n_rows == 0 || n_seqs == 0) return 0;
+    int* err = op_err_word();
+    if (!err) return ceb_set_error(3, "attention: device error word");
+    return ceb_attention(static_cast<const __half*>(d_qkv), n_rows, d_cu_seqlens, n_seqs, max_len, d, n_head,
+                         static_cast<__half*>(d_out), err, static_cast<cudaStream_t>(stream));
+}
+
 struct ceb_linear {
     ceb_wplane w;
 };

@@ -19,8 +19,12 @@ int ceb_add_ln(const float* res, const float* y, int M, int d, const float* gamm
 int ceb_moe_combine_ln(const float* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
                        const float* cur, int M, int d, const float* gamma, const float* beta, float eps, float* out32,
                        __half* out16, cudaStream_t st);
-int ceb_attention(const __half* qkv, const int32_t* cu, int n_seqs, int max_len, int d, int n_head, __half* out,
-                  cudaStream_t st);
+int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
+                  __half* out, int* d_err, cudaStream_t st);
+// tcgen05 CTA-pair attention (attn_tc.cu); returns 1 without launching when the
+// shape is not handled there (head_dim != 64 or a sequence longer than 512)
+int ceb_attention_tc(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
+                     __half* out, int* d_err, cudaStream_t st);
 int ceb_pool_l2_launch(const float* hidden, const int32_t* cu, int n_seqs, int d, int out_dim, float* out,
                        cudaStream_t st, int mode = 0);
 

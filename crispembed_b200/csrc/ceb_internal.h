@@ -67,6 +67,9 @@ const char* ceb_last_error_message();
 // tensor maps
 int ceb_make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
                      uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, bool swizzle128);
+// Same with the shared-memory swizzle span in bytes (0, 32, 64 or 128).
+int ceb_make_tmap_2d_sw(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes);
 int ceb_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
                          uint32_t box_inner, uint32_t box_rows);
 

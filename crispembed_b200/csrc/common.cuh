@@ -172,6 +172,15 @@ CEB_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr)
         : "memory");
 }
+// 32 lanes x 32 bit, 16 consecutive columns
+CEB_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 CEB_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor (tcgen05 format): K-major operand, 128-byte
@@ -184,6 +193,18 @@ CEB_DEV uint64_t smem_desc_sw128(uint32_t saddr) {
     d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset [32,46)
     d |= (uint64_t)1 << 46;                         // descriptor version (sm100)
     d |= (uint64_t)2 << 61;                         // SWIZZLE_128B
+    return d;
+}
+
+// MN-major operand, 64-byte swizzle: rows of 64 B (32 fp16 along N) consecutive
+// along K, 8-row (512 B) swizzle atoms; one atom along N (N <= 32 per CTA).
+CEB_DEV uint64_t smem_desc_mn_sw64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFF) >> 4);        // start address  [0,14)
+    d |= (uint64_t)1 << 16;                         // leading byte offset (single atom along N)
+    d |= (uint64_t)(512 >> 4) << 32;                // stride byte offset: next 8 K-rows
+    d |= (uint64_t)1 << 46;                         // descriptor version (sm100)
+    d |= (uint64_t)4 << 61;                         // SWIZZLE_64B
     return d;
 }
 
@@ -261,6 +282,16 @@ CEB_DEV void mma_pair_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, 
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// A from tensor memory (TS form): each CTA's TMEM holds its M/2 rows of A,
+// 32-bit column c = fp16 K elements 2c, 2c+1.
+CEB_DEV void mma_pair_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 // arrive on the mbarrier at cluster address `cl_bar` when this thread's MMAs complete

@@ -794,6 +794,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                     mma_pair_commit(mapa_shared(bar(B_ACC_FULL(ab)), 1));
                 }
             }
+            // rank 1's last ACC_EMPTY signals (16-byte copies into this CTA) have landed
+            for (uint32_t l = lt >= 2 ? lt - 2 : 0; l < lt; ++l)
+                mbar_wait_cluster(bar(B_ACC_EMPTY(l & 1)), (l >> 1) & 1, nullptr, nullptr, 0);
             // every issued MMA (they write both CTAs' tensor memory) retires before TMEM is released
             mma_pair_commit(bar(B_DRAIN()));
             mbar_wait(bar(B_DRAIN()), 0, nullptr, nullptr, 0);

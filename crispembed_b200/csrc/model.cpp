@@ -400,7 +400,7 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
         a.epi = CEB_EPI_F16_OUT | (Ly.qkv_b ? CEB_EPI_BIAS : 0);
         a.bias = Ly.qkv_b;
         if ((rc = ceb_gemm_launch(Ly.qkv, ws.x16, M, a, st))) return rc;
-        if ((rc = ceb_attention(ws.qkv16, d_cu, n_seqs, max_len, d, hp.n_head, ws.a16, st))) return rc;
+        if ((rc = ceb_attention(ws.qkv16, M, d_cu, n_seqs, max_len, d, hp.n_head, ws.a16, d_err, st))) return rc;
         // output projection (+bias) -> fp32, residual + LN1
         a.out = ws.t32;
         a.ldo = d;

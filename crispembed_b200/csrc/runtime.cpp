@@ -68,6 +68,12 @@ EncodeTiledFn encode_fn() {
 
 int ceb_make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
                      uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+    return ceb_make_tmap_2d_sw(map, base, elem_bytes, inner, rows, row_stride_bytes, box_inner, box_rows,
+                               swizzle128 ? 128 : 0);
+}
+
+int ceb_make_tmap_2d_sw(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return ceb_set_error(3, "cuTensorMapEncodeTiled unavailable");
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15))
@@ -79,7 +85,10 @@ int ceb_make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_
     cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                    : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                    : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                          : CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return ceb_set_error(3, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return 0;

@@ -113,6 +113,19 @@ CEB_API int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int 
                         float* d_out, void* stream);
 
 /*
+ * Multi-head self-attention over packed sequences, the attention block of the
+ * encoder graph (src/crispembed.cpp:1278-1297): for every sequence s (rows
+ * cu[s] .. cu[s+1]-1) and head h, softmax(Q K^T / sqrt(head_dim)) V, no mask
+ * beyond the sequence bounds.  d_qkv [n_rows x 3d] fp16 holds Q | K | V per row
+ * (head h at columns h*64 .. h*64+63 of each third); d_out [n_rows x d] fp16.
+ * head_dim must be 64.  Sequences of up to 512 tokens run on the tcgen05
+ * CTA-pair kernel, longer ones on an mma.sync kernel.  Asynchronous on
+ * `stream`; device-side failures surface through ceb_sync_check.
+ */
+CEB_API int ceb_attention_forward(const void* d_qkv, int n_rows, const int32_t* d_cu_seqlens, int n_seqs, int max_len,
+                                  int d, int n_head, void* d_out, void* stream);
+
+/*
  * A device-resident linear layer (one ggml_mul_mat weight of the encoder,
  * src/crispembed.cpp:1160-1416): W [n_out rows x k] given as GGUF bytes on the
  * host, repacked once into the planes the tensor-core GEMM streams.
