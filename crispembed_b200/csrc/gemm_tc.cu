@@ -971,6 +971,7 @@ int launch_pair(const CUtensorMap& xmap, const CUtensorMap& omap, const ceb_wpla
     return 0;
 }
 
+
 }  // namespace
 
 // The CTA-pair kernel takes quantized weights whose output width is a multiple of
