@@ -73,6 +73,15 @@ def load_library(path: Optional[str] = None):
                         ctypes.c_int),
         "ceb_moe_ffn_static": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_tokenizer_load": ([ctypes.c_char_p, ctypes.c_int], vp),
+        "ceb_tokenizer_encode": ([vp, ctypes.c_char_p, vp, ctypes.c_int], ctypes.c_int),
+        "ceb_tokenizer_kind_of": ([vp], ctypes.c_int),
+        "ceb_tokenizer_free": ([vp], None),
+        "crispembed_encode_tokens": ([vp, ctypes.c_char_p, vp, vp], vp),
+        "crispembed_encode_tokens_raw": ([vp, ctypes.c_char_p, vp, vp], vp),
+        "crispembed_last_token_ids": ([vp], vp),
+        "crispembed_token_str": ([vp, ctypes.c_int32], ctypes.c_char_p),
+        "crispembed_tokenizer_kind": ([vp], ctypes.c_int),
         "ceb_attention_forward": ([vp, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp],
                                   ctypes.c_int),
         "ceb_matmul": ([ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
@@ -172,6 +181,28 @@ class CrispEmbed:
         finally:
             if matryoshka_dim is not None:
                 self.set_dim(0)
+
+    def encode_tokens(self, text: str, raw: bool = False):
+        """Per-token final hidden states [n_tokens, n_embd] (L2-normalised unless raw) and their ids."""
+        n = ctypes.c_int(0)
+        dim = ctypes.c_int(0)
+        fn = self._lib.crispembed_encode_tokens_raw if raw else self._lib.crispembed_encode_tokens
+        ptr = fn(self._ctx, text.encode("utf-8"), ctypes.byref(n), ctypes.byref(dim))
+        if not ptr:
+            raise CrispEmbedError(f"encode_tokens failed: {last_error()}")
+        vec = np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_float)),
+                                    shape=(n.value * dim.value,)).copy().reshape(n.value, dim.value)
+        ids_ptr = ctypes.cast(self._lib.crispembed_last_token_ids(self._ctx), ctypes.POINTER(ctypes.c_int32))
+        ids = np.ctypeslib.as_array(ids_ptr, shape=(n.value,)).copy()
+        return vec, ids
+
+    def token_str(self, token_id: int) -> str:
+        r = self._lib.crispembed_token_str(self._ctx, int(token_id))
+        return r.decode("utf-8", "replace") if r is not None else ""
+
+    @property
+    def tokenizer_kind(self) -> int:
+        return self._lib.crispembed_tokenizer_kind(self._ctx)
 
     def encode_ids(self, ids: np.ndarray, lens: Sequence[int]) -> np.ndarray:
         ids = np.ascontiguousarray(ids, dtype=np.int32)
@@ -308,6 +339,40 @@ def attention(qkv, cu_seqlens, n_head: int, max_len: Optional[int] = None, strea
     _check(lib.ceb_attention_forward(qkv.data_ptr(), rows, cu_seqlens.data_ptr(), n, max_len, d, n_head,
                                      out.data_ptr(), _stream_ptr(stream)), "ceb_attention_forward")
     return out
+
+
+class Tokenizer:
+    """The text tokenizer of a GGUF (WordPiece or SentencePiece Unigram), without a device."""
+
+    def __init__(self, gguf_path: str, max_tokens: int = 512):
+        self._lib = load_library()
+        self._h = self._lib.ceb_tokenizer_load(gguf_path.encode(), int(max_tokens))
+        if not self._h:
+            raise CrispEmbedError(f"ceb_tokenizer_load failed: {last_error()}")
+        self.max_tokens = int(max_tokens)
+
+    @property
+    def kind(self) -> int:
+        return self._lib.ceb_tokenizer_kind_of(self._h)
+
+    def encode(self, text: str):
+        cap = self.max_tokens
+        buf = (ctypes.c_int32 * cap)()
+        n = self._lib.ceb_tokenizer_encode(self._h, text.encode("utf-8"), buf, cap)
+        if n < 0:
+            raise CrispEmbedError(f"ceb_tokenizer_encode failed: {last_error()}")
+        return [int(buf[i]) for i in range(min(n, cap))]
+
+    def close(self):
+        if self._h:
+            self._lib.ceb_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def sync_check(stream=None):

@@ -17,6 +17,8 @@
 #include "../../include/ceb_ops.h"
 #include "../../include/crispembed.h"
 #include "ceb_encoder_internal.h"
+#include "gguf.h"
+#include "tokenizer.h"
 
 static_assert(sizeof(crispembed_hparams) == sizeof(ceb_hparams_c), "hparams layout");
 
@@ -32,11 +34,10 @@ struct crispembed_context {
     std::string prefix;
     int matryoshka_dim = 0;
     std::vector<float> last_output;
-    // WordPiece tokenizer (tokenizer.ggml.type == 0)
-    int tok_type = 0;
-    int cls_id = 101, sep_id = 102, unk_id = 100, pad_id = 0;
-    bool lower = true;
-    std::unordered_map<std::string, int> vocab;
+    ceb_tokenizer tok;
+    // per-token results (crispembed_encode_tokens*)
+    std::vector<float> last_tokens;
+    std::vector<int32_t> last_token_ids;
     // pinned staging for host-buffer calls
     int32_t* h_ids = nullptr;
     int32_t* h_cu = nullptr;
@@ -141,83 +142,51 @@ const float* encode_ids_host(crispembed_context* ctx, const int32_t* ids, const 
     return ctx->last_output.data();
 }
 
-// ---- WordPiece (BERT basic tokenizer + greedy longest-match-first) ----------
-bool is_punct(unsigned char c) {
-    return (c >= 33 && c <= 47) || (c >= 58 && c <= 64) || (c >= 91 && c <= 96) || (c >= 123 && c <= 126);
-}
-
-std::vector<int32_t> wordpiece(const crispembed_context* ctx, const std::string& text) {
-    std::vector<std::string> words;
-    std::string cur;
-    for (unsigned char c : text) {
-        if (std::isspace(c)) {
-            if (!cur.empty()) words.push_back(cur), cur.clear();
-        } else if (c < 128 && is_punct(c)) {
-            if (!cur.empty()) words.push_back(cur), cur.clear();
-            words.push_back(std::string(1, (char)c));
-        } else {
-            cur.push_back(ctx->lower && c < 128 ? (char)std::tolower(c) : (char)c);
-        }
-    }
-    if (!cur.empty()) words.push_back(cur);
-    std::vector<int32_t> ids;
-    ids.push_back(ctx->cls_id);
-    const size_t limit = (size_t)std::max(2, ctx->model.hp.n_max_tokens) - 1;
-    for (const auto& w : words) {
-        if (ids.size() >= limit) break;
-        if (w.size() > 100) {
-            ids.push_back(ctx->unk_id);
-            continue;
-        }
-        std::vector<int32_t> pieces;
-        size_t start = 0;
-        bool bad = false;
-        while (start < w.size()) {
-            size_t end = w.size();
-            int found = -1;
-            while (start < end) {
-                std::string sub = w.substr(start, end - start);
-                if (start > 0) sub = "##" + sub;
-                auto it = ctx->vocab.find(sub);
-                if (it != ctx->vocab.end()) {
-                    found = it->second;
-                    break;
-                }
-                --end;
-            }
-            if (found < 0) {
-                bad = true;
-                break;
-            }
-            pieces.push_back(found);
-            start = end;
-        }
-        if (bad) ids.push_back(ctx->unk_id);
-        else
-            for (int32_t p : pieces) {
-                if (ids.size() >= limit) break;
-                ids.push_back(p);
-            }
-    }
-    ids.push_back(ctx->sep_id);
-    return ids;
-}
-
 const float* encode_texts(crispembed_context* ctx, const char** texts, int n, int* out_n_dim) {
-    if (ctx->tok_type != 0) {
-        ceb_set_error(1, "tokenizer type %d is not implemented by this build (WordPiece only); "
-                         "use crispembed_encode_ids_batch",
-                      ctx->tok_type);
-        return nullptr;
-    }
-    std::vector<int32_t> ids, lens;
+    std::vector<int32_t> ids, lens, t;
     for (int i = 0; i < n; ++i) {
-        std::string s = ctx->prefix + (texts[i] ? texts[i] : "");
-        std::vector<int32_t> t = wordpiece(ctx, s);
+        if (ctx->tok.encode(ctx->prefix + (texts[i] ? texts[i] : ""), &t)) return nullptr;
         lens.push_back((int32_t)t.size());
         ids.insert(ids.end(), t.begin(), t.end());
     }
     return encode_ids_host(ctx, ids.data(), lens.data(), n, out_n_dim);
+}
+
+// Final hidden states [T x d] of one tokenized text (the reference's encode_tokens
+// path, src/crispembed.cpp:3272-3373): the encoder runs as for a batch of one and
+// the last layer's output rows are copied back; `normalize` L2-normalises each row
+// as the reference does (sum of squares in float, sqrt(max(., 1e-12))).
+const float* encode_tokens(crispembed_context* ctx, const char* text, int* out_n_tokens, int* out_dim,
+                           bool normalize) {
+    if (out_n_tokens) *out_n_tokens = 0;
+    if (out_dim) *out_dim = 0;
+    if (!ctx || !text) return nullptr;
+    std::vector<int32_t> ids;
+    if (ctx->tok.encode(ctx->prefix + text, &ids)) return nullptr;
+    if (ids.empty()) return nullptr;
+    const int T = (int)ids.size();
+    if (!encode_ids_host(ctx, ids.data(), &T, 1, nullptr)) return nullptr;
+    const int d = ctx->model.hp.n_embd;
+    ctx->last_tokens.resize((size_t)T * d);
+    cudaStream_t st = ctx->stream;
+    if (cudaMemcpyAsync(ctx->last_tokens.data(), ctx->ws.x32, (size_t)T * d * 4, cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+        ceb_set_error(3, "hidden-state download failed");
+        return nullptr;
+    }
+    if (normalize)
+        for (int t = 0; t < T; ++t) {
+            float* v = ctx->last_tokens.data() + (size_t)t * d;
+            float ss = 0.0f;
+            for (int j = 0; j < d; ++j) ss += v[j] * v[j];
+            const float nrm = std::sqrt(std::max(ss, 1e-12f));
+            for (int j = 0; j < d; ++j) v[j] /= nrm;
+        }
+    ctx->last_token_ids = ids;
+    if (out_n_tokens) *out_n_tokens = T;
+    if (out_dim) *out_dim = d;
+    return ctx->last_tokens.data();
 }
 
 std::string g_str;  // backing store for the registry helpers
@@ -235,19 +204,19 @@ extern "C" crispembed_context* crispembed_init(const char* model_path, int n_thr
         return nullptr;
     }
     std::string err;
-    std::vector<std::string> vocab;
-    if (ceb_model_load(&ctx->model, model_path, &err, &vocab, &ctx->tok_type, &ctx->cls_id, &ctx->sep_id, &ctx->unk_id,
-                       &ctx->pad_id)) {
+    if (ceb_model_load(&ctx->model, model_path, &err)) {
         delete ctx;
         return nullptr;
     }
-    ctx->vocab.reserve(vocab.size());
-    for (size_t i = 0; i < vocab.size(); ++i) ctx->vocab.emplace(vocab[i], (int)i);
-    for (const auto& t : vocab)
-        if (t.size() == 1 && t[0] >= 'A' && t[0] <= 'Z') {
-            ctx->lower = false;
-            break;
+    {
+        ceb_gguf g;
+        if (!g.open(model_path, &err) || ctx->tok.load(g, ctx->model.hp.n_max_tokens)) {
+            if (!err.empty()) ceb_set_error(1, "%s", err.c_str());
+            ceb_model_free(&ctx->model);
+            delete ctx;
+            return nullptr;
         }
+    }
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) {
         ceb_set_error(3, "context setup failed");
@@ -319,6 +288,26 @@ extern "C" void crispembed_free(crispembed_context* ctx) {
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
+
+extern "C" const float* crispembed_encode_tokens(crispembed_context* ctx, const char* text, int* out_n_tokens,
+                                                 int* out_dim) {
+    return encode_tokens(ctx, text, out_n_tokens, out_dim, true);
+}
+
+extern "C" const float* crispembed_encode_tokens_raw(crispembed_context* ctx, const char* text, int* out_n_tokens,
+                                                     int* out_dim) {
+    return encode_tokens(ctx, text, out_n_tokens, out_dim, false);
+}
+
+extern "C" const int32_t* crispembed_last_token_ids(const crispembed_context* ctx) {
+    return (ctx && !ctx->last_token_ids.empty()) ? ctx->last_token_ids.data() : nullptr;
+}
+
+extern "C" const char* crispembed_token_str(const crispembed_context* ctx, int32_t id) {
+    return ctx ? ctx->tok.token_str(id).c_str() : nullptr;
+}
+
+extern "C" int crispembed_tokenizer_kind(const crispembed_context* ctx) { return ctx ? ctx->tok.kind() : 0; }
 
 extern "C" int crispembed_has_sparse(const crispembed_context*) { return 0; }
 extern "C" int crispembed_has_colbert(const crispembed_context*) { return 0; }
@@ -572,3 +561,37 @@ extern "C" int ceb_sync_check(void* stream) {
     }
     return 0;
 }
+
+// ---------------------------------------------------- tokenizer (no device needed)
+struct ceb_text_tokenizer {
+    ceb_tokenizer tok;
+};
+
+extern "C" ceb_text_tokenizer* ceb_tokenizer_load(const char* gguf_path, int max_tokens) {
+    if (!gguf_path) return nullptr;
+    ceb_gguf g;
+    std::string err;
+    if (!g.open(gguf_path, &err)) {
+        ceb_set_error(1, "%s", err.c_str());
+        return nullptr;
+    }
+    auto* t = new ceb_text_tokenizer;
+    if (t->tok.load(g, max_tokens)) {
+        delete t;
+        return nullptr;
+    }
+    return t;
+}
+
+extern "C" int ceb_tokenizer_encode(const ceb_text_tokenizer* t, const char* text, int32_t* ids, int cap) {
+    if (!t || !text) return ceb_set_error(1, "null argument"), -1;
+    std::vector<int32_t> v;
+    if (t->tok.encode(text, &v)) return -1;
+    const int n = (int)v.size();
+    for (int i = 0; i < n && i < cap; ++i) ids[i] = v[i];
+    return n;
+}
+
+extern "C" int ceb_tokenizer_kind_of(const ceb_text_tokenizer* t) { return t ? t->tok.kind() : 0; }
+
+extern "C" void ceb_tokenizer_free(ceb_text_tokenizer* t) { delete t; }

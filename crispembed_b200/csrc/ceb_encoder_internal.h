@@ -69,9 +69,7 @@ struct ceb_workspace {
     float* out = nullptr;      // [cap_seqs x d]
 };
 
-int ceb_model_load(ceb_model* m, const std::string& path, std::string* vocab_err,
-                   std::vector<std::string>* vocab_out, int* tok_type, int* cls_id, int* sep_id, int* unk_id,
-                   int* pad_id);
+int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out);
 void ceb_model_free(ceb_model* m);
 int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int seqs);
 void ceb_workspace_free(ceb_workspace* ws);

@@ -99,8 +99,7 @@ struct Loader {
 
 }  // namespace
 
-int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out, std::vector<std::string>* vocab_out,
-                   int* tok_type, int* cls_id, int* sep_id, int* unk_id, int* pad_id) {
+int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) {
     ceb_gguf g;
     std::string err;
     if (!g.open(path, &err)) return ceb_set_error(1, "failed to open '%s': %s", path.c_str(), err.c_str());
@@ -142,15 +141,6 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out, 
     if (L.u32({"bert.pre_ln"}, 0) != 0)
         return ceb_set_error(1, "pre-LN encoders are outside this build's NomicBERT-MoE path");
 
-    // tokenizer metadata
-    if (const ceb_gguf_value* v = g.find("tokenizer.ggml.tokens")) {
-        if (vocab_out) *vocab_out = v->arr_str;
-    }
-    *tok_type = L.u32({"tokenizer.ggml.type"}, g.get_str("tokenizer.ggml.model").empty() ? 0 : -1);
-    *cls_id = L.u32({"tokenizer.ggml.cls_token_id"}, 101);
-    *sep_id = L.u32({"tokenizer.ggml.sep_token_id"}, 102);
-    *unk_id = L.u32({"tokenizer.ggml.unknown_token_id"}, 100);
-    *pad_id = L.u32({"tokenizer.ggml.padding_token_id"}, 0);
     (void)err_out;
 
     cudaStream_t st;

@@ -79,8 +79,11 @@ def tiny_spec(wtype: int = G.GGML_Q8_0, **kw) -> ModelSpec:
     return ModelSpec(**base)
 
 
-def write_model(path: str, spec: ModelSpec) -> List[str]:
-    """Write the synthetic GGUF; returns the tensor order."""
+def write_model(path: str, spec: ModelSpec, tokenizer=None) -> List[str]:
+    """Write the synthetic GGUF; returns the tensor order.
+
+    `tokenizer(writer)` replaces the default synthetic WordPiece keys (it must
+    write spec.n_vocab tokens)."""
     rng = np.random.default_rng(spec.seed)
     w = G.GGUFWriter(path)
     w.add_str("general.architecture", "nomic-bert-moe")
@@ -96,12 +99,15 @@ def write_model(path: str, spec: ModelSpec) -> List[str]:
     if spec.n_experts > 0:
         w.add_u32("bert.num_experts", spec.n_experts)
         w.add_u32("bert.num_experts_per_tok", spec.top_k)
-    w.add_u32("tokenizer.ggml.type", 0)
-    w.add_str_array("tokenizer.ggml.tokens", [vocab_word(i) for i in range(spec.n_vocab)])
-    w.add_u32("tokenizer.ggml.padding_token_id", 0)
-    w.add_u32("tokenizer.ggml.cls_token_id", 1)
-    w.add_u32("tokenizer.ggml.sep_token_id", 2)
-    w.add_u32("tokenizer.ggml.unknown_token_id", 3)
+    if tokenizer is not None:
+        tokenizer(w)
+    else:
+        w.add_u32("tokenizer.ggml.type", 0)
+        w.add_str_array("tokenizer.ggml.tokens", [vocab_word(i) for i in range(spec.n_vocab)])
+        w.add_u32("tokenizer.ggml.padding_token_id", 0)
+        w.add_u32("tokenizer.ggml.cls_token_id", 1)
+        w.add_u32("tokenizer.ggml.sep_token_id", 2)
+        w.add_u32("tokenizer.ggml.unknown_token_id", 3)
 
     order: List[str] = []
     d, wt = spec.d, spec.wtype

@@ -113,6 +113,20 @@ CEB_API int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int 
                         float* d_out, void* stream);
 
 /*
+ * The text tokenizer of a GGUF on its own (no device needed): the family the
+ * reference would pick (src/tokenizer.h:37-52), WordPiece or SentencePiece
+ * Unigram, wrapping and truncation to max_tokens as the text ABI applies them.
+ * ceb_tokenizer_encode writes up to `cap` ids and returns the full count (-1 on
+ * error).  No counterpart in the reference's exported API: the reference keeps
+ * its tokenizers internal; these serve tests and tools.
+ */
+typedef struct ceb_text_tokenizer ceb_text_tokenizer;
+CEB_API ceb_text_tokenizer* ceb_tokenizer_load(const char* gguf_path, int max_tokens);
+CEB_API int ceb_tokenizer_encode(const ceb_text_tokenizer* tok, const char* text, int32_t* ids, int cap);
+CEB_API int ceb_tokenizer_kind_of(const ceb_text_tokenizer* tok);
+CEB_API void ceb_tokenizer_free(ceb_text_tokenizer* tok);
+
+/*
  * Multi-head self-attention over packed sequences, the attention block of the
  * encoder graph (src/crispembed.cpp:1278-1297): for every sequence s (rows
  * cu[s] .. cu[s+1]-1) and head h, softmax(Q K^T / sqrt(head_dim)) V, no mask

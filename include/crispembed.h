@@ -63,8 +63,9 @@ CRISPEMBED_API const char* crispembed_get_prefix(const crispembed_context* ctx);
 /* src/crispembed.h:103 / src/crispembed.cpp:2604 */
 CRISPEMBED_API const crispembed_hparams* crispembed_get_hparams(const crispembed_context* ctx);
 
-/* src/crispembed.h:128-131 / src/crispembed.cpp:2672.  WordPiece GGUFs only
- * (tokenizer.ggml.type 0); other tokenizers return NULL with a message. */
+/* src/crispembed.h:128-131 / src/crispembed.cpp:2672.  WordPiece and
+ * SentencePiece Unigram GGUFs (tokenizer.ggml.type 0 / 2, or the
+ * tokenizer.ggml.model string); a BPE tokenizer returns NULL with a message. */
 CRISPEMBED_API const float* crispembed_encode(crispembed_context* ctx, const char* text, int* out_n_dim);
 
 /* src/crispembed.h:133-137 / src/crispembed.cpp:2856.  Flat [n_texts x dim]. */
@@ -73,6 +74,20 @@ CRISPEMBED_API const float* crispembed_encode_batch(crispembed_context* ctx, con
 
 /* src/crispembed.cpp:4938-4976 */
 CRISPEMBED_API void crispembed_free(crispembed_context* ctx);
+
+/* Per-token outputs, src/crispembed.h:189-211 / src/crispembed.cpp:3272-3393.
+ * encode_tokens: the final hidden state of every token of `text` (prefix
+ * applied, wrap tokens included), each row L2-normalised; _raw: unnormalised.
+ * Flat [*out_n_tokens x *out_dim], ctx-owned until the next encode_tokens call.
+ * last_token_ids: the [n_tokens] ids of that call.  token_str: the piece of an
+ * id ("" out of range).  tokenizer_kind: 1 WordPiece, 2 SentencePiece, 3 BPE. */
+CRISPEMBED_API const float* crispembed_encode_tokens(crispembed_context* ctx, const char* text, int* out_n_tokens,
+                                                     int* out_dim);
+CRISPEMBED_API const float* crispembed_encode_tokens_raw(crispembed_context* ctx, const char* text,
+                                                         int* out_n_tokens, int* out_dim);
+CRISPEMBED_API const int32_t* crispembed_last_token_ids(const crispembed_context* ctx);
+CRISPEMBED_API const char* crispembed_token_str(const crispembed_context* ctx, int32_t id);
+CRISPEMBED_API int crispembed_tokenizer_kind(const crispembed_context* ctx);
 
 /* Capability queries the reference bindings call at setup
  * (src/crispembed.cpp:3009-3024): this build has no sparse/ColBERT/reranker

@@ -1,0 +1,154 @@
+"""Host tokenizers of the text ABI (crispembed_b200/csrc/tokenizer.cpp), no device.
+
+SentencePiece Unigram is checked against the sentencepiece package on a model
+trained here (tests/spm_fixture.py): the segmentation between <s> and </s> must
+be identical.  The family decision follows the reference's table
+(src/tokenizer.h:37-52); byte fallback and wrapping follow
+src/tokenizer_spm.cpp.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+sys.path.insert(0, os.path.dirname(__file__))
+import spm_fixture  # noqa: E402
+
+from crispembed_b200 import binding  # noqa: E402
+from crispembed_b200 import gguf_io as G  # noqa: E402
+
+
+def _gguf(path, fill):
+    w = G.GGUFWriter(str(path))
+    fill(w)
+    w.write()
+    return str(path)
+
+
+@pytest.fixture(scope="module")
+def spm_model(tmp_path_factory):
+    d = tmp_path_factory.mktemp("spm")
+    sp = spm_fixture.train(str(d))
+    path = _gguf(d / "tok.gguf", lambda w: spm_fixture.write_keys(w, sp))
+    return sp, path
+
+
+def test_sentencepiece_segmentation_matches_sentencepiece(spm_model):
+    sp, path = spm_model
+    tok = binding.Tokenizer(path, max_tokens=512)
+    assert tok.kind == 2
+    rng = np.random.default_rng(11)
+    texts = spm_fixture.corpus(200, seed=3)
+    # unseen combinations, repeated and edge spaces, glued words
+    texts += ["a", "the", "  two  spaces", "trailing ", "embeddingmodel", "routergatelayer expert",
+              "kernel" * 7, " ".join(spm_fixture.WORDS[:80])]
+    for _ in range(50):
+        k = int(rng.integers(1, 6))
+        texts.append("".join(spm_fixture.WORDS[int(i)] for i in rng.integers(0, len(spm_fixture.WORDS), size=k)))
+    for t in texts:
+        ids = tok.encode(t)
+        assert ids[0] == sp.bos_id() and ids[-1] == sp.eos_id()
+        assert ids[1:-1] == sp.encode(t), t
+
+
+def test_sentencepiece_empty_text_is_the_space_marker(spm_model):
+    """The reference prepends a space before replacing spaces by U+2581, so an empty
+    text is the single '▁' piece between <s> and </s> (the sentencepiece package
+    itself returns no pieces for an empty input)."""
+    sp, path = spm_model
+    tok = binding.Tokenizer(path)
+    assert tok.encode("") == [sp.bos_id(), sp.piece_to_id("▁"), sp.eos_id()]
+
+
+def test_sentencepiece_truncates_and_keeps_eos(spm_model):
+    sp, path = spm_model
+    tok = binding.Tokenizer(path, max_tokens=16)
+    text = " ".join(spm_fixture.WORDS[:60])
+    ids = tok.encode(text)
+    assert len(ids) == 16 and ids[0] == sp.bos_id() and ids[-1] == sp.eos_id()
+    full = sp.encode(text)
+    assert ids[1:-1] == full[:14]
+
+
+def test_sentencepiece_byte_fallback(tmp_path):
+    """Bytes no piece covers: '<0xXX>' pieces when present, else <unk>, one per byte."""
+    pieces = ["<unk>", "<s>", "</s>", "▁", "▁a", "b", "<0xC3>", "<0xA9>"]
+    scores = [0.0, 0.0, 0.0, -2.0, -1.0, -1.5, 0.0, 0.0]
+
+    def fill(w):
+        w.add_str("tokenizer.ggml.model", "llama")
+        w.add_str_array("tokenizer.ggml.tokens", pieces)
+        w.add_f32_array("tokenizer.ggml.scores", scores)
+        w.add_u32("tokenizer.ggml.unknown_token_id", 0)
+        w.add_u32("tokenizer.ggml.bos_token_id", 1)
+        w.add_u32("tokenizer.ggml.eos_token_id", 2)
+
+    tok = binding.Tokenizer(_gguf(tmp_path / "b.gguf", fill))
+    assert tok.kind == 2
+    # " abé" -> [▁a][b][<0xC3>][<0xA9>]; "é" is the two bytes C3 A9
+    assert tok.encode("abé") == [1, 4, 5, 6, 7, 2]
+    # a byte with no <0xXX> piece becomes <unk>
+    assert tok.encode("a!") == [1, 4, 0, 2]
+
+
+def test_sentencepiece_picks_the_max_score_segmentation(tmp_path):
+    pieces = ["<unk>", "<s>", "</s>", "▁ab", "▁a", "bc", "c", "▁"]
+    # "▁abc": [▁ab][c] = -3 -1.5 = -4.5 vs [▁a][bc] = -1 -1 = -2
+    scores = [0.0, 0.0, 0.0, -3.0, -1.0, -1.0, -1.5, -4.0]
+
+    def fill(w):
+        w.add_str("tokenizer.ggml.model", "t5")
+        w.add_str_array("tokenizer.ggml.tokens", pieces)
+        w.add_f32_array("tokenizer.ggml.scores", scores)
+
+    tok = binding.Tokenizer(_gguf(tmp_path / "v.gguf", fill))
+    assert tok.encode("abc")[1:-1] == [4, 5]
+
+
+@pytest.mark.parametrize("keys,n_vocab,kind", [
+    ({"type": 0}, 120000, 1),           # an explicit WordPiece type is final, even for a big vocab
+    ({"type": 2}, 100, 2),
+    ({"model": "t5"}, 100, 2),
+    ({"model": "unigram"}, 100, 2),
+    ({"model": "bert"}, 120000, 1),     # the model string overrides the size heuristic
+    ({"model": "gpt2"}, 100, 3),
+    ({}, 120000, 2),                    # neither key: vocabularies above 100k are SentencePiece
+    ({}, 1000, 1),
+])
+def test_tokenizer_family_decision(tmp_path, keys, n_vocab, kind):
+    def fill(w):
+        if "type" in keys:
+            w.add_u32("tokenizer.ggml.type", keys["type"])
+        if "model" in keys:
+            w.add_str("tokenizer.ggml.model", keys["model"])
+        w.add_str_array("tokenizer.ggml.tokens", [f"t{i}" for i in range(n_vocab)])
+
+    tok = binding.Tokenizer(_gguf(tmp_path / "f.gguf", fill))
+    assert tok.kind == kind
+
+
+def test_bpe_family_is_rejected_loudly(tmp_path):
+    def fill(w):
+        w.add_str("tokenizer.ggml.model", "gpt2")
+        w.add_str_array("tokenizer.ggml.tokens", ["a", "b"])
+
+    tok = binding.Tokenizer(_gguf(tmp_path / "g.gguf", fill))
+    with pytest.raises(binding.CrispEmbedError, match="BPE"):
+        tok.encode("ab")
+
+
+def test_wordpiece_greedy_longest_match(tmp_path):
+    vocab = ["[PAD]", "[CLS]", "[SEP]", "[UNK]", "un", "##aff", "##able", "aff", ",", "hello", "##s"]
+
+    def fill(w):
+        w.add_u32("tokenizer.ggml.type", 0)
+        w.add_str_array("tokenizer.ggml.tokens", vocab)
+        w.add_u32("tokenizer.ggml.cls_token_id", 1)
+        w.add_u32("tokenizer.ggml.sep_token_id", 2)
+        w.add_u32("tokenizer.ggml.unknown_token_id", 3)
+
+    tok = binding.Tokenizer(_gguf(tmp_path / "w.gguf", fill))
+    assert tok.kind == 1
+    assert tok.encode("Unaffable, hellos") == [1, 4, 5, 6, 8, 9, 10, 2]
+    assert tok.encode("zzz") == [1, 3, 2]
