@@ -72,6 +72,8 @@ def load_library(path: Optional[str] = None):
         "ceb_moe_ffn": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp, ctypes.c_size_t, vp],
                         ctypes.c_int),
         "ceb_moe_ffn_static": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_moe_route_ln": ([vp, vp, vp, ctypes.c_int, vp, vp, ctypes.c_float, vp, vp, vp, vp, vp, vp,
+                              ctypes.c_size_t, vp], ctypes.c_int),
         "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
         "ceb_tokenizer_load": ([ctypes.c_char_p, ctypes.c_int], vp),
         "ceb_tokenizer_encode": ([vp, ctypes.c_char_p, vp, ctypes.c_int], ctypes.c_int),
@@ -269,6 +271,14 @@ class MoELayer:
                                    _ptr(counts), _ptr(logits), workspace.data_ptr(), workspace.numel(),
                                    _stream_ptr(stream))
         _check(rc, "ceb_moe_ffn")
+
+    def route_ln(self, res, y, out, workspace, gamma=None, beta=None, eps=1e-5, out16=None, ids=None, weights=None,
+                 logits=None, stream=None):
+        """ceb_moe_route_ln: out = LN(res + y), and the router on the normalised rows in the same pass."""
+        rc = self._lib.ceb_moe_route_ln(self._h, res.data_ptr(), y.data_ptr(), res.shape[0], _ptr(gamma), _ptr(beta),
+                                        float(eps), out.data_ptr(), _ptr(out16), _ptr(ids), _ptr(weights),
+                                        _ptr(logits), workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+        _check(rc, "ceb_moe_route_ln")
 
 
 class Linear:

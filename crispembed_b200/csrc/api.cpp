@@ -461,6 +461,36 @@ extern "C" int ceb_moe_ffn(const ceb_moe_layer* L, const void* d_x, int x_dtype,
     return 0;
 }
 
+extern "C" int ceb_moe_route_ln(const ceb_moe_layer* L, const float* d_res, const float* d_y, int n_tokens,
+                                const float* d_gamma, const float* d_beta, float eps, float* d_out, void* d_out16,
+                                int32_t* d_ids, float* d_weights, float* d_logits, void* d_workspace,
+                                size_t workspace_bytes, void* stream) {
+    if (!L || !d_res || !d_y || !d_out || n_tokens < 0 || (n_tokens > 0 && !d_workspace))
+        return ceb_set_error(1, "moe_route_ln: bad arguments");
+    if (n_tokens == 0) return 0;
+    const size_t need = ceb_moe_workspace_size(L, n_tokens);
+    if (workspace_bytes < need)
+        return ceb_set_error(1, "moe_route_ln: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    if (reinterpret_cast<uintptr_t>(d_workspace) & 255)
+        return ceb_set_error(1, "moe_route_ln: workspace not 256-B aligned");
+    if ((reinterpret_cast<uintptr_t>(d_res) | reinterpret_cast<uintptr_t>(d_y) | reinterpret_cast<uintptr_t>(d_out) |
+         reinterpret_cast<uintptr_t>(d_out16) | reinterpret_cast<uintptr_t>(d_gamma) |
+         reinterpret_cast<uintptr_t>(d_beta)) & 15)
+        return ceb_set_error(1, "moe_route_ln: rows must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ceb_moe_ws ws;
+    ceb_moe_ws_layout(n_tokens, L->w.d, L->w.n_experts, L->w.top_k, L->w.ffn, &ws, static_cast<uint8_t*>(d_workspace));
+    int rc = ceb_add_ln_route(d_res, d_y, n_tokens, L->w.d, d_gamma, d_beta, eps, d_out, static_cast<__half*>(d_out16),
+                              L->w, ws, d_logits, st);
+    if (rc) return rc;
+    const size_t S = (size_t)n_tokens * L->w.top_k;
+    if (d_ids && cudaMemcpyAsync(d_ids, ws.ids, S * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return ceb_set_error(3, "ids copy");
+    if (d_weights && cudaMemcpyAsync(d_weights, ws.wts, S * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return ceb_set_error(3, "weights copy");
+    return 0;
+}
+
 extern "C" int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int n_seqs, int d, int out_dim,
                            float* d_out, void* stream) {
     if (!d_hidden || !d_cu_seqlens || !d_out || n_seqs < 0 || d <= 0) return ceb_set_error(1, "pool_l2: bad arguments");

@@ -43,6 +43,15 @@ size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint
 // caller fuses the combine (the permuted expert outputs stay in ws.down).
 int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
                 const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st);
+// The two halves of ceb_moe_run: ceb_add_ln_route computes out = LN(res + y)
+// and routes the normalised rows in the same pass (ids, wts, block_counts of
+// ws), then ceb_moe_dispatch (scan, scatter, expert GEMMs, optional combine)
+// runs on those routes with x = out32 (x_dtype F32) and x16 = out16.
+int ceb_add_ln_route(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
+                     float* out32, __half* out16, const ceb_moe_weights& mw, const ceb_moe_ws& ws, float* logits_out,
+                     cudaStream_t st);
+int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
+                     const ceb_moe_ws& ws, int32_t* expert_counts, int* dev_err, cudaStream_t st);
 
 // Handle behind the ceb_moe_layer* of include/ceb_ops.h.
 struct ceb_moe_layer {

@@ -11,63 +11,13 @@
 #include "ceb_encoder_internal.h"
 #include "ceb_internal.h"
 #include "common.cuh"
+#include "rowwise.cuh"
 
 namespace {
 
-constexpr int LN_MAXV = 8;  // float4 per lane: d <= 1024
-
-CEB_DEV float wsum(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// LayerNorm of one row held as float4 registers by a warp (lane owns float4
-// i*32+lane).  ggml_norm order: mean, centred values, variance of the centred
-// values, scale = 1/sqrtf(var+eps), then *gamma, +beta as separate roundings.
-CEB_DEV void ln_row_store(float4 (&v)[LN_MAXV], int nv, int d, const float* gamma, const float* beta, float eps,
-                          float* out32, __half* out16, int lane) {
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < LN_MAXV; ++i)
-        if (i < nv) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    const float mean = wsum(s) / (float)d;
-    float s2 = 0.0f;
-#pragma unroll
-    for (int i = 0; i < LN_MAXV; ++i)
-        if (i < nv) {
-            v[i].x = __fsub_rn(v[i].x, mean);
-            v[i].y = __fsub_rn(v[i].y, mean);
-            v[i].z = __fsub_rn(v[i].z, mean);
-            v[i].w = __fsub_rn(v[i].w, mean);
-            s2 += (__fmul_rn(v[i].x, v[i].x) + __fmul_rn(v[i].y, v[i].y)) +
-                  (__fmul_rn(v[i].z, v[i].z) + __fmul_rn(v[i].w, v[i].w));
-        }
-    const float var = wsum(s2) / (float)d;
-    const float scale = 1.0f / sqrtf(var + eps);
-#pragma unroll
-    for (int i = 0; i < LN_MAXV; ++i)
-        if (i < nv) {
-            const int c = (i * 32 + lane) * 4;
-            const float4 g = gamma ? *reinterpret_cast<const float4*>(gamma + c) : make_float4(1.f, 1.f, 1.f, 1.f);
-            const float4 b = beta ? *reinterpret_cast<const float4*>(beta + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            float4 o;
-            o.x = __fadd_rn(__fmul_rn(__fmul_rn(v[i].x, scale), g.x), b.x);
-            o.y = __fadd_rn(__fmul_rn(__fmul_rn(v[i].y, scale), g.y), b.y);
-            o.z = __fadd_rn(__fmul_rn(__fmul_rn(v[i].z, scale), g.z), b.z);
-            o.w = __fadd_rn(__fmul_rn(__fmul_rn(v[i].w, scale), g.w), b.w);
-            if (out32) *reinterpret_cast<float4*>(out32 + c) = o;
-            if (out16) {
-                __half2* h = reinterpret_cast<__half2*>(out16 + c);
-                h[0] = __floats2half2_rn(o.x, o.y);
-                h[1] = __floats2half2_rn(o.z, o.w);
-            }
-        }
-}
-
-CEB_DEV float4 f4add(float4 a, float4 b) {
-    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
-}
+using ceb_row::LN_MAXV;
+using ceb_row::f4add;
+using ceb_row::wsum;
 
 CEB_DEV int find_seq(const int32_t* cu, int n_seqs, int t) {
     int lo = 0, hi = n_seqs - 1;
@@ -114,7 +64,7 @@ __global__ void embed_ln_kernel(const int32_t* __restrict__ ids, const int32_t* 
             v[i] = x;
         }
     if (gamma) {
-        ln_row_store(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
+        ceb_row::ln_row(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
     } else {
 #pragma unroll
         for (int i = 0; i < LN_MAXV; ++i)
@@ -144,7 +94,7 @@ __global__ void add_ln_kernel(const float* res, const float* __restrict__ y, int
                          *reinterpret_cast<const float4*>(y + (size_t)t * d + c));
         }
     __syncwarp();
-    ln_row_store(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
+    ceb_row::ln_row(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
 }
 
 // ffn = sum_j w_j * down[pos_j] (fmaf in slot order) + moe_bias; out = LN(cur + ffn)
@@ -181,7 +131,7 @@ __global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int3
             acc[i] = f4add(*reinterpret_cast<const float4*>(cur + (size_t)t * d + c), acc[i]);
         }
     __syncwarp();
-    ln_row_store(acc, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
+    ceb_row::ln_row(acc, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
 }
 
 // ------------------------------------------------------------------ attention

@@ -397,14 +397,17 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
         a.epi = Ly.o_b ? CEB_EPI_BIAS : 0;
         a.bias = Ly.o_b;
         if ((rc = ceb_gemm_launch(Ly.o, ws.a16, M, a, st))) return rc;
-        if ((rc = ceb_add_ln(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, st))) return rc;
         if (Ly.moe) {
             const ceb_moe_weights& mw = Ly.moew;
-            if ((rc = ceb_moe_run(mw, ws.c32, CEB_ACT_F32, ws.c16, M, nullptr, ws.moe, nullptr, nullptr, d_err, st))) return rc;
+            if ((rc = ceb_add_ln_route(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, mw, ws.moe,
+                                       nullptr, st)))
+                return rc;
+            if ((rc = ceb_moe_dispatch(mw, ws.c32, CEB_ACT_F32, ws.c16, M, nullptr, ws.moe, nullptr, d_err, st))) return rc;
             if ((rc = ceb_moe_combine_ln(ws.moe.down, ws.moe.slot_pos, ws.moe.wts, mw.top_k, mw.bias, ws.c32, M, d,
                                          Ly.ln2_w, Ly.ln2_b, eps, ws.x32, ws.x16, st)))
                 return rc;
         } else {
+            if ((rc = ceb_add_ln(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, st))) return rc;
             a.out = ws.h16;
             a.ldo = Ly.fc1.n_out;
             a.epi = CEB_EPI_F16_OUT | CEB_EPI_GELU | (Ly.fc1_b ? CEB_EPI_BIAS : 0);

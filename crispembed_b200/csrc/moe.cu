@@ -10,7 +10,8 @@
 //   down   = W2[ids] up                 (ggml_mul_mat_id, :1371)
 //   y      = sum_k w_k down_k (+ bias)  (permute + ggml_mul_mat + ggml_add, :1375-1381)
 //
-// Device pipeline: route_kernel (one warp per token) -> scan_kernel (one CTA)
+// Device pipeline: route_rows_kernel (router, optionally fused with the
+// residual + LayerNorm that produces its input) -> scan_kernel (one CTA)
 // -> scatter_kernel (stable counting sort by expert, gathers fp16 rows) ->
 // grouped GEMM fc1 (+GELU) -> grouped GEMM fc2 -> combine_kernel.  The expert
 // row order is (expert, token, slot), the order ggml_mul_mat_id groups rows
@@ -18,19 +19,28 @@
 #include <cstdio>
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 #include "ceb_internal.h"
 #include "ceb_moe_internal.h"
 #include "common.cuh"
+#include "rowwise.cuh"
 
 namespace {
 
-constexpr int ROUTE_WARPS = 16;         // tokens per route CTA = ROUTE_WARPS * TOK_PER_WARP
-constexpr int TOK_PER_WARP = 4;
-constexpr int CHUNK = ROUTE_WARPS * TOK_PER_WARP;  // tokens per histogram block (256)
+using ceb_row::LN_MAXV;
+
+constexpr int CHUNK = 64;                            // tokens per histogram block
+constexpr int RT_WARPS = 8;                          // warps per router CTA
+constexpr int RT_TOK_PER_WARP = CHUNK / RT_WARPS;    // 8
+constexpr int RT_GROUP = 4;                          // tokens a warp routes side by side (lane = token x 8)
+#ifndef CEB_RT_MIN_BLOCKS
+#define CEB_RT_MIN_BLOCKS 4                          // resident router CTAs per SM the register budget aims at
+#endif
+constexpr int RT_MIN_BLOCKS = CEB_RT_MIN_BLOCKS;
 constexpr int MAXE = 64;
-constexpr int MAXD = 1024;  // the router gives each lane one 32-value block
+constexpr int MAXD = 128 * LN_MAXV;  // rows live in registers, 4 values per lane per 128 columns
 
 template <typename T>
 CEB_DEV float ld_act(const T* p, size_t i);
@@ -75,179 +85,344 @@ CEB_DEV float warp_sum(float v) {
 // Router.  Q8_0 router weights reproduce ggml's CPU arithmetic bit for bit:
 // the token row is re-quantized to Q8_0 (amax/127 scale stored as fp16,
 // multiplier 127/amax, round half to even), each 32-block contributes eight
-// 4-product integer partial sums (dp4a) scaled by d_w*d_x with one FMA per lane
-// and block, and the eight lanes are summed as ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)).
-// The Q8_0 weights are staged once per CTA in shared memory (quants padded by
-// 32 B per expert row so the four experts of a pass hit distinct banks).
-// F32 router weights use a plain fp32 dot read through the L1 cache.
-// One warp per token, ROUTE_WARPS warps per CTA, CHUNK tokens per CTA.
+// 4-product integer partial sums (dp4a), partial l accumulates
+// fma(d_w*d_x, (float)isum_l, acc_l) over the blocks in order, and the eight
+// partials are summed as ((a0+a4)+(a2+a6))+((a1+a5)+(a3+a7)).  F32 router
+// weights use a plain fp32 dot.
+//
+// Work layout: a CTA of RT_WARPS warps loops over histogram blocks of CHUNK
+// tokens (persistent grid; the router weights are staged in shared memory
+// once per CTA).  A warp takes RT_GROUP tokens at a time: it brings each row
+// into registers (lane holds 4 values per 128 columns), quantizes it into
+// shared memory, then lane (token tt = lane/8, expert e = lane%8 + 8j) computes
+// all eight partial sums of its (token, expert) pairs from 16-byte shared
+// loads, so the softmax and top-K of the RT_GROUP tokens run side by side in
+// 8-lane groups.  The next row is prefetched into L2 while a row is processed.
 // ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(ROUTE_WARPS * 32)
-    route_kernel(const T* __restrict__ x, int T_tokens, int d, int E, int K, int rtype, const uint8_t* __restrict__ rw,
-                 int32_t* __restrict__ ids, float* __restrict__ wts, float* __restrict__ logits_out,
-                 int32_t* __restrict__ block_counts) {
-    extern __shared__ __align__(16) uint8_t sm[];
-    const int nb = d / 32;
-    const int wpitch = d + 32;
-    int* s_cnt = reinterpret_cast<int*>(sm);                                            // [MAXE]
-    float* s_wd = reinterpret_cast<float*>(sm + MAXE * 4);                              // [E][nb]
-    float* s_xd = s_wd + (size_t)E * nb;                                                // [warps][nb]
-    int8_t* s_wq = reinterpret_cast<int8_t*>(s_xd + (size_t)ROUTE_WARPS * nb);         // [E][wpitch]
-    int8_t* s_xq = s_wq + (size_t)E * wpitch;                                           // [warps][d]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < E; i += blockDim.x) s_cnt[i] = 0;
-    if (rtype == CEB_GGML_Q8_0) {
-        // stage weights: block (e, b) -> scale s_wd[e][b], quants s_wq[e][b*32 .. +31]
-        for (int i = threadIdx.x; i < E * nb; i += blockDim.x) {
-            const uint8_t* blk = rw + (size_t)i * 34;
-            const int e = i / nb, b = i - e * nb;
-            s_wd[i] = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
-            int8_t* dst = s_wq + (size_t)e * wpitch + b * 32;
-#pragma unroll 8
-            for (int j = 0; j < 32; ++j) dst[j] = (int8_t)blk[2 + j];
-        }
-    }
-    __syncthreads();
-    int8_t* q = s_xq + (size_t)warp * d;
-    float* qd = s_xd + (size_t)warp * nb;
+constexpr int RT_MAXJ = 4;  // experts per lane: E <= 8 * RT_MAXJ
 
-    for (int tt = 0; tt < TOK_PER_WARP; ++tt) {
-        const int t = blockIdx.x * CHUNK + warp * TOK_PER_WARP + tt;
-        if (t >= T_tokens) break;
-        const T* xr = x + (size_t)t * d;
-        float lg_mine = -INFINITY;  // lane e < E ends up holding logit e
-        if (rtype == CEB_GGML_Q8_0) {
-            // 128 values per pass, 4 per lane (coalesced); 8 lanes hold one 32-value
-            // block, whose amax three xor-shuffles combine.  Packed quants land in
-            // consecutive shared-memory words.
-            for (int seg = 0; seg < d / 128; ++seg) {
-                const float4 v = ld_act4<T>(xr, (size_t)seg * 128 + 4 * lane);
-                float am = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
-                const float id = am != 0.0f ? 127.0f / am : 0.0f;
-                const uint32_t b0 = (uint32_t)(__float2int_rn(v.x * id) & 0xFF);
-                const uint32_t b1 = (uint32_t)(__float2int_rn(v.y * id) & 0xFF);
-                const uint32_t b2 = (uint32_t)(__float2int_rn(v.z * id) & 0xFF);
-                const uint32_t b3 = (uint32_t)(__float2int_rn(v.w * id) & 0xFF);
-                reinterpret_cast<uint32_t*>(q)[seg * 32 + lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-                if ((lane & 7) == 0) qd[seg * 4 + (lane >> 3)] = __half2float(__float2half_rn(am / 127.0f));
-            }
-            __syncwarp();
-            // lane = (expert-in-pass, partial-lane): 4 experts x 8 lanes per pass
-            for (int e0 = 0; e0 < E; e0 += 4) {
-                const int e = e0 + (lane >> 3), l = lane & 7;
-                float acc = 0.0f;
-                if (e < E) {
-                    const int8_t* wq = s_wq + (size_t)e * wpitch + 4 * l;
-                    const float* wd = s_wd + (size_t)e * nb;
-                    const int8_t* xq = q + 4 * l;
-                    for (int b = 0; b < nb; ++b) {
-                        const int s = __dp4a(*reinterpret_cast<const int*>(wq + b * 32),
-                                             *reinterpret_cast<const int*>(xq + b * 32), 0);
-                        acc = __fmaf_rn(__fmul_rn(wd[b], qd[b]), (float)s, acc);
-                    }
-                }
-                // ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)) within each group of 8 lanes
-                const float p4 = __shfl_xor_sync(0xffffffffu, acc, 4);
-                const float s1 = __fadd_rn(acc, p4);                       // lane l<4: l + (l+4)
-                const float p2 = __shfl_xor_sync(0xffffffffu, s1, 2);
-                const float s2 = __fadd_rn(s1, p2);                        // l=0: (0+4)+(2+6), l=1: (1+5)+(3+7)
-                const float p1 = __shfl_xor_sync(0xffffffffu, s2, 1);
-                const float tot = __fadd_rn(s2, p1);
-                // lane 8j holds expert e0+j; hand it to lane e0+j
-                for (int j = 0; j < 4; ++j) {
-                    const float r = __shfl_sync(0xffffffffu, tot, j * 8);
-                    if (lane == e0 + j) lg_mine = r;
-                }
-            }
-            __syncwarp();
-        } else {
-            for (int e = 0; e < E; ++e) {
-                const float* wr = reinterpret_cast<const float*>(rw) + (size_t)e * d;
-                float acc = 0.0f;
-                for (int i = lane; i < d; i += 32) acc = __fmaf_rn(ld_act<T>(xr, i), __ldg(wr + i), acc);
-                acc = warp_sum(acc);
-                if (lane == e) lg_mine = acc;
-            }
-        }
-        // softmax over lanes 0..E-1 (E <= 32 handled in registers)
-        const float mx = warp_max(lane < E ? lg_mine : -INFINITY);
-        const float ex = lane < E ? expf(lg_mine - mx) : 0.0f;
-        double sum = ex;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        const float p = lane < E ? ex * (float)(1.0 / sum) : -1.0f;
-        if (logits_out && lane < E) logits_out[(size_t)t * E + lane] = lg_mine;
-        // top-K: repeated argmax, ties to the lower expert index
-        bool taken = false;
-        for (int j = 0; j < K; ++j) {
-            float v = (lane < E && !taken) ? p : -2.0f;
-            int idx = lane;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-                if (ov > v || (ov == v && oi < idx)) {
-                    v = ov;
-                    idx = oi;
-                }
-            }
-            if (lane == idx) taken = true;
-            if (lane == 0) {
-                ids[(size_t)t * K + j] = idx;
-                wts[(size_t)t * K + j] = v;
-                atomicAdd(&s_cnt[idx], 1);
-            }
-        }
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < E; i += blockDim.x) block_counts[(size_t)blockIdx.x * E + i] = s_cnt[i];
+struct RouteSmem {
+    int* cnt;     // [MAXE] expert histogram of the current block
+    float* wd;    // [nb][E] router block scales
+    float* xd;    // [warps][RT_GROUP][nb] activation block scales
+    int8_t* wq;   // [E][d + 16] router quants (row pitch spreads 8 experts over the 32 banks)
+    int8_t* xq;   // [warps][RT_GROUP][d] activation quants
+    int nb, wpitch;
+};
+
+__host__ __device__ inline size_t route_smem_bytes(int d, int E) {
+    const int nb = d / 32;
+    return MAXE * 4 + (size_t)nb * E * 4 + (size_t)RT_WARPS * RT_GROUP * nb * 4 + (size_t)E * (d + 16) +
+           (size_t)RT_WARPS * RT_GROUP * d;
 }
 
-// One CTA: expert offsets (exclusive scan of the totals) and, per histogram
-// block, the first output row of each expert.  The per-block counts are staged
-// in shared memory first (coalesced), then each expert's thread walks them.
-constexpr int SCAN_MAX_SMEM_INTS = 48 * 1024 / 4;
+CEB_DEV RouteSmem route_carve(uint8_t* sm, int d, int E) {
+    RouteSmem s;
+    s.nb = d / 32;
+    s.wpitch = d + 16;
+    s.cnt = reinterpret_cast<int*>(sm);
+    s.wd = reinterpret_cast<float*>(sm + MAXE * 4);
+    s.xd = s.wd + (size_t)s.nb * E;
+    s.wq = reinterpret_cast<int8_t*>(s.xd + (size_t)RT_WARPS * RT_GROUP * s.nb);
+    s.xq = s.wq + (size_t)E * s.wpitch;
+    return s;
+}
 
-__global__ void __launch_bounds__(256) scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E,
-                                                   int32_t* __restrict__ block_base, int32_t* __restrict__ offsets,
-                                                   int32_t* __restrict__ expert_counts) {
-    extern __shared__ int sc[];  // [nblk*E] counts (when they fit), then [E] totals
-    const int n = nblk * E;
-    const bool staged = n <= SCAN_MAX_SMEM_INTS - MAXE;
-    int* tot = staged ? sc + n : sc;
-    if (staged)
-        for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = block_counts[i];
-    __syncthreads();
-    const int e = threadIdx.x;
-    if (e < E) {
-        int s = 0;
-        if (staged)
-            for (int b = 0; b < nblk; ++b) s += sc[b * E + e];
-        else
-            for (int b = 0; b < nblk; ++b) s += block_counts[(size_t)b * E + e];
-        tot[e] = s;
-        if (expert_counts) expert_counts[e] = s;
+// Q8_0 router weights to shared memory: block (e, b) -> scale wd[b][e], quants
+// wq[e][b*32 .. +31]; one thread per 4 quants (the 34-byte ggml blocks leave
+// them 2-byte aligned).  Ends with __syncthreads().
+CEB_DEV void route_stage(const RouteSmem& s, int E, int rtype, const uint8_t* __restrict__ rw) {
+    if (rtype == CEB_GGML_Q8_0) {
+        for (int i = threadIdx.x; i < E * s.nb * 8; i += blockDim.x) {
+            const int blk_i = i >> 3, j = i & 7;
+            const int e = blk_i / s.nb, b = blk_i - e * s.nb;
+            const uint16_t* blk = reinterpret_cast<const uint16_t*>(rw + (size_t)blk_i * 34);
+            if (j == 0) s.wd[b * E + e] = __half2float(__ushort_as_half(__ldg(blk)));
+            const uint32_t q = (uint32_t)__ldg(blk + 1 + 2 * j) | ((uint32_t)__ldg(blk + 2 + 2 * j) << 16);
+            *reinterpret_cast<uint32_t*>(s.wq + (size_t)e * s.wpitch + b * 32 + 4 * j) = q;
+        }
     }
     __syncthreads();
-    if (e < E) {
+}
+
+CEB_DEV void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+// Row sources: where a token's row comes from before it is routed.
+template <typename T, int NV>
+struct ActRows {  // the activations, already in memory
+    const T* x;
+    CEB_DEV void prefetch(int t, int lane) const {
+        constexpr int LINES = NV * 128 * (int)sizeof(T) / 128;
+        const char* r = reinterpret_cast<const char*>(x + (size_t)t * NV * 128);
+        for (int i = lane; i < LINES; i += 32) prefetch_l2(r + (size_t)i * 128);
+    }
+    CEB_DEV void row(int t, float4 (&v)[NV], int lane) const {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) v[i] = ld_act4<T>(x + (size_t)t * NV * 128, (size_t)(i * 32 + lane) * 4);
+    }
+};
+
+template <int NV>
+struct AddLnRows {  // out = LN(res + y), stored, and routed from the registers
+    const float* res;
+    const float* y;
+    const float* gamma;
+    const float* beta;
+    float eps;
+    float* out32;
+    __half* out16;
+    CEB_DEV void prefetch(int t, int lane) const {
+        constexpr int LINES = NV * 4;  // 128-byte lines per fp32 row
+        for (int i = lane; i < 2 * LINES; i += 32) {
+            const float* base = i < LINES ? res : y;
+            prefetch_l2(base + (size_t)t * NV * 128 + (size_t)(i < LINES ? i : i - LINES) * 32);
+        }
+    }
+    CEB_DEV void row(int t, float4 (&v)[NV], int lane) const {
+        constexpr int d = NV * 128;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const size_t c = (size_t)t * d + (i * 32 + lane) * 4;
+            v[i] = ceb_row::f4add(*reinterpret_cast<const float4*>(res + c), __ldg(reinterpret_cast<const float4*>(y + c)));
+        }
+        ceb_row::ln_row(v, NV, d, gamma, beta, eps, out32 + (size_t)t * d, out16 ? out16 + (size_t)t * d : nullptr, lane);
+    }
+};
+
+// Q8_0 quants and block scales of one row held in registers.  8 lanes hold one
+// 32-value block, whose amax three xor-shuffles combine.
+template <int NV>
+CEB_DEV void quantize_row(const float4 (&v)[NV], int8_t* q, float* qd, int lane) {
+#pragma unroll
+    for (int seg = 0; seg < NV; ++seg) {
+        const float4 x = v[seg];
+        float am = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+        const float id = am != 0.0f ? 127.0f / am : 0.0f;
+        const uint32_t b0 = (uint32_t)(__float2int_rn(x.x * id) & 0xFF);
+        const uint32_t b1 = (uint32_t)(__float2int_rn(x.y * id) & 0xFF);
+        const uint32_t b2 = (uint32_t)(__float2int_rn(x.z * id) & 0xFF);
+        const uint32_t b3 = (uint32_t)(__float2int_rn(x.w * id) & 0xFF);
+        reinterpret_cast<uint32_t*>(q)[seg * 32 + lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        if ((lane & 7) == 0) qd[seg * 4 + (lane >> 3)] = __half2float(__float2half_rn(am / 127.0f));
+    }
+}
+
+// F32 router: logits of one row (all experts) by warp dots; lane (tt, el)
+// keeps expert el + 8j of token tt in lgv[j].
+template <int NV>
+CEB_DEV void f32_logits(const float4 (&v)[NV], const float* __restrict__ wf, int E, int lane, int tt,
+                        float (&lgv)[RT_MAXJ]) {
+    constexpr int d = NV * 128;
+#pragma unroll
+    for (int j = 0; j < RT_MAXJ; ++j) {
+        for (int el = 0; el < 8; ++el) {
+            const int e = 8 * j + el;
+            if (e >= E) break;
+            const float* wr = wf + (size_t)e * d;
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const float4 w = __ldg(reinterpret_cast<const float4*>(wr + (i * 32 + lane) * 4));
+                acc = __fmaf_rn(v[i].x, w.x, acc);
+                acc = __fmaf_rn(v[i].y, w.y, acc);
+                acc = __fmaf_rn(v[i].z, w.z, acc);
+                acc = __fmaf_rn(v[i].w, w.w, acc);
+            }
+            acc = warp_sum(acc);
+            if ((lane >> 3) == tt && (lane & 7) == el) lgv[j] = acc;
+        }
+    }
+}
+
+// Q8_0 router: lane (tt, el) computes the logits of experts el + 8j for token
+// tt of the group from the quantized row in shared memory.
+template <int NV>
+CEB_DEV void q8_logits(const RouteSmem& s, const int8_t* xrow, const float* xd, int E, int el,
+                       float (&lgv)[RT_MAXJ]) {
+    constexpr int nb = NV * 4;
+#pragma unroll
+    for (int j = 0; j < RT_MAXJ; ++j) {
+        const int e = el + 8 * j;
+        if (e >= E) break;
+        const int8_t* wrow = s.wq + (size_t)e * s.wpitch;
+        float a[8];
+#pragma unroll
+        for (int l = 0; l < 8; ++l) a[l] = 0.0f;
+#pragma unroll 2
+        for (int b = 0; b < nb; ++b) {
+            const int4 w0 = *reinterpret_cast<const int4*>(wrow + b * 32);
+            const int4 w1 = *reinterpret_cast<const int4*>(wrow + b * 32 + 16);
+            const int4 x0 = *reinterpret_cast<const int4*>(xrow + b * 32);
+            const int4 x1 = *reinterpret_cast<const int4*>(xrow + b * 32 + 16);
+            const float sc = __fmul_rn(s.wd[b * E + e], xd[b]);
+            a[0] = __fmaf_rn(sc, (float)__dp4a(w0.x, x0.x, 0), a[0]);
+            a[1] = __fmaf_rn(sc, (float)__dp4a(w0.y, x0.y, 0), a[1]);
+            a[2] = __fmaf_rn(sc, (float)__dp4a(w0.z, x0.z, 0), a[2]);
+            a[3] = __fmaf_rn(sc, (float)__dp4a(w0.w, x0.w, 0), a[3]);
+            a[4] = __fmaf_rn(sc, (float)__dp4a(w1.x, x1.x, 0), a[4]);
+            a[5] = __fmaf_rn(sc, (float)__dp4a(w1.y, x1.y, 0), a[5]);
+            a[6] = __fmaf_rn(sc, (float)__dp4a(w1.z, x1.z, 0), a[6]);
+            a[7] = __fmaf_rn(sc, (float)__dp4a(w1.w, x1.w, 0), a[7]);
+        }
+        lgv[j] = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[2], a[6])),
+                           __fadd_rn(__fadd_rn(a[1], a[5]), __fadd_rn(a[3], a[7])));
+    }
+}
+
+// Softmax over the E logits of each 8-lane group's token, then top-K by repeated
+// argmax (ties to the lower expert index); weights are the probabilities, not
+// renormalised.  All lanes take part (shuffles); `valid` gates the stores.
+CEB_DEV void group_route(const float (&lgv)[RT_MAXJ], int E, int K, bool valid, size_t t, int el,
+                         int32_t* __restrict__ ids, float* __restrict__ wts, float* __restrict__ logits_out,
+                         int* cnt) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < RT_MAXJ; ++j)
+        if (el + 8 * j < E) mx = fmaxf(mx, lgv[j]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    float ex[RT_MAXJ];
+    double sum = 0.0;
+#pragma unroll
+    for (int j = 0; j < RT_MAXJ; ++j) {
+        ex[j] = el + 8 * j < E ? expf(lgv[j] - mx) : 0.0f;
+        sum += ex[j];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    const float inv = (float)(1.0 / sum);
+    if (logits_out && valid) {
+#pragma unroll
+        for (int j = 0; j < RT_MAXJ; ++j)
+            if (el + 8 * j < E) logits_out[t * E + el + 8 * j] = lgv[j];
+    }
+    unsigned taken = 0;
+    for (int k = 0; k < K; ++k) {
+        float bv = -2.0f;
+        int bi = 1 << 20;
+#pragma unroll
+        for (int j = 0; j < RT_MAXJ; ++j) {
+            const float p = ex[j] * inv;
+            if (el + 8 * j < E && !((taken >> j) & 1u) && p > bv) {
+                bv = p;
+                bi = el + 8 * j;
+            }
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 7) == el) taken |= 1u << (bi >> 3);
+        if (el == 0 && valid) {
+            ids[t * K + k] = bi;
+            wts[t * K + k] = bv;
+            atomicAdd(&cnt[bi], 1);
+        }
+    }
+}
+
+// The router over histogram blocks [blockIdx.x, nblk) step gridDim.x; rows come
+// from `rows` (activations in memory, or the fused residual + LayerNorm).
+template <int NV, class Rows>
+__global__ void __launch_bounds__(RT_WARPS * 32, RT_MIN_BLOCKS)
+    route_rows_kernel(Rows rows, int T_tokens, int nblk, int E, int K, int rtype, const uint8_t* __restrict__ rw,
+                      int32_t* __restrict__ ids, float* __restrict__ wts, float* __restrict__ logits_out,
+                      int32_t* __restrict__ block_counts) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    constexpr int d = NV * 128;
+    const RouteSmem s = route_carve(sm, d, E);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tt_l = lane >> 3, el = lane & 7;
+    route_stage(s, E, rtype, rw);
+    int8_t* xq = s.xq + (size_t)warp * RT_GROUP * d;
+    float* xd = s.xd + (size_t)warp * RT_GROUP * s.nb;
+    for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+        for (int i = threadIdx.x; i < E; i += blockDim.x) s.cnt[i] = 0;
+        __syncthreads();
+        const int t_base = blk * CHUNK + warp * RT_TOK_PER_WARP;
+        if (t_base < T_tokens) rows.prefetch(t_base, lane);
+        for (int g = 0; g < RT_TOK_PER_WARP; g += RT_GROUP) {
+            float lgv[RT_MAXJ];
+#pragma unroll
+            for (int j = 0; j < RT_MAXJ; ++j) lgv[j] = -INFINITY;
+            for (int tt = 0; tt < RT_GROUP; ++tt) {
+                const int t = t_base + g + tt;
+                if (t >= T_tokens) break;
+                if (g + tt + 1 < RT_TOK_PER_WARP && t + 1 < T_tokens) rows.prefetch(t + 1, lane);
+                float4 v[NV];
+                rows.row(t, v, lane);
+                if (rtype == CEB_GGML_Q8_0)
+                    quantize_row<NV>(v, xq + (size_t)tt * d, xd + tt * s.nb, lane);
+                else
+                    f32_logits<NV>(v, reinterpret_cast<const float*>(rw), E, lane, tt, lgv);
+            }
+            __syncwarp();
+            const int t_mine = t_base + g + tt_l;
+            const bool valid = t_mine < T_tokens;
+            if (rtype == CEB_GGML_Q8_0 && valid) q8_logits<NV>(s, xq + (size_t)tt_l * d, xd + tt_l * s.nb, E, el, lgv);
+            __syncwarp();
+            group_route(lgv, E, K, valid, (size_t)t_mine, el, ids, wts, logits_out, s.cnt);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < E; i += blockDim.x) block_counts[(size_t)blk * E + i] = s.cnt[i];
+        __syncthreads();
+    }
+}
+
+// Expert offsets (exclusive scan of the totals) and, per histogram block, the
+// first output row of each expert.  One warp per expert; lane l owns a run of
+// consecutive blocks, so the block order is a warp scan of the lanes' sums.
+__global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E,
+                                                    int32_t* __restrict__ block_base, int32_t* __restrict__ offsets,
+                                                    int32_t* __restrict__ expert_counts) {
+    __shared__ int tot[MAXE];
+    __shared__ int lane_base[MAXE][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const int per = (nblk + 31) / 32;
+    const int b0 = min(nblk, lane * per), b1 = min(nblk, b0 + per);
+    for (int e = warp; e < E; e += nwarps) {
+        int s = 0;
+        for (int b = b0; b < b1; ++b) s += block_counts[(size_t)b * E + e];
+        int incl = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
+        lane_base[e][lane] = incl - s;
+        if (lane == 31) tot[e] = incl;
+    }
+    __syncthreads();
+    for (int e = warp; e < E; e += nwarps) {
         int base = 0;
         for (int i = 0; i < e; ++i) base += tot[i];
-        if (e == 0) offsets[0] = 0;
-        offsets[e + 1] = base + tot[e];
-        for (int b = 0; b < nblk; ++b) {
-            block_base[(size_t)b * E + e] = base;
-            base += staged ? sc[b * E + e] : block_counts[(size_t)b * E + e];
+        if (lane == 0) {
+            if (e == 0) offsets[0] = 0;
+            offsets[e + 1] = base + tot[e];
+            if (expert_counts) expert_counts[e] = tot[e];
+        }
+        int run = base + lane_base[e][lane];
+        for (int b = b0; b < b1; ++b) {
+            block_base[(size_t)b * E + e] = run;
+            run += block_counts[(size_t)b * E + e];
         }
     }
 }
 
 // Stable placement of every (token, slot) into its expert's row range, then a
 // gather of the token rows (converted to fp16) into the permuted activation
-// matrix consumed by fc1.
+// matrix consumed by fc1: one warp per token reads the row once and writes it
+// to each of the token's K rows.
 template <typename T>
 __global__ void __launch_bounds__(256)
     scatter_kernel(const T* __restrict__ x, const __half* __restrict__ x16, int T_tokens, int d, int E, int K,
@@ -286,22 +461,29 @@ __global__ void __launch_bounds__(256)
         }
     }
     __syncthreads();
-    // gather rows: one warp per slot.  With an fp16 copy of x available the rows
-    // move as 16-byte vectors; otherwise they are converted on the fly.
-    for (int s = warp; s < n_slots; s += blockDim.x / 32) {
-        const int pos = s_pos[s];
-        if (pos < 0) continue;
-        __half* dst = x_perm + (size_t)pos * d;
-        if (x16) {
-            const uint4* src = reinterpret_cast<const uint4*>(x16 + (size_t)(t0 + s / K) * d);
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-            for (int c = lane; c < d / 8; c += 32) d4[c] = __ldg(src + c);
-        } else {
-            const T* src = x + (size_t)(t0 + s / K) * d;
-            for (int c = lane * 2; c < d; c += 64) {
-                const float a = ld_act<T>(src, c), b = ld_act<T>(src, c + 1);
-                *reinterpret_cast<__half2*>(dst + c) = __floats2half2_rn(a, b);
+    const int nv = d / 128;
+    for (int tl = warp; tl < n_tok; tl += blockDim.x / 32) {
+        const size_t t = (size_t)(t0 + tl);
+        uint2 r[LN_MAXV];  // 4 fp16 values per lane per 128-column segment
+#pragma unroll
+        for (int i = 0; i < LN_MAXV; ++i)
+            if (i < nv) {
+                const size_t c = (size_t)(i * 32 + lane) * 4;
+                if (x16) {
+                    r[i] = __ldg(reinterpret_cast<const uint2*>(x16 + t * d + c));
+                } else {
+                    const float4 f = ld_act4<T>(x + t * d, c);
+                    const __half2 lo = __floats2half2_rn(f.x, f.y), hi = __floats2half2_rn(f.z, f.w);
+                    r[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+                }
             }
+        for (int j = 0; j < K; ++j) {
+            const int pos = s_pos[tl * K + j];
+            if (pos < 0) continue;
+            __half* dst = x_perm + (size_t)pos * d;
+#pragma unroll
+            for (int i = 0; i < LN_MAXV; ++i)
+                if (i < nv) *reinterpret_cast<uint2*>(dst + (i * 32 + lane) * 4) = r[i];
         }
     }
 }
@@ -351,38 +533,78 @@ size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint
     return off;
 }
 
-int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
-                const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st) {
+namespace {
+
+int moe_shape_check(const ceb_moe_weights& mw) {
     const int d = mw.d, E = mw.n_experts, K = mw.top_k, F = mw.ffn;
-    if (T <= 0) return 0;
     if (E > 32 || E < 1 || K < 1 || K > E || K > 4 || d > MAXD || F % 128 || d % 128)
         return ceb_set_error(2, "moe: unsupported shape d=%d E=%d K=%d F=%d", d, E, K, F);
+    return 0;
+}
+
+// One launch of route_rows_kernel: a persistent grid of (resident CTAs per SM) x SMs.
+template <int NV, class Rows>
+int launch_route_rows(const Rows& rows, int T, int E, int K, int rtype, const uint8_t* rw, const ceb_moe_ws& ws,
+                      float* logits_out, cudaStream_t st) {
+    auto kern = route_rows_kernel<NV, Rows>;
+    const size_t smem = route_smem_bytes(NV * 128, E);
+    static int occ = 0;
+    static size_t occ_smem = 0;
+    if (!occ || occ_smem != smem) {
+        CEB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        int n = 0;
+        CEB_CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, RT_WARPS * 32, smem));
+        occ = std::max(n, 1);
+        occ_smem = smem;
+    }
     const int nblk = (T + CHUNK - 1) / CHUNK;
-    const size_t route_smem = MAXE * 4 + (size_t)(E + ROUTE_WARPS) * (d / 32) * 4 + (size_t)E * (d + 32) +
-                              (size_t)ROUTE_WARPS * d;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(route_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-        cudaFuncSetAttribute(route_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-        cudaFuncSetAttribute(route_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-        attr = true;
-    }
-    if (x_dtype == CEB_ACT_F32) {
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, route_kernel<float><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>((const float*)x, T, d, E, K, mw.router_type,
-                                                                        mw.router, ws.ids, ws.wts, logits_out,
-                                                                        ws.block_counts));
-    } else if (x_dtype == CEB_ACT_BF16) {
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, route_kernel<__nv_bfloat16><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>(
-            (const __nv_bfloat16*)x, T, d, E, K, mw.router_type, mw.router, ws.ids, ws.wts, logits_out,
-            ws.block_counts));
-    } else {
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, route_kernel<__half><<<nblk, ROUTE_WARPS * 32, route_smem, st>>>((const __half*)x, T, d, E, K, mw.router_type,
-                                                                         mw.router, ws.ids, ws.wts, logits_out,
-                                                                         ws.block_counts));
-    }
+    const int grid = std::min(nblk, occ * ceb_num_sms());
+    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+               kern<<<grid, RT_WARPS * 32, smem, st>>>(rows, T, nblk, E, K, rtype, rw, ws.ids, ws.wts, logits_out,
+                                                       ws.block_counts));
     CEB_CUDA_OK(cudaGetLastError());
-    const size_t scan_smem = (size_t)std::min(nblk * E + MAXE, SCAN_MAX_SMEM_INTS) * sizeof(int);
-    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scan_kernel<<<1, 256, scan_smem, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts));
+    return 0;
+}
+
+// Calls f(std::integral_constant<int, d / 128>) for the supported widths.
+template <class F>
+int with_nv(int d, F&& f) {
+    switch (d / 128) {
+        case 1: return f(std::integral_constant<int, 1>{});
+        case 2: return f(std::integral_constant<int, 2>{});
+        case 3: return f(std::integral_constant<int, 3>{});
+        case 4: return f(std::integral_constant<int, 4>{});
+        case 5: return f(std::integral_constant<int, 5>{});
+        case 6: return f(std::integral_constant<int, 6>{});
+        case 7: return f(std::integral_constant<int, 7>{});
+        case 8: return f(std::integral_constant<int, 8>{});
+        default: return ceb_set_error(2, "moe: d=%d unsupported", d);
+    }
+}
+
+}  // namespace
+
+int ceb_add_ln_route(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
+                     float* out32, __half* out16, const ceb_moe_weights& mw, const ceb_moe_ws& ws, float* logits_out,
+                     cudaStream_t st) {
+    if (int rc = moe_shape_check(mw)) return rc;
+    if (d != mw.d) return ceb_set_error(2, "add_ln_route: d=%d but the MoE block has d=%d", d, mw.d);
+    if (M <= 0) return 0;
+    return with_nv(d, [&](auto nvc) {
+        constexpr int NV = decltype(nvc)::value;
+        const AddLnRows<NV> rows{res, y, gamma, beta, eps, out32, out16};
+        return launch_route_rows<NV>(rows, M, mw.n_experts, mw.top_k, mw.router_type, mw.router, ws, logits_out, st);
+    });
+}
+
+int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
+                     const ceb_moe_ws& ws, int32_t* expert_counts, int* dev_err, cudaStream_t st) {
+    if (int rc = moe_shape_check(mw)) return rc;
+    const int d = mw.d, E = mw.n_experts, K = mw.top_k, F = mw.ffn;
+    if (T <= 0) return 0;
+    const int nblk = (T + CHUNK - 1) / CHUNK;
+    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+               scan_kernel<<<1, 32 * E, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts));
     CEB_CUDA_OK(cudaGetLastError());
     if (x_dtype == CEB_ACT_F32)
         CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<float><<<nblk, 256, 0, st>>>((const float*)x, x16, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
@@ -419,4 +641,24 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __h
         CEB_CUDA_OK(cudaGetLastError());
     }
     return 0;
+}
+
+int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
+                const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st) {
+    if (int rc = moe_shape_check(mw)) return rc;
+    const int d = mw.d, E = mw.n_experts, K = mw.top_k;
+    if (T <= 0) return 0;
+    int rc = with_nv(d, [&](auto nvc) {
+        constexpr int NV = decltype(nvc)::value;
+        if (x_dtype == CEB_ACT_F32)
+            return launch_route_rows<NV>(ActRows<float, NV>{(const float*)x}, T, E, K, mw.router_type, mw.router, ws,
+                                         logits_out, st);
+        if (x_dtype == CEB_ACT_BF16)
+            return launch_route_rows<NV>(ActRows<__nv_bfloat16, NV>{(const __nv_bfloat16*)x}, T, E, K,
+                                         mw.router_type, mw.router, ws, logits_out, st);
+        return launch_route_rows<NV>(ActRows<__half, NV>{(const __half*)x}, T, E, K, mw.router_type, mw.router, ws,
+                                     logits_out, st);
+    });
+    if (rc) return rc;
+    return ceb_moe_dispatch(mw, x, x_dtype, x16, T, y, ws, expert_counts, dev_err, st);
 }

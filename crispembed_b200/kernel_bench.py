@@ -2,6 +2,7 @@
 
     python -m crispembed_b200.kernel_bench gemm --type q8_0 --m 16384 --n 3072 --k 768 [--gelu] [--f16-out]
     python -m crispembed_b200.kernel_bench moe --T 65536 --type q4_k --zipf 1.2
+    python -m crispembed_b200.kernel_bench route_ln --T 70825 --router-type q8_0
 
 Used for the roofline numbers of single kernels and as the command that ncu
 captures (small cases: a few launches, a few GB at most).  Prints one JSON line.
@@ -87,6 +88,46 @@ def bench_moe(a):
             "breakdown_ms": {k: v["ms"] / a.iters for k, v in prof.items()}}
 
 
+def bench_route_ln(a):
+    """ceb_moe_route_ln over T rows: residual + LayerNorm + router in one pass.
+    Algorithmic bytes: res and y read (fp32), out written in fp32 and fp16."""
+    import numpy as np
+    import torch
+
+    from . import binding, synth
+    inp = synth.make_moe_op_inputs(256, d=a.d, n_experts=a.E, top_k=a.topk, ffn=a.F, wtype=TYPES[a.type],
+                                   router_wtype=TYPES[a.router_type], zipf_s=None, seed=0)
+    layer = binding.MoELayer(inp.d, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
+                             inp.fc1_raw, inp.fc2_raw, inp.bias)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    res = torch.randn((a.T, a.d), device="cuda", generator=g)
+    y = torch.randn((a.T, a.d), device="cuda", generator=g)
+    gamma = torch.ones(a.d, device="cuda")
+    beta = torch.zeros(a.d, device="cuda")
+    out = torch.empty_like(res)
+    out16 = torch.empty((a.T, a.d), dtype=torch.float16, device="cuda")
+    ws = torch.empty(layer.workspace_size(a.T), dtype=torch.uint8, device="cuda")
+    run = lambda: layer.route_ln(res, y, out, ws, gamma=gamma, beta=beta, eps=1e-12, out16=out16)  # noqa: E731
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    ms_all = []
+    for _ in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        ms_all.append(e0.elapsed_time(e1))
+    layer.close()
+    ms = float(np.median(ms_all))
+    nbytes = a.T * a.d * (4 + 4 + 4 + 2)
+    peaks, src = _peaks()
+    pk = peaks["hbm_gbs"]
+    return {"kernel": "moe_route_ln", "T": a.T, "d": a.d, "E": a.E, "router_type": a.router_type, "ms": ms,
+            "gbs": nbytes / (ms / 1e3) / 1e9, "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / pk, "peak_source": src}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -112,8 +153,18 @@ def main(argv=None):
     m.add_argument("--iters", type=int, default=10)
     m.add_argument("--f32-input", action="store_true")
     m.add_argument("--warmup", type=int, default=3)
+    r = sub.add_parser("route_ln")
+    r.add_argument("--T", type=int, default=70825)
+    r.add_argument("--d", type=int, default=768)
+    r.add_argument("--E", type=int, default=8)
+    r.add_argument("--topk", type=int, default=2)
+    r.add_argument("--F", type=int, default=256)
+    r.add_argument("--type", default="q8_0", choices=list(TYPES))
+    r.add_argument("--router-type", default="q8_0", choices=["f32", "q8_0"])
+    r.add_argument("--iters", type=int, default=20)
+    r.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
-    r = bench_gemm(a) if a.what == "gemm" else bench_moe(a)
+    r = {"gemm": bench_gemm, "moe": bench_moe, "route_ln": bench_route_ln}[a.what](a)
     print(json.dumps(r), flush=True)
     return 0
 

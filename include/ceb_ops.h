@@ -76,6 +76,23 @@ CEB_API int ceb_moe_ffn(const ceb_moe_layer* layer, const void* d_x, int x_dtype
                         size_t workspace_bytes, void* stream);
 
 /*
+ * The residual + LayerNorm that feeds the MoE block and the block's router in
+ * one pass (src/crispembed.cpp:1316-1323 post-attention LN, then :1333-1345
+ * router, softmax, top_k, gate weights): d_out = LN(d_res + d_y) * gamma + beta
+ * (ggml_norm, then separate *gamma and +beta roundings; gamma/beta may be NULL),
+ * and the expert choice of every normalised row computed from the registers
+ * that hold it, so the router never re-reads the activations.
+ * d_res, d_y, d_out: [n_tokens x d] floats (d_out may alias d_res).  d_out16:
+ * optional fp16 copy of d_out.  d_ids / d_weights / d_logits as in ceb_moe_ffn
+ * (optional).  d_workspace as for ceb_moe_ffn; its routing part keeps the
+ * routes.  The encoder uses this form in front of every MoE block.
+ */
+CEB_API int ceb_moe_route_ln(const ceb_moe_layer* layer, const float* d_res, const float* d_y, int n_tokens,
+                             const float* d_gamma, const float* d_beta, float eps, float* d_out, void* d_out16,
+                             int32_t* d_ids, float* d_weights, float* d_logits, void* d_workspace,
+                             size_t workspace_bytes, void* stream);
+
+/*
  * ceb_moe_ffn without any device allocation (no counterpart in the reference).
  *
  * For callers that must not allocate device memory once running -- a host whose

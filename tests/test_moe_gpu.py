@@ -113,3 +113,58 @@ def test_moe_input_dtypes(cuda, oracle, dtype):
     # x holds bf16-representable values, exactly representable in f32 and (at this range) f16
     assert np.array_equal(ids, idsb)
     assert np.abs(y - yb).max() <= 1e-6 * max(1.0, np.abs(yb).max())
+
+
+@pytest.mark.parametrize("name", ["q8_small", "c3_q8router", "c3_zipf", "c5_wide", "one_token", "skew_empty"])
+def test_route_ln_matches_oracle(cuda, oracle, name):
+    """ceb_moe_route_ln: LN(res + y) and the router on the normalised rows, one pass.
+
+    The normalised rows match the oracle's LayerNorm to rounding; the router
+    logits are then bit-identical (Q8_0) to the oracle's router applied to the
+    kernel's own normalised rows, and the routes follow from them as in
+    ceb_moe_ffn.  The fp16 copy is the rounding of the fp32 rows; an aliased
+    output (out = res) gives the same results."""
+    import torch
+    from crispembed_b200 import binding
+    cfg = dict(CONFIGS[name])
+    T = cfg.pop("T")
+    inp = synth.make_moe_op_inputs(T, seed=13, **cfg)
+    d, E, K = inp.d, inp.n_experts, inp.top_k
+    rng = np.random.default_rng(7)
+    res = rng.standard_normal((T, d)).astype(np.float32)
+    yv = (rng.standard_normal((T, d)) * 0.5).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    beta = (0.05 * rng.standard_normal(d)).astype(np.float32)
+    eps = 1e-12
+    layer = binding.MoELayer(d, E, K, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype, inp.fc1_raw, inp.fc2_raw,
+                             inp.bias)
+    dev = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    ws = torch.empty(layer.workspace_size(T), dtype=torch.uint8, device=cuda)
+    out = torch.empty((T, d), dtype=torch.float32, device=cuda)
+    out16 = torch.empty((T, d), dtype=torch.float16, device=cuda)
+    ids = torch.empty((T, K), dtype=torch.int32, device=cuda)
+    w = torch.empty((T, K), dtype=torch.float32, device=cuda)
+    lg = torch.empty((T, E), dtype=torch.float32, device=cuda)
+    layer.route_ln(dev(res), dev(yv), out, ws, gamma=dev(gamma), beta=dev(beta), eps=eps, out16=out16, ids=ids,
+                   weights=w, logits=lg)
+    binding.sync_check()
+    o, o16, ids_, w_, lg_ = (t.cpu().numpy() for t in (out, out16, ids, w, lg))
+    ref_ln = oracle.layernorm(res + yv, gamma, beta, eps)
+    assert np.allclose(o, ref_ln, rtol=1e-5, atol=2e-5), np.abs(o - ref_ln).max()
+    assert np.array_equal(o16, o.astype(np.float16))
+    _, _, _, rlg = oracle.moe_ffn(o, E, K, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype, inp.fc1_raw,
+                                  inp.fc2_raw, inp.bias, oracle.GGML)
+    if inp.router_wtype == GGML_Q8_0:
+        assert np.array_equal(lg_, rlg), np.abs(lg_ - rlg).max()
+    else:
+        assert np.allclose(lg_, rlg, rtol=1e-5, atol=1e-5)
+    rids, rw, _ = oracle.route(rlg, K)
+    sure = _kth_gap(rlg, K) > 1e-4
+    assert np.array_equal(ids_[sure], rids[sure])
+    assert np.allclose(w_[sure], rw[sure], rtol=1e-5, atol=1e-7)
+    # in place: out aliases res
+    alias = dev(res)
+    layer.route_ln(alias, dev(yv), alias, ws, gamma=dev(gamma), beta=dev(beta), eps=eps)
+    binding.sync_check()
+    assert np.array_equal(alias.cpu().numpy(), o)
+    layer.close()
