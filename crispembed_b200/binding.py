@@ -72,6 +72,13 @@ def load_library(path: Optional[str] = None):
         "ceb_moe_ffn": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp, ctypes.c_size_t, vp],
                         ctypes.c_int),
         "ceb_moe_ffn_static": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_ep_create": ([ctypes.c_int] * 7, vp),
+        "ceb_ep_ipc_handle": ([vp, vp], ctypes.c_int),
+        "ceb_ep_connect": ([vp, vp], ctypes.c_int),
+        "ceb_ep_set_timeout_ms": ([vp, ctypes.c_int], None),
+        "ceb_ep_free": ([vp], None),
+        "ceb_ep_attach": ([vp, vp], ctypes.c_int),
+        "ceb_moe_ffn_ep": ([vp, vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, ctypes.c_size_t, vp], ctypes.c_int),
         "ceb_moe_route_ln": ([vp, vp, vp, ctypes.c_int, vp, vp, ctypes.c_float, vp, vp, vp, vp, vp, vp,
                               ctypes.c_size_t, vp], ctypes.c_int),
         "ceb_pool_l2": ([vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
@@ -206,6 +213,11 @@ class CrispEmbed:
     def tokenizer_kind(self) -> int:
         return self._lib.crispembed_tokenizer_kind(self._ctx)
 
+    def attach_ep(self, ep: "ExpertParallel"):
+        """Route every MoE block through `ep` (this context keeps only ep's experts)."""
+        _check(self._lib.ceb_ep_attach(self._ctx, ep._h), "ceb_ep_attach")
+        self._ep = ep  # the exchange must outlive the context's use of it
+
     def encode_ids(self, ids: np.ndarray, lens: Sequence[int]) -> np.ndarray:
         ids = np.ascontiguousarray(ids, dtype=np.int32)
         lens = np.ascontiguousarray(lens, dtype=np.int32)
@@ -272,6 +284,14 @@ class MoELayer:
                                    _stream_ptr(stream))
         _check(rc, "ceb_moe_ffn")
 
+    def forward_ep(self, ep: "ExpertParallel", x, y, workspace, stream=None):
+        """ceb_moe_ffn_ep: this rank's tokens through the expert-parallel exchange."""
+        import torch
+        act = {torch.float32: ACT_F32, torch.bfloat16: ACT_BF16, torch.float16: ACT_F16}[x.dtype]
+        rc = self._lib.ceb_moe_ffn_ep(self._h, ep._h, x.data_ptr(), act, x.shape[0], y.data_ptr(),
+                                      workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+        _check(rc, "ceb_moe_ffn_ep")
+
     def route_ln(self, res, y, out, workspace, gamma=None, beta=None, eps=1e-5, out16=None, ids=None, weights=None,
                  logits=None, stream=None):
         """ceb_moe_route_ln: out = LN(res + y), and the router on the normalised rows in the same pass."""
@@ -279,6 +299,48 @@ class MoELayer:
                                         float(eps), out.data_ptr(), _ptr(out16), _ptr(ids), _ptr(weights),
                                         _ptr(logits), workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
         _check(rc, "ceb_moe_route_ln")
+
+
+EP_HANDLE_BYTES = 64
+
+
+class ExpertParallel:
+    """Expert-parallel exchange of one rank (ceb_ep_create / _ipc_handle / _connect).
+
+    `connect(handles)` takes every rank's handle bytes in rank order; see
+    crispembed_b200.dist.connect_expert_parallel for the torch.distributed form."""
+
+    def __init__(self, rank: int, world: int, n_experts: int, top_k: int, d: int, ffn: int, max_local_tokens: int):
+        self._lib = load_library()
+        self.rank, self.world = rank, world
+        self._h = self._lib.ceb_ep_create(rank, world, n_experts, top_k, d, ffn, max_local_tokens)
+        if not self._h:
+            raise CrispEmbedError(f"ceb_ep_create failed: {last_error()}")
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(EP_HANDLE_BYTES)
+        _check(self._lib.ceb_ep_ipc_handle(self._h, buf), "ceb_ep_ipc_handle")
+        return buf.raw
+
+    def connect(self, handles: Sequence[bytes]):
+        if len(handles) != self.world or any(len(h) != EP_HANDLE_BYTES for h in handles):
+            raise CrispEmbedError("connect: one handle of EP_HANDLE_BYTES per rank expected")
+        blob = ctypes.create_string_buffer(b"".join(handles), EP_HANDLE_BYTES * self.world)
+        _check(self._lib.ceb_ep_connect(self._h, blob), "ceb_ep_connect")
+
+    def set_timeout_ms(self, ms: int):
+        self._lib.ceb_ep_set_timeout_ms(self._h, int(ms))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.ceb_ep_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Linear:

@@ -434,6 +434,8 @@ int* op_err_word() {
 }
 }  // namespace
 
+int* ceb_op_error_word() { return op_err_word(); }
+
 extern "C" int ceb_moe_ffn(const ceb_moe_layer* L, const void* d_x, int x_dtype, int n_tokens, float* d_y,
                            int32_t* d_ids, float* d_weights, int32_t* d_expert_counts, float* d_logits,
                            void* d_workspace, size_t workspace_bytes, void* stream) {
@@ -489,6 +491,12 @@ extern "C" int ceb_moe_route_ln(const ceb_moe_layer* L, const float* d_res, cons
     if (d_weights && cudaMemcpyAsync(d_weights, ws.wts, S * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return ceb_set_error(3, "weights copy");
     return 0;
+}
+
+extern "C" int ceb_ep_attach(crispembed_context* ctx, ceb_ep* ep) {
+    if (!ctx || !ep) return ceb_set_error(1, "ep_attach: bad arguments");
+    cudaSetDevice(ctx->device);
+    return ceb_model_ep_attach(&ctx->model, ep);
 }
 
 extern "C" int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int n_seqs, int d, int out_dim,

@@ -54,6 +54,7 @@ struct ceb_model {
     std::vector<ceb_layer> layers;
     std::vector<void*> allocs;  // every device buffer owned by the model
     size_t weight_bytes = 0;
+    struct ceb_ep* ep = nullptr;  // expert-parallel exchange (not owned); the MoE planes then hold its experts only
 };
 
 struct ceb_workspace {
@@ -70,6 +71,9 @@ struct ceb_workspace {
 };
 
 int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out);
+// Keeps only the exchange's local experts of every MoE block (the other experts'
+// weights are freed) and routes the MoE blocks through it from then on.
+int ceb_model_ep_attach(ceb_model* m, struct ceb_ep* ep);
 void ceb_model_free(ceb_model* m);
 int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int seqs);
 void ceb_workspace_free(ceb_workspace* ws);

@@ -81,6 +81,8 @@ int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int
 void ceb_wplane_free(ceb_wplane* w);
 
 int ceb_num_sms();
+// device error word shared by the operator-level entry points (api.cpp)
+int* ceb_op_error_word();
 
 // ---- launch accounting and optional per-category CUDA-event timing ---------
 enum ceb_prof_cat : int {

@@ -28,9 +28,26 @@ enum ceb_dev_error : int {
     CEB_DEVERR_TIMEOUT_EPI = 0x104,
     CEB_DEVERR_BAD_GROUP = 0x105,
     CEB_DEVERR_BAD_INDEX = 0x106,
+    CEB_DEVERR_TIMEOUT_PEER = 0x107,  // a peer GPU's signal did not arrive (expert-parallel exchange)
+    CEB_DEVERR_EP_OVERFLOW = 0x108,   // expert-parallel rows beyond a receive buffer
 };
 
 CEB_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// ------------------------------------------------------------------ system-scope flags (peer GPUs)
+CEB_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+CEB_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+CEB_DEV uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 // ------------------------------------------------------------------ mbarrier
 CEB_DEV void mbar_init(uint32_t bar, uint32_t count) {

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "ceb_encoder_internal.h"
+#include "ceb_ep_internal.h"
 #include "gguf.h"
 
 namespace {
@@ -296,6 +297,39 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
     return rc;
 }
 
+int ceb_model_ep_attach(ceb_model* m, ceb_ep* ep) {
+    if (!ep || !ep->connected) return ceb_set_error(1, "ep_attach: the exchange is not connected");
+    if (m->ep) return ceb_set_error(1, "ep_attach: the model already runs expert-parallel");
+    for (auto& Ly : m->layers) {
+        if (!Ly.moe) continue;
+        const ceb_moe_weights& mw = Ly.moew;
+        if (mw.n_experts != ep->E || mw.top_k != ep->K || mw.d != ep->d || mw.ffn != ep->F)
+            return ceb_set_error(1, "ep_attach: MoE block (E=%d K=%d d=%d F=%d) does not match the exchange "
+                                    "(E=%d K=%d d=%d F=%d)",
+                                 mw.n_experts, mw.top_k, mw.d, mw.ffn, ep->E, ep->K, ep->d, ep->F);
+    }
+    for (auto& Ly : m->layers) {
+        if (!Ly.moe) continue;
+        for (ceb_wplane* w : {&Ly.moew.fc1, &Ly.moew.fc2}) {
+            const ceb_wplane view = ceb_wplane_slice(*w, ep->rank * ep->E_loc, ep->E_loc);
+            ceb_wplane local = view;
+            local.q = nullptr;
+            if (cudaMalloc(&local.q, view.q_bytes) != cudaSuccess)
+                return ceb_set_error(4, "ep_attach: out of device memory for the local experts");
+            const cudaError_t e = cudaMemcpy(local.q, view.q, view.q_bytes, cudaMemcpyDeviceToDevice);
+            if (e != cudaSuccess) {
+                cudaFree(local.q);
+                return ceb_set_cuda_error(e, "ep_attach: local expert copy", __FILE__, __LINE__);
+            }
+            m->weight_bytes -= w->q_bytes + w->s_bytes - local.q_bytes - local.s_bytes;
+            ceb_wplane_free(w);
+            *w = local;
+        }
+    }
+    m->ep = ep;
+    return 0;
+}
+
 void ceb_model_free(ceb_model* m) {
     for (auto& Ly : m->layers) {
         ceb_wplane_free(&Ly.qkv);
@@ -402,8 +436,15 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
             if ((rc = ceb_add_ln_route(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, mw, ws.moe,
                                        nullptr, st)))
                 return rc;
-            if ((rc = ceb_moe_dispatch(mw, ws.c32, CEB_ACT_F32, ws.c16, M, nullptr, ws.moe, nullptr, d_err, st))) return rc;
-            if ((rc = ceb_moe_combine_ln(ws.moe.down, ws.moe.slot_pos, ws.moe.wts, mw.top_k, mw.bias, ws.c32, M, d,
+            const float* down = ws.moe.down;
+            if (m.ep) {
+                if ((rc = ceb_ep_moe(m.ep, mw, ws.c32, CEB_ACT_F32, ws.c16, M, ws.moe, d_err, st))) return rc;
+                down = m.ep->self.ret;
+            } else if ((rc = ceb_moe_dispatch(mw, ws.c32, CEB_ACT_F32, ws.c16, M, nullptr, ws.moe, nullptr, d_err,
+                                              st))) {
+                return rc;
+            }
+            if ((rc = ceb_moe_combine_ln(down, ws.moe.slot_pos, ws.moe.wts, mw.top_k, mw.bias, ws.c32, M, d,
                                          Ly.ln2_w, Ly.ln2_b, eps, ws.x32, ws.x16, st)))
                 return rc;
         } else {

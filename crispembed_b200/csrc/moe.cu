@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "ceb_internal.h"
+#include "ceb_ep_internal.h"
 #include "ceb_moe_internal.h"
 #include "common.cuh"
 #include "rowwise.cuh"
@@ -382,9 +383,11 @@ __global__ void __launch_bounds__(RT_WARPS * 32, RT_MIN_BLOCKS)
 // Expert offsets (exclusive scan of the totals) and, per histogram block, the
 // first output row of each expert.  One warp per expert; lane l owns a run of
 // consecutive blocks, so the block order is a warp scan of the lanes' sums.
+// Expert-parallel runs also publish the totals: row `rank` of every peer's count
+// matrix, then a release of the peer's counts flag.
 __global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E,
                                                     int32_t* __restrict__ block_base, int32_t* __restrict__ offsets,
-                                                    int32_t* __restrict__ expert_counts) {
+                                                    int32_t* __restrict__ expert_counts, ceb_ep_args ep) {
     __shared__ int tot[MAXE];
     __shared__ int lane_base[MAXE][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
@@ -416,6 +419,14 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ 
             block_base[(size_t)b * E + e] = run;
             run += block_counts[(size_t)b * E + e];
         }
+        if (ep.peers && lane < ep.world)
+            ep.peers[lane].counts[((size_t)ep.par * ep.world + ep.rank) * E + e] = tot[e];
+    }
+    if (ep.peers) {
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x < ep.world)
+            st_release_sys(ep.peers[threadIdx.x].flags + CEB_EPF_COUNTS * ep.world + ep.rank, ep.epoch);
     }
 }
 
@@ -423,17 +434,43 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ 
 // gather of the token rows (converted to fp16) into the permuted activation
 // matrix consumed by fc1: one warp per token reads the row once and writes it
 // to each of the token's K rows.
+//
+// Expert-parallel runs (ep.peers set) write each row straight into the receive
+// buffer of the rank owning its expert, at (the expert's rows from lower ranks
+// and lower local experts of that owner) + (the row's rank within this rank's
+// rows of the expert); the last CTA to finish releases every peer's dispatch
+// flag.  CTA 0 also derives the row ranges of the local experts in the local
+// receive buffer for the expert GEMMs.
 template <typename T>
 __global__ void __launch_bounds__(256)
     scatter_kernel(const T* __restrict__ x, const __half* __restrict__ x16, int T_tokens, int d, int E, int K,
                    const int32_t* __restrict__ ids, const int32_t* __restrict__ block_base,
-                   int32_t* __restrict__ slot_pos, __half* __restrict__ x_perm) {
+                   int32_t* __restrict__ slot_pos, __half* __restrict__ x_perm, int* __restrict__ err,
+                   ceb_ep_args ep) {
     __shared__ int running[MAXE];
     __shared__ int s_pos[CHUNK * 4];
+    __shared__ int s_key[CHUNK * 4];
+    __shared__ long long s_dst[MAXE];  // EP: destination row of local position 0 of each expert
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * CHUNK;
     const int n_tok = min(CHUNK, T_tokens - t0);
     const int n_slots = n_tok * K;
+    if (ep.peers && threadIdx.x >= 32 && threadIdx.x < 32 + E) {
+        const int e = threadIdx.x - 32, q = e / ep.E_loc;
+        long long base = 0;
+        for (int e2 = q * ep.E_loc; e2 < e; ++e2)
+            for (int p = 0; p < ep.world; ++p) base += ep.C[p * E + e2];
+        for (int p = 0; p < ep.rank; ++p) base += ep.C[p * E + e];
+        s_dst[e] = base - ep.my_offsets[e];
+    }
+    if (ep.peers && blockIdx.x == 0) {  // first row of each local expert in the local receive buffer
+        for (int el = threadIdx.x; el <= ep.E_loc; el += blockDim.x) {
+            long long r = 0;
+            for (int e2 = 0; e2 < el; ++e2)
+                for (int p = 0; p < ep.world; ++p) r += ep.C[p * E + ep.rank * ep.E_loc + e2];
+            ep.offsets_recv[el] = (int32_t)r;
+        }
+    }
     if (warp == 0) {
         for (int e = lane; e < E; e += 32) running[e] = block_base[(size_t)blockIdx.x * E + e];
         __syncwarp();
@@ -456,6 +493,7 @@ __global__ void __launch_bounds__(256)
             __syncwarp();
             if (act) {
                 s_pos[s] = pos;
+                s_key[s] = key;
                 slot_pos[(size_t)t0 * K + s] = pos;
             }
         }
@@ -480,10 +518,33 @@ __global__ void __launch_bounds__(256)
         for (int j = 0; j < K; ++j) {
             const int pos = s_pos[tl * K + j];
             if (pos < 0) continue;
-            __half* dst = x_perm + (size_t)pos * d;
+            __half* dst;
+            if (ep.peers) {
+                const int e = s_key[tl * K + j];
+                const long long row = s_dst[e] + pos;
+                if (row < 0 || row >= ep.recv_rows) {
+                    if (lane == 0) atomicCAS(err, 0, (int)CEB_DEVERR_EP_OVERFLOW);
+                    continue;
+                }
+                dst = ep.peers[e / ep.E_loc].recv + (size_t)row * d;
+            } else {
+                dst = x_perm + (size_t)pos * d;
+            }
 #pragma unroll
             for (int i = 0; i < LN_MAXV; ++i)
                 if (i < nv) *reinterpret_cast<uint2*>(dst + (i * 32 + lane) * 4) = r[i];
+        }
+    }
+    if (ep.peers) {  // the last CTA to finish tells every peer that this rank's rows have landed
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (atomicAdd(ep.done, 1) == (int)gridDim.x - 1) {
+                atomicExch(ep.done, 0);
+                __threadfence_system();
+                for (int p = 0; p < ep.world; ++p)
+                    st_release_sys(ep.peers[p].flags + CEB_EPF_DISPATCH * ep.world + ep.rank, ep.epoch);
+            }
         }
     }
 }
@@ -597,25 +658,44 @@ int ceb_add_ln_route(const float* res, const float* y, int M, int d, const float
     });
 }
 
+int ceb_moe_permute(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T,
+                    const ceb_moe_ws& ws, int32_t* expert_counts, const ceb_ep_args* ep, int* dev_err,
+                    cudaStream_t st) {
+    const int d = mw.d, E = mw.n_experts, K = mw.top_k;
+    const int nblk = (T + CHUNK - 1) / CHUNK;
+    const ceb_ep_args none;
+    const ceb_ep_args& ea = ep ? *ep : none;
+    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+               scan_kernel<<<1, 32 * E, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts,
+                                                 ea));
+    CEB_CUDA_OK(cudaGetLastError());
+    if (ep)
+        if (int rc = ceb_ep_wait(*ep, CEB_EPF_COUNTS, dev_err, st)) return rc;
+    const int grid = std::max(nblk, 1);  // an expert-parallel rank without tokens still signals its peers
+    int* err = dev_err;
+    if (x_dtype == CEB_ACT_F32)
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+                   scatter_kernel<float><<<grid, 256, 0, st>>>((const float*)x, x16, T, d, E, K, ws.ids, ws.block_base,
+                                                               ws.slot_pos, ws.x_perm, err, ea));
+    else if (x_dtype == CEB_ACT_BF16)
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+                   scatter_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, x16, T, d, E, K,
+                                                                       ws.ids, ws.block_base, ws.slot_pos, ws.x_perm,
+                                                                       err, ea));
+    else
+        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+                   scatter_kernel<__half><<<grid, 256, 0, st>>>((const __half*)x, x16, T, d, E, K, ws.ids,
+                                                                ws.block_base, ws.slot_pos, ws.x_perm, err, ea));
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
 int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
                      const ceb_moe_ws& ws, int32_t* expert_counts, int* dev_err, cudaStream_t st) {
     if (int rc = moe_shape_check(mw)) return rc;
-    const int d = mw.d, E = mw.n_experts, K = mw.top_k, F = mw.ffn;
+    const int d = mw.d, K = mw.top_k, F = mw.ffn;
     if (T <= 0) return 0;
-    const int nblk = (T + CHUNK - 1) / CHUNK;
-    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
-               scan_kernel<<<1, 32 * E, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts));
-    CEB_CUDA_OK(cudaGetLastError());
-    if (x_dtype == CEB_ACT_F32)
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<float><<<nblk, 256, 0, st>>>((const float*)x, x16, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
-                                                    ws.x_perm));
-    else if (x_dtype == CEB_ACT_BF16)
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__nv_bfloat16><<<nblk, 256, 0, st>>>((const __nv_bfloat16*)x, x16, T, d, E, K, ws.ids,
-                                                            ws.block_base, ws.slot_pos, ws.x_perm));
-    else
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0, scatter_kernel<__half><<<nblk, 256, 0, st>>>((const __half*)x, x16, T, d, E, K, ws.ids, ws.block_base, ws.slot_pos,
-                                                     ws.x_perm));
-    CEB_CUDA_OK(cudaGetLastError());
+    if (int rc = ceb_moe_permute(mw, x, x_dtype, x16, T, ws, expert_counts, nullptr, dev_err, st)) return rc;
 
     const int rows = T * K;
     ceb_gemm_args a1;
@@ -643,12 +723,12 @@ int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, cons
     return 0;
 }
 
-int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
-                const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st) {
+int ceb_moe_route(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, const ceb_moe_ws& ws,
+                  float* logits_out, cudaStream_t st) {
     if (int rc = moe_shape_check(mw)) return rc;
     const int d = mw.d, E = mw.n_experts, K = mw.top_k;
     if (T <= 0) return 0;
-    int rc = with_nv(d, [&](auto nvc) {
+    return with_nv(d, [&](auto nvc) {
         constexpr int NV = decltype(nvc)::value;
         if (x_dtype == CEB_ACT_F32)
             return launch_route_rows<NV>(ActRows<float, NV>{(const float*)x}, T, E, K, mw.router_type, mw.router, ws,
@@ -659,6 +739,18 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __h
         return launch_route_rows<NV>(ActRows<__half, NV>{(const __half*)x}, T, E, K, mw.router_type, mw.router, ws,
                                      logits_out, st);
     });
-    if (rc) return rc;
+}
+
+int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
+                const ceb_moe_ws& ws, int32_t* expert_counts, float* logits_out, int* dev_err, cudaStream_t st) {
+    if (int rc = ceb_moe_route(mw, x, x_dtype, T, ws, logits_out, st)) return rc;
     return ceb_moe_dispatch(mw, x, x_dtype, x16, T, y, ws, expert_counts, dev_err, st);
+}
+
+int ceb_moe_combine(const float* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
+                    const float* bias, float* y, cudaStream_t st) {
+    if (T <= 0) return 0;
+    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, combine_kernel<<<T, 256, 0, st>>>(down, slot_pos, wts, T, d, K, bias, y));
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
 }

@@ -130,6 +130,53 @@ CEB_API int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int 
                         float* d_out, void* stream);
 
 /*
+ * Expert parallelism across the GPUs of one node (no counterpart in the
+ * reference, which runs every expert of a block on one device inside
+ * ggml_mul_mat_id, src/crispembed.cpp:1365-1371).  One process per GPU, rank r
+ * of `world` owns experts [r*E/world, (r+1)*E/world) of every MoE block and
+ * routes its own tokens.  Each rank exports one device region through CUDA IPC;
+ * the permutation kernel stores every routed row straight into the owner's
+ * receive buffer over NVLink and the owner stores the expert outputs back, with
+ * release/acquire flags and bounded on-device waits (status 5, code 0x107, when
+ * a peer does not answer within the timeout).  No host synchronisation.
+ *
+ * Setup (every rank, same arguments except rank):
+ *   ep = ceb_ep_create(rank, world, E, K, d, F, max_local_tokens);
+ *   ceb_ep_ipc_handle(ep, mine);              // CEB_EP_HANDLE_BYTES bytes
+ *   ...all-gather the handles in rank order (host collective of the caller)...
+ *   ceb_ep_connect(ep, all_handles);          // world * CEB_EP_HANDLE_BYTES
+ * Every rank must then issue the same sequence of expert-parallel calls (each
+ * MoE block is one exchange), also when it has no tokens of its own.
+ * ceb_ep_free waits for the device and unmaps the peers' regions.
+ */
+#define CEB_EP_HANDLE_BYTES 64
+typedef struct ceb_ep ceb_ep;
+CEB_API ceb_ep* ceb_ep_create(int rank, int world, int n_experts, int top_k, int d, int ffn, int max_local_tokens);
+CEB_API int ceb_ep_ipc_handle(const ceb_ep* ep, void* handle_out);
+CEB_API int ceb_ep_connect(ceb_ep* ep, const void* handles);
+CEB_API void ceb_ep_set_timeout_ms(ceb_ep* ep, int ms);
+CEB_API void ceb_ep_free(ceb_ep* ep);
+
+/*
+ * Runs every MoE block of an encoder context through the exchange from now on
+ * (crispembed_encode* and crispembed_encode_ids_batch on this rank's own
+ * sequences; every rank must encode in lockstep, one call per call).  The
+ * context keeps only this rank's experts; the other experts' weights are freed.
+ * The exchange must outlive the context's use of it.
+ */
+typedef struct crispembed_context crispembed_context;
+CEB_API int ceb_ep_attach(crispembed_context* ctx, ceb_ep* ep);
+
+/*
+ * ceb_moe_ffn over the exchange: this rank's n_tokens rows (0 allowed) are
+ * routed here, their rows go to the experts' owners and the outputs come back
+ * for the combine.  y is bit-identical to ceb_moe_ffn on one GPU.  The layer
+ * holds all experts; only this rank's slice is used.
+ */
+CEB_API int ceb_moe_ffn_ep(const ceb_moe_layer* layer, ceb_ep* ep, const void* d_x, int x_dtype, int n_tokens,
+                           float* d_y, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/*
  * The text tokenizer of a GGUF on its own (no device needed): the family the
  * reference would pick (src/tokenizer.h:37-52), WordPiece or SentencePiece
  * Unigram, wrapping and truncation to max_tokens as the text ABI applies them.
