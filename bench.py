@@ -2,7 +2,7 @@
 """MoE-encoder throughput on B200 -- one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c3]
+                    [--workload c2|c3|c4] [--no-ep] [--no-cpu-baseline]
 
 Workloads (inputs synthetic and seeded, weights random-init
 of the nomic-embed-text-v2-moe architecture, see crispembed_b200/synth.py):
@@ -17,7 +17,11 @@ value  : tokens/s of the whole job with ids already in HBM (device entry point,
 e2e    : same metric through the host-buffer C-ABI call (crispembed_encode_ids_batch:
          ids copied host->device and embeddings device->host inside the timed call).
 Multi-GPU (torchrun): data-parallel replicas, every rank encodes its own copy of
-the config-2 batch (weak scaling, no collective on the data path).
+the config-2 batch (weak scaling, no collective on the data path).  The line also
+carries "expert_parallel": BASELINE config 4 (512 x 512 tokens per step for the
+whole job, sequences sharded over the ranks and the MoE experts split over them,
+exchange by the library's own peer-memory kernels), at every N (N=1 runs the
+exchange with itself).  --workload c4 prints that measurement as the main line.
 --impl reference: the CPU restatement of the reference's ggml CPU path (oracle/,
 the reference itself cannot be built here) on all host threads, bounded sample.
 """
@@ -199,6 +203,80 @@ def run_reference(args, rank):
     return 0
 
 
+def c4_config(world, tokens):
+    return {"workload": "c4: NomicBERT-MoE Q8_0 encoder, 512 seqs x 512 tokens seed 3 per step (whole job), "
+                        "sequences sharded over the ranks, MoE experts split over the ranks",
+            "tokens_per_step": tokens, "global_batch": 512, "seq_len": 512,
+            "parallelism": f"ep{world} (experts {8 // world} per GPU) x dp{world} sequence shards",
+            "exchange": "per MoE block: counts, dispatch rows (fp16) and expert outputs (fp32) stored into peer "
+                        "memory by the permutation / return kernels over NVLink, bounded flag waits",
+            "l2": "inputs larger than L2"}
+
+
+def bench_ep(args, rank, world, local, path, dist):
+    """expert-parallel encoder over the ranks of this job (one per GPU)."""
+    import torch
+
+    from crispembed_b200 import binding, synth
+    from crispembed_b200.dist import connect_expert_parallel, max_over_ranks, shard_sequences
+    ids, lens = synth.config_ids(4)
+    total = int(lens.sum())
+    s0, cnt, tok0, ntok = shard_sequences(lens, rank, world)
+    my_ids, my_lens = np.ascontiguousarray(ids[tok0:tok0 + ntok]), np.ascontiguousarray(lens[s0:s0 + cnt])
+    m = binding.CrispEmbed(path)
+    h = m.hparams
+    n_embd = int(h.n_embd)
+    ep = binding.ExpertParallel(rank, world, h.n_experts, h.n_experts_per_tok, n_embd,
+                                synth.nomic_moe_spec().expert_ffn, ntok)
+    connect_expert_parallel(ep)
+    ep.set_timeout_ms(30000)
+    m.attach_ep(ep)
+    d_ids = torch.from_numpy(my_ids).cuda()
+    out = torch.empty((cnt, m.dim), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        m.encode_ids_device(d_ids, my_lens, out)
+    torch.cuda.synchronize()
+    binding.sync_check()
+    if dist:
+        dist.barrier()
+    n0 = binding.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        clk.wait_first()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            m.encode_ids_device(d_ids, my_lens, out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = binding.launch_count() - n0
+    binding.sync_check()
+    t = max_over_ranks(ev0.elapsed_time(ev1) / 1000.0, "cuda")
+    if dist:
+        dist.barrier()
+    for _ in range(2):
+        m.encode_ids(my_ids, my_lens)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        emb = m.encode_ids(my_ids, my_lens)
+    te = max_over_ranks(time.perf_counter() - t0, "cuda")
+    assert np.allclose(np.linalg.norm(emb, axis=1), 1.0, atol=1e-4)
+    if dist:
+        dist.barrier()
+    m.close()
+    ep.close()
+    if dist:
+        dist.barrier()
+    return {"value": total * args.steps / t, "unit": "tokens/s", "per_gpu_tokens_per_s": total * args.steps / t / world,
+            "ms_per_step": 1000.0 * t / args.steps, "config": c4_config(world, total),
+            "e2e": {"value": total * args.steps / te, "unit": "tokens/s", "h2d_bytes_per_step": int(my_ids.nbytes),
+                    "d2h_bytes_per_step": int(cnt * n_embd * 4), "note": "rank 0's bytes; every rank copies its shard"},
+            "gpu_launches": int(launches), "clocks": clk.summary()}
+
+
 def traffic_from_profile(workload):
     p = os.path.join(ROOT, "profiles", f"gemm_traffic_{workload}.json")
     if os.path.exists(p):
@@ -213,8 +291,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c3"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel (config 4) block of the c2 line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -233,11 +312,25 @@ def main():
     from crispembed_b200 import binding, synth
     from crispembed_b200.dist import max_over_ranks
 
-    path = model_path(local) if args.workload == "c2" else None
+    path = model_path(local) if args.workload in ("c2", "c4") else None
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     if args.workload == "c3":
         return bench_moe_op(args, rank, world, local)
+    if args.workload == "c4":
+        r = bench_ep(args, rank, world, local, path, dist)
+        if rank == 0:
+            line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+                    "scaling": "strong", "vs_baseline": None,
+                    "dtype": "fp16 (Q8_0 weights dequantized to fp16, fp32 accumulate)",
+                    "data": "synthetic (seeded ids; random-init weights of the nomic-embed-text-v2-moe architecture)",
+                    "config": r["config"], "per_gpu_tokens_per_s": r["per_gpu_tokens_per_s"], "e2e": r["e2e"],
+                    "gpu_launches": r["gpu_launches"], "clocks": r["clocks"]}
+            print(json.dumps(line), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return 0
 
     ids, lens = synth.config_ids(2)
     n_seqs, tokens = len(lens), int(lens.sum())
@@ -318,6 +411,10 @@ def main():
         "breakdown_ms_per_step": {k: v["ms"] / args.steps for k, v in prof.items()},
         "clocks": clk.summary(),
     }
+    if not args.no_ep:
+        if dist:
+            dist.barrier()
+        result["expert_parallel"] = bench_ep(args, rank, world, local, path, dist)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(path, ids, lens)
     if rank == 0:
