@@ -2,7 +2,7 @@
 """MoE-encoder throughput on B200 -- one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c3|c4] [--no-ep] [--no-cpu-baseline]
+                    [--workload c2|c3|c4|c5] [--no-ep] [--no-cpu-baseline]
 
 Workloads (inputs synthetic and seeded, weights random-init
 of the nomic-embed-text-v2-moe architecture, see crispembed_b200/synth.py):
@@ -10,7 +10,10 @@ of the nomic-embed-text-v2-moe architecture, see crispembed_b200/synth.py):
                 U[32,512] (seed 2, 70825 tokens) per step; one step = embed,
                 12 layers (6 MoE), mean-pool + L2 of the whole batch.
   c3            the isolated MoE FFN operator, Q4_K experts, T=65536 bf16 tokens,
-                Zipf(1.2) expert loads (seed 0).
+                Zipf(1.2) expert loads (seed 0); T=512 and 8192 as other_cases.
+  c4            the expert-parallel encoder alone (see below).
+  c5            wide routing through the same operator: d=1024, E=32, top-4,
+                F=1536, Q4_K, T=131072, balanced; Zipf(1.5) as other_cases.
 
 value  : tokens/s of the whole job with ids already in HBM (device entry point,
          CUDA events on the launching stream, max over ranks).
@@ -291,7 +294,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel (config 4) block of the c2 line")
     args = ap.parse_args()
@@ -315,8 +318,8 @@ def main():
     path = model_path(local) if args.workload in ("c2", "c4") else None
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    if args.workload == "c3":
-        return bench_moe_op(args, rank, world, local)
+    if args.workload in ("c3", "c5"):
+        return bench_moe_op(args, rank, world, local) if rank == 0 else 0
     if args.workload == "c4":
         r = bench_ep(args, rank, world, local, path, dist)
         if rank == 0:
@@ -425,56 +428,127 @@ def main():
     return 0
 
 
-def bench_moe_op(args, rank, world, local):
-    """isolated MoE FFN operator, Q4_K experts, T=65536, Zipf 1.2."""
+OP_WORKLOADS = {
+    # isolated MoE FFN operator, Q4_K experts, Zipf(1.2) loads; T sweep {512, 8192, 65536}
+    "c3": dict(d=768, n_experts=8, top_k=2, ffn=3072, T=65536, zipf=1.2, sweep=[512, 8192], variants=[]),
+    # wide routing, E=32 top-4, Q4_K, T=131072, balanced and Zipf(1.5)
+    "c5": dict(d=1024, n_experts=32, top_k=4, ffn=1536, T=131072, zipf=None, sweep=[], variants=[1.5]),
+}
+
+
+def _time_moe_op(args, cfg, T, zipf, local, with_clocks=False):
     import torch
 
     from crispembed_b200 import binding, synth
     from crispembed_b200.gguf_io import GGML_F32, GGML_Q4_K
-    T = 65536
-    inp = synth.make_moe_op_inputs(T, d=768, n_experts=8, top_k=2, ffn=3072, wtype=GGML_Q4_K, router_wtype=GGML_F32,
-                                   zipf_s=1.2, seed=0)
+    inp = synth.make_moe_op_inputs(T, d=cfg["d"], n_experts=cfg["n_experts"], top_k=cfg["top_k"], ffn=cfg["ffn"],
+                                   wtype=GGML_Q4_K, router_wtype=GGML_F32, zipf_s=zipf, seed=0)
     layer = binding.MoELayer(inp.d, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
                              inp.fc1_raw, inp.fc2_raw, inp.bias)
     x = torch.from_numpy(inp.x).cuda().to(torch.bfloat16)
     y = torch.empty((T, inp.d), dtype=torch.float32, device="cuda")
     ws = torch.empty(layer.workspace_size(T), dtype=torch.uint8, device="cuda")
+    cnt = torch.empty((inp.n_experts,), dtype=torch.int32, device="cuda")
     for _ in range(args.warmup):
-        layer.forward(x, y, ws)
+        layer.forward(x, y, ws, counts=cnt)
     torch.cuda.synchronize()
+    binding.sync_check()
+    steps = args.steps if T >= 8192 else max(args.steps, 200)
     n0 = binding.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    clk = ClockSampler(local) if with_clocks else None
+    if clk:
+        clk.__enter__()
         clk.wait_first()
-        ev0.record()
-        for _ in range(args.steps):
-            layer.forward(x, y, ws)
-        ev1.record()
-        torch.cuda.synchronize()
-    launches = binding.launch_count() - n0
+    ev0.record()
+    for _ in range(steps):
+        layer.forward(x, y, ws)
+    ev1.record()
+    torch.cuda.synchronize()
+    if clk:
+        clk.__exit__(None, None, None)
+    launches = (binding.launch_count() - n0) // steps * args.steps
     binding.profile_enable(True)  # per-launch events in a second pass of the same steps
-    for _ in range(args.steps):
+    for _ in range(steps):
         layer.forward(x, y, ws)
     torch.cuda.synchronize()
     prof = binding.profile_read()
     binding.profile_enable(False)
-    t = ev0.elapsed_time(ev1) / 1000.0
-    value = T * args.steps / t
-    pk, pk_src = peaks()
+    t = ev0.elapsed_time(ev1) / 1000.0 / steps
+    # end to end: x from pinned host memory, y back to the host, inside the timed region
+    hx = x.cpu().pin_memory()
+    hy = torch.empty((T, inp.d), dtype=torch.float32).pin_memory()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        x.copy_(hx, non_blocking=True)
+        layer.forward(x, y, ws)
+        hy.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    te = (time.perf_counter() - t0) / steps
+    loads = cnt.cpu().numpy()
     g = prof["gemm"]
-    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12
-    peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    result = {"metric": "MoE FFN operator tokens/s (Q4_K, T=65536, Zipf 1.2)", "value": value, "unit": "tokens/s",
-              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * t / args.steps,
-              "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (Q4_K dequant)",
-              "data": "synthetic", "config": {"workload": "c3 MoE op d=768 E=8 k=2 F=3072 T=65536 bf16 x"},
-              "gpu_launches": int(launches),
-              "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                           "frac": achieved / peak, "peak_source": f"{pk_src} bf16_tflops (burst)",
-                           "traffic": None},
-              "breakdown_ms_per_step": {k: v["ms"] / args.steps for k, v in prof.items()},
-              "clocks": clk.summary()}
+    r = {"T": T, "zipf": zipf, "ms": 1000 * t, "tokens_per_s": T / t, "e2e_tokens_per_s": T / te,
+         "h2d_bytes": int(hx.numel() * hx.element_size()), "d2h_bytes": int(hy.numel() * 4),
+         "gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
+         "gemm_ms": g["ms"] / steps, "launches": int(launches), "max_over_mean_expert_load": float(loads.max() / loads.mean()),
+         "breakdown_ms": {k: v["ms"] / steps for k, v in prof.items()}, "clocks": clk.summary() if clk else None}
     layer.close()
+    return r, inp
+
+
+def op_cpu_baseline(inp, budget_s=10.0, n=256):
+    """Oracle MoE op (ggml-faithful CPU restatement) on the first n tokens, repeated for ~budget_s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = O.set_threads(os.cpu_count() or 1)
+    x = inp.x[:n]
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or done == 0:
+        O.moe_ffn(x, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype, inp.fc1_raw,
+                  inp.fc2_raw, inp.bias, O.GGML)
+        done += len(x)
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"the first {n} tokens of the workload, MoE op repeated for {dt:.1f}s, ggml-faithful mode"}
+
+
+def bench_moe_op(args, rank, world, local):
+    """BASELINE configs 3 and 5: the isolated MoE FFN operator (ceb_moe_ffn), Q4_K experts."""
+    cfg = OP_WORKLOADS[args.workload]
+    main_r, inp = _time_moe_op(args, cfg, cfg["T"], cfg["zipf"], local, with_clocks=True)
+    pk, pk_src = peaks()
+    peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    flops_tok = 2.0 * 2 * cfg["top_k"] * cfg["d"] * cfg["ffn"]
+    skew = f"Zipf {cfg['zipf']}" if cfg["zipf"] else "balanced"
+    result = {"metric": f"MoE FFN operator tokens/s (Q4_K, d={cfg['d']} E={cfg['n_experts']} top-{cfg['top_k']} "
+                        f"F={cfg['ffn']}, T={cfg['T']}, {skew})",
+              "value": main_r["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": main_r["ms"], "higher_is_better": True, "scaling": "weak",
+              "vs_baseline": None, "dtype": "fp16 (Q4_K dequant, fp32 accumulate)", "data": "synthetic",
+              "config": {"workload": f"{args.workload}: MoE op, x bf16 N(0,1), router F32, experts Q4_K, {skew}",
+                         "tokens": cfg["T"], "l2": "inputs larger than L2" if cfg["T"] >= 65536 else "fits L2"},
+              "e2e": {"value": main_r["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": main_r["h2d_bytes"],
+                      "d2h_bytes_per_step": main_r["d2h_bytes"]},
+              "gpu_launches": main_r["launches"],
+              "roofline": {"bound": "tensor", "kernel": "grouped tcgen05 GEMM (fc1+GELU, fc2)",
+                           "achieved": main_r["gemm_tflops"], "peak": peak, "unit": "TFLOP/s",
+                           "frac": main_r["gemm_tflops"] / peak, "peak_source": f"{pk_src} bf16_tflops (burst)",
+                           "op_tflops": main_r["tokens_per_s"] * flops_tok / 1e12, "traffic": None},
+              "max_over_mean_expert_load": main_r["max_over_mean_expert_load"],
+              "breakdown_ms_per_step": main_r["breakdown_ms"], "clocks": main_r["clocks"]}
+    others = []
+    for T in cfg["sweep"]:
+        r, _ = _time_moe_op(args, cfg, T, cfg["zipf"], local)
+        others.append({k: r[k] for k in ("T", "zipf", "ms", "tokens_per_s", "e2e_tokens_per_s", "gemm_tflops",
+                                         "max_over_mean_expert_load")})
+    for z in cfg["variants"]:
+        r, _ = _time_moe_op(args, cfg, cfg["T"], z, local)
+        others.append({k: r[k] for k in ("T", "zipf", "ms", "tokens_per_s", "e2e_tokens_per_s", "gemm_tflops",
+                                         "max_over_mean_expert_load")})
+    if others:
+        result["other_cases"] = others
+    if not args.no_cpu_baseline:
+        result["cpu_baseline"] = op_cpu_baseline(inp)
     print(json.dumps(result), flush=True)
     return 0
 
