@@ -211,30 +211,47 @@ CEB_DEV void quantize_row(const float4 (&v)[NV], int8_t* q, float* qd, int lane)
     }
 }
 
-// F32 router: logits of one row (all experts) by warp dots; lane (tt, el)
-// keeps expert el + 8j of token tt in lgv[j].
+// F32 router: logits of one row, all experts.  Each lane forms its partial dot
+// with every expert (its 4 columns per 128), then one butterfly reduces the 32
+// vectors at once (31 shuffles: at offset o a lane keeps half of its values and
+// adds its partner's copy of that half), leaving expert l's logit in lane l;
+// lane (tt, el) then takes experts el + 8j of token tt into lgv[j].
 template <int NV>
 CEB_DEV void f32_logits(const float4 (&v)[NV], const float* __restrict__ wf, int E, int lane, int tt,
                         float (&lgv)[RT_MAXJ]) {
     constexpr int d = NV * 128;
+    float acc[32];
 #pragma unroll
-    for (int j = 0; j < RT_MAXJ; ++j) {
-        for (int el = 0; el < 8; ++el) {
-            const int e = 8 * j + el;
-            if (e >= E) break;
+    for (int e = 0; e < 32; ++e) {
+        float a = 0.0f;
+        if (e < E) {
             const float* wr = wf + (size_t)e * d;
-            float acc = 0.0f;
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
                 const float4 w = __ldg(reinterpret_cast<const float4*>(wr + (i * 32 + lane) * 4));
-                acc = __fmaf_rn(v[i].x, w.x, acc);
-                acc = __fmaf_rn(v[i].y, w.y, acc);
-                acc = __fmaf_rn(v[i].z, w.z, acc);
-                acc = __fmaf_rn(v[i].w, w.w, acc);
+                a = __fmaf_rn(v[i].x, w.x, a);
+                a = __fmaf_rn(v[i].y, w.y, a);
+                a = __fmaf_rn(v[i].z, w.z, a);
+                a = __fmaf_rn(v[i].w, w.w, a);
             }
-            acc = warp_sum(acc);
-            if ((lane >> 3) == tt && (lane & 7) == el) lgv[j] = acc;
         }
+        acc[e] = a;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; ++i) {
+            const float send = up ? acc[i] : acc[i + o];
+            const float keep = up ? acc[i + o] : acc[i];
+            acc[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+        }
+    }
+    const int el = lane & 7;
+#pragma unroll
+    for (int j = 0; j < RT_MAXJ; ++j) {
+        const float r = __shfl_sync(0xffffffffu, acc[0], el + 8 * j);
+        if ((lane >> 3) == tt) lgv[j] = r;
     }
 }
 
@@ -334,9 +351,11 @@ CEB_DEV void group_route(const float (&lgv)[RT_MAXJ], int E, int K, bool valid, 
 
 // The router over histogram blocks [blockIdx.x, nblk) step gridDim.x; rows come
 // from `rows` (activations in memory, or the fused residual + LayerNorm).
-template <int NV, class Rows>
-__global__ void __launch_bounds__(RT_WARPS * 32, RT_MIN_BLOCKS)
-    route_rows_kernel(Rows rows, int T_tokens, int nblk, int E, int K, int rtype, const uint8_t* __restrict__ rw,
+// Q8 = true: Q8_0 router weights; false: F32 (its 32 per-lane partial sums get a
+// register budget of their own).
+template <int NV, bool Q8, class Rows>
+__global__ void __launch_bounds__(RT_WARPS * 32, Q8 ? RT_MIN_BLOCKS : 2)
+    route_rows_kernel(Rows rows, int T_tokens, int nblk, int E, int K, const uint8_t* __restrict__ rw,
                       int32_t* __restrict__ ids, float* __restrict__ wts, float* __restrict__ logits_out,
                       int32_t* __restrict__ block_counts) {
     extern __shared__ __align__(16) uint8_t sm[];
@@ -344,7 +363,7 @@ __global__ void __launch_bounds__(RT_WARPS * 32, RT_MIN_BLOCKS)
     const RouteSmem s = route_carve(sm, d, E);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tt_l = lane >> 3, el = lane & 7;
-    route_stage(s, E, rtype, rw);
+    route_stage(s, E, Q8 ? CEB_GGML_Q8_0 : CEB_GGML_F32, rw);
     int8_t* xq = s.xq + (size_t)warp * RT_GROUP * d;
     float* xd = s.xd + (size_t)warp * RT_GROUP * s.nb;
     for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
@@ -362,7 +381,7 @@ __global__ void __launch_bounds__(RT_WARPS * 32, RT_MIN_BLOCKS)
                 if (g + tt + 1 < RT_TOK_PER_WARP && t + 1 < T_tokens) rows.prefetch(t + 1, lane);
                 float4 v[NV];
                 rows.row(t, v, lane);
-                if (rtype == CEB_GGML_Q8_0)
+                if (Q8)
                     quantize_row<NV>(v, xq + (size_t)tt * d, xd + tt * s.nb, lane);
                 else
                     f32_logits<NV>(v, reinterpret_cast<const float*>(rw), E, lane, tt, lgv);
@@ -370,7 +389,7 @@ __global__ void __launch_bounds__(RT_WARPS * 32, RT_MIN_BLOCKS)
             __syncwarp();
             const int t_mine = t_base + g + tt_l;
             const bool valid = t_mine < T_tokens;
-            if (rtype == CEB_GGML_Q8_0 && valid) q8_logits<NV>(s, xq + (size_t)tt_l * d, xd + tt_l * s.nb, E, el, lgv);
+            if (Q8 && valid) q8_logits<NV>(s, xq + (size_t)tt_l * d, xd + tt_l * s.nb, E, el, lgv);
             __syncwarp();
             group_route(lgv, E, K, valid, (size_t)t_mine, el, ids, wts, logits_out, s.cnt);
         }
@@ -604,10 +623,10 @@ int moe_shape_check(const ceb_moe_weights& mw) {
 }
 
 // One launch of route_rows_kernel: a persistent grid of (resident CTAs per SM) x SMs.
-template <int NV, class Rows>
-int launch_route_rows(const Rows& rows, int T, int E, int K, int rtype, const uint8_t* rw, const ceb_moe_ws& ws,
-                      float* logits_out, cudaStream_t st) {
-    auto kern = route_rows_kernel<NV, Rows>;
+template <int NV, bool Q8, class Rows>
+int launch_route_rows_t(const Rows& rows, int T, int E, int K, const uint8_t* rw, const ceb_moe_ws& ws,
+                        float* logits_out, cudaStream_t st) {
+    auto kern = route_rows_kernel<NV, Q8, Rows>;
     const size_t smem = route_smem_bytes(NV * 128, E);
     static int occ = 0;
     static size_t occ_smem = 0;
@@ -621,10 +640,17 @@ int launch_route_rows(const Rows& rows, int T, int E, int K, int rtype, const ui
     const int nblk = (T + CHUNK - 1) / CHUNK;
     const int grid = std::min(nblk, occ * ceb_num_sms());
     CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
-               kern<<<grid, RT_WARPS * 32, smem, st>>>(rows, T, nblk, E, K, rtype, rw, ws.ids, ws.wts, logits_out,
+               kern<<<grid, RT_WARPS * 32, smem, st>>>(rows, T, nblk, E, K, rw, ws.ids, ws.wts, logits_out,
                                                        ws.block_counts));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
+}
+
+template <int NV, class Rows>
+int launch_route_rows(const Rows& rows, int T, int E, int K, int rtype, const uint8_t* rw, const ceb_moe_ws& ws,
+                      float* logits_out, cudaStream_t st) {
+    if (rtype == CEB_GGML_Q8_0) return launch_route_rows_t<NV, true>(rows, T, E, K, rw, ws, logits_out, st);
+    return launch_route_rows_t<NV, false>(rows, T, E, K, rw, ws, logits_out, st);
 }
 
 // Calls f(std::integral_constant<int, d / 128>) for the supported widths.
