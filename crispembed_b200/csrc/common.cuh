@@ -363,3 +363,25 @@ CEB_DEV void i8x4_to_h2x2(uint32_t w, __half2 d2, uint32_t& lo, uint32_t& hi) {
         cudaError_t e__ = (expr);                             \
         if (e__ != cudaSuccess) return ceb_set_cuda_error(e__, #expr, __FILE__, __LINE__); \
     } while (0)
+
+// ------------------------------------------------------------------ exp2 on the FMA pipe
+// 2^x for x <= 0 on the FMA pipe, so attention softmaxes can share their
+// exponentials between the MUFU unit and the FMA pipe.  x = n + f with
+// n = rint(x) (the 1.5*2^23 rounding constant) and f in [-0.5, 0.5]; 2^f by a
+// degree-4 polynomial fitted here for relative error on [-0.5, 0.5] (weighted
+// least squares, Lawson iterations: max relative error 2.7e-6 in fp32, far below
+// the fp16 rounding of P); 2^n enters through the exponent field.  x is clamped
+// at -125 so the result stays a normal float (2^-125 rounds to 0 in fp16 P).
+CEB_DEV float ex2_poly(float x) {
+    x = fmaxf(x, -125.0f);
+    const float t = x + 12582912.0f;
+    const float n = t - 12582912.0f;
+    const float f = x - n;
+    float p = 0.009570101276040077f;
+    p = fmaf(p, f, 0.05591785907745361f);
+    p = fmaf(p, f, 0.240247443318367f);
+    p = fmaf(p, f, 0.6931217908859253f);
+    p = fmaf(p, f, 0.9999992847442627f);
+    const uint32_t e = (uint32_t)(__float_as_int(t) - 0x4B400000) << 23;  // n in the exponent field
+    return __uint_as_float(__float_as_uint(p) + e);
+}

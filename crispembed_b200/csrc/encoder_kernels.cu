@@ -145,6 +145,10 @@ CEB_DEV float ex2_approx(float x) {  // MUFU 2^x (ex2(-inf) = 0)
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
+#ifndef CEB_ATTN_POLY_J
+#define CEB_ATTN_POLY_J 0xC0  // key n-tiles (bit j) whose exponentials use ex2_poly instead of MUFU
+#endif
+
 CEB_DEV void cp_async16(uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
@@ -277,10 +281,18 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         uint32_t pf[4][4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float p0 = ex2_approx(fmaf(s[j][0], scale_log2, nm[0]));
-            const float p1 = ex2_approx(fmaf(s[j][1], scale_log2, nm[0]));
-            const float p2 = ex2_approx(fmaf(s[j][2], scale_log2, nm[1]));
-            const float p3 = ex2_approx(fmaf(s[j][3], scale_log2, nm[1]));
+            float p0, p1, p2, p3;
+            if ((CEB_ATTN_POLY_J >> j) & 1) {
+                p0 = ex2_poly(fmaf(s[j][0], scale_log2, nm[0]));
+                p1 = ex2_poly(fmaf(s[j][1], scale_log2, nm[0]));
+                p2 = ex2_poly(fmaf(s[j][2], scale_log2, nm[1]));
+                p3 = ex2_poly(fmaf(s[j][3], scale_log2, nm[1]));
+            } else {
+                p0 = ex2_approx(fmaf(s[j][0], scale_log2, nm[0]));
+                p1 = ex2_approx(fmaf(s[j][1], scale_log2, nm[0]));
+                p2 = ex2_approx(fmaf(s[j][2], scale_log2, nm[1]));
+                p3 = ex2_approx(fmaf(s[j][3], scale_log2, nm[1]));
+            }
             rs[0] += p0 + p1;
             rs[1] += p2 + p3;
             const int kk = j >> 1, hi = j & 1;
@@ -294,12 +306,14 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
             l_r[r] = l_r[r] * corr[r] + rs[r];
             m_r[r] = mx[r];
         }
+        if (__any_sync(0xffffffffu, corr[0] != 1.0f || corr[1] != 1.0f)) {  // the running max moved
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            o[i][0] *= corr[0];
-            o[i][1] *= corr[0];
-            o[i][2] *= corr[1];
-            o[i][3] *= corr[1];
+            for (int i = 0; i < 8; ++i) {
+                o[i][0] *= corr[0];
+                o[i][1] *= corr[0];
+                o[i][2] *= corr[1];
+                o[i][3] *= corr[1];
+            }
         }
         // O += P V : k = 64 keys (4 steps of 16), n = 64 dims (8 tiles of 8)
 #pragma unroll

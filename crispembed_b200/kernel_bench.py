@@ -3,6 +3,7 @@
     python -m crispembed_b200.kernel_bench gemm --type q8_0 --m 16384 --n 3072 --k 768 [--gelu] [--f16-out]
     python -m crispembed_b200.kernel_bench moe --T 65536 --type q4_k --zipf 1.2
     python -m crispembed_b200.kernel_bench route_ln --T 70825 --router-type q8_0
+    python -m crispembed_b200.kernel_bench attn --seqs 256 [--impl mma|tc]
 
 Used for the roofline numbers of single kernels and as the command that ncu
 captures (small cases: a few launches, a few GB at most).  Prints one JSON line.
@@ -128,6 +129,41 @@ def bench_route_ln(a):
             "gbs": nbytes / (ms / 1e3) / 1e9, "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / pk, "peak_source": src}
 
 
+def bench_attn(a):
+    """Varlen attention (ceb_attention_forward) on config-2 lengths: n_seqs sequences,
+    lengths U[lo, hi] seed 2, d = 64 * n_head, fp16 qkv N(0,1).  FLOPs: 4*L^2*d per
+    sequence (QK^T and PV)."""
+    import os
+
+    import numpy as np
+    import torch
+
+    from . import binding
+    if a.impl == "tc":
+        os.environ["CEB_ATTN_TC"] = "1"
+    rng = np.random.default_rng(2)
+    lens = rng.integers(a.lo, a.hi + 1, size=a.seqs).astype(np.int32)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).cuda()
+    rows, d = int(lens.sum()), 64 * a.heads
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qkv = torch.randn((rows, 3 * d), device="cuda", generator=g).to(torch.float16)
+    for _ in range(a.warmup):
+        binding.attention(qkv, cu, a.heads, int(lens.max()))
+    torch.cuda.synchronize()
+    ms_all = []
+    for _ in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        binding.attention(qkv, cu, a.heads, int(lens.max()))
+        e1.record()
+        torch.cuda.synchronize()
+        ms_all.append(e0.elapsed_time(e1))
+    ms = float(np.median(ms_all))
+    flops = 4.0 * float((lens.astype(np.float64) ** 2).sum()) * d
+    return {"kernel": "attention", "impl": a.impl, "seqs": a.seqs, "tokens": rows, "heads": a.heads, "ms": ms,
+            "tflops": flops / (ms / 1e3) / 1e12}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -163,8 +199,16 @@ def main(argv=None):
     r.add_argument("--router-type", default="q8_0", choices=["f32", "q8_0"])
     r.add_argument("--iters", type=int, default=20)
     r.add_argument("--warmup", type=int, default=3)
+    t = sub.add_parser("attn")
+    t.add_argument("--seqs", type=int, default=256)
+    t.add_argument("--lo", type=int, default=32)
+    t.add_argument("--hi", type=int, default=512)
+    t.add_argument("--heads", type=int, default=12)
+    t.add_argument("--impl", choices=["mma", "tc"], default="mma")
+    t.add_argument("--iters", type=int, default=20)
+    t.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
-    r = {"gemm": bench_gemm, "moe": bench_moe, "route_ln": bench_route_ln}[a.what](a)
+    r = {"gemm": bench_gemm, "moe": bench_moe, "route_ln": bench_route_ln, "attn": bench_attn}[a.what](a)
     print(json.dumps(r), flush=True)
     return 0
 
