@@ -72,6 +72,7 @@ def load_library(path: Optional[str] = None):
         "ceb_moe_ffn": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp, ctypes.c_size_t, vp],
                         ctypes.c_int),
         "ceb_moe_ffn_static": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_gguf_dequantize": ([ctypes.c_int, vp, ctypes.c_int64, ctypes.c_int64, vp], ctypes.c_int),
         "ceb_ep_create": ([ctypes.c_int] * 7, vp),
         "ceb_ep_ipc_handle": ([vp, vp], ctypes.c_int),
         "ceb_ep_connect": ([vp, vp], ctypes.c_int),
@@ -410,6 +411,15 @@ def attention(qkv, cu_seqlens, n_head: int, max_len: Optional[int] = None, strea
     out = torch.empty((rows, d), dtype=torch.float16, device=qkv.device)
     _check(lib.ceb_attention_forward(qkv.data_ptr(), rows, cu_seqlens.data_ptr(), n, max_len, d, n_head,
                                      out.data_ptr(), _stream_ptr(stream)), "ceb_attention_forward")
+    return out
+
+
+def gguf_dequantize(ggml_type: int, raw: np.ndarray, n_rows: int, k: int) -> np.ndarray:
+    """ceb_gguf_dequantize: host decoding of n_rows GGUF rows of k values to fp32."""
+    raw = np.ascontiguousarray(raw)
+    out = np.empty((n_rows, k), dtype=np.float32)
+    _check(load_library().ceb_gguf_dequantize(int(ggml_type), raw.ctypes.data, int(n_rows), int(k),
+                                              out.ctypes.data), "ceb_gguf_dequantize")
     return out
 
 

@@ -499,6 +499,16 @@ extern "C" int ceb_ep_attach(crispembed_context* ctx, ceb_ep* ep) {
     return ceb_model_ep_attach(&ctx->model, ep);
 }
 
+extern "C" int ceb_gguf_dequantize(int ggml_type, const void* h_src, int64_t n_rows, int64_t k, float* h_dst) {
+    const int64_t rb = ceb_ggml_row_bytes(ggml_type, k);
+    if (!h_src || !h_dst || n_rows < 0 || rb < 0)
+        return ceb_set_error(1, "gguf_dequantize: type %d with rows of %lld values unsupported", ggml_type,
+                             (long long)k);
+    const uint8_t* src = static_cast<const uint8_t*>(h_src);
+    for (int64_t r = 0; r < n_rows; ++r) ceb_ggml_dequant_row(ggml_type, src + r * rb, k, h_dst + r * k);
+    return 0;
+}
+
 extern "C" int ceb_pool_l2(const float* d_hidden, const int32_t* d_cu_seqlens, int n_seqs, int d, int out_dim,
                            float* d_out, void* stream) {
     if (!d_hidden || !d_cu_seqlens || !d_out || n_seqs < 0 || d <= 0) return ceb_set_error(1, "pool_l2: bad arguments");

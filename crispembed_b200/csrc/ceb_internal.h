@@ -11,7 +11,19 @@
 #include <vector>
 
 // ggml tensor types used on the path (values are ggml's enum)
-enum { CEB_GGML_F32 = 0, CEB_GGML_F16 = 1, CEB_GGML_Q8_0 = 8, CEB_GGML_Q4_K = 12 };
+enum {
+    CEB_GGML_F32 = 0, CEB_GGML_F16 = 1, CEB_GGML_Q4_0 = 2, CEB_GGML_Q4_1 = 3, CEB_GGML_Q5_0 = 6, CEB_GGML_Q5_1 = 7,
+    CEB_GGML_Q8_0 = 8, CEB_GGML_Q4_K = 12, CEB_GGML_Q5_K = 13, CEB_GGML_Q6_K = 14, CEB_GGML_IQ4_NL = 20,
+    CEB_GGML_IQ4_XS = 23, CEB_GGML_BF16 = 30,
+};
+
+// GGUF block formats (gguf_quants.cpp): bytes of a k-value row (-1: unsupported type
+// or k not a whole number of blocks), host decoding of one row to fp32, and the
+// types the Q8_0 GEMM path runs after a re-encoding into Q8_0 blocks (Q8_0 itself,
+// IQ4_NL, IQ4_XS).
+int64_t ceb_ggml_row_bytes(int type, int64_t k);
+bool ceb_ggml_dequant_row(int type, const uint8_t* src, int64_t k, float* dst);
+bool ceb_ggml_as_q8_0_blocks(int type, const uint8_t* src, int64_t k, uint8_t* dst);
 
 // Device weight formats consumed by the grouped GEMM.  Weights are stored
 // tile-major: one contiguous block per (group, 128-row feature tile, 64-wide

@@ -66,16 +66,26 @@ double read_num(Cursor& c, int t) {
     return 0;
 }
 
+// Storage size of a row of ne0 values for every ggml type a GGUF may hold (ggml's
+// published block sizes), so a file opens even when some of its tensors use a
+// format this library does not compute with; the loader rejects those by name.
 uint64_t type_row_bytes(int type, int64_t ne0, bool* ok) {
-    switch (type) {
-        case 0: return (uint64_t)ne0 * 4;
-        case 1: return (uint64_t)ne0 * 2;
-        case 8: if (ne0 % 32) break; return (uint64_t)ne0 / 32 * 34;
-        case 12: if (ne0 % 256) break; return (uint64_t)ne0 / 256 * 144;
-        case 24: return (uint64_t)ne0;       // I8
-        case 26: return (uint64_t)ne0 * 4;   // I32
-        case 30: return (uint64_t)ne0 * 2;   // BF16
-    }
+    struct B {
+        int type, block, bytes;
+    };
+    static const B kSizes[] = {
+        {0, 1, 4},      {1, 1, 2},      {2, 32, 18},     {3, 32, 20},     {6, 32, 22},     {7, 32, 24},
+        {8, 32, 34},    {9, 32, 40},    {10, 256, 84},   {11, 256, 110},  {12, 256, 144},  {13, 256, 176},
+        {14, 256, 210}, {15, 256, 292}, {16, 256, 66},   {17, 256, 74},   {18, 256, 98},   {19, 256, 50},
+        {20, 32, 18},   {21, 256, 110}, {22, 256, 82},   {23, 256, 136},  {24, 1, 1},      {25, 1, 2},
+        {26, 1, 4},     {27, 1, 8},     {28, 1, 8},      {29, 256, 56},   {30, 1, 2},      {34, 256, 54},
+        {35, 256, 66},
+    };
+    for (const B& b : kSizes)
+        if (b.type == type) {
+            if (ne0 % b.block) break;
+            return (uint64_t)(ne0 / b.block) * b.bytes;
+        }
     *ok = false;
     return 0;
 }

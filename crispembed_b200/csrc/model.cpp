@@ -66,7 +66,14 @@ struct Loader {
                 h[(size_t)i] = __half2float(__half(r));
             }
         } else {
-            return ceb_set_error(1, "tensor '%s': type %d not supported for a float table", t->name.c_str(), t->type);
+            // quantized tables (llama.cpp exports quantize the token embeddings): decoded row by row
+            const int64_t k = t->ne.empty() ? n : t->ne[0];
+            const int64_t rb = ceb_ggml_row_bytes(t->type, k);
+            if (rb < 0)
+                return ceb_set_error(1, "tensor '%s': type %d not supported for a float table", t->name.c_str(),
+                                     t->type);
+            const uint8_t* src = static_cast<const uint8_t*>(g.data(*t));
+            for (int64_t r = 0; r < n / k; ++r) ceb_ggml_dequant_row(t->type, src + r * rb, k, h.data() + r * k);
         }
         void* d = nullptr;
         if (cudaMalloc(&d, (size_t)n * 4) != cudaSuccess) return ceb_set_error(4, "out of device memory (%s)", t->name.c_str());
@@ -206,6 +213,32 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
             memcpy(cat.data() + rbytes, g.data(*k), (size_t)rbytes);
             memcpy(cat.data() + 2 * rbytes, g.data(*v), (size_t)rbytes);
             rc = ceb_repack_weights(&Ly.qkv, q->type, cat.data(), 1, 3 * d, d, st);
+        } else if (q && k && v) {
+            // mixed formats (llama.cpp's K-quant mixes give attn_v its own type): rows
+            // re-encoded as Q8_0 blocks when every part allows it, else decoded to fp32
+            const ceb_gguf_tensor* parts[3] = {q, k, v};
+            auto q8able = [](int t) { return t == CEB_GGML_Q8_0 || t == CEB_GGML_IQ4_NL || t == CEB_GGML_IQ4_XS; };
+            const bool as_q8 = q8able(q->type) && q8able(k->type) && q8able(v->type);
+            const int64_t orb = as_q8 ? ceb_ggml_row_bytes(CEB_GGML_Q8_0, d) : (int64_t)d * 4;
+            std::vector<uint8_t> cat((size_t)(3 * d * orb));
+            for (int j = 0; j < 3 && !rc; ++j) {
+                const int64_t rb = ceb_ggml_row_bytes(parts[j]->type, d);
+                if (rb < 0 || parts[j]->ne.size() < 2 || parts[j]->ne[0] != d || parts[j]->ne[1] != d) {
+                    rc = ceb_set_error(1, "layer %d: attention weight of type %d / shape unsupported", il,
+                                       parts[j]->type);
+                    break;
+                }
+                const uint8_t* src = static_cast<const uint8_t*>(g.data(*parts[j]));
+                for (int r = 0; r < d; ++r) {
+                    uint8_t* dst = cat.data() + ((size_t)j * d + r) * orb;
+                    if (as_q8)
+                        ceb_ggml_as_q8_0_blocks(parts[j]->type, src + r * rb, d, dst);
+                    else
+                        ceb_ggml_dequant_row(parts[j]->type, src + r * rb, d, reinterpret_cast<float*>(dst));
+                }
+            }
+            if (!rc)
+                rc = ceb_repack_weights(&Ly.qkv, as_q8 ? CEB_GGML_Q8_0 : CEB_GGML_F32, cat.data(), 1, 3 * d, d, st);
         } else {
             rc = ceb_set_error(1, "layer %d: missing attention q/k/v weights", il);
         }

@@ -123,27 +123,39 @@ inline void q4k_scale_min(int j, const uint8_t* s, int* sc, int* mn) {
 }
 }  // namespace
 
-int64_t ceb_ggml_row_bytes(int type, int64_t k) {
-    switch (type) {
-        case CEB_GGML_F32: return k * 4;
-        case CEB_GGML_F16: return k * 2;
-        case CEB_GGML_Q8_0: return k % 32 ? -1 : k / 32 * 34;
-        case CEB_GGML_Q4_K: return k % 256 ? -1 : k / 256 * 144;
-    }
-    return -1;
-}
-
 // GGUF rows -> tile-major device blocks (layout in ceb_internal.h).  Values are
 // not changed: Q8_0 keeps its int8 quants and fp16 scales, Q4_K its nibbles with
 // (d*sc, dmin*m) computed per sub-block exactly as ggml's dequantizer does, F32
-// weights are rounded to fp16 (nearest even).
+// weights are rounded to fp16 (nearest even).  IQ4_NL / IQ4_XS rows are first
+// re-encoded as Q8_0 blocks (codebook value as int8, block scale as fp16), every
+// other block format is decoded to fp32 and rounded to fp16 (gguf_quants.cpp).
 int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int n_groups, int n_out, int k,
                        cudaStream_t stream) {
-    const int64_t rb = ceb_ggml_row_bytes(ggml_type, k);
+    int64_t rb = ceb_ggml_row_bytes(ggml_type, k);
     if (rb < 0) return ceb_set_error(2, "repack: unsupported type %d for k=%d", ggml_type, k);
     if (n_out % 128 || k % 64)
         return ceb_set_error(2, "repack: n_out=%d must be a multiple of 128 and k=%d of 64", n_out, k);
     const uint8_t* src = static_cast<const uint8_t*>(host_raw);
+    const int64_t rows = (int64_t)n_groups * n_out;
+    std::vector<uint8_t> conv;  // re-encoded (Q8_0 blocks) or decoded (fp32) rows
+    if (ggml_type == CEB_GGML_IQ4_NL || ggml_type == CEB_GGML_IQ4_XS) {
+        const int64_t qrb = ceb_ggml_row_bytes(CEB_GGML_Q8_0, k);
+        conv.resize((size_t)(rows * qrb));
+        for (int64_t r = 0; r < rows; ++r)
+            if (!ceb_ggml_as_q8_0_blocks(ggml_type, src + r * rb, k, conv.data() + r * qrb))
+                return ceb_set_error(2, "repack: type %d rows of %d values cannot be re-encoded", ggml_type, k);
+        src = conv.data();
+        rb = qrb;
+        ggml_type = CEB_GGML_Q8_0;
+    } else if (ggml_type != CEB_GGML_Q8_0 && ggml_type != CEB_GGML_Q4_K && ggml_type != CEB_GGML_F16 &&
+               ggml_type != CEB_GGML_F32) {
+        conv.resize((size_t)(rows * k * 4));
+        for (int64_t r = 0; r < rows; ++r)
+            ceb_ggml_dequant_row(ggml_type, src + r * rb, k, reinterpret_cast<float*>(conv.data()) + r * k);
+        src = conv.data();
+        rb = (int64_t)k * 4;
+        ggml_type = CEB_GGML_F32;
+    }
     ceb_wplane w;
     w.n_groups = n_groups;
     w.n_out = n_out;

@@ -29,15 +29,28 @@ DEFAULT_ALIGNMENT = 32
 # gguf value types
 T_UINT8, T_INT8, T_UINT16, T_INT16, T_UINT32, T_INT32, T_FLOAT32, T_BOOL, T_STRING, T_ARRAY, T_UINT64, T_INT64, T_FLOAT64 = range(13)
 
-# ggml tensor types used on this path
+# ggml tensor types the library reads (ggml's numbering)
 GGML_F32 = 0
 GGML_F16 = 1
+GGML_Q4_0 = 2
+GGML_Q4_1 = 3
+GGML_Q5_0 = 6
+GGML_Q5_1 = 7
 GGML_Q8_0 = 8
 GGML_Q4_K = 12
+GGML_Q5_K = 13
+GGML_Q6_K = 14
+GGML_IQ4_NL = 20
+GGML_IQ4_XS = 23
+GGML_BF16 = 30
 
 # (block elements, block bytes)
-BLOCK_INFO = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144)}
-TYPE_NAMES = {GGML_F32: "F32", GGML_F16: "F16", GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K"}
+BLOCK_INFO = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_Q4_0: (32, 18), GGML_Q4_1: (32, 20), GGML_Q5_0: (32, 22),
+              GGML_Q5_1: (32, 24), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144), GGML_Q5_K: (256, 176),
+              GGML_Q6_K: (256, 210), GGML_IQ4_NL: (32, 18), GGML_IQ4_XS: (256, 136), GGML_BF16: (1, 2)}
+TYPE_NAMES = {GGML_F32: "F32", GGML_F16: "F16", GGML_Q4_0: "Q4_0", GGML_Q4_1: "Q4_1", GGML_Q5_0: "Q5_0",
+              GGML_Q5_1: "Q5_1", GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K", GGML_Q5_K: "Q5_K", GGML_Q6_K: "Q6_K",
+              GGML_IQ4_NL: "IQ4_NL", GGML_IQ4_XS: "IQ4_XS", GGML_BF16: "BF16"}
 
 _SCALAR_FMT = {
     T_UINT8: "<B", T_INT8: "<b", T_UINT16: "<H", T_INT16: "<h", T_UINT32: "<I", T_INT32: "<i",

@@ -61,6 +61,9 @@ class ModelSpec:
     router_wtype: Optional[int] = None  # None = same as wtype (the converter quantizes the router too)
     moe_bias: bool = True
     seed: int = 0
+    # per-tensor block types by name suffix ("attn.o.weight", "ffn.expert_fc2.weight",
+    # "token_embd.weight", ...), for mixed-format files such as llama.cpp's Q4_K_M
+    type_overrides: Dict[str, int] = field(default_factory=dict)
 
     def is_moe(self, il: int) -> bool:
         return self.n_experts > 0 and self.moe_every > 0 and il % self.moe_every == self.moe_every - 1
@@ -123,6 +126,9 @@ def write_model(path: str, spec: ModelSpec, tokenizer=None) -> List[str]:
     def add(name, np_shape, gtype, gen):
         ne = tuple(reversed(np_shape))
         order.append(name)
+        for suffix, t in spec.type_overrides.items():
+            if name.endswith(suffix):
+                gtype = t
         w.add_tensor(name, ne, gtype, lambda: quantize(gen(), gtype))
 
     add("token_embd.weight", (spec.n_vocab, d), G.GGML_F32, lambda: normal((spec.n_vocab, d)))

@@ -177,6 +177,15 @@ CEB_API int ceb_moe_ffn_ep(const ceb_moe_layer* layer, ceb_ep* ep, const void* d
                            float* d_y, void* d_workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Host decoding of GGUF weight rows to fp32 (no device needed): F32, F16, BF16,
+ * Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K, IQ4_NL, IQ4_XS -- ggml's block
+ * formats, as the model loader decodes tensors the GEMM does not read in their
+ * stored form.  h_src holds n_rows rows of k values; returns 0, or 1 for an
+ * unsupported type or a k that is not a whole number of blocks.
+ */
+CEB_API int ceb_gguf_dequantize(int ggml_type, const void* h_src, int64_t n_rows, int64_t k, float* h_dst);
+
+/*
  * The text tokenizer of a GGUF on its own (no device needed): the family the
  * reference would pick (src/tokenizer.h:37-52), WordPiece or SentencePiece
  * Unigram, wrapping and truncation to max_tokens as the text ABI applies them.

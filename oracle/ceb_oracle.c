@@ -35,7 +35,10 @@
 #endif
 
 enum { CEO_EXACT = 0, CEO_GGML = 1, CEO_F16 = 2 };
-enum { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12 };
+enum {
+    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13,
+    T_Q6_K = 14, T_IQ4_NL = 20, T_IQ4_XS = 23, T_BF16 = 30
+};
 
 #define QK8_0 32
 #define QK_K 256
@@ -100,6 +103,10 @@ static inline float round_f16(float x) { return ceo_f16_to_f32(ceo_f32_to_f16(x)
 static inline uint16_t rd_u16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
 
 /* ------------------------------------------------------------- dequant --- */
+/* ggml's published block formats.  IQ4_NL / IQ4_XS index ggml's non-linear
+ * 16-value codebook (kvalues_iq4nl). */
+static const int8_t IQ4NL_VALUES[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+int64_t ceo_row_bytes(int type, int64_t k);
 /* Q4_K 6-bit scale/min unpacking: sub-block j < 4 keeps its 6 bits in bytes
  * j / j+4; j >= 4 splits 4 low bits in byte j+4 and 2 high bits in the top of
  * bytes j-4 / j (the published Q4_K block layout). */
@@ -125,6 +132,86 @@ void ceo_dequant_row(int type, const uint8_t *src, int64_t k, float *dst) {
             const int8_t *q = (const int8_t *)(blk + 2);
             for (int j = 0; j < QK8_0; j++) dst[b * QK8_0 + j] = (float)q[j] * d;
         }
+    } else if (type == T_BF16) {
+        for (int64_t i = 0; i < k; i++) {
+            uint32_t u = (uint32_t)rd_u16(src + 2 * i) << 16;
+            memcpy(dst + i, &u, 4);
+        }
+    } else if (type == T_Q4_0 || type == T_Q4_1 || type == T_Q5_0 || type == T_Q5_1 || type == T_IQ4_NL) {
+        /* 32-value blocks: fp16 d (+ fp16 m for _1), (+ uint32 fifth bits for Q5), 16 nibble bytes
+           (value j in the low nibble of byte j, value j+16 in its high nibble) */
+        const int64_t bytes = ceo_row_bytes(type, 32);
+        for (int64_t b = 0; b < k / 32; b++) {
+            const uint8_t *blk = src + b * bytes;
+            float d = ceo_f16_to_f32(rd_u16(blk)), m = 0.0f;
+            const uint8_t *qs = blk + 2;
+            uint32_t qh = 0;
+            if (type == T_Q4_1 || type == T_Q5_1) { m = ceo_f16_to_f32(rd_u16(blk + 2)); qs += 2; }
+            if (type == T_Q5_0 || type == T_Q5_1) { memcpy(&qh, qs, 4); qs += 4; }
+            for (int j = 0; j < 32; j++) {
+                int q = j < 16 ? (qs[j] & 0xF) : (qs[j - 16] >> 4);
+                float v;
+                if (type == T_Q4_0) v = d * (float)(q - 8);
+                else if (type == T_Q4_1) v = d * (float)q + m;
+                else if (type == T_Q5_0) v = d * (float)((q | (int)(((qh >> j) & 1) << 4)) - 16);
+                else if (type == T_Q5_1) v = d * (float)(q | (int)(((qh >> j) & 1) << 4)) + m;
+                else v = d * (float)IQ4NL_VALUES[q];
+                dst[b * 32 + j] = v;
+            }
+        }
+    } else if (type == T_IQ4_XS) {
+        for (int64_t b = 0; b < k / QK_K; b++) {
+            const uint8_t *blk = src + b * 136;
+            float d = ceo_f16_to_f32(rd_u16(blk));
+            uint16_t sh = rd_u16(blk + 2);
+            for (int ib = 0; ib < 8; ib++) {
+                int ls = ((blk[4 + ib / 2] >> (4 * (ib % 2))) & 0xF) | (((sh >> (2 * ib)) & 3) << 4);
+                float dl = d * (float)(ls - 32);
+                const uint8_t *qs = blk + 8 + 16 * ib;
+                for (int j = 0; j < 16; j++) {
+                    dst[b * QK_K + 32 * ib + j] = dl * (float)IQ4NL_VALUES[qs[j] & 0xF];
+                    dst[b * QK_K + 32 * ib + j + 16] = dl * (float)IQ4NL_VALUES[qs[j] >> 4];
+                }
+            }
+        }
+    } else if (type == T_Q5_K) {
+        for (int64_t b = 0; b < k / QK_K; b++) {
+            const uint8_t *blk = src + b * 176;
+            float d = ceo_f16_to_f32(rd_u16(blk)), dmin = ceo_f16_to_f32(rd_u16(blk + 2));
+            const uint8_t *sc = blk + 4, *qh = blk + 16, *qs = blk + 48;
+            for (int c = 0; c < 4; c++) {
+                int s0, m0, s1, m1;
+                q4k_scale_min(2 * c, sc, &s0, &m0);
+                q4k_scale_min(2 * c + 1, sc, &s1, &m1);
+                for (int l = 0; l < 32; l++) {
+                    int lo = (qs[32 * c + l] & 0xF) | (((qh[l] >> (2 * c)) & 1) << 4);
+                    int hi = (qs[32 * c + l] >> 4) | (((qh[l] >> (2 * c + 1)) & 1) << 4);
+                    dst[b * QK_K + 64 * c + l] = d * (float)s0 * (float)lo - dmin * (float)m0;
+                    dst[b * QK_K + 64 * c + 32 + l] = d * (float)s1 * (float)hi - dmin * (float)m1;
+                }
+            }
+        }
+    } else if (type == T_Q6_K) {
+        for (int64_t b = 0; b < k / QK_K; b++) {
+            const uint8_t *blk = src + b * 210;
+            float d = ceo_f16_to_f32(rd_u16(blk + 208));
+            for (int n = 0; n < 2; n++) {
+                const uint8_t *ql = blk + 64 * n, *qh = blk + 128 + 32 * n;
+                const int8_t *sc = (const int8_t *)(blk + 192 + 8 * n);
+                float *y = dst + b * QK_K + 128 * n;
+                for (int l = 0; l < 32; l++) {
+                    int is = l / 16;
+                    int q1 = (int)((ql[l] & 0xF) | ((qh[l] & 3) << 4)) - 32;
+                    int q2 = (int)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                    int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                    int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                    y[l] = d * (float)sc[is] * (float)q1;
+                    y[l + 32] = d * (float)sc[is + 2] * (float)q2;
+                    y[l + 64] = d * (float)sc[is + 4] * (float)q3;
+                    y[l + 96] = d * (float)sc[is + 6] * (float)q4;
+                }
+            }
+        }
     } else if (type == T_Q4_K) {
         for (int64_t b = 0; b < k / QK_K; b++) {
             const uint8_t *blk = src + b * Q4_K_BYTES;
@@ -149,8 +236,17 @@ int64_t ceo_row_bytes(int type, int64_t k) {
     switch (type) {
         case T_F32: return k * 4;
         case T_F16: return k * 2;
+        case T_BF16: return k * 2;
+        case T_Q4_0: return k / 32 * 18;
+        case T_Q4_1: return k / 32 * 20;
+        case T_Q5_0: return k / 32 * 22;
+        case T_Q5_1: return k / 32 * 24;
         case T_Q8_0: return k / QK8_0 * Q8_0_BYTES;
         case T_Q4_K: return k / QK_K * Q4_K_BYTES;
+        case T_Q5_K: return k / QK_K * 176;
+        case T_Q6_K: return k / QK_K * 210;
+        case T_IQ4_NL: return k / 32 * 18;
+        case T_IQ4_XS: return k / QK_K * 136;
     }
     return -1;
 }
@@ -298,6 +394,36 @@ void ceo_matmul(int type, const uint8_t *w, int64_t n_out, int64_t k, const floa
         free(xq);
         return;
     }
+    float *xa = NULL;
+    if (mode == CEO_GGML && type != T_F32 && type != T_F16 && type != T_BF16) {
+        /* other block formats: the activations are re-quantized to the format's ggml
+         * vec_dot type (Q8_0-valued for the 32-value formats, Q8_K for the 256-value
+         * ones) and dotted in float with the decoded weights.  The activation
+         * rounding is ggml's; the accumulation order of its integer dots is not
+         * reproduced (float rounding differences only). */
+        const int kq = (type == T_Q5_K || type == T_Q6_K || type == T_IQ4_XS) ? 1 : 0;
+        const int64_t qb = kq ? k / QK_K * Q8_K_BYTES : k / QK8_0 * Q8_0_BYTES;
+        xa = (float *)malloc((size_t)(m_rows * k) * sizeof(float));
+#pragma omp parallel for schedule(static)
+        for (int64_t m = 0; m < m_rows; m++) {
+            uint8_t *tmp = (uint8_t *)malloc((size_t)qb);
+            float *xr = xa + m * k;
+            if (kq) {
+                ceo_quant_act_q8_k(x + m * k, k, tmp);
+                for (int64_t b = 0; b < k / QK_K; b++) {
+                    float d;
+                    memcpy(&d, tmp + b * Q8_K_BYTES, 4);
+                    const int8_t *q = (const int8_t *)(tmp + b * Q8_K_BYTES + 4);
+                    for (int j = 0; j < QK_K; j++) xr[b * QK_K + j] = d * (float)q[j];
+                }
+            } else {
+                ceo_quant_act_q8_0(x + m * k, k, tmp);
+                ceo_dequant_row(T_Q8_0, tmp, k, xr);
+            }
+            free(tmp);
+        }
+        x = xa;
+    }
     /* exact / f16 / (ggml with float weights): dequantize weights once */
     float *wf = (float *)malloc((size_t)(n_out * k) * sizeof(float));
 #pragma omp parallel for schedule(static)
@@ -329,6 +455,7 @@ void ceo_matmul(int type, const uint8_t *w, int64_t n_out, int64_t k, const floa
             out[m * n_out + n] = bias ? s + bias[n] : s;
         }
     free(xf);
+    free(xa);
     free(wf);
 }
 
@@ -451,10 +578,12 @@ void ceo_route(const float *logits, int64_t T, int E, int k, int32_t *ids, float
  * fc1 is [E][F][d], fc2 is [E][d][F] (rows of `wtype`); router is [E][d].
  * If ids_in is non-NULL the routing is taken from it (and wts_in) instead of
  * being computed, so the expert math can be checked on a given routing. */
-void ceo_moe_ffn(const float *x, int64_t T, int d, int E, int k, int F, int router_type, const uint8_t *router,
-                 int wtype, const uint8_t *fc1, const uint8_t *fc2, const float *bias, int mode,
-                 const int32_t *ids_in, const float *wts_in, float *y, int32_t *ids_out, float *wts_out,
-                 float *logits_out) {
+/* fc1 and fc2 may use different block formats (wtype2: fc2's; llama.cpp K-quant
+ * mixes keep the down projection at a wider type) */
+void ceo_moe_ffn2(const float *x, int64_t T, int d, int E, int k, int F, int router_type, const uint8_t *router,
+                  int wtype, const uint8_t *fc1, int wtype2, const uint8_t *fc2, const float *bias, int mode,
+                  const int32_t *ids_in, const float *wts_in, float *y, int32_t *ids_out, float *wts_out,
+                  float *logits_out) {
     float *logits = (float *)malloc((size_t)(T * E) * sizeof(float));
     int rmode = mode == CEO_F16 ? CEO_GGML : mode; /* the device router reproduces the ggml router */
     ceo_matmul(router_type, router, E, d, x, T, NULL, logits, rmode);
@@ -469,7 +598,7 @@ void ceo_moe_ffn(const float *x, int64_t T, int d, int E, int k, int F, int rout
     }
     free(logits);
 
-    const int64_t rb1 = ceo_row_bytes(wtype, d), rb2 = ceo_row_bytes(wtype, F);
+    const int64_t rb1 = ceo_row_bytes(wtype, d), rb2 = ceo_row_bytes(wtype2, F);
     float *down = (float *)calloc((size_t)(T * k) * d, sizeof(float));
     /* gather rows per expert (stable in token order) */
     int64_t *rows = (int64_t *)malloc((size_t)(T * k) * sizeof(int64_t));
@@ -485,7 +614,7 @@ void ceo_moe_ffn(const float *x, int64_t T, int d, int E, int k, int F, int rout
         for (int64_t i = 0; i < n; i++) memcpy(xe + i * d, x + (rows[i] / k) * d, (size_t)d * sizeof(float));
         ceo_matmul(wtype, fc1 + (int64_t)e * F * rb1, F, d, xe, n, NULL, he, mode);
         ceo_gelu_erf(he, n * F);
-        ceo_matmul(wtype, fc2 + (int64_t)e * d * rb2, d, F, he, n, NULL, oe, mode);
+        ceo_matmul(wtype2, fc2 + (int64_t)e * d * rb2, d, F, he, n, NULL, oe, mode);
         for (int64_t i = 0; i < n; i++) memcpy(down + rows[i] * d, oe + i * d, (size_t)d * sizeof(float));
         free(xe);
         free(he);
@@ -506,6 +635,14 @@ void ceo_moe_ffn(const float *x, int64_t T, int d, int E, int k, int F, int rout
 /* Mean pool + L2 normalise per sequence (src/crispembed.cpp:1822-1846):
  * sequential float accumulation t-outer / h-inner, divide by the count, then
  * p /= sqrtf(max(sum p^2, 1e-12)). */
+void ceo_moe_ffn(const float *x, int64_t T, int d, int E, int k, int F, int router_type, const uint8_t *router,
+                 int wtype, const uint8_t *fc1, const uint8_t *fc2, const float *bias, int mode,
+                 const int32_t *ids_in, const float *wts_in, float *y, int32_t *ids_out, float *wts_out,
+                 float *logits_out) {
+    ceo_moe_ffn2(x, T, d, E, k, F, router_type, router, wtype, fc1, wtype, fc2, bias, mode, ids_in, wts_in, y,
+                 ids_out, wts_out, logits_out);
+}
+
 void ceo_pool_l2(const float *hidden, const int32_t *cu_seqlens, int n_seqs, int d, float *out) {
     for (int s = 0; s < n_seqs; s++) {
         float *p = out + (int64_t)s * d;

@@ -25,6 +25,10 @@ LIB_PATH = os.path.join(HERE, "libceb_oracle.so")
 
 EXACT, GGML, F16 = 0, 1, 2
 T_F32, T_F16, T_Q8_0, T_Q4_K = 0, 1, 8, 12
+T_Q4_0, T_Q4_1, T_Q5_0, T_Q5_1, T_Q5_K, T_Q6_K, T_IQ4_NL, T_IQ4_XS, T_BF16 = 2, 3, 6, 7, 13, 14, 20, 23, 30
+_BLOCK = {T_F32: (1, 4), T_F16: (1, 2), T_BF16: (1, 2), T_Q4_0: (32, 18), T_Q4_1: (32, 20), T_Q5_0: (32, 22),
+          T_Q5_1: (32, 24), T_Q8_0: (32, 34), T_Q4_K: (256, 144), T_Q5_K: (256, 176), T_Q6_K: (256, 210),
+          T_IQ4_NL: (32, 18), T_IQ4_XS: (256, 136)}
 
 _lib = None
 
@@ -66,6 +70,9 @@ def lib():
         L.ceo_moe_ffn.argtypes = [_fp, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int, _up, ctypes.c_int, _up, _up, _fp, ctypes.c_int, _ip, _fp, _fp, _ip,
                                   _fp, _fp]
+        L.ceo_moe_ffn2.argtypes = [_fp, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_int, _up, ctypes.c_int, _up, ctypes.c_int, _up, _fp, ctypes.c_int, _ip,
+                                   _fp, _fp, _ip, _fp, _fp]
         L.ceo_pool_l2.argtypes = [_fp, _ip, ctypes.c_int, ctypes.c_int, _fp]
         L.ceo_truncate_renorm.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp]
         L.ceo_set_threads.argtypes = [ctypes.c_int]
@@ -102,7 +109,8 @@ def f16_round(x: np.ndarray) -> np.ndarray:
 
 
 def row_bytes(t: int, k: int) -> int:
-    return {T_F32: 4 * k, T_F16: 2 * k, T_Q8_0: k // 32 * 34, T_Q4_K: k // 256 * 144}[t]
+    be, bb = _BLOCK[t]
+    return k // be * bb
 
 
 def dequant(t: int, raw: np.ndarray, k: int) -> np.ndarray:
@@ -158,8 +166,10 @@ def route(logits: np.ndarray, k: int):
 
 def moe_ffn(x: np.ndarray, E: int, k: int, F: int, router_type: int, router_raw: np.ndarray, wtype: int,
             fc1_raw: np.ndarray, fc2_raw: np.ndarray, bias: Optional[np.ndarray], mode: int,
-            ids_in: Optional[np.ndarray] = None, wts_in: Optional[np.ndarray] = None):
-    """Returns (y [T,d], ids [T,k], gate weights [T,k], router logits [T,E])."""
+            ids_in: Optional[np.ndarray] = None, wts_in: Optional[np.ndarray] = None,
+            wtype2: Optional[int] = None):
+    """Returns (y [T,d], ids [T,k], gate weights [T,k], router logits [T,E]).
+    wtype2: fc2's block format when it differs from fc1's."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     T, d = x.shape
     y = np.empty((T, d), dtype=np.float32)
@@ -171,8 +181,8 @@ def moe_ffn(x: np.ndarray, E: int, k: int, F: int, router_type: int, router_raw:
     p2, k2 = _u(fc2_raw)
     ids_in = None if ids_in is None else np.ascontiguousarray(ids_in, dtype=np.int32)
     wts_in = None if wts_in is None else np.ascontiguousarray(wts_in, dtype=np.float32)
-    lib().ceo_moe_ffn(_f(x), T, d, E, k, F, router_type, pr, wtype, p1, p2, _f(bias), mode, _i(ids_in), _f(wts_in),
-                      _f(y), _i(ids), _f(w), _f(logits))
+    lib().ceo_moe_ffn2(_f(x), T, d, E, k, F, router_type, pr, wtype, p1, wtype if wtype2 is None else wtype2, p2,
+                       _f(bias), mode, _i(ids_in), _f(wts_in), _f(y), _i(ids), _f(w), _f(logits))
     return y, ids, w, logits
 
 
@@ -220,10 +230,14 @@ class OracleModel:
     moe_layers: List[int] = field(default_factory=list)
 
     def f32(self, name: str) -> Optional[np.ndarray]:
+        """A float table; block-format tables (llama.cpp exports quantize the token
+        embeddings) are decoded row by row."""
         if name not in self.t:
             return None
-        assert self.types[name] == T_F32
-        return np.ascontiguousarray(self.t[name]).view(np.float32)
+        if self.types[name] == T_F32:
+            return np.ascontiguousarray(self.t[name]).view(np.float32)
+        k = int(self.shapes[name][0])
+        return dequant(self.types[name], self.t[name], k).reshape(-1)
 
 
 def load_model(path: str) -> OracleModel:
@@ -318,7 +332,8 @@ def encode(model: OracleModel, ids: np.ndarray, lens: np.ndarray, mode: int = GG
             F = int(model.shapes[f1][1])
             ffn, rid, rw, logits = moe_ffn(cur, E, K, F, model.types[gname], model.t[gname], model.types[f1],
                                            model.t[f1], model.t[p + "ffn.expert_fc2.weight"],
-                                           model.f32(p + "ffn.moe_bias"), mode)
+                                           model.f32(p + "ffn.moe_bias"), mode,
+                                           wtype2=model.types[p + "ffn.expert_fc2.weight"])
             if dump is not None:
                 dump[f"router_in_{il}"] = cur.copy()
                 dump[f"ids_{il}"] = rid

@@ -2,6 +2,9 @@
 
     python tests/golden/make_golden.py
 
+gguf_variants.npz -- blocks of the llama.cpp community / registry formats (Q4_0,
+                Q4_1, Q5_0, Q5_1, Q5_K, Q6_K, IQ4_NL, IQ4_XS, BF16) from
+                crispembed_b200.quant and gguf-py's decoding of them.
 formats.npz  -- pins the GGUF block formats against gguf-py, the library the
                 reference's converter calls (models/convert-bert-to-gguf.py:68-77):
                 * q8_x / q8_blocks / q8_deq: a seeded float matrix, gguf-py's Q8_0
@@ -39,6 +42,29 @@ def make_formats():
                         q4_deq=q4_deq.astype(np.float32), gguf_version=np.array(getattr(gguf, "__version__", "?")))
 
 
+def make_variants():
+    """gguf_variants.npz -- for each block format of the community / registry GGUFs:
+    our encoder's blocks of a seeded matrix and gguf-py's decoding of them."""
+    import gguf
+    from gguf import quants
+
+    from crispembed_b200 import gguf_io as G
+    from crispembed_b200 import quant
+    rng = np.random.default_rng(4321)
+    x = (rng.standard_normal((8, 512), dtype=np.float32) * 0.05).astype(np.float32)
+    x[0, :256] = 0.0                        # all-zero super-block
+    x[1, :32] = np.linspace(-1, 1, 32)      # a wide block
+    out = {"x": x}
+    for name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q5_K", "Q6_K", "IQ4_NL", "IQ4_XS", "BF16"):
+        t = getattr(G, "GGML_" + name)
+        blocks = quant.quantize(x, t).view(np.uint8).reshape(x.shape[0], -1)
+        out[name + "_blocks"] = blocks
+        out[name + "_deq"] = quants.dequantize(blocks, getattr(gguf.GGMLQuantizationType, name)).reshape(
+            x.shape).astype(np.float32)
+    out["gguf_version"] = np.array(getattr(gguf, "__version__", "?"))
+    np.savez_compressed(os.path.join(HERE, "gguf_variants.npz"), **out)
+
+
 def make_oracle():
     import tempfile
 
@@ -62,5 +88,6 @@ def make_oracle():
 
 if __name__ == "__main__":
     make_formats()
+    make_variants()
     make_oracle()
     print("wrote", os.listdir(HERE))

@@ -117,3 +117,28 @@ def test_other_weight_types(cuda, oracle, tmp_path, wtype_name):
     m.close()
     ref = oracle.encode(oracle.load_model(path), ids, lens, oracle.GGML)
     _check(emb, ref)
+
+
+# GGUF files as llama.cpp writes them beside the reference converter's: a Q4_K_M-like
+# mix (Q4_K, with Q6_K for attn_v, the second FFN matrices and the token table) and
+# an IQ4_XS file (IQ4_NL attn_v, Q4_0 token table); routers stay F32 as llama.cpp
+# keeps ffn_gate_inp.  Mixed q/k/v formats load through a common form.
+MIXES = {
+    "q4_k_m": dict(wtype=12, router_wtype=0, type_overrides={
+        "attn.v.weight": 14, "ffn.expert_fc2.weight": 14, "ffn.fc2.weight": 14, "token_embd.weight": 14}),
+    "iq4_xs": dict(wtype=23, router_wtype=0, type_overrides={"attn.v.weight": 20, "token_embd.weight": 2}),
+    "legacy": dict(wtype=6, router_wtype=8, type_overrides={"attn.o.weight": 3, "ffn.expert_fc1.weight": 7}),
+}
+
+
+@pytest.mark.parametrize("mix", list(MIXES))
+def test_mixed_format_models_match_oracle(cuda, oracle, tmp_path, mix):
+    from crispembed_b200 import binding
+    path = str(tmp_path / f"{mix}.gguf")
+    synth.write_model(path, synth.tiny_spec(**MIXES[mix]))
+    m = binding.CrispEmbed(path)
+    ids, lens = synth.ids_ragged(8, 2, 100, seed=12, hi=1000)
+    emb = m.encode_ids(ids, lens)
+    m.close()
+    ref = oracle.encode(oracle.load_model(path), ids, lens, oracle.GGML)
+    _check(emb, ref)

@@ -14,6 +14,7 @@ import numpy as np
 import pytest
 
 from crispembed_b200 import quant
+from crispembed_b200 import gguf_io as G
 from crispembed_b200.gguf_io import GGML_F16, GGML_F32, GGML_Q4_K, GGML_Q8_0
 
 pytestmark = pytest.mark.gpu
@@ -127,3 +128,24 @@ def test_pair_and_single_cta_kernels_agree(cuda, tmp_path):
     subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=root, timeout=300)
     single = np.load(tmp_path / "single.npy")
     assert np.abs(single - pair_out).max() <= 2e-3 * max(1.0, float(np.abs(pair_out).max()))
+
+
+# llama.cpp community / registry formats: IQ4_NL and IQ4_XS run re-encoded as Q8_0
+# blocks (pair kernel for widths of 256), the others as fp16 planes (single-CTA
+# kernel).  IQ4_XS's sub-block scale d*(ls-32) is rounded to fp16 there, one
+# rounding the oracle's fp16(dequant) does not make: wider tolerance for it.
+VARIANT_CASES = [(getattr(G, "GGML_" + n), 256, 512, 300) for n in
+                 ("Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q5_K", "Q6_K", "IQ4_NL", "IQ4_XS", "BF16")]
+VARIANT_CASES += [(G.GGML_Q6_K, 384, 768, 77), (G.GGML_IQ4_XS, 768, 3072, 129), (G.GGML_IQ4_NL, 128, 64, 1)]
+
+
+@pytest.mark.parametrize("w_type,n_out,k,m", VARIANT_CASES)
+def test_matmul_gguf_variants(cuda, oracle, w_type, n_out, k, m):
+    import torch
+    from crispembed_b200 import binding
+    raw, x, bias = _inputs(w_type, n_out, k, m, seed=3 * n_out + k + m + w_type)
+    xd = torch.from_numpy(x).to(cuda)
+    out = binding.matmul(w_type, raw, n_out, k, xd).cpu().numpy()
+    ref = oracle.matmul(w_type, raw, n_out, k, x.astype(np.float32), oracle.F16)
+    tol = (2e-3 if w_type == G.GGML_IQ4_XS else 2e-4) * max(1.0, float(np.abs(ref).max()))
+    assert np.abs(out - ref).max() <= tol, np.abs(out - ref).max()
