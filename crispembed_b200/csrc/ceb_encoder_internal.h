@@ -25,6 +25,10 @@ int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_se
 // shape is not handled there (head_dim != 64 or a sequence longer than 512)
 int ceb_attention_tc(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
                      __half* out, int* d_err, cudaStream_t st);
+// RoPE, NEOX pairing (dims i and i + 32 of each 64-dim head), on the Q and K thirds of
+// fused fp16 qkv rows in place; position = row - cu[seq] + pos_offset.
+int ceb_rope_neox(__half* qkv, int M, const int32_t* cu, int n_seqs, int d, int n_head, int pos_offset, float theta,
+                  cudaStream_t st);
 int ceb_pool_l2_launch(const float* hidden, const int32_t* cu, int n_seqs, int d, int out_dim, float* out,
                        cudaStream_t st, int mode = 0);
 
@@ -48,7 +52,9 @@ struct ceb_model {
     int pos_offset = 0;
     int n_pos = 0;
     float* tok = nullptr;  // [n_vocab x d] f32
-    float* pos = nullptr;  // [n_pos x d] f32 or null
+    float* pos = nullptr;  // [n_pos x d] f32 or null (RoPE models)
+    bool use_rope = false;  // no position table: RoPE (NEOX pairing) on Q and K
+    float rope_theta = 10000.0f;
     float* type0 = nullptr;  // row 0 of the token-type table or null
     float *embd_ln_w = nullptr, *embd_ln_b = nullptr;
     std::vector<ceb_layer> layers;

@@ -134,6 +134,28 @@ __global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int3
     ceb_row::ln_row(acc, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
 }
 
+// ------------------------------------------------------------------ RoPE
+// One CTA per token, thread = (head, pair i < 32): dims i and i + 32 of the head's
+// Q and K rotate by pos * theta^(-2i/64) (NEOX pairing, ggml_rope_ext with n_dims =
+// head_dim, no frequency scaling), in fp32, stored back as fp16.
+__global__ void rope_neox_kernel(__half* __restrict__ qkv, const int32_t* __restrict__ cu, int n_seqs, int d,
+                                 int pos_offset, float log2_theta) {
+    const int t = blockIdx.x;
+    const int seq = find_seq(cu, n_seqs, t);
+    const float pos = (float)(t - cu[seq] + pos_offset);
+    const int h = threadIdx.x >> 5, i = threadIdx.x & 31;
+    const float ang = pos * exp2f(-(float)(2 * i) / 64.0f * log2_theta);
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {  // Q, then K
+        __half* base = qkv + (size_t)t * 3 * d + part * d + h * 64;
+        const float x0 = __half2float(base[i]), x1 = __half2float(base[i + 32]);
+        base[i] = __float2half_rn(x0 * cs - x1 * sn);
+        base[i + 32] = __float2half_rn(x0 * sn + x1 * cs);
+    }
+}
+
 // ------------------------------------------------------------------ attention
 // One CTA = 64 queries of one (sequence, head); 4 warps x 16 query rows.
 // S = Q K^T and O = P V on mma.sync m16n8k16 (fp16 in, fp32 accumulate) with a
@@ -390,6 +412,16 @@ int ceb_embed_ln(const int32_t* ids, const int32_t* cu, int n_seqs, int M, int d
     const int threads = 256, per = threads / 32;
     CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, embed_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(ids, cu, n_seqs, M, d, n_vocab, tok, pos, n_pos,
                                                              pos_offset, type0, gamma, beta, eps, out32, out16, err));
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
+int ceb_rope_neox(__half* qkv, int M, const int32_t* cu, int n_seqs, int d, int n_head, int pos_offset, float theta,
+                  cudaStream_t st) {
+    if (d != n_head * 64 || n_head > 32) return ceb_set_error(2, "rope: head_dim 64 and <= 32 heads supported");
+    if (M <= 0) return 0;
+    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0,
+               rope_neox_kernel<<<M, 32 * n_head, 0, st>>>(qkv, cu, n_seqs, d, pos_offset, log2f(theta)));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }

@@ -176,8 +176,13 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
     if (!rc) rc = L.upload_f32(tok, &m->tok, (int64_t)hp.n_vocab * d);
     if (!rc) {
         const ceb_gguf_tensor* pe = g.tensor("position_embd.weight");
-        if (!pe) rc = ceb_set_error(1, "model has no position_embd.weight (RoPE encoders are outside this build)");
-        else {
+        if (!pe) {
+            // no position table: RoPE with NEOX pairing (src/crispembed.cpp:788-795, :1182-1195); base from
+            // bert.rope_theta or <arch>.rope.freq_base (src/crispembed.cpp:482-483)
+            m->use_rope = true;
+            m->rope_theta = L.f32({"bert.rope_theta", L.ak("rope.freq_base")}, 10000.0f);
+            m->n_pos = hp.n_max_tokens + m->pos_offset;
+        } else {
             m->n_pos = (int)pe->ne[1];
             rc = L.upload_f32(pe, &m->pos, (int64_t)m->n_pos * d);
         }
@@ -457,6 +462,9 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
         a.epi = CEB_EPI_F16_OUT | (Ly.qkv_b ? CEB_EPI_BIAS : 0);
         a.bias = Ly.qkv_b;
         if ((rc = ceb_gemm_launch(Ly.qkv, ws.x16, M, a, st))) return rc;
+        if (m.use_rope &&
+            (rc = ceb_rope_neox(ws.qkv16, M, d_cu, n_seqs, d, hp.n_head, m.pos_offset, m.rope_theta, st)))
+            return rc;
         if ((rc = ceb_attention(ws.qkv16, M, d_cu, n_seqs, max_len, d, hp.n_head, ws.a16, d_err, st))) return rc;
         // output projection (+bias) -> fp32, residual + LN1
         a.out = ws.t32;

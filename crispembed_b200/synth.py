@@ -64,6 +64,8 @@ class ModelSpec:
     # per-tensor block types by name suffix ("attn.o.weight", "ffn.expert_fc2.weight",
     # "token_embd.weight", ...), for mixed-format files such as llama.cpp's Q4_K_M
     type_overrides: Dict[str, int] = field(default_factory=dict)
+    rope_theta: float = 0.0  # > 0: no position table, RoPE (NEOX) with this base, as NomicBERT v1 GGUFs
+    qk_scale: float = 0.02   # std of the q/k projection weights (larger: sharper attention)
 
     def is_moe(self, il: int) -> bool:
         return self.n_experts > 0 and self.moe_every > 0 and il % self.moe_every == self.moe_every - 1
@@ -132,7 +134,10 @@ def write_model(path: str, spec: ModelSpec, tokenizer=None) -> List[str]:
         w.add_tensor(name, ne, gtype, lambda: quantize(gen(), gtype))
 
     add("token_embd.weight", (spec.n_vocab, d), G.GGML_F32, lambda: normal((spec.n_vocab, d)))
-    add("position_embd.weight", (spec.n_ctx, d), G.GGML_F32, lambda: normal((spec.n_ctx, d)))
+    if spec.rope_theta > 0:
+        w.add_f32("bert.rope_theta", spec.rope_theta)
+    else:
+        add("position_embd.weight", (spec.n_ctx, d), G.GGML_F32, lambda: normal((spec.n_ctx, d)))
     if spec.type_vocab > 0:
         add("token_type_embd.weight", (spec.type_vocab, d), G.GGML_F32, lambda: normal((spec.type_vocab, d)))
     add("embd_ln.weight", (d,), G.GGML_F32, lambda: normal((d,), loc=1.0))
@@ -140,7 +145,8 @@ def write_model(path: str, spec: ModelSpec, tokenizer=None) -> List[str]:
     for il in range(spec.n_layer):
         p = f"enc.{il}."
         for nm in ("q", "k", "v"):
-            add(p + f"attn.{nm}.weight", (d, d), wt, lambda: normal((d, d)))
+            sc = spec.qk_scale if nm != "v" else 0.02
+            add(p + f"attn.{nm}.weight", (d, d), wt, lambda sc=sc: normal((d, d), scale=sc))
             add(p + f"attn.{nm}.bias", (d,), G.GGML_F32, lambda: normal((d,)))
         add(p + "attn.o.weight", (d, d), wt, lambda: normal((d, d)))
         add(p + "attn.o.bias", (d,), G.GGML_F32, lambda: normal((d,)))

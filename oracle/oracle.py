@@ -265,6 +265,7 @@ def load_model(path: str) -> OracleModel:
         n_experts=int(first(["bert.num_experts", f"{arch}.expert_count"], 0)),
         top_k=int(first(["bert.num_experts_per_tok", f"{arch}.expert_used_count"], 0)),
         pos_offset=int(first(["bert.position_offset"], 0)),
+        rope_theta=float(first(["bert.rope_theta", f"{arch}.rope.freq_base"], 10000.0)),
     )
     t, types, shapes = {}, {}, {}
     for name, info in g.tensors.items():
@@ -274,6 +275,29 @@ def load_model(path: str) -> OracleModel:
     m = OracleModel(hp=hp, t=t, types=types, shapes=shapes)
     m.moe_layers = [il for il in range(hp["n_layer"]) if f"enc.{il}.ffn.moe_gate.weight" in t]
     return m
+
+
+def rope_neox(x: np.ndarray, pos: np.ndarray, n_head: int, theta: float) -> np.ndarray:
+    """ggml_rope_ext, NEOX pairing, n_dims = head_dim, no scaling (src/crispembed.cpp:1182-1195):
+    dims i and i + hd/2 of each head rotate by pos * theta^(-2i/hd); the angle is
+    built as ggml's rope cache builds it, multiplying by theta^(-2/hd) once per pair
+    in float32, and cos/sin are taken in float32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, d = x.shape
+    hd = d // n_head
+    half = hd // 2
+    xs = x.reshape(M, n_head, hd)
+    scale = np.float32(np.power(np.float32(theta), np.float32(-2.0 / hd), dtype=np.float32))
+    th = pos.astype(np.float32)
+    out = xs.copy()
+    for i in range(half):
+        c = np.cos(th).astype(np.float32)[:, None]
+        s = np.sin(th).astype(np.float32)[:, None]
+        x0, x1 = xs[:, :, i], xs[:, :, i + half]
+        out[:, :, i] = x0 * c - x1 * s
+        out[:, :, i + half] = x0 * s + x1 * c
+        th = (th * scale).astype(np.float32)
+    return out.reshape(M, d)
 
 
 def encode(model: OracleModel, ids: np.ndarray, lens: np.ndarray, mode: int = GGML,
@@ -310,6 +334,8 @@ def encode(model: OracleModel, ids: np.ndarray, lens: np.ndarray, mode: int = GG
     if dump is not None:
         dump["emb_ln_out"] = x.copy()
 
+    use_rope = "position_embd.weight" not in model.t  # src/crispembed.cpp:790-795
+
     def lin(name_w, name_b, inp, k_in):
         ne = model.shapes[name_w]
         n_out = int(ne[1])
@@ -321,6 +347,9 @@ def encode(model: OracleModel, ids: np.ndarray, lens: np.ndarray, mode: int = GG
         q = lin(p + "attn.q.weight", p + "attn.q.bias", x, d)
         k = lin(p + "attn.k.weight", p + "attn.k.bias", x, d)
         v = lin(p + "attn.v.weight", p + "attn.v.bias", x, d)
+        if use_rope:
+            q = rope_neox(q, pos, nh, hp["rope_theta"])
+            k = rope_neox(k, pos, nh, hp["rope_theta"])
         qkv = np.concatenate([q, k, v], axis=1)
         attn = attention(qkv, cu, nh, d)
         attn = lin(p + "attn.o.weight", p + "attn.o.bias", attn, d)

@@ -142,3 +142,18 @@ def test_mixed_format_models_match_oracle(cuda, oracle, tmp_path, mix):
     m.close()
     ref = oracle.encode(oracle.load_model(path), ids, lens, oracle.GGML)
     _check(emb, ref)
+
+
+@pytest.mark.parametrize("theta", [10000.0, 1000.0])
+def test_rope_model_matches_oracle(cuda, oracle, tmp_path, theta):
+    """A GGUF without a position table runs RoPE with NEOX pairing on Q and K
+    (src/crispembed.cpp:788-795, :1182-1195), base from bert.rope_theta."""
+    from crispembed_b200 import binding
+    path = str(tmp_path / "rope.gguf")
+    synth.write_model(path, synth.tiny_spec(rope_theta=theta, qk_scale=0.12))  # sharp attention: positions matter
+    m = binding.CrispEmbed(path)
+    ids, lens = synth.ids_ragged(8, 2, 128, seed=14, hi=1000)
+    emb = m.encode_ids(ids, lens)
+    m.close()
+    ref = oracle.encode(oracle.load_model(path), ids, lens, oracle.GGML)
+    _check(emb, ref)
