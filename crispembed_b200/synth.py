@@ -84,11 +84,26 @@ def tiny_spec(wtype: int = G.GGML_Q8_0, **kw) -> ModelSpec:
     return ModelSpec(**base)
 
 
-def write_model(path: str, spec: ModelSpec, tokenizer=None) -> List[str]:
+LLAMA_NAMES = {  # CrispEmbed-native suffix -> llama.cpp nomic-bert-moe name (src/crispembed.cpp:800-845)
+    "attn.o.weight": "attn_output.weight", "attn.o.bias": "attn_output.bias",
+    "ln1.weight": "attn_output_norm.weight", "ln1.bias": "attn_output_norm.bias",
+    "ln2.weight": "layer_output_norm.weight", "ln2.bias": "layer_output_norm.bias",
+    "ffn.fc1.weight": "ffn_up.weight", "ffn.fc1.bias": "ffn_up.bias",
+    "ffn.fc2.weight": "ffn_down.weight", "ffn.fc2.bias": "ffn_down.bias",
+    "ffn.moe_gate.weight": "ffn_gate_inp.weight", "ffn.expert_fc1.weight": "ffn_up_exps.weight",
+    "ffn.expert_fc2.weight": "ffn_down_exps.weight",
+}
+
+
+def write_model(path: str, spec: ModelSpec, tokenizer=None, naming: str = "crisp") -> List[str]:
     """Write the synthetic GGUF; returns the tensor order.
 
     `tokenizer(writer)` replaces the default synthetic WordPiece keys (it must
-    write spec.n_vocab tokens)."""
+    write spec.n_vocab tokens).  naming="llama" writes the same weights under
+    llama.cpp's nomic-bert-moe names (blk.N.*, a fused attn_qkv with rows q|k|v,
+    token_embd_norm, nomic-bert-moe.* keys) as community exports do."""
+    if naming == "llama":
+        return _write_llama_naming(path, spec, tokenizer)
     rng = np.random.default_rng(spec.seed)
     w = G.GGUFWriter(path)
     w.add_str("general.architecture", "nomic-bert-moe")
@@ -173,7 +188,82 @@ def write_model(path: str, spec: ModelSpec, tokenizer=None) -> List[str]:
     return order
 
 
+def _write_llama_naming(path: str, spec: ModelSpec, tokenizer=None) -> List[str]:
+    """The tensors of write_model(spec) (same draws, same bytes per row) under
+    llama.cpp's names and keys."""
+    import os
+    import tempfile
+    with tempfile.TemporaryDirectory() as td:
+        tmp = os.path.join(td, "crisp.gguf")
+        write_model(tmp, spec, tokenizer)
+        src = G.read_gguf(tmp)
+        arch = "nomic-bert-moe"
+        w = G.GGUFWriter(path)
+        w.add_str("general.architecture", arch)
+        w.add_str("general.name", "crispembed-b200 synthetic nomic-bert-moe (llama.cpp naming)")
+        keys = {"bert.vocab_size": None, "bert.max_position_embeddings": "context_length",
+                "bert.hidden_size": "embedding_length", "bert.num_attention_heads": "attention.head_count",
+                "bert.num_hidden_layers": "block_count", "bert.intermediate_size": "feed_forward_length",
+                "bert.layer_norm_eps": "attention.layer_norm_epsilon", "bert.num_experts": "expert_count",
+                "bert.num_experts_per_tok": "expert_used_count", "bert.rope_theta": "rope.freq_base"}
+        for k, v in src.kv.items():
+            if k in keys:
+                if keys[k] is None:
+                    continue
+                val = v
+                if isinstance(val, float):
+                    w.add_f32(f"{arch}.{keys[k]}", val)
+                else:
+                    w.add_u32(f"{arch}.{keys[k]}", int(val))
+            elif k.startswith("tokenizer."):
+                if isinstance(v, list):
+                    if v and isinstance(v[0], str):
+                        w.add_str_array(k, v)
+                    else:
+                        w.add_f32_array(k, v)
+                elif isinstance(v, str):
+                    w.add_str(k, v)
+                elif isinstance(v, bool):
+                    w.add_bool(k, v)
+                else:
+                    w.add_u32(k, int(v))
+        w.add_u32(f"{arch}.pooling_type", 1)  # llama.cpp's MEAN
+        order: List[str] = []
+
+        def put(name, info_name, data=None, ne=None, gtype=None):
+            info = src.tensors[info_name]
+            raw = src.raw(info_name) if data is None else data
+            w.add_tensor(name, info.ne if ne is None else ne, info.ggml_type if gtype is None else gtype,
+                         lambda raw=raw: raw)
+            order.append(name)
+
+        renames = {"embd_ln.weight": "token_embd_norm.weight", "embd_ln.bias": "token_embd_norm.bias",
+                   "token_type_embd.weight": "token_types.weight"}
+        for name in src.tensors:
+            if not name.startswith("enc."):
+                put(renames.get(name, name), name)
+                continue
+            il, rest = name[4:].split(".", 1)
+            b = f"blk.{il}."
+            if rest in ("attn.q.weight", "attn.q.bias"):
+                part = rest.split(".")[2]
+                names = [f"enc.{il}.attn.{x}.{part}" for x in "qkv"]
+                raws = [np.ascontiguousarray(src.raw(n)).view(np.uint8).reshape(-1) for n in names]
+                ne = src.tensors[names[0]].ne
+                fused_ne = (ne[0], 3 * ne[1]) if len(ne) == 2 else (3 * ne[0],)
+                put(b + "attn_qkv." + part, names[0], data=np.concatenate(raws), ne=fused_ne)
+            elif rest.startswith("attn.k.") or rest.startswith("attn.v."):
+                continue
+            elif rest == "ffn.moe_bias":  # the reference reads the expert bias under its native name only
+                put(name, name)
+            else:
+                put(b + LLAMA_NAMES[rest], name)
+        w.write()
+        return order
+
+
 # ---------------------------------------------------------------------------
+# token-id batches (BASELINE configs 1, 2, 4)# ---------------------------------------------------------------------------
 # token-id batches (BASELINE configs 1, 2, 4)
 # ---------------------------------------------------------------------------
 

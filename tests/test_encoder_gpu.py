@@ -157,3 +157,22 @@ def test_rope_model_matches_oracle(cuda, oracle, tmp_path, theta):
     m.close()
     ref = oracle.encode(oracle.load_model(path), ids, lens, oracle.GGML)
     _check(emb, ref)
+
+
+@pytest.mark.parametrize("spec_kw", [dict(), dict(wtype=12, router_wtype=0, type_overrides={"ffn.expert_fc2.weight": 14})])
+def test_llama_cpp_naming_loads_the_same_model(cuda, tmp_path, spec_kw):
+    """llama.cpp's nomic-bert-moe export of the same weights (blk.N.* names, fused
+    attn_qkv, ffn_gate_inp / ffn_up_exps / ffn_down_exps, nomic-bert-moe.* keys,
+    src/crispembed.cpp:800-845) gives bit-identical embeddings."""
+    from crispembed_b200 import binding
+    a, b = str(tmp_path / "crisp.gguf"), str(tmp_path / "llama.gguf")
+    spec = synth.tiny_spec(**spec_kw)
+    synth.write_model(a, spec)
+    synth.write_model(b, spec, naming="llama")
+    ids, lens = synth.ids_ragged(6, 2, 90, seed=21, hi=1000)
+    outs = []
+    for p in (a, b):
+        m = binding.CrispEmbed(p)
+        outs.append(m.encode_ids(ids, lens))
+        m.close()
+    assert np.array_equal(outs[0], outs[1])
