@@ -255,8 +255,18 @@ def bench_ep(args, rank, world, local, path, dist):
         torch.cuda.synchronize()
     launches = binding.launch_count() - n0
     binding.sync_check()
+    binding.profile_enable(True)  # per-launch events in a second pass of the same steps
+    for _ in range(args.steps):
+        m.encode_ids_device(d_ids, my_lens, out)
+    torch.cuda.synchronize()
+    prof = binding.profile_read()
+    binding.profile_enable(False)
     t = max_over_ranks(ev0.elapsed_time(ev1) / 1000.0, "cuda")
+    brk = {k: v["ms"] / args.steps for k, v in prof.items()}
+    per_rank = [brk]
     if dist:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, brk)
         dist.barrier()
     for _ in range(2):
         m.encode_ids(my_ids, my_lens)
@@ -277,7 +287,10 @@ def bench_ep(args, rank, world, local, path, dist):
             "ms_per_step": 1000.0 * t / args.steps, "config": c4_config(world, total),
             "e2e": {"value": total * args.steps / te, "unit": "tokens/s", "h2d_bytes_per_step": int(my_ids.nbytes),
                     "d2h_bytes_per_step": int(cnt * n_embd * 4), "note": "rank 0's bytes; every rank copies its shard"},
-            "gpu_launches": int(launches), "clocks": clk.summary()}
+            "gpu_launches": int(launches), "clocks": clk.summary(),
+            "breakdown_ms_per_step_rank0": brk,
+            "breakdown_ms_per_step_min_max_over_ranks": {
+                k: [min(b[k] for b in per_rank), max(b[k] for b in per_rank)] for k in brk}}
 
 
 def traffic_from_profile(workload):

@@ -461,7 +461,7 @@ def sync_check(stream=None):
     _check(load_library().ceb_sync_check(_stream_ptr(stream)), "device check")
 
 
-PROFILE_CATEGORIES = ("gemm", "attention", "routing", "rowwise")
+PROFILE_CATEGORIES = ("gemm", "attention", "routing", "rowwise", "exchange", "exchange_wait")
 
 
 def launch_count() -> int:

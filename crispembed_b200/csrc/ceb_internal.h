@@ -102,7 +102,9 @@ enum ceb_prof_cat : int {
     CEB_PROF_ATTN = 1,
     CEB_PROF_ROUTE = 2,   // router + histogram/scan + permutation
     CEB_PROF_ROWWISE = 3, // embedding, residual+LN, combine+LN, pooling
-    CEB_PROF_NCAT = 4,
+    CEB_PROF_EXCHANGE = 4, // expert-parallel peer copies (dispatching permutation, return)
+    CEB_PROF_EP_WAIT = 5,  // expert-parallel waits for peers' flags
+    CEB_PROF_NCAT = 6,
 };
 // Counts one kernel launch; when profiling is on, records a start event on `st`.
 int ceb_prof_begin(cudaStream_t st, int cat);

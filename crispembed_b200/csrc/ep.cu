@@ -90,7 +90,13 @@ __global__ void __launch_bounds__(256)
         }
         const float4* src = reinterpret_cast<const float4*>(down + (size_t)r * d);
         float4* dst = reinterpret_cast<float4*>(ep.peers[seg_peer[s]].ret + (size_t)row * d);
-        for (int i = 0; i < nv; ++i) dst[i * 32 + lane] = __ldg(src + i * 32 + lane);
+        float4 v[8];  // the whole row in flight before the peer stores (d <= 1024)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < nv) v[i] = __ldg(src + i * 32 + lane);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < nv) dst[i * 32 + lane] = v[i];
     }
     __threadfence_system();
     __syncthreads();
@@ -165,7 +171,7 @@ ceb_wplane ceb_wplane_slice(const ceb_wplane& w, int g0, int n) {
 }
 
 int ceb_ep_wait(const ceb_ep_args& a, int row, int* dev_err, cudaStream_t st) {
-    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+    CEB_LAUNCH(CEB_PROF_EP_WAIT, st, 0.0, 0.0,
                ep_wait_kernel<<<1, 32, 0, st>>>(a.my_flags + (size_t)row * a.world, a.world, a.epoch, a.timeout_ns,
                                                 dev_err));
     CEB_CUDA_OK(cudaGetLastError());
@@ -220,7 +226,7 @@ int ceb_ep_moe(ceb_ep* ep, const ceb_moe_weights& mwl, const void* x, int x_dtyp
     a2.err = dev_err;
     if ((rc = ceb_gemm_launch(mwl.fc2, ep->h, rows, a2, st))) return rc;
     const int grid = 2 * ceb_num_sms();
-    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+    CEB_LAUNCH(CEB_PROF_EXCHANGE, st, 0.0, 0.0,
                ep_return_kernel<<<grid, 256, 0, st>>>(ep->down, ep->d, ep->E, a, dev_err));
     CEB_CUDA_OK(cudaGetLastError());
     return ceb_ep_wait(a, CEB_EPF_RETURN, dev_err, st);

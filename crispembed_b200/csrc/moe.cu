@@ -519,20 +519,45 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
     const int nv = d / 128;
-    for (int tl = warp; tl < n_tok; tl += blockDim.x / 32) {
+    if (x16) {  // fp16 rows: 16-byte chunks, chunk i*32 + lane of a row per lane
+        const int nc = d / 8;
+        for (int tl = warp; tl < n_tok; tl += blockDim.x / 32) {
+            const uint4* src = reinterpret_cast<const uint4*>(x16 + (size_t)(t0 + tl) * d);
+            uint4 r[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (i * 32 + lane < nc) r[i] = __ldg(src + i * 32 + lane);
+            for (int j = 0; j < K; ++j) {
+                const int pos = s_pos[tl * K + j];
+                if (pos < 0) continue;
+                __half* dst;
+                if (ep.peers) {
+                    const int e = s_key[tl * K + j];
+                    const long long row = s_dst[e] + pos;
+                    if (row < 0 || row >= ep.recv_rows) {
+                        if (lane == 0) atomicCAS(err, 0, (int)CEB_DEVERR_EP_OVERFLOW);
+                        continue;
+                    }
+                    dst = ep.peers[e / ep.E_loc].recv + (size_t)row * d;
+                } else {
+                    dst = x_perm + (size_t)pos * d;
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (i * 32 + lane < nc) reinterpret_cast<uint4*>(dst)[i * 32 + lane] = r[i];
+            }
+        }
+    }
+    for (int tl = warp; tl < n_tok && !x16; tl += blockDim.x / 32) {
         const size_t t = (size_t)(t0 + tl);
         uint2 r[LN_MAXV];  // 4 fp16 values per lane per 128-column segment
 #pragma unroll
         for (int i = 0; i < LN_MAXV; ++i)
             if (i < nv) {
                 const size_t c = (size_t)(i * 32 + lane) * 4;
-                if (x16) {
-                    r[i] = __ldg(reinterpret_cast<const uint2*>(x16 + t * d + c));
-                } else {
-                    const float4 f = ld_act4<T>(x + t * d, c);
-                    const __half2 lo = __floats2half2_rn(f.x, f.y), hi = __floats2half2_rn(f.z, f.w);
-                    r[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
-                }
+                const float4 f = ld_act4<T>(x + t * d, c);
+                const __half2 lo = __floats2half2_rn(f.x, f.y), hi = __floats2half2_rn(f.z, f.w);
+                r[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
             }
         for (int j = 0; j < K; ++j) {
             const int pos = s_pos[tl * K + j];
@@ -699,17 +724,18 @@ int ceb_moe_permute(const ceb_moe_weights& mw, const void* x, int x_dtype, const
         if (int rc = ceb_ep_wait(*ep, CEB_EPF_COUNTS, dev_err, st)) return rc;
     const int grid = std::max(nblk, 1);  // an expert-parallel rank without tokens still signals its peers
     int* err = dev_err;
+    const int cat = ep ? CEB_PROF_EXCHANGE : CEB_PROF_ROUTE;
     if (x_dtype == CEB_ACT_F32)
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+        CEB_LAUNCH(cat, st, 0.0, 0.0,
                    scatter_kernel<float><<<grid, 256, 0, st>>>((const float*)x, x16, T, d, E, K, ws.ids, ws.block_base,
                                                                ws.slot_pos, ws.x_perm, err, ea));
     else if (x_dtype == CEB_ACT_BF16)
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+        CEB_LAUNCH(cat, st, 0.0, 0.0,
                    scatter_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, x16, T, d, E, K,
                                                                        ws.ids, ws.block_base, ws.slot_pos, ws.x_perm,
                                                                        err, ea));
     else
-        CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+        CEB_LAUNCH(cat, st, 0.0, 0.0,
                    scatter_kernel<__half><<<grid, 256, 0, st>>>((const __half*)x, x16, T, d, E, K, ws.ids,
                                                                 ws.block_base, ws.slot_pos, ws.x_perm, err, ea));
     CEB_CUDA_OK(cudaGetLastError());

@@ -243,7 +243,8 @@ CEB_API int ceb_matmul(int w_type, const void* h_w, int n_out, int k, const void
  * ceb_profile_enable(1): from now on record CUDA events around every launch,
  * on the launch's own stream.  ceb_profile_read: per category (0 grouped GEMM,
  * 1 attention, 2 routing + permutation, 3 row-wise: embedding / LayerNorm /
- * combine / pooling) the number of launches, summed kernel milliseconds and
+ * combine / pooling, 4 expert-parallel peer copies, 5 expert-parallel waits for
+ * peers) the number of launches, summed kernel milliseconds and
  * algorithmic flops / bytes; synchronises on the recorded events and clears
  * them.  Returns 0 on success.
  */

@@ -142,3 +142,17 @@ def test_silent_rank_makes_peer_waits_expire(cuda, tmp_path):
     assert "error" not in res[0] and "error" not in res[1], res
     t = res[0]["timeout"]
     assert t["raised"] and "0x" in t["message"] and "107" in t["message"], t
+
+
+@pytest.mark.skipif("not __import__('torch').cuda.is_available() or __import__('torch').cuda.device_count() < 4")
+def test_all_gpu_exchange_op_bit_identical(cuda, tmp_path):
+    """Every visible GPU (4 or 8) as one rank: the cases whose expert count splits."""
+    import torch
+    n = 8 if torch.cuda.device_count() >= 8 else 4
+    res = _launch(n, "op", "-", tmp_path)
+    for r in res:
+        assert "error" not in r, r
+        cases = {k: v for k, v in r.items() if isinstance(v, dict)}
+        assert cases, r
+        for name, v in cases.items():
+            assert v["equal"], (r["rank"], name, v)
