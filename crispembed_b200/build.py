@@ -22,7 +22,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libcrispembed.so")
 
 SOURCES = ["gemm_tc.cu", "attn_tc.cu", "moe.cu", "moe_static.cu", "ep.cu", "encoder_kernels.cu", "runtime.cpp", "gguf_quants.cpp", "gguf.cpp", "tokenizer.cpp", "model.cpp", "api.cpp"]
-HEADERS = ["common.cuh", "rowwise.cuh", "ceb_internal.h", "ceb_moe_internal.h", "ceb_ep_internal.h", "ceb_encoder_internal.h", "gguf.h", "tokenizer.h"]
+HEADERS = ["common.cuh", "rowwise.cuh", "ceb_internal.h", "ceb_moe_internal.h", "ceb_ep_internal.h", "ceb_encoder_internal.h", "gguf.h", "tokenizer.h", "spm_norm_table.inc"]
 PUBLIC_HEADERS = [os.path.join(ROOT, "include", h) for h in ("crispembed.h", "ceb_ops.h")]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -29,7 +29,67 @@ bool kv_bool(const ceb_gguf& g, const char* key, bool dflt) {
 bool is_ascii_punct(unsigned char c) {
     return (c >= 33 && c <= 47) || (c >= 58 && c <= 64) || (c >= 91 && c <= 96) || (c >= 123 && c <= 126);
 }
+
+#include "spm_norm_table.inc"
+
+// Next codepoint of a UTF-8 string at i (advanced); a byte that does not start a
+// valid sequence is returned as itself (>= 0x80 values then pass through unchanged).
+uint32_t utf8_next(const std::string& s, size_t& i, size_t* len) {
+    const unsigned char c = (unsigned char)s[i];
+    int n = c < 0x80 ? 1 : (c >> 5) == 6 ? 2 : (c >> 4) == 14 ? 3 : (c >> 3) == 30 ? 4 : 0;
+    if (n == 0 || i + n > s.size()) n = 1;
+    uint32_t cp = n == 1 ? c : n == 2 ? (c & 0x1F) : n == 3 ? (c & 0x0F) : (c & 0x07);
+    for (int k = 1; k < n; ++k) {
+        const unsigned char d = (unsigned char)s[i + k];
+        if ((d & 0xC0) != 0x80) {  // broken sequence: the lead byte alone
+            n = 1;
+            cp = 0xFFFFFFFFu;
+            break;
+        }
+        cp = (cp << 6) | (d & 0x3F);
+    }
+    *len = (size_t)n;
+    i += n;
+    return cp;
+}
 }  // namespace
+
+// SentencePiece nmt_nfkc normalisation one codepoint at a time (the table in
+// spm_norm_table.inc), applied before the space -> U+2581 marking as the
+// reference does for the embedding path (src/tokenizer_spm.cpp:57-70,
+// src/crispembed.cpp:624).
+std::string ceb_spm_normalize(const std::string& text) {
+    std::string out;
+    out.reserve(text.size());
+    size_t i = 0;
+    while (i < text.size()) {
+        const unsigned char c = (unsigned char)text[i];
+        if (c >= 0x20 && c < 0x7F) {  // printable ASCII is unchanged
+            out += (char)c;
+            ++i;
+            continue;
+        }
+        const size_t at = i;
+        size_t len = 0;
+        const uint32_t cp = utf8_next(text, i, &len);
+        int lo = 0, hi = kSpmNormN - 1, hit = -1;
+        while (lo <= hi && cp != 0xFFFFFFFFu) {
+            const int mid = (lo + hi) >> 1;
+            if (kSpmNormCp[mid] == cp) {
+                hit = mid;
+                break;
+            }
+            if (kSpmNormCp[mid] < cp) lo = mid + 1;
+            else hi = mid - 1;
+        }
+        if (hit < 0)
+            out.append(text, at, len);
+        else
+            out.append(reinterpret_cast<const char*>(kSpmNormUtf8) + kSpmNormOff[hit],
+                       kSpmNormOff[hit + 1] - kSpmNormOff[hit]);
+    }
+    return out;
+}
 
 int ceb_tokenizer::load(const ceb_gguf& g, int max_tok) {
     max_tokens = max_tok > 2 ? max_tok : 512;
@@ -225,7 +285,7 @@ int ceb_tokenizer::encode(const std::string& text, std::vector<int32_t>* ids) co
                              family);
     std::string marked;
     marked.reserve(text.size() * 3 + 3);
-    for (char c : " " + text) {
+    for (char c : " " + (spm_normalize ? ceb_spm_normalize(text) : text)) {
         if (c == ' ')
             marked += "\xe2\x96\x81";  // U+2581
         else

@@ -12,9 +12,11 @@
 //                  over UTF-8 character boundaries; bytes no piece covers fall
 //                  back to "<0xXX>" pieces (score -100) or <unk>; wrapped
 //                  <s> ... </s> as tokenizer.ggml.add_bos_token / add_eos_token say.
-// Not implemented: GPT-2 BPE (decoder-style models) and the nmt_nfkc
-// normalisation charsmap the reference applies before SentencePiece; text that
-// is already NFKC-normal (ASCII, most Latin script) tokenizes the same without it.
+//                  Before that, every codepoint goes through SentencePiece's
+//                  nmt_nfkc charsmap (fullwidth forms, U+2026, U+3000, ligatures,
+//                  control characters, ...), one codepoint at a time as the
+//                  reference's embedding path does (ceb_spm_normalize).
+// Not implemented: GPT-2 BPE (decoder-style models).
 #pragma once
 
 #include <stdint.h>
@@ -30,6 +32,9 @@ class ceb_gguf;
 // are SentencePiece.
 int ceb_tokenizer_family(bool type_key_present, int declared_type, const std::string& model_str, int64_t vocab_n);
 
+// SentencePiece nmt_nfkc normalisation, codepoint by codepoint (printable ASCII unchanged).
+std::string ceb_spm_normalize(const std::string& text);
+
 struct ceb_tokenizer {
     int family = 0;
     int max_tokens = 512;  // including the wrap tokens
@@ -42,6 +47,7 @@ struct ceb_tokenizer {
     std::vector<float> scores;
     int bos_id = 0, eos_id = 2;
     bool add_bos = true, add_eos = true;
+    bool spm_normalize = true;  // nmt_nfkc charsmap before segmentation (the reference's embedding path)
     std::vector<int32_t> byte_piece;  // id of "<0xXX>" per byte value, -1 when absent
 
     // Reads the tokenizer keys of an open GGUF; returns 0 or an error code (message via ceb_set_error).

@@ -1,9 +1,10 @@
 """A small SentencePiece Unigram model trained here (sentencepiece package) and
 its GGUF tokenizer keys, shared by the tokenizer tests.
 
-Normalisation is the identity and repeated spaces are kept, so the text the
-model segments is exactly " " + text with spaces as U+2581 -- the input the
-reference's SentencePiece tokenizer (src/tokenizer_spm.cpp) segments.
+Normalisation is the identity (or nmt_nfkc for the normalisation tests) and
+repeated spaces are kept, so the text the model segments is " " + text with
+spaces as U+2581 -- the input the reference's SentencePiece tokenizer
+(src/tokenizer_spm.cpp) segments.
 """
 import os
 
@@ -37,15 +38,21 @@ def corpus(n_lines: int = 4000, seed: int = 0):
     return lines
 
 
-def train(tmpdir: str, vocab_size: int = 300):
+EXTRA_LINES = ["1 2 3 10 12 2026 ... a.b fi fl ( ) kg IV", "model 1... search 2 ... end. kg"]
+
+
+def train(tmpdir: str, vocab_size: int = 300, rule: str = "identity"):
+    """rule "nmt_nfkc": the normaliser XLM-R-family models declare (the corpus gains
+    a few lines with digits and dots so its replacements have pieces)."""
     import sentencepiece as spm
     txt = os.path.join(tmpdir, "corpus.txt")
+    lines = corpus() + (EXTRA_LINES * 50 if rule != "identity" else [])
     with open(txt, "w") as f:
-        f.write("\n".join(corpus()) + "\n")
+        f.write("\n".join(lines) + "\n")
     prefix = os.path.join(tmpdir, "spm")
     spm.SentencePieceTrainer.train(
         input=txt, model_prefix=prefix, vocab_size=vocab_size, model_type="unigram",
-        normalization_rule_name="identity", add_dummy_prefix=True, remove_extra_whitespaces=False,
+        normalization_rule_name=rule, add_dummy_prefix=True, remove_extra_whitespaces=False,
         character_coverage=1.0, unk_id=0, bos_id=1, eos_id=2, pad_id=3, num_threads=1, minloglevel=2,
         hard_vocab_limit=False)
     return spm.SentencePieceProcessor(model_file=prefix + ".model")

@@ -152,3 +152,32 @@ def test_wordpiece_greedy_longest_match(tmp_path):
     assert tok.kind == 1
     assert tok.encode("Unaffable, hellos") == [1, 4, 5, 6, 8, 9, 10, 2]
     assert tok.encode("zzz") == [1, 3, 2]
+
+
+@pytest.fixture(scope="module")
+def spm_nfkc_model(tmp_path_factory):
+    d = tmp_path_factory.mktemp("spm_nfkc")
+    sp = spm_fixture.train(str(d), rule="nmt_nfkc")
+    path = _gguf(d / "tok.gguf", lambda w: spm_fixture.write_keys(w, sp))
+    return sp, path
+
+
+NFKC_TEXTS = ["ｍｏｄｅｌ １２",   # fullwidth "model 12"
+              "search… end",                              # ellipsis -> "..."
+              "model　search",                             # ideographic space -> word boundary
+              "ﬁ ﬂ",                                 # ligatures fi fl
+              "① Ⅱ ㎏",                          # circled 1, roman II, kg
+              "tab\there\nnew line",                           # \t \n -> spaces
+              "plain ascii stays the same"]
+
+
+@pytest.mark.parametrize("text", NFKC_TEXTS)
+def test_sentencepiece_nmt_nfkc_normalisation_matches_sentencepiece(spm_nfkc_model, text):
+    """The nmt_nfkc charsmap (fullwidth forms, U+2026, U+3000, ligatures, enclosed
+    and compatibility characters, control characters) is applied before
+    segmentation, as the reference's embedding path does (src/tokenizer_spm.cpp:57-70):
+    the ids equal sentencepiece's for a model trained with that rule."""
+    sp, path = spm_nfkc_model
+    tok = binding.Tokenizer(path, max_tokens=512)
+    ids = tok.encode(text)
+    assert ids[1:-1] == sp.encode(text), (text, ids, sp.encode(text))
