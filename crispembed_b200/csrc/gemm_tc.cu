@@ -623,19 +623,24 @@ CEB_DEV Tile decode(const Smem& S_, int G, int n_fp, int t) {
     return ti;
 }
 
-// one 32-row x 32-column fp32 accumulator block -> bias (+GELU) in place
-CEB_DEV void epi_math(float (&x)[32], const uint32_t (&v)[32], const float* bias, bool gelu) {
+// one 32-row x 32-column fp32 accumulator block -> bias (+GELU), in place: the
+// accumulator bits become the float results (no second 32-register array)
+CEB_DEV void epi_math(uint32_t (&v)[32], const float* bias, bool gelu) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
         float4 b = bias ? __ldg(reinterpret_cast<const float4*>(bias + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        x[j] = __uint_as_float(v[j]) + b.x;
-        x[j + 1] = __uint_as_float(v[j + 1]) + b.y;
-        x[j + 2] = __uint_as_float(v[j + 2]) + b.z;
-        x[j + 3] = __uint_as_float(v[j + 3]) + b.w;
-    }
-    if (gelu) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = gelu_as(x[j]);
+        float x0 = __uint_as_float(v[j]) + b.x, x1 = __uint_as_float(v[j + 1]) + b.y;
+        float x2 = __uint_as_float(v[j + 2]) + b.z, x3 = __uint_as_float(v[j + 3]) + b.w;
+        if (gelu) {
+            x0 = gelu_as(x0);
+            x1 = gelu_as(x1);
+            x2 = gelu_as(x2);
+            x3 = gelu_as(x3);
+        }
+        v[j] = __float_as_uint(x0);
+        v[j + 1] = __float_as_uint(x1);
+        v[j + 2] = __float_as_uint(x2);
+        v[j + 3] = __float_as_uint(x3);
     }
 }
 
@@ -883,8 +888,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                     uint32_t v[32];
                     tmem_ld32(tmem + lane_addr + col0 + (uint32_t)(c0 + h), v);
                     tmem_ld_wait();
-                    float x[32];
-                    epi_math(x, v, bias ? bias + f_base + c0 + h : nullptr, gelu);
+                    epi_math(v, bias ? bias + f_base + c0 + h : nullptr, gelu);
+                    const float* x = reinterpret_cast<const float*>(v);
                     if (f16) {
                         uint32_t p[16];
 #pragma unroll
