@@ -38,6 +38,19 @@ struct crispembed_context {
     // per-token results (crispembed_encode_tokens*)
     std::vector<float> last_tokens;
     std::vector<int32_t> last_token_ids;
+    // CUDA graphs of the forward pass, one per batch shape seen twice (see run_device)
+    struct Graph {
+        int M = 0, n_seqs = 0, max_len = 0, out_dim = 0, variant = 0;
+        const int32_t* d_ids = nullptr;
+        float* d_out = nullptr;
+        cudaStream_t st = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        long long launches = 0, last_use = 0;
+    };
+    std::vector<Graph> graphs;
+    std::vector<Graph> graph_seen;  // shapes met once (captured on the second call)
+    void* graph_ws_base = nullptr;
+    long long graph_clock = 0;
     // pinned staging for host-buffer calls
     int32_t* h_ids = nullptr;
     int32_t* h_cu = nullptr;
@@ -83,6 +96,107 @@ int check_device(crispembed_context* ctx, cudaStream_t st) {
     return 0;
 }
 
+void drop_graphs(crispembed_context* ctx) {
+    for (auto& g : ctx->graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+    ctx->graphs.clear();
+    ctx->graph_seen.clear();
+}
+
+bool graphs_enabled() {
+    static const bool off = [] {
+        const char* e = getenv("CEB_GRAPHS");
+        return e && e[0] == '0';
+    }();
+    return !off;
+}
+
+// The forward pass of one batch.  Small batches are launch-bound (about a hundred
+// kernels for a few microseconds of work each), so a batch shape met a second time
+// -- same token and sequence counts, longest sequence, output width, id / output
+// buffers and workspace -- is captured into a CUDA graph on that call and replayed
+// from then on (every pointer and grid the kernels take is fixed by that key; ids
+// and row offsets are uploaded into the fixed workspace buffers before the
+// replay).  Not used while per-launch profiling runs, for expert-parallel contexts
+// (each exchange carries a new epoch), or with CEB_GRAPHS=0.
+int forward_maybe_graph(crispembed_context* ctx, const int32_t* d_ids, int n_seqs, int M, int max_len, float* d_out,
+                        cudaStream_t st) {
+    const int out_dim = out_dim_of(ctx);
+    auto eager = [&] {
+        return ceb_encoder_forward(ctx->model, ctx->ws, d_ids, ctx->ws.cu, n_seqs, M, max_len, d_out, out_dim,
+                                   ctx->d_err, st);
+    };
+    if (!graphs_enabled() || ctx->model.ep || ceb_profiling_on()) return eager();
+    if (ctx->graph_ws_base != ctx->ws.base) {  // a new workspace: every recorded pointer is stale
+        drop_graphs(ctx);
+        ctx->graph_ws_base = ctx->ws.base;
+    }
+    const char* tc = getenv("CEB_ATTN_TC");  // the attention kernel is chosen per call
+    const int variant = (tc && tc[0] == '1') ? 1 : 0;
+    auto same = [&](const crispembed_context::Graph& g) {
+        return g.M == M && g.n_seqs == n_seqs && g.max_len == max_len && g.out_dim == out_dim && g.d_ids == d_ids &&
+               g.d_out == d_out && g.st == st && g.variant == variant;
+    };
+    ++ctx->graph_clock;
+    for (auto& g : ctx->graphs)
+        if (same(g)) {
+            g.last_use = ctx->graph_clock;
+            const cudaError_t le = cudaGraphLaunch(g.exec, st);
+            if (le != cudaSuccess) return ceb_set_cuda_error(le, "graph launch", __FILE__, __LINE__);
+            ceb_count_launches(g.launches);
+            return 0;
+        }
+    bool seen = false;
+    for (auto& g : ctx->graph_seen) seen = seen || same(g);
+    crispembed_context::Graph key;
+    key.M = M;
+    key.n_seqs = n_seqs;
+    key.max_len = max_len;
+    key.out_dim = out_dim;
+    key.d_ids = d_ids;
+    key.d_out = d_out;
+    key.st = st;
+    key.variant = variant;
+    if (!seen) {
+        if (ctx->graph_seen.size() >= 64) ctx->graph_seen.erase(ctx->graph_seen.begin());
+        ctx->graph_seen.push_back(key);
+        return eager();
+    }
+    const long long n0 = ceb_launch_count();
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return eager();
+    }
+    const int rc = eager();
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+    if (rc || ce != cudaSuccess || !graph) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return rc ? rc : eager();  // capture refused: the same work, launched directly
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+        cudaGetLastError();
+        return eager();
+    }
+    key.exec = exec;
+    key.launches = ceb_launch_count() - n0;
+    key.last_use = ctx->graph_clock;
+    if (ctx->graphs.size() >= 8) {  // keep the 8 most recently used shapes
+        auto lru = std::min_element(ctx->graphs.begin(), ctx->graphs.end(),
+                                    [](const auto& a, const auto& b) { return a.last_use < b.last_use; });
+        cudaGraphExecDestroy(lru->exec);
+        ctx->graphs.erase(lru);
+    }
+    ctx->graphs.push_back(key);
+    const cudaError_t le = cudaGraphLaunch(exec, st);
+    if (le != cudaSuccess) return ceb_set_cuda_error(le, "graph launch", __FILE__, __LINE__);
+    return 0;
+}
+
 // Runs the encoder on device ids; cu_host [n_seqs+1] row offsets.
 int run_device(crispembed_context* ctx, const int32_t* d_ids, const int32_t* h_lens, int n_seqs, float* d_out,
                cudaStream_t st) {
@@ -104,8 +218,7 @@ int run_device(crispembed_context* ctx, const int32_t* d_ids, const int32_t* h_l
     if ((rc = ceb_workspace_reserve(&ctx->ws, ctx->model, (int)M, n_seqs))) return rc;
     cudaError_t e = cudaMemcpyAsync(ctx->ws.cu, ctx->h_cu, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "cu_seqlens upload", __FILE__, __LINE__);
-    return ceb_encoder_forward(ctx->model, ctx->ws, d_ids, ctx->ws.cu, n_seqs, (int)M, max_len, d_out,
-                               out_dim_of(ctx), ctx->d_err, st);
+    return forward_maybe_graph(ctx, d_ids, n_seqs, (int)M, max_len, d_out, st);
 }
 
 const float* encode_ids_host(crispembed_context* ctx, const int32_t* ids, const int32_t* lens, int n_seqs,
@@ -279,6 +392,7 @@ extern "C" void* crispembed_stream(crispembed_context* ctx) { return ctx ? (void
 extern "C" void crispembed_free(crispembed_context* ctx) {
     if (!ctx) return;
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    drop_graphs(ctx);
     ceb_workspace_free(&ctx->ws);
     ceb_model_free(&ctx->model);
     if (ctx->d_err) cudaFree(ctx->d_err);

@@ -112,6 +112,13 @@ int ceb_prof_begin(cudaStream_t st, int cat);
 // with the launch's algorithmic flops / bytes.
 void ceb_prof_end(int token, cudaStream_t st, double flops, double bytes);
 
+// Adds n launches to the count (a CUDA-graph replay of n recorded kernels), and
+// whether per-launch profiling events are being recorded.
+void ceb_count_launches(long long n);
+bool ceb_profiling_on();
+// Current value of the launch counter (ceb_launch_count).
+extern "C" long long ceb_launch_count(void);
+
 // Wraps one kernel launch statement with ceb_prof_begin / ceb_prof_end.
 #define CEB_LAUNCH(cat, st, flops, bytes, ...)          \
     do {                                                \

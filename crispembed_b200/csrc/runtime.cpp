@@ -262,6 +262,16 @@ void ceb_prof_end(int token, cudaStream_t st, double flops, double bytes) {
     cudaEventRecord(r.b, st);
 }
 
+void ceb_count_launches(long long n) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_launches += n;
+}
+
+bool ceb_profiling_on() {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    return g_prof_on;
+}
+
 extern "C" long long ceb_launch_count(void) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
     return g_launches;
