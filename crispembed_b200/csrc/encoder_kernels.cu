@@ -97,41 +97,63 @@ __global__ void add_ln_kernel(const float* res, const float* __restrict__ y, int
     ceb_row::ln_row(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
 }
 
-// ffn = sum_j w_j * down[pos_j] (fmaf in slot order) + moe_bias; out = LN(cur + ffn)
+// ffn = sum_j w_j * down[pos_j] (fmaf in slot order) + moe_bias; out = LN(cur + ffn).
+// NV = d / 128 float4 registers per lane; the residual row and two slots' expert rows
+// are requested together so a warp has three rows of loads in flight.
+template <int NV>
 __global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int32_t* __restrict__ slot_pos,
                                       const float* __restrict__ wts, int K, const float* __restrict__ moe_bias,
-                                      const float* cur, int M, int d, const float* __restrict__ gamma,
+                                      const float* cur, int M, const float* __restrict__ gamma,
                                       const float* __restrict__ beta, float eps, float* out32,
                                       __half* __restrict__ out16) {
+    constexpr int d = NV * 128;
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (t >= M) return;
-    const int nv = d / 128;
-    float4 acc[LN_MAXV];
+    float4 acc[NV], res[NV];
 #pragma unroll
-    for (int i = 0; i < LN_MAXV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < K; ++j) {
-        const int p = slot_pos[(size_t)t * K + j];
-        const float w = wts[(size_t)t * K + j];
+    for (int i = 0; i < NV; ++i) {
+        acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        res[i] = *reinterpret_cast<const float4*>(cur + (size_t)t * d + (i * 32 + lane) * 4);
+    }
+    int jj = 0;
+    for (; jj + 1 < K; jj += 2) {  // two slots' rows per pass, accumulated in slot order
+        const int p0 = slot_pos[(size_t)t * K + jj], p1 = slot_pos[(size_t)t * K + jj + 1];
+        const float w0 = wts[(size_t)t * K + jj], w1 = wts[(size_t)t * K + jj + 1];
+        float4 d0[NV], d1[NV];
 #pragma unroll
-        for (int i = 0; i < LN_MAXV; ++i)
-            if (i < nv) {
-                const int c = (i * 32 + lane) * 4;
-                const float4 dv = *reinterpret_cast<const float4*>(down + (size_t)p * d + c);
-                acc[i].x = __fmaf_rn(w, dv.x, acc[i].x);
-                acc[i].y = __fmaf_rn(w, dv.y, acc[i].y);
-                acc[i].z = __fmaf_rn(w, dv.z, acc[i].z);
-                acc[i].w = __fmaf_rn(w, dv.w, acc[i].w);
-            }
+        for (int i = 0; i < NV; ++i) {
+            const int c = (i * 32 + lane) * 4;
+            d0[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p0 * d + c));
+            d1[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p1 * d + c));
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            acc[i].x = __fmaf_rn(w1, d1[i].x, __fmaf_rn(w0, d0[i].x, acc[i].x));
+            acc[i].y = __fmaf_rn(w1, d1[i].y, __fmaf_rn(w0, d0[i].y, acc[i].y));
+            acc[i].z = __fmaf_rn(w1, d1[i].z, __fmaf_rn(w0, d0[i].z, acc[i].z));
+            acc[i].w = __fmaf_rn(w1, d1[i].w, __fmaf_rn(w0, d0[i].w, acc[i].w));
+        }
+    }
+    for (; jj < K; ++jj) {
+        const int p = slot_pos[(size_t)t * K + jj];
+        const float w = wts[(size_t)t * K + jj];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const float4 dv = __ldg(reinterpret_cast<const float4*>(down + (size_t)p * d + (i * 32 + lane) * 4));
+            acc[i].x = __fmaf_rn(w, dv.x, acc[i].x);
+            acc[i].y = __fmaf_rn(w, dv.y, acc[i].y);
+            acc[i].z = __fmaf_rn(w, dv.z, acc[i].z);
+            acc[i].w = __fmaf_rn(w, dv.w, acc[i].w);
+        }
     }
 #pragma unroll
-    for (int i = 0; i < LN_MAXV; ++i)
-        if (i < nv) {
-            const int c = (i * 32 + lane) * 4;
-            if (moe_bias) acc[i] = f4add(acc[i], *reinterpret_cast<const float4*>(moe_bias + c));
-            acc[i] = f4add(*reinterpret_cast<const float4*>(cur + (size_t)t * d + c), acc[i]);
-        }
+    for (int i = 0; i < NV; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        if (moe_bias) acc[i] = f4add(acc[i], *reinterpret_cast<const float4*>(moe_bias + c));
+        acc[i] = f4add(res[i], acc[i]);
+    }
     __syncwarp();
-    ceb_row::ln_row(acc, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
+    ceb_row::ln_row(acc, NV, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
 }
 
 // ------------------------------------------------------------------ RoPE
@@ -439,9 +461,24 @@ int ceb_moe_combine_ln(const float* down, const int32_t* slot_pos, const float* 
                        const float* cur, int M, int d, const float* gamma, const float* beta, float eps, float* out32,
                        __half* out16, cudaStream_t st) {
     if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "combine: d=%d unsupported", d);
-    const int threads = 256, per = threads / 32;
-    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, moe_combine_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(down, slot_pos, wts, K, moe_bias, cur, M, d, gamma,
-                                                                   beta, eps, out32, out16));
+    const int threads = 128, per = threads / 32, grid = (M + per - 1) / per;  // small CTAs: ~88 registers a thread
+#define CEB_COMBINE_CASE(NVC)                                                                                    \
+    case NVC:                                                                                                   \
+        CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0,                                                              \
+                   moe_combine_ln_kernel<NVC><<<grid, threads, 0, st>>>(down, slot_pos, wts, K, moe_bias, cur, M, \
+                                                                       gamma, beta, eps, out32, out16));        \
+        break;
+    switch (d / 128) {
+        CEB_COMBINE_CASE(1)
+        CEB_COMBINE_CASE(2)
+        CEB_COMBINE_CASE(3)
+        CEB_COMBINE_CASE(4)
+        CEB_COMBINE_CASE(5)
+        CEB_COMBINE_CASE(6)
+        CEB_COMBINE_CASE(7)
+        CEB_COMBINE_CASE(8)
+    }
+#undef CEB_COMBINE_CASE
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
