@@ -91,6 +91,9 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows_capac
 int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int n_groups, int n_out, int k,
                        cudaStream_t stream);
 void ceb_wplane_free(ceb_wplane* w);
+// Replace a Q8_0 / Q4_K plane by the fp16 plane of the same values (the GEMM's own
+// dequantizer run once over every block); fp16 planes are left as they are.
+int ceb_wplane_expand_f16(ceb_wplane* w, cudaStream_t st);
 
 int ceb_num_sms();
 // device error word shared by the operator-level entry points (api.cpp)

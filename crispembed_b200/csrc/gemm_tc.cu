@@ -649,8 +649,12 @@ CEB_DEV void epi_math(uint32_t (&v)[32], const float* bias, bool gelu) {
 template <int FMT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     ceb_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap omap,
-                         const ceb_wplane w, const ceb_gemm_args a) {
+                         const __grid_constant__ CUtensorMap wmap, const ceb_wplane w, const ceb_gemm_args a) {
     using namespace pair;
+    // fp16 weight blocks are already the MMA's swizzled image: both CTAs load them with
+    // the pair TMA straight into the weight stage, counted on the leader's FULL barrier
+    // (no raw stage, no dequant warps, no relayed signal).
+    constexpr bool kTmaW = FMT == CEB_W_F16;
     extern __shared__ uint8_t smem_raw[];
     const Smem SH = pair::carve(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -665,7 +669,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NB; ++i) {
             uint32_t cnt = 1;
-            if (i < PS) cnt = 1 + 4;                                        // expect_tx + leader dequant warps
+            if (i < PS) cnt = kTmaW ? 1 : 1 + 4;                            // expect_tx (+ leader dequant warps)
             if (i >= 2 * PS + 2 && i < 2 * PS + 4) cnt = 4 * EPI_WG;        // leader epilogue warps (one with expect_tx)
             if (i >= 2 * PS + 5 + PR && i < 2 * PS + 5 + 2 * PR) cnt = 4;   // this CTA's dequant warpgroup
             if (i >= B_W_FULL(0) && i < B_W_FULL(0) + PS) cnt = 4;          // rank 1's dequant warpgroup
@@ -694,6 +698,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&xmap);
         tma_prefetch_desc(&omap);
+        if (kTmaW) tma_prefetch_desc(&wmap);
     }
     if (warp == 1) {
         tmem_alloc_pair(smem_u32(SH.tmem_slot), TMEM_COLS);
@@ -733,7 +738,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(bar(B_FULL(s)), 2 * X_BYTES + SIG);
+                    if (leader) mbar_arrive_expect_tx(bar(B_FULL(s)), kTmaW ? 2 * (X_BYTES + W_BYTES) : 2 * X_BYTES + SIG);
                     tma_load_2d_pair(smem_u32(x_stage(s)), &xmap, lead_bar(B_FULL(s)), kb * BK,
                                      ti.row0 + TOK * (int)rank);
                 }
@@ -746,7 +751,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp == 1 && !leader) {
         // ------------------------------------------------ relay: rank 1's weight tiles ready -> leader's FULL
-        if (lane == 0) {
+        if (lane == 0 && !kTmaW) {
             const int my_tiles = pair_id < total ? (total - 1 - pair_id) / n_pairs + 1 : 0;
             const uint32_t n_items = (uint32_t)(my_tiles * nkb);
             for (uint32_t it = 0; it < n_items; ++it) {
@@ -806,6 +811,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             mma_pair_commit(bar(B_DRAIN()));
             mbar_wait(bar(B_DRAIN()), 0, nullptr, nullptr, 0);
         }
+    } else if (warp == 2 && kTmaW) {
+        // ------------------------------------------------ weight loader (fp16 blocks, pair TMA)
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int t = pair_id; t < total; t += n_pairs) {
+                const Tile ti = pair::decode(SH, G, n_fp, t);
+                const int ft = 2 * ti.fp + (int)rank;
+                bool ok = true;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % PS;
+                    if (!wait_at(B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
+                        ok = false;
+                        break;
+                    }
+                    // block (g, ft, kb) is rows [128 * index, +128) of the [blocks * 128, 64] fp16 view
+                    tma_load_2d_pair(smem_u32(w_stage(s)), &wmap, lead_bar(B_FULL(s)), 0,
+                                     (int)((((size_t)ti.g * n_ftiles + ft) * nkb + kb) * 128));
+                }
+                if (!ok) break;
+            }
+        }
     } else if (warp == 2) {
         // ------------------------------------------------ weight loader (this CTA's quantized blocks)
         if (lane == 0) {
@@ -830,7 +856,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                     mbar_wait(bar(B_RAW_FULL(i % PR)), (i / PR) & 1, nullptr, nullptr, 0);
             }
         }
-    } else if (warp >= DEQ_WARP0 && warp < EPI_WARP0) {
+    } else if (!kTmaW && warp >= DEQ_WARP0 && warp < EPI_WARP0) {
         // ------------------------------------------------ dequant (raw stage -> fp16 weight stage)
         const int wg = (warp - DEQ_WARP0) >> 2;
         const int r = 32 * (warp & 3) + lane;
@@ -955,8 +981,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 }
 
 template <int FMT>
-int launch_pair(const CUtensorMap& xmap, const CUtensorMap& omap, const ceb_wplane& w, const ceb_gemm_args& a,
-                int max_pairs, cudaStream_t st) {
+int launch_pair(const CUtensorMap& xmap, const CUtensorMap& omap, const CUtensorMap& wmap, const ceb_wplane& w,
+                const ceb_gemm_args& a, int max_pairs, cudaStream_t st) {
     static int pairs_resident = -1;
     if (pairs_resident < 0) {
         CEB_CUDA_OK(cudaFuncSetAttribute(ceb_gemm_pair_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -971,17 +997,64 @@ int launch_pair(const CUtensorMap& xmap, const CUtensorMap& omap, const ceb_wpla
     }
     int pairs = pairs_resident < max_pairs ? pairs_resident : max_pairs;
     if (pairs < 1) pairs = 1;
-    ceb_gemm_pair_kernel<FMT><<<2 * pairs, NTHREADS, pair::SMEM, st>>>(xmap, omap, w, a);
+    ceb_gemm_pair_kernel<FMT><<<2 * pairs, NTHREADS, pair::SMEM, st>>>(xmap, omap, wmap, w, a);
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
 
 
+// One CTA per block, thread = row: a quantized block -> the fp16 block of the same
+// (group, feature tile, k-block), through the GEMM's own dequantizer, so the values
+// are the fp16 numbers the dequant warps would have put in shared memory.
+template <int FMT>
+__global__ void expand_f16_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t src_blk) {
+    const int r = threadIdx.x;
+    const uint8_t* blk = src + (size_t)blockIdx.x * src_blk;
+    Raw<FMT> raw;
+    load_raw_smem<FMT>(blk, r, raw);  // generic pointer: the block layout is the same in global memory
+    uint32_t o[32];
+    convert<FMT>(raw, o);
+    uint8_t* row = dst + (size_t)blockIdx.x * 16384 + r * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+}
+
 }  // namespace
 
-// The CTA-pair kernel takes quantized weights whose output width is a multiple of
-// 256 (every linear layer of the supported encoders); fp16 weights, narrower or
-// odd widths and unaligned bias vectors use the single-CTA kernel.  Setting
+int ceb_wplane_expand_f16(ceb_wplane* w, cudaStream_t st) {
+    if (w->format == CEB_W_F16) return 0;
+    if (w->format != CEB_W_Q8_0 && w->format != CEB_W_Q4_K) return ceb_set_error(2, "expand: format %d", w->format);
+    const int64_t blocks = (int64_t)w->n_groups * (w->n_out / BM) * (w->k / BK);
+    if (blocks <= 0) return 0;
+    if (blocks > 0x7fffffff) return ceb_set_error(2, "expand: %lld blocks", (long long)blocks);
+    ceb_wplane e = *w;
+    e.format = CEB_W_F16;
+    e.blk_bytes = ceb_wblock_bytes(CEB_W_F16);
+    e.q_bytes = (size_t)blocks * (size_t)e.blk_bytes;
+    e.s_bytes = 0;
+    if (cudaMalloc(&e.q, e.q_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return ceb_set_error(4, "expand: out of device memory (%zu bytes)", e.q_bytes);
+    }
+    if (w->format == CEB_W_Q8_0)
+        expand_f16_kernel<CEB_W_Q8_0><<<(unsigned)blocks, BM, 0, st>>>(w->q, e.q, w->blk_bytes);
+    else
+        expand_f16_kernel<CEB_W_Q4_K><<<(unsigned)blocks, BM, 0, st>>>(w->q, e.q, w->blk_bytes);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess) {
+        cudaFree(e.q);
+        return ceb_set_cuda_error(err, "expand", __FILE__, __LINE__);
+    }
+    ceb_wplane_free(w);
+    *w = e;
+    return 0;
+}
+
+// The CTA-pair kernel takes weights whose output width is a multiple of 256 (every
+// linear layer of the supported encoders) in any plane format; narrower or odd
+// widths and unaligned bias vectors use the single-CTA kernel.  Setting
 // CEB_GEMM_SINGLE_CTA=1 in the environment forces the single-CTA kernel.
 static bool ceb_gemm_use_pairs(const ceb_wplane& w, const ceb_gemm_args& a) {
     static const bool forced_single = [] {
@@ -989,7 +1062,6 @@ static bool ceb_gemm_use_pairs(const ceb_wplane& w, const ceb_gemm_args& a) {
         return e && e[0] == '1';
     }();
     if (forced_single) return false;
-    if (w.format != CEB_W_Q8_0 && w.format != CEB_W_Q4_K) return false;
     if (w.n_out % pair::FEAT) return false;
     if ((a.epi & CEB_EPI_BIAS) &&
         ((reinterpret_cast<uintptr_t>(a.bias) & 15) || (a.offsets && (a.bias_group_stride & 3))))
@@ -1027,11 +1099,19 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
         int max_pairs = ceb_num_sms() / 2;
         if (max_ctas > 0 && max_ctas / 2 < max_pairs) max_pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
         if (bound < max_pairs) max_pairs = (int)bound;
+        CUtensorMap wmap = {};
+        if (w.format == CEB_W_F16) {  // the plane as [blocks * 128 rows, 64] fp16, blocks already swizzled
+            const uint64_t blocks = (uint64_t)w.n_groups * (w.n_out / BM) * (w.k / BK);
+            mrc = ceb_make_tmap_2d(&wmap, w.q, 2, (uint64_t)BK, blocks * BM, (uint64_t)BK * 2, BK, BM, false);
+            if (mrc) return mrc;
+        }
         int rc = 0;
-        if (w.format == CEB_W_Q8_0)
-            CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q8_0>(map, omap, w, a, max_pairs, stream));
-        else
-            CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q4_K>(map, omap, w, a, max_pairs, stream));
+        switch (w.format) {
+            case CEB_W_Q8_0: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q8_0>(map, omap, wmap, w, a, max_pairs, stream)); break;
+            case CEB_W_Q4_K: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q4_K>(map, omap, wmap, w, a, max_pairs, stream)); break;
+            case CEB_W_F16: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_F16>(map, omap, wmap, w, a, max_pairs, stream)); break;
+            default: return ceb_set_error(2, "gemm: unknown weight format %d", w.format);
+        }
         return rc;
     }
     mrc = ceb_make_tmap_2d_f16(&map, act_f16, (uint64_t)w.k, (uint64_t)act_rows, (uint64_t)w.k * 2, BK, BN);

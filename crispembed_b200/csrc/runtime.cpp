@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -212,6 +213,17 @@ int ceb_repack_weights(ceb_wplane* dst, int ggml_type, const void* host_raw, int
     if (e != cudaSuccess) {
         cudaFree(w.q);
         return ceb_set_cuda_error(e, "repack upload", __FILE__, __LINE__);
+    }
+    // Planes the CTA-pair GEMM takes (widths a multiple of 256) are expanded once to
+    // fp16 on the device, so the GEMM loads the MMA's operand image directly instead of
+    // dequantizing every tile again; CEB_WEIGHT_EXPAND=0 keeps the quantized blocks
+    // (half to a quarter of the bytes, dequantized in the GEMM).
+    const char* ex = getenv("CEB_WEIGHT_EXPAND");
+    if (!(ex && ex[0] == '0') && n_out % 256 == 0 && w.format != CEB_W_F16) {
+        if (int rc = ceb_wplane_expand_f16(&w, stream)) {
+            ceb_wplane_free(&w);
+            return rc;
+        }
     }
     *dst = w;
     return 0;

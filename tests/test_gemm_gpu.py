@@ -1,9 +1,11 @@
 """Grouped-GEMM kernels (tcgen05) against the oracle.
 
-Quantized weights with an output width that is a multiple of 256 run on the
-CTA-pair kernel (cta_group::2); other widths and fp16/f32 weights on the
-single-CTA kernel.  The cases below cover both, including partial token tiles
-where only the first CTA of a pair has rows (m mod 256 in 1..128).
+Weights with an output width that is a multiple of 256 run on the CTA-pair
+kernel (cta_group::2), by default from an fp16 plane the loader expanded once on
+the device (CEB_WEIGHT_EXPAND=0 keeps Q8_0 / Q4_K blocks and dequantizes them
+in the kernel); other widths run on the single-CTA kernel.  The cases below
+cover both, including partial token tiles where only the first CTA of a pair
+has rows (m mod 256 in 1..128).
 
 The oracle's F16 mode rounds operands exactly as the kernel does (weights to
 fp16(dequant), activations fp16) and accumulates in double, so the remaining
@@ -149,3 +151,18 @@ def test_matmul_gguf_variants(cuda, oracle, w_type, n_out, k, m):
     ref = oracle.matmul(w_type, raw, n_out, k, x.astype(np.float32), oracle.F16)
     tol = (2e-3 if w_type == G.GGML_IQ4_XS else 2e-4) * max(1.0, float(np.abs(ref).max()))
     assert np.abs(out - ref).max() <= tol, np.abs(out - ref).max()
+
+
+@pytest.mark.parametrize("w_type,n_out,k,m", [CASES[1], CASES[3], CASES[6], CASES[10], CASES[12]])
+def test_expanded_and_streamed_quant_planes_bit_identical(cuda, monkeypatch, w_type, n_out, k, m):
+    """The fp16 plane expanded at load and the quantized plane dequantized inside the
+    pair kernel feed the MMA the same fp16 operands in the same order."""
+    import torch
+    from crispembed_b200 import binding
+    raw, x, bias = _inputs(w_type, n_out, k, m, seed=5 * m + n_out)
+    xd = torch.from_numpy(x).to(cuda)
+    bd = torch.from_numpy(bias).to(cuda)
+    expanded = binding.matmul(w_type, raw, n_out, k, xd, bias=bd, gelu=True).cpu().numpy()
+    monkeypatch.setenv("CEB_WEIGHT_EXPAND", "0")
+    streamed = binding.matmul(w_type, raw, n_out, k, xd, bias=bd, gelu=True).cpu().numpy()
+    assert np.array_equal(expanded, streamed)
