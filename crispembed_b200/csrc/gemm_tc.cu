@@ -546,31 +546,11 @@ int launch_fmt(const CUtensorMap& map, const CUtensorMap& omap, const ceb_wplane
 namespace pair {
 constexpr int TOK = 128;                     // tokens per CTA
 constexpr int FEAT = 256;                    // features per pair tile (MMA N)
-constexpr int PS = 4;                         // A+B stages
-constexpr int PR = 4;                         // raw weight stages
 constexpr int X_BYTES = TOK * BK * 2;        // 16 KB activation tile
-constexpr int W_BYTES = 128 * BK * 2;        // 16 KB dequantized weight tile (this CTA's 128 features)
+constexpr int W_BYTES = 128 * BK * 2;        // 16 KB fp16 weight tile (this CTA's 128 features)
 constexpr int STAGE = X_BYTES + W_BYTES;
 constexpr int SLOT = 32 * 128;               // 32 rows x 128 B, 128-byte swizzled
-constexpr int STAGING = 4 * EPI_WG * SLOT;
-constexpr int NB = 2 * PS + 4 + 1 + 2 * PR + PS + 2;
 constexpr int SIG = 16;                      // bytes of one relayed signal
-constexpr int SIG_BYTES = (PS + 2 + 1) * SIG;  // sinks for FULL[s], ACC_EMPTY[b] + one source
-constexpr size_t SMEM = 1024 + (size_t)PS * STAGE + (size_t)PR * RAW_STAGE + STAGING + SIG_BYTES + NB * 8 + 16 +
-                        3 * (MAXG + 1) * 4;
-static_assert(SMEM <= 227 * 1024, "shared memory budget");
-static_assert(PR % DEQ_WG == 0, "raw stages must map to one dequant warpgroup each");
-static_assert((PS * STAGE + PR * RAW_STAGE) % 1024 == 0, "staging slots must stay 1024-byte aligned");
-
-CEB_DEV int B_FULL(int s) { return s; }
-CEB_DEV int B_EMPTY(int s) { return PS + s; }
-CEB_DEV int B_ACC_FULL(int b) { return 2 * PS + b; }
-CEB_DEV int B_ACC_EMPTY(int b) { return 2 * PS + 2 + b; }
-CEB_DEV int B_DRAIN() { return 2 * PS + 4; }
-CEB_DEV int B_RAW_FULL(int r) { return 2 * PS + 5 + r; }
-CEB_DEV int B_RAW_EMPTY(int r) { return 2 * PS + 5 + PR + r; }
-CEB_DEV int B_W_FULL(int s) { return 2 * PS + 5 + 2 * PR + s; }       // rank 1 only
-CEB_DEV int B_ACC_FREE(int b) { return 3 * PS + 5 + 2 * PR + b; }     // rank 1 only
 
 struct Smem {
     uint64_t* bars;
@@ -584,27 +564,66 @@ struct Smem {
     uint8_t* staging;
     uint8_t* sig;  // [0, PS): FULL sinks, [PS, PS+2): ACC_EMPTY sinks, PS+2: source
 };
-CEB_DEV Smem carve(uint8_t* base) {
-    Smem s;
-    uintptr_t p = (reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023);
-    s.stages = reinterpret_cast<uint8_t*>(p);
-    p += (size_t)PS * STAGE;
-    s.raw = reinterpret_cast<uint8_t*>(p);
-    p += (size_t)PR * RAW_STAGE;
-    s.staging = reinterpret_cast<uint8_t*>(p);
-    p += STAGING;
-    s.sig = reinterpret_cast<uint8_t*>(p);
-    p += SIG_BYTES;
-    s.bars = reinterpret_cast<uint64_t*>(p);
-    p += NB * 8;
-    s.tmem_slot = reinterpret_cast<uint32_t*>(p);
-    s.abort = reinterpret_cast<int*>(p + 4);
-    p += 16;
-    s.g_tile = reinterpret_cast<int*>(p);
-    s.g_row = s.g_tile + (MAXG + 1);
-    s.g_cnt = s.g_row + (MAXG + 1);
-    return s;
-}
+
+// Shared-memory plan and barrier indices for PS A+B stages and PR raw weight stages
+// (PR = 0: fp16 weights loaded by TMA, no raw stage).
+template <int PS_, int PR_, int NSLOT_>
+struct Lay {
+    static constexpr int PS = PS_, PR = PR_;
+    static constexpr int NSLOT = NSLOT_;                        // staging slots per epilogue warp
+    static constexpr int STAGING = 4 * EPI_WG * NSLOT * SLOT;
+    static constexpr int NB = 2 * PS + 4 + 1 + 2 * PR + PS + 2;
+    static constexpr int SIG_BYTES = (PS + 2 + 1) * SIG;  // sinks for FULL[s], ACC_EMPTY[b] + one source
+    static constexpr size_t SMEM = 1024 + (size_t)PS * STAGE + (size_t)PR * RAW_STAGE + STAGING + SIG_BYTES +
+                                   NB * 8 + 16 + 3 * (MAXG + 1) * 4;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(PR % DEQ_WG == 0, "raw stages must map to one dequant warpgroup each");
+    static_assert((PS * STAGE + PR * RAW_STAGE) % 1024 == 0, "staging slots must stay 1024-byte aligned");
+
+    static CEB_DEV int B_FULL(int s) { return s; }
+    static CEB_DEV int B_EMPTY(int s) { return PS + s; }
+    static CEB_DEV int B_ACC_FULL(int b) { return 2 * PS + b; }
+    static CEB_DEV int B_ACC_EMPTY(int b) { return 2 * PS + 2 + b; }
+    static CEB_DEV int B_DRAIN() { return 2 * PS + 4; }
+    static CEB_DEV int B_RAW_FULL(int r) { return 2 * PS + 5 + r; }
+    static CEB_DEV int B_RAW_EMPTY(int r) { return 2 * PS + 5 + PR + r; }
+    static CEB_DEV int B_W_FULL(int s) { return 2 * PS + 5 + 2 * PR + s; }    // rank 1 only
+    static CEB_DEV int B_ACC_FREE(int b) { return 3 * PS + 5 + 2 * PR + b; }  // rank 1 only
+
+    static CEB_DEV Smem carve(uint8_t* base) {
+        Smem s;
+        uintptr_t p = (reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023);
+        s.stages = reinterpret_cast<uint8_t*>(p);
+        p += (size_t)PS * STAGE;
+        s.raw = reinterpret_cast<uint8_t*>(p);
+        p += (size_t)PR * RAW_STAGE;
+        s.staging = reinterpret_cast<uint8_t*>(p);
+        p += STAGING;
+        s.sig = reinterpret_cast<uint8_t*>(p);
+        p += SIG_BYTES;
+        s.bars = reinterpret_cast<uint64_t*>(p);
+        p += NB * 8;
+        s.tmem_slot = reinterpret_cast<uint32_t*>(p);
+        s.abort = reinterpret_cast<int*>(p + 4);
+        p += 16;
+        s.g_tile = reinterpret_cast<int*>(p);
+        s.g_row = s.g_tile + (MAXG + 1);
+        s.g_cnt = s.g_row + (MAXG + 1);
+        return s;
+    }
+};
+#ifndef CEB_PAIR_PS_F16
+#define CEB_PAIR_PS_F16 5
+#endif
+#ifndef CEB_PAIR_SLOTS_F16
+#define CEB_PAIR_SLOTS_F16 2
+#endif
+#ifndef CEB_PAIR_DIRECT_STORE
+#define CEB_PAIR_DIRECT_STORE 0  // 1: every output row stored from registers (no staging, no TMA store)
+#endif
+// quantized weights: 4 A+B stages + 4 raw stages; fp16 weights: the raw bytes become more A+B stages
+template <int FMT>
+using LayOf = Lay<FMT == CEB_W_F16 ? CEB_PAIR_PS_F16 : 4, FMT == CEB_W_F16 ? 0 : 4, FMT == CEB_W_F16 ? CEB_PAIR_SLOTS_F16 : 1>;
 
 struct Tile {
     int g, fp, row0, rows;  // group, feature-pair tile, first token of the pair tile, tokens in it (<= 256)
@@ -655,8 +674,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     // the pair TMA straight into the weight stage, counted on the leader's FULL barrier
     // (no raw stage, no dequant warps, no relayed signal).
     constexpr bool kTmaW = FMT == CEB_W_F16;
+    using L = LayOf<FMT>;
+    constexpr int PS = L::PS, PR = L::PR, NB = L::NB;
     extern __shared__ uint8_t smem_raw[];
-    const Smem SH = pair::carve(smem_raw);
+    const Smem SH = L::carve(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
@@ -672,8 +693,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             if (i < PS) cnt = kTmaW ? 1 : 1 + 4;                            // expect_tx (+ leader dequant warps)
             if (i >= 2 * PS + 2 && i < 2 * PS + 4) cnt = 4 * EPI_WG;        // leader epilogue warps (one with expect_tx)
             if (i >= 2 * PS + 5 + PR && i < 2 * PS + 5 + 2 * PR) cnt = 4;   // this CTA's dequant warpgroup
-            if (i >= B_W_FULL(0) && i < B_W_FULL(0) + PS) cnt = 4;          // rank 1's dequant warpgroup
-            if (i >= B_ACC_FREE(0) && i < B_ACC_FREE(0) + 2) cnt = 4 * EPI_WG;  // rank 1's epilogue warps
+            if (i >= L::B_W_FULL(0) && i < L::B_W_FULL(0) + PS) cnt = 4;          // rank 1's dequant warpgroup
+            if (i >= L::B_ACC_FREE(0) && i < L::B_ACC_FREE(0) + 2) cnt = 4 * EPI_WG;  // rank 1's epilogue warps
             mbar_init(smem_u32(&SH.bars[i]), cnt);
         }
         fence_mbar_init();
@@ -734,19 +755,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                 const Tile ti = pair::decode(SH, G, n_fp, t);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % PS;
-                    if (!wait_at(B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
+                    if (!wait_at(L::B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(bar(B_FULL(s)), kTmaW ? 2 * (X_BYTES + W_BYTES) : 2 * X_BYTES + SIG);
-                    tma_load_2d_pair(smem_u32(x_stage(s)), &xmap, lead_bar(B_FULL(s)), kb * BK,
+                    if (leader) mbar_arrive_expect_tx(bar(L::B_FULL(s)), kTmaW ? 2 * (X_BYTES + W_BYTES) : 2 * X_BYTES + SIG);
+                    tma_load_2d_pair(smem_u32(x_stage(s)), &xmap, lead_bar(L::B_FULL(s)), kb * BK,
                                      ti.row0 + TOK * (int)rank);
                 }
             }
             if (!ok && leader) {  // let issued copies land before the CTA can exit
                 const uint32_t n = it < PS ? it : PS;
                 for (uint32_t i = it - n; i < it; ++i)
-                    mbar_wait_cluster(bar(B_FULL(i % PS)), (i / PS) & 1, nullptr, nullptr, 0);
+                    mbar_wait_cluster(bar(L::B_FULL(i % PS)), (i / PS) & 1, nullptr, nullptr, 0);
             }
         }
     } else if (warp == 1 && !leader) {
@@ -756,9 +777,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             const uint32_t n_items = (uint32_t)(my_tiles * nkb);
             for (uint32_t it = 0; it < n_items; ++it) {
                 const int s = it % PS;
-                if (!wait_at(B_W_FULL(s), (it / PS) & 1, CEB_DEVERR_TIMEOUT_DEQ)) break;
+                if (!wait_at(L::B_W_FULL(s), (it / PS) & 1, CEB_DEVERR_TIMEOUT_DEQ)) break;
                 bulk_copy_to_cluster(mapa_shared(smem_u32(SH.sig + s * SIG), 0), smem_u32(SH.sig + (PS + 2) * SIG),
-                                     SIG, lead_bar(B_FULL(s)));
+                                     SIG, lead_bar(L::B_FULL(s)));
             }
         }
     } else if (warp == 3 && !leader) {
@@ -767,9 +788,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             uint32_t lt = 0;
             for (int t = pair_id; t < total; t += n_pairs, ++lt) {
                 const int ab = lt & 1;
-                if (!wait_at(B_ACC_FREE(ab), (lt >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI)) break;
+                if (!wait_at(L::B_ACC_FREE(ab), (lt >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI)) break;
                 bulk_copy_to_cluster(mapa_shared(smem_u32(SH.sig + (PS + ab) * SIG), 0),
-                                     smem_u32(SH.sig + (PS + 2) * SIG), SIG, lead_bar(B_ACC_EMPTY(ab)));
+                                     smem_u32(SH.sig + (PS + 2) * SIG), SIG, lead_bar(L::B_ACC_EMPTY(ab)));
             }
         }
     } else if (warp == 1) {
@@ -780,12 +801,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             bool ok = true;
             for (int t = pair_id; t < total && ok; t += n_pairs, ++lt) {
                 const int ab = lt & 1;
-                if (!wait_cl(B_ACC_EMPTY(ab), ((lt >> 1) & 1) ^ 1, CEB_DEVERR_TIMEOUT_MMA)) break;
+                if (!wait_cl(L::B_ACC_EMPTY(ab), ((lt >> 1) & 1) ^ 1, CEB_DEVERR_TIMEOUT_MMA)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + (uint32_t)(ab * FEAT);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % PS;
-                    if (!wait_cl(B_FULL(s), (it / PS) & 1, CEB_DEVERR_TIMEOUT_MMA)) {
+                    if (!wait_cl(L::B_FULL(s), (it / PS) & 1, CEB_DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
                     }
@@ -796,20 +817,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                     for (int kk = 0; kk < BK / 16; ++kk)
                         mma_pair_f16_ss(d_tmem, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
                                         (kb | kk) != 0);
-                    mma_pair_commit(bar(B_EMPTY(s)));
-                    mma_pair_commit(mapa_shared(bar(B_EMPTY(s)), 1));
+                    mma_pair_commit(bar(L::B_EMPTY(s)));
+                    mma_pair_commit(mapa_shared(bar(L::B_EMPTY(s)), 1));
                 }
                 if (ok) {
-                    mma_pair_commit(bar(B_ACC_FULL(ab)));
-                    mma_pair_commit(mapa_shared(bar(B_ACC_FULL(ab)), 1));
+                    mma_pair_commit(bar(L::B_ACC_FULL(ab)));
+                    mma_pair_commit(mapa_shared(bar(L::B_ACC_FULL(ab)), 1));
                 }
             }
             // rank 1's last ACC_EMPTY signals (16-byte copies into this CTA) have landed
             for (uint32_t l = lt >= 2 ? lt - 2 : 0; l < lt; ++l)
-                mbar_wait_cluster(bar(B_ACC_EMPTY(l & 1)), (l >> 1) & 1, nullptr, nullptr, 0);
+                mbar_wait_cluster(bar(L::B_ACC_EMPTY(l & 1)), (l >> 1) & 1, nullptr, nullptr, 0);
             // every issued MMA (they write both CTAs' tensor memory) retires before TMEM is released
-            mma_pair_commit(bar(B_DRAIN()));
-            mbar_wait(bar(B_DRAIN()), 0, nullptr, nullptr, 0);
+            mma_pair_commit(bar(L::B_DRAIN()));
+            mbar_wait(bar(L::B_DRAIN()), 0, nullptr, nullptr, 0);
         }
     } else if (warp == 2 && kTmaW) {
         // ------------------------------------------------ weight loader (fp16 blocks, pair TMA)
@@ -821,12 +842,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                 bool ok = true;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % PS;
-                    if (!wait_at(B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
+                    if (!wait_at(L::B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
                     // block (g, ft, kb) is rows [128 * index, +128) of the [blocks * 128, 64] fp16 view
-                    tma_load_2d_pair(smem_u32(w_stage(s)), &wmap, lead_bar(B_FULL(s)), 0,
+                    tma_load_2d_pair(smem_u32(w_stage(s)), &wmap, lead_bar(L::B_FULL(s)), 0,
                                      (int)((((size_t)ti.g * n_ftiles + ft) * nkb + kb) * 128));
                 }
                 if (!ok) break;
@@ -834,6 +855,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp == 2) {
         // ------------------------------------------------ weight loader (this CTA's quantized blocks)
+        if constexpr (!kTmaW) {
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
@@ -841,37 +863,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                 const Tile ti = pair::decode(SH, G, n_fp, t);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int rs = it % PR;
-                    if (!wait_at(B_RAW_EMPTY(rs), ((it / PR) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
+                    if (!wait_at(L::B_RAW_EMPTY(rs), ((it / PR) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(bar(B_RAW_FULL(rs)), (uint32_t)w.blk_bytes);
+                    mbar_arrive_expect_tx(bar(L::B_RAW_FULL(rs)), (uint32_t)w.blk_bytes);
                     bulk_load(smem_u32(SH.raw + (size_t)rs * RAW_STAGE), wblock(ti, kb), (uint32_t)w.blk_bytes,
-                              bar(B_RAW_FULL(rs)));
+                              bar(L::B_RAW_FULL(rs)));
                 }
             }
             if (!ok) {
                 const uint32_t n = it < PR ? it : PR;
                 for (uint32_t i = it - n; i < it; ++i)
-                    mbar_wait(bar(B_RAW_FULL(i % PR)), (i / PR) & 1, nullptr, nullptr, 0);
+                    mbar_wait(bar(L::B_RAW_FULL(i % PR)), (i / PR) & 1, nullptr, nullptr, 0);
             }
+        }
         }
     } else if (!kTmaW && warp >= DEQ_WARP0 && warp < EPI_WARP0) {
         // ------------------------------------------------ dequant (raw stage -> fp16 weight stage)
+        if constexpr (!kTmaW) {
         const int wg = (warp - DEQ_WARP0) >> 2;
         const int r = 32 * (warp & 3) + lane;
         const int my_tiles = pair_id < total ? (total - 1 - pair_id) / n_pairs + 1 : 0;
         const int n_items = my_tiles * nkb;
         for (int i = wg; i < n_items; i += DEQ_WG) {
             const int rs = i % PR, s = i % PS;
-            if (!__all_sync(0xffffffffu, wait_at(B_RAW_FULL(rs), (i / PR) & 1, CEB_DEVERR_TIMEOUT_DEQ))) break;
+            if (!__all_sync(0xffffffffu, wait_at(L::B_RAW_FULL(rs), (i / PR) & 1, CEB_DEVERR_TIMEOUT_DEQ))) break;
             Raw<FMT> raw;
             load_raw_smem<FMT>(SH.raw + (size_t)rs * RAW_STAGE, r, raw);
             uint32_t o[32];
             convert<FMT>(raw, o);
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_RAW_EMPTY(rs)));
-            if (!__all_sync(0xffffffffu, wait_at(B_EMPTY(s), ((i / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_DEQ))) break;
+            if (lane == 0) mbar_arrive(bar(L::B_RAW_EMPTY(rs)));
+            if (!__all_sync(0xffffffffu, wait_at(L::B_EMPTY(s), ((i / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_DEQ))) break;
             uint8_t* row = w_stage(s) + r * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
@@ -879,7 +903,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                     make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(leader ? B_FULL(s) : B_W_FULL(s)));
+            if (lane == 0) mbar_arrive(bar(leader ? L::B_FULL(s) : L::B_W_FULL(s)));
+        }
         }
     } else if (warp >= EPI_WARP0) {
         // ------------------------------------------------ epilogue (this CTA's 128 tokens)
@@ -888,13 +913,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         const int q = warp & 3;                 // TMEM lanes (tokens) 32q .. 32q+31
         const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
         const bool f16 = (a.epi & CEB_EPI_F16_OUT) != 0, gelu = (a.epi & CEB_EPI_GELU) != 0;
-        uint8_t* slot = SH.staging + (size_t)ew * SLOT;
-        const uint32_t slot_u32 = smem_u32(slot);
+        constexpr int NSLOT = L::NSLOT;
         uint32_t lt = 0, nstore = 0;
         for (int t = pair_id; t < total; t += n_pairs, ++lt) {
             const Tile ti = pair::decode(SH, G, n_fp, t);
             const int ab = lt & 1;
-            if (!__all_sync(0xffffffffu, wait_at(B_ACC_FULL(ab), (lt >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI))) break;
+            if (!__all_sync(0xffffffffu, wait_at(L::B_ACC_FULL(ab), (lt >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI))) break;
             tc_fence_after();
             const int my_rows = ti.rows - TOK * (int)rank;   // tokens of the pair tile held by this CTA
             const int lim = my_rows - 32 * q;                 // valid rows of this warp's 32
@@ -905,9 +929,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             const int chunk_cols = f16 ? 64 : 32;
             for (int c0 = 0; c0 < 128; c0 += chunk_cols) {
                 if (lim <= 0) break;
-                const bool full = lim >= 32;
-                if (full && nstore >= 1) {  // the previous store has finished reading the slot
-                    if (lane == 0) bulk_wait_read<0>();
+                const bool full = !CEB_PAIR_DIRECT_STORE && lim >= 32;
+                // slots are used in turn; the store that last used this one has finished reading it
+                uint8_t* slot = SH.staging + (size_t)(ew * NSLOT + (int)(nstore % NSLOT)) * SLOT;
+                const uint32_t slot_u32 = smem_u32(slot);
+                if (full && nstore >= NSLOT) {
+                    if (lane == 0) bulk_wait_read<NSLOT - 1>();
                     __syncwarp();
                 }
                 for (int h = 0; h < chunk_cols; h += 32) {
@@ -961,11 +988,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             __syncwarp();
             if (lane == 0) {
                 if (!leader)
-                    mbar_arrive(bar(B_ACC_FREE(ab)));
+                    mbar_arrive(bar(L::B_ACC_FREE(ab)));
                 else if (ew == 0)
-                    mbar_arrive_expect_tx(bar(B_ACC_EMPTY(ab)), SIG);  // + rank 1's relayed signal
+                    mbar_arrive_expect_tx(bar(L::B_ACC_EMPTY(ab)), SIG);  // + rank 1's relayed signal
                 else
-                    mbar_arrive(bar(B_ACC_EMPTY(ab)));
+                    mbar_arrive(bar(L::B_ACC_EMPTY(ab)));
             }
         }
         if (lane == 0) bulk_wait<0>();  // output stores complete before the CTA retires
@@ -986,18 +1013,18 @@ int launch_pair(const CUtensorMap& xmap, const CUtensorMap& omap, const CUtensor
     static int pairs_resident = -1;
     if (pairs_resident < 0) {
         CEB_CUDA_OK(cudaFuncSetAttribute(ceb_gemm_pair_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)pair::SMEM));
+                                         (int)pair::LayOf<FMT>::SMEM));
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * ceb_num_sms(), 1, 1);
         cfg.blockDim = dim3(NTHREADS, 1, 1);
-        cfg.dynamicSmemBytes = pair::SMEM;
+        cfg.dynamicSmemBytes = pair::LayOf<FMT>::SMEM;
         int n = 0;  // cluster size comes from the kernel's __cluster_dims__
         CEB_CUDA_OK(cudaOccupancyMaxActiveClusters(&n, ceb_gemm_pair_kernel<FMT>, &cfg));
         pairs_resident = n > 0 ? n : 1;
     }
     int pairs = pairs_resident < max_pairs ? pairs_resident : max_pairs;
     if (pairs < 1) pairs = 1;
-    ceb_gemm_pair_kernel<FMT><<<2 * pairs, NTHREADS, pair::SMEM, st>>>(xmap, omap, wmap, w, a);
+    ceb_gemm_pair_kernel<FMT><<<2 * pairs, NTHREADS, pair::LayOf<FMT>::SMEM, st>>>(xmap, omap, wmap, w, a);
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
