@@ -30,10 +30,10 @@ struct crispembed_context {
     cudaStream_t stream = nullptr;
     int device = 0;
     int* d_err = nullptr;
+    int* h_err = nullptr;  // pinned copy of the device error word
     int n_threads = 1;
     std::string prefix;
     int matryoshka_dim = 0;
-    std::vector<float> last_output;
     ceb_tokenizer tok;
     // per-token results (crispembed_encode_tokens*)
     std::vector<float> last_tokens;
@@ -84,11 +84,12 @@ int grow_pinned(T** p, size_t* cap, size_t n) {
 
 // Checks the device error word written by bounded waits / index checks.
 int check_device(crispembed_context* ctx, cudaStream_t st) {
-    cudaError_t e = cudaStreamSynchronize(st);
-    if (e != cudaSuccess) return ceb_set_cuda_error(e, "stream synchronize", __FILE__, __LINE__);
-    int h = 0;
-    e = cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    // the error word rides the stream behind the work (one synchronisation per call)
+    cudaError_t e = cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st);
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "error word read", __FILE__, __LINE__);
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "stream synchronize", __FILE__, __LINE__);
+    const int h = *ctx->h_err;
     if (h) {
         cudaMemset(ctx->d_err, 0, sizeof(int));
         return ceb_set_error(5, "device-side check failed (code 0x%x)", h);
@@ -250,9 +251,8 @@ const float* encode_ids_host(crispembed_context* ctx, const int32_t* ids, const 
         return nullptr;
     }
     if (check_device(ctx, st)) return nullptr;
-    ctx->last_output.assign(ctx->h_out, ctx->h_out + (size_t)n_seqs * dim);
     if (out_n_dim) *out_n_dim = dim;
-    return ctx->last_output.data();
+    return ctx->h_out;  // pinned, owned by the context, valid until the next call
 }
 
 const float* encode_texts(crispembed_context* ctx, const char** texts, int n, int* out_n_dim) {
@@ -331,7 +331,8 @@ extern "C" crispembed_context* crispembed_init(const char* model_path, int n_thr
         }
     }
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) {
+        cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess ||
+        cudaMallocHost((void**)&ctx->h_err, sizeof(int)) != cudaSuccess) {
         ceb_set_error(3, "context setup failed");
         crispembed_free(ctx);
         return nullptr;
@@ -399,6 +400,7 @@ extern "C" void crispembed_free(crispembed_context* ctx) {
     if (ctx->h_ids) cudaFreeHost(ctx->h_ids);
     if (ctx->h_cu) cudaFreeHost(ctx->h_cu);
     if (ctx->h_out) cudaFreeHost(ctx->h_out);
+    if (ctx->h_err) cudaFreeHost(ctx->h_err);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
