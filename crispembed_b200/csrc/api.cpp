@@ -28,6 +28,7 @@ struct crispembed_context {
     ceb_model model;
     ceb_workspace ws;
     cudaStream_t stream = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;  // fences around work moved off the legacy stream
     int device = 0;
     int* d_err = nullptr;
     int* h_err = nullptr;  // pinned copy of the device error word
@@ -217,9 +218,18 @@ int run_device(crispembed_context* ctx, const int32_t* d_ids, const int32_t* h_l
     }
     if (M > (1 << 30)) return ceb_set_error(1, "too many tokens");
     if ((rc = ceb_workspace_reserve(&ctx->ws, ctx->model, (int)M, n_seqs))) return rc;
-    cudaError_t e = cudaMemcpyAsync(ctx->ws.cu, ctx->h_cu, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st);
+    // The legacy default stream cannot be captured into a graph: its work runs on the
+    // context's stream between two event fences, in the caller's stream order.
+    const bool legacy = st == nullptr || st == cudaStreamLegacy;
+    cudaStream_t run = legacy ? ctx->stream : st;
+    if (legacy && (cudaEventRecord(ctx->ev_in, st) != cudaSuccess || cudaStreamWaitEvent(run, ctx->ev_in, 0) != cudaSuccess))
+        return ceb_set_error(3, "stream fence failed");
+    cudaError_t e = cudaMemcpyAsync(ctx->ws.cu, ctx->h_cu, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, run);
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "cu_seqlens upload", __FILE__, __LINE__);
-    return forward_maybe_graph(ctx, d_ids, n_seqs, (int)M, max_len, d_out, st);
+    rc = forward_maybe_graph(ctx, d_ids, n_seqs, (int)M, max_len, d_out, run);
+    if (legacy && (cudaEventRecord(ctx->ev_out, run) != cudaSuccess || cudaStreamWaitEvent(st, ctx->ev_out, 0) != cudaSuccess))
+        return rc ? rc : ceb_set_error(3, "stream fence failed");
+    return rc;
 }
 
 const float* encode_ids_host(crispembed_context* ctx, const int32_t* ids, const int32_t* lens, int n_seqs,
@@ -332,7 +342,9 @@ extern "C" crispembed_context* crispembed_init(const char* model_path, int n_thr
     }
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess ||
-        cudaMallocHost((void**)&ctx->h_err, sizeof(int)) != cudaSuccess) {
+        cudaMallocHost((void**)&ctx->h_err, sizeof(int)) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_out, cudaEventDisableTiming) != cudaSuccess) {
         ceb_set_error(3, "context setup failed");
         crispembed_free(ctx);
         return nullptr;
@@ -401,6 +413,8 @@ extern "C" void crispembed_free(crispembed_context* ctx) {
     if (ctx->h_cu) cudaFreeHost(ctx->h_cu);
     if (ctx->h_out) cudaFreeHost(ctx->h_out);
     if (ctx->h_err) cudaFreeHost(ctx->h_err);
+    if (ctx->ev_in) cudaEventDestroy(ctx->ev_in);
+    if (ctx->ev_out) cudaEventDestroy(ctx->ev_out);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }

@@ -199,3 +199,27 @@ def test_graph_replay_matches_eager(cuda, tiny_model):
         assert np.array_equal(o, first)
     assert len(set(counts)) == 1 and counts[0] > 0
     assert np.array_equal(other, ref2)
+
+
+def test_device_calls_on_default_and_side_streams(cuda, tiny_model):
+    """encode_ids_device on torch's default (legacy) stream runs on the context's own
+    stream between event fences, so it can be graph-captured; the result is ordered
+    before the caller's next work on its stream.  Same embeddings as the host call,
+    on the default stream and on a side stream, first (eager) call and replays."""
+    import torch
+    from crispembed_b200 import binding
+    m = binding.CrispEmbed(tiny_model)
+    ids, lens = synth.ids_ragged(6, 2, 60, seed=41, hi=1000)
+    ref = m.encode_ids(ids, lens)
+    d_ids = torch.from_numpy(ids).to(cuda)
+    for stream in (None, torch.cuda.Stream()):
+        with torch.cuda.stream(stream) if stream is not None else torch.cuda.stream(torch.cuda.current_stream()):
+            out = torch.empty((len(lens), m.dim), dtype=torch.float32, device=cuda)
+            for _ in range(4):
+                out.zero_()
+                m.encode_ids_device(d_ids, lens, out)
+                norms = out.norm(dim=1)                 # queued behind the encode, no host sync
+                got = out.cpu().numpy()
+                assert np.array_equal(got, ref)
+                assert torch.allclose(norms.cpu(), torch.ones(len(lens)), atol=1e-4)
+    m.close()
