@@ -330,6 +330,8 @@ def main():
 
     path = model_path(local) if args.workload in ("c2", "c4") else None
     if world > 1:
+        # NCCL's own log lines (its version banner) go to stderr: stdout carries the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     if args.workload in ("c3", "c5"):
         return bench_moe_op(args, rank, world, local) if rank == 0 else 0
