@@ -418,7 +418,7 @@ def main():
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(ids.nbytes),
                 "d2h_bytes_per_step": int(n_seqs * dim * 4)},
         "gpu_launches": int(launches),
-        "roofline": {"kernel": "ceb_gemm_kernel (grouped tcgen05 GEMM, all linear layers)", "bound": "tensor",
+        "roofline": {"kernel": "ceb_gemm_pair_kernel (grouped tcgen05 CTA-pair GEMM, all linear layers)", "bound": "tensor",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": f"{pk_src} bf16_tflops_sustained", "launches": g["launches"],
                      "flops_per_launch": per_launch_flops, "avg_launch_ms": g["ms"] / max(1, g["launches"]),
