@@ -223,3 +223,23 @@ def test_device_calls_on_default_and_side_streams(cuda, tiny_model):
                 assert np.array_equal(got, ref)
                 assert torch.allclose(norms.cpu(), torch.ones(len(lens)), atol=1e-4)
     m.close()
+
+
+@pytest.mark.parametrize("wtype", [8, 12])  # Q8_0, Q4_K
+def test_expanded_and_quantized_planes_give_identical_embeddings(cuda, tmp_path, monkeypatch, wtype):
+    """The loader expands Q8_0 / Q4_K planes of pair-GEMM width to fp16 once; with
+    CEB_WEIGHT_EXPAND=0 the GEMM dequantizes the blocks per tile instead.  Both feed
+    the MMA the same fp16 values in the same order: bit-identical embeddings."""
+    from crispembed_b200 import binding
+    spec = synth.tiny_spec(wtype=wtype)
+    p = str(tmp_path / f"tiny_{wtype}.gguf")
+    synth.write_model(p, spec)
+    ids, lens = synth.ids_ragged(7, 2, 90, seed=51, hi=1000)
+    m = binding.CrispEmbed(p)
+    expanded = m.encode_ids(ids, lens)
+    m.close()
+    monkeypatch.setenv("CEB_WEIGHT_EXPAND", "0")
+    m = binding.CrispEmbed(p)
+    streamed = m.encode_ids(ids, lens)
+    m.close()
+    assert np.array_equal(expanded, streamed)
