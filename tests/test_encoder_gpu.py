@@ -231,7 +231,7 @@ def test_expanded_and_quantized_planes_give_identical_embeddings(cuda, tmp_path,
     CEB_WEIGHT_EXPAND=0 the GEMM dequantizes the blocks per tile instead.  Both feed
     the MMA the same fp16 values in the same order: bit-identical embeddings."""
     from crispembed_b200 import binding
-    spec = synth.tiny_spec(wtype=wtype)
+    spec = synth.tiny_spec(wtype=wtype, router_wtype=0 if wtype == 12 else None)  # routers: F32 or Q8_0
     p = str(tmp_path / f"tiny_{wtype}.gguf")
     synth.write_model(p, spec)
     ids, lens = synth.ids_ragged(7, 2, 90, seed=51, hi=1000)
