@@ -211,47 +211,68 @@ CEB_DEV void quantize_row(const float4 (&v)[NV], int8_t* q, float* qd, int lane)
     }
 }
 
-// F32 router: logits of one row, all experts.  Each lane forms its partial dot
-// with every expert (its 4 columns per 128), then one butterfly reduces the 32
-// vectors at once (31 shuffles: at offset o a lane keeps half of its values and
-// adds its partner's copy of that half), leaving expert l's logit in lane l;
-// lane (tt, el) then takes experts el + 8j of token tt into lgv[j].
-template <int NV>
-CEB_DEV void f32_logits(const float4 (&v)[NV], const float* __restrict__ wf, int E, int lane, int tt,
-                        float (&lgv)[RT_MAXJ]) {
+// F32 router for two tokens of the group at once (tt0, tt0 + 1): every weight float4
+// loaded feeds both rows, halving the L1 traffic of the router weights, which are
+// re-read for every token.  Experts in passes of P (8 or 16): lane l's partial dot
+// products over its columns, then a transposing butterfly leaves expert e0 + (l % P)
+// of the pass on lane l.  Logits differ from the one-token form only in the order of
+// the cross-lane fp32 sums.
+template <int NV, int P>
+CEB_DEV void f32_logits_pair(const float4 (&v0)[NV], const float4 (&v1)[NV], const float* __restrict__ wf, int E,
+                             int lane, int tt0, float (&lgv)[RT_MAXJ]) {
     constexpr int d = NV * 128;
-    float acc[32];
+    const int tt_l = lane >> 3, el = lane & 7;
+    for (int e0 = 0; e0 < E; e0 += P) {
+        float a0[P], a1[P];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        float a = 0.0f;
-        if (e < E) {
-            const float* wr = wf + (size_t)e * d;
+        for (int e = 0; e < P; ++e) {
+            float s0 = 0.0f, s1 = 0.0f;
+            if (e0 + e < E) {
+                const float* wr = wf + (size_t)(e0 + e) * d;
 #pragma unroll
-            for (int i = 0; i < NV; ++i) {
-                const float4 w = __ldg(reinterpret_cast<const float4*>(wr + (i * 32 + lane) * 4));
-                a = __fmaf_rn(v[i].x, w.x, a);
-                a = __fmaf_rn(v[i].y, w.y, a);
-                a = __fmaf_rn(v[i].z, w.z, a);
-                a = __fmaf_rn(v[i].w, w.w, a);
+                for (int i = 0; i < NV; ++i) {
+                    const float4 w = __ldg(reinterpret_cast<const float4*>(wr + (i * 32 + lane) * 4));
+                    s0 = __fmaf_rn(v0[i].x, w.x, s0);
+                    s0 = __fmaf_rn(v0[i].y, w.y, s0);
+                    s0 = __fmaf_rn(v0[i].z, w.z, s0);
+                    s0 = __fmaf_rn(v0[i].w, w.w, s0);
+                    s1 = __fmaf_rn(v1[i].x, w.x, s1);
+                    s1 = __fmaf_rn(v1[i].y, w.y, s1);
+                    s1 = __fmaf_rn(v1[i].z, w.z, s1);
+                    s1 = __fmaf_rn(v1[i].w, w.w, s1);
+                }
+            }
+            a0[e] = s0;
+            a1[e] = s1;
+        }
+#pragma unroll
+        for (int o = P / 2; o >= 1; o >>= 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < o; ++i) {
+                const float snd0 = up ? a0[i] : a0[i + o], kp0 = up ? a0[i + o] : a0[i];
+                const float snd1 = up ? a1[i] : a1[i + o], kp1 = up ? a1[i + o] : a1[i];
+                a0[i] = __fadd_rn(kp0, __shfl_xor_sync(0xffffffffu, snd0, o));
+                a1[i] = __fadd_rn(kp1, __shfl_xor_sync(0xffffffffu, snd1, o));
             }
         }
-        acc[e] = a;
-    }
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-        const bool up = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < o; ++i) {
-            const float send = up ? acc[i] : acc[i + o];
-            const float keep = up ? acc[i + o] : acc[i];
-            acc[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+        for (int o = P; o < 32; o <<= 1) {
+            a0[0] = __fadd_rn(a0[0], __shfl_xor_sync(0xffffffffu, a0[0], o));
+            a1[0] = __fadd_rn(a1[0], __shfl_xor_sync(0xffffffffu, a1[0], o));
         }
-    }
-    const int el = lane & 7;
 #pragma unroll
-    for (int j = 0; j < RT_MAXJ; ++j) {
-        const float r = __shfl_sync(0xffffffffu, acc[0], el + 8 * j);
-        if ((lane >> 3) == tt) lgv[j] = r;
+        for (int jj = 0; jj < P / 8; ++jj) {
+            const float r0 = __shfl_sync(0xffffffffu, a0[0], el + 8 * jj);
+            const float r1 = __shfl_sync(0xffffffffu, a1[0], el + 8 * jj);
+            const int j = e0 / 8 + jj;
+#pragma unroll
+            for (int q = 0; q < RT_MAXJ; ++q)
+                if (q == j) {
+                    if (tt_l == tt0) lgv[q] = r0;
+                    if (tt_l == tt0 + 1) lgv[q] = r1;
+                }
+        }
     }
 }
 
@@ -375,16 +396,35 @@ __global__ void __launch_bounds__(RT_WARPS * 32, Q8 ? RT_MIN_BLOCKS : 2)
             float lgv[RT_MAXJ];
 #pragma unroll
             for (int j = 0; j < RT_MAXJ; ++j) lgv[j] = -INFINITY;
-            for (int tt = 0; tt < RT_GROUP; ++tt) {
-                const int t = t_base + g + tt;
-                if (t >= T_tokens) break;
-                if (g + tt + 1 < RT_TOK_PER_WARP && t + 1 < T_tokens) rows.prefetch(t + 1, lane);
-                float4 v[NV];
-                rows.row(t, v, lane);
-                if (Q8)
+            if constexpr (Q8) {
+                for (int tt = 0; tt < RT_GROUP; ++tt) {
+                    const int t = t_base + g + tt;
+                    if (t >= T_tokens) break;
+                    if (g + tt + 1 < RT_TOK_PER_WARP && t + 1 < T_tokens) rows.prefetch(t + 1, lane);
+                    float4 v[NV];
+                    rows.row(t, v, lane);
                     quantize_row<NV>(v, xq + (size_t)tt * d, xd + tt * s.nb, lane);
-                else
-                    f32_logits<NV>(v, reinterpret_cast<const float*>(rw), E, lane, tt, lgv);
+                }
+            } else {
+                static_assert(RT_GROUP % 2 == 0, "tokens are routed in pairs");
+                for (int tt = 0; tt < RT_GROUP; tt += 2) {
+                    const int t = t_base + g + tt;
+                    if (t >= T_tokens) break;
+                    for (int n = 2; n < 4; ++n)
+                        if (g + tt + n < RT_TOK_PER_WARP && t + n < T_tokens) rows.prefetch(t + n, lane);
+                    float4 v0[NV], v1[NV];
+                    rows.row(t, v0, lane);
+                    if (t + 1 < T_tokens) {
+                        rows.row(t + 1, v1, lane);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < NV; ++i) v1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    if (E > 8)
+                        f32_logits_pair<NV, 16>(v0, v1, reinterpret_cast<const float*>(rw), E, lane, tt, lgv);
+                    else
+                        f32_logits_pair<NV, 8>(v0, v1, reinterpret_cast<const float*>(rw), E, lane, tt, lgv);
+                }
             }
             __syncwarp();
             const int t_mine = t_base + g + tt_l;
@@ -414,6 +454,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ 
     const int b0 = min(nblk, lane * per), b1 = min(nblk, b0 + per);
     for (int e = warp; e < E; e += nwarps) {
         int s = 0;
+#pragma unroll 8
         for (int b = b0; b < b1; ++b) s += block_counts[(size_t)b * E + e];
         int incl = s;
 #pragma unroll
@@ -434,6 +475,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ 
             if (expert_counts) expert_counts[e] = tot[e];
         }
         int run = base + lane_base[e][lane];
+#pragma unroll 8
         for (int b = b0; b < b1; ++b) {
             block_base[(size_t)b * E + e] = run;
             run += block_counts[(size_t)b * E + e];
@@ -609,6 +651,66 @@ __global__ void combine_kernel(const float* __restrict__ down, const int32_t* __
     }
 }
 
+#ifndef CEB_COMBINE_ROWS
+#define CEB_COMBINE_ROWS 1
+#endif
+// Same sums as combine_kernel, one warp per token with NV float4 columns per lane:
+// the rows of two slots are requested whole before their FMAs (accumulated in slot
+// order), so two expert rows of every token are in flight.
+template <int NV>
+__global__ void __launch_bounds__(128) combine_rows_kernel(const float* __restrict__ down,
+                                                           const int32_t* __restrict__ slot_pos,
+                                                           const float* __restrict__ wts, int T_tokens, int K,
+                                                           const float* __restrict__ bias, float* __restrict__ y) {
+    constexpr int d = NV * 128;
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= T_tokens) return;
+    float4 acc[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int j = 0;
+    for (; j + 1 < K; j += 2) {
+        const int p0 = slot_pos[(size_t)t * K + j], p1 = slot_pos[(size_t)t * K + j + 1];
+        const float w0 = wts[(size_t)t * K + j], w1 = wts[(size_t)t * K + j + 1];
+        float4 r0[NV], r1[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = (i * 32 + lane) * 4;
+            r0[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p0 * d + c));
+            r1[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p1 * d + c));
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            acc[i].x = __fmaf_rn(w1, r1[i].x, __fmaf_rn(w0, r0[i].x, acc[i].x));
+            acc[i].y = __fmaf_rn(w1, r1[i].y, __fmaf_rn(w0, r0[i].y, acc[i].y));
+            acc[i].z = __fmaf_rn(w1, r1[i].z, __fmaf_rn(w0, r0[i].z, acc[i].z));
+            acc[i].w = __fmaf_rn(w1, r1[i].w, __fmaf_rn(w0, r0[i].w, acc[i].w));
+        }
+    }
+    for (; j < K; ++j) {
+        const int p = slot_pos[(size_t)t * K + j];
+        const float w = wts[(size_t)t * K + j];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const float4 r = __ldg(reinterpret_cast<const float4*>(down + (size_t)p * d + (i * 32 + lane) * 4));
+            acc[i].x = __fmaf_rn(w, r.x, acc[i].x);
+            acc[i].y = __fmaf_rn(w, r.y, acc[i].y);
+            acc[i].z = __fmaf_rn(w, r.z, acc[i].z);
+            acc[i].w = __fmaf_rn(w, r.w, acc[i].w);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        float4 o = acc[i];
+        if (bias) {
+            const float4 b = *reinterpret_cast<const float4*>(bias + c);
+            o = make_float4(__fadd_rn(o.x, b.x), __fadd_rn(o.y, b.y), __fadd_rn(o.z, b.z), __fadd_rn(o.w, b.w));
+        }
+        *reinterpret_cast<float4*>(y + (size_t)t * d + c) = o;
+    }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -694,6 +796,26 @@ int with_nv(int d, F&& f) {
     }
 }
 
+// combine of T tokens' K expert rows into y [T, d] (fp32)
+int launch_combine(const float* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
+                   const float* bias, float* y, cudaStream_t st) {
+    const bool vec = CEB_COMBINE_ROWS && d % 128 == 0 && d <= 1024 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+    if (!vec) {
+        CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, combine_kernel<<<T, 256, 0, st>>>(down, slot_pos, wts, T, d, K, bias, y));
+        CEB_CUDA_OK(cudaGetLastError());
+        return 0;
+    }
+    const int grid = (T + 3) / 4;
+    return with_nv(d, [&](auto nvc) {
+        constexpr int NV = decltype(nvc)::value;
+        CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0,
+                   combine_rows_kernel<NV><<<grid, 128, 0, st>>>(down, slot_pos, wts, T, K, bias, y));
+        CEB_CUDA_OK(cudaGetLastError());
+        return 0;
+    });
+}
+
+
 }  // namespace
 
 int ceb_add_ln_route(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
@@ -769,7 +891,7 @@ int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, cons
     rc = ceb_gemm_launch(mw.fc2, ws.h_perm, rows, a2, st);
     if (rc) return rc;
     if (y) {
-        CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, combine_kernel<<<T, 256, 0, st>>>(ws.down, ws.slot_pos, ws.wts, T, d, K, mw.bias, y));
+        if (int rc = launch_combine(ws.down, ws.slot_pos, ws.wts, T, d, K, mw.bias, y, st)) return rc;
         CEB_CUDA_OK(cudaGetLastError());
     }
     return 0;
@@ -802,7 +924,7 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __h
 int ceb_moe_combine(const float* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
                     const float* bias, float* y, cudaStream_t st) {
     if (T <= 0) return 0;
-    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, combine_kernel<<<T, 256, 0, st>>>(down, slot_pos, wts, T, d, K, bias, y));
+    if (int rc = launch_combine(down, slot_pos, wts, T, d, K, bias, y, st)) return rc;
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
