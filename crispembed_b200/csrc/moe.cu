@@ -440,50 +440,65 @@ __global__ void __launch_bounds__(RT_WARPS * 32, Q8 ? RT_MIN_BLOCKS : 2)
 }
 
 // Expert offsets (exclusive scan of the totals) and, per histogram block, the
-// first output row of each expert.  One warp per expert; lane l owns a run of
-// consecutive blocks, so the block order is a warp scan of the lanes' sums.
+// first output row of each expert.  Warp w owns a run of consecutive histogram
+// blocks and lane l the experts l, l + 32, ...: every load and store of a block's
+// counts is one coalesced row, the warps' per-expert sums are scanned across warps
+// in shared memory, and a second pass over the same rows writes the bases.
 // Expert-parallel runs also publish the totals: row `rank` of every peer's count
 // matrix, then a release of the peer's counts flag.
-__global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E,
-                                                    int32_t* __restrict__ block_base, int32_t* __restrict__ offsets,
-                                                    int32_t* __restrict__ expert_counts, ceb_ep_args ep) {
+constexpr int SCAN_WARPS = 32;
+__global__ void __launch_bounds__(SCAN_WARPS * 32) scan_kernel(const int32_t* __restrict__ block_counts, int nblk,
+                                                               int E, int32_t* __restrict__ block_base,
+                                                               int32_t* __restrict__ offsets,
+                                                               int32_t* __restrict__ expert_counts, ceb_ep_args ep) {
+    __shared__ int wbase[SCAN_WARPS][MAXE];  // per warp and expert: sum, then the warp's first row
     __shared__ int tot[MAXE];
-    __shared__ int lane_base[MAXE][32];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    const int per = (nblk + 31) / 32;
-    const int b0 = min(nblk, lane * per), b1 = min(nblk, b0 + per);
-    for (int e = warp; e < E; e += nwarps) {
-        int s = 0;
-#pragma unroll 8
-        for (int b = b0; b < b1; ++b) s += block_counts[(size_t)b * E + e];
-        int incl = s;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += n;
-        }
-        lane_base[e][lane] = incl - s;
-        if (lane == 31) tot[e] = incl;
+    __shared__ int ebase[MAXE];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = (nblk + SCAN_WARPS - 1) / SCAN_WARPS;
+    const int b0 = min(nblk, warp * per), b1 = min(nblk, b0 + per);
+    for (int e = lane; e < E; e += 32) {
+        int sum = 0;
+#pragma unroll 4
+        for (int b = b0; b < b1; ++b) sum += block_counts[(size_t)b * E + e];
+        wbase[warp][e] = sum;
     }
     __syncthreads();
-    for (int e = warp; e < E; e += nwarps) {
-        int base = 0;
-        for (int i = 0; i < e; ++i) base += tot[i];
-        if (lane == 0) {
-            if (e == 0) offsets[0] = 0;
-            offsets[e + 1] = base + tot[e];
-            if (expert_counts) expert_counts[e] = tot[e];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int run = 0;
+        for (int w = 0; w < SCAN_WARPS; ++w) {
+            const int v = wbase[w][e];
+            wbase[w][e] = run;
+            run += v;
         }
-        int run = base + lane_base[e][lane];
-#pragma unroll 8
+        tot[e] = run;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int base = 0;
+        offsets[0] = 0;
+        for (int e = 0; e < E; ++e) {
+            ebase[e] = base;
+            base += tot[e];
+            offsets[e + 1] = base;
+        }
+    }
+    __syncthreads();
+    if (expert_counts)
+        for (int e = threadIdx.x; e < E; e += blockDim.x) expert_counts[e] = tot[e];
+    for (int e = lane; e < E; e += 32) {
+        int run = ebase[e] + wbase[warp][e];
+#pragma unroll 4
         for (int b = b0; b < b1; ++b) {
             block_base[(size_t)b * E + e] = run;
             run += block_counts[(size_t)b * E + e];
         }
-        if (ep.peers && lane < ep.world)
-            ep.peers[lane].counts[((size_t)ep.par * ep.world + ep.rank) * E + e] = tot[e];
     }
     if (ep.peers) {
+        for (int i = threadIdx.x; i < ep.world * E; i += blockDim.x) {
+            const int p = i / E, e = i - p * E;
+            ep.peers[p].counts[((size_t)ep.par * ep.world + ep.rank) * E + e] = tot[e];
+        }
         __threadfence_system();
         __syncthreads();
         if (threadIdx.x < ep.world)
@@ -839,7 +854,7 @@ int ceb_moe_permute(const ceb_moe_weights& mw, const void* x, int x_dtype, const
     const ceb_ep_args none;
     const ceb_ep_args& ea = ep ? *ep : none;
     CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
-               scan_kernel<<<1, 32 * E, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts,
+               scan_kernel<<<1, SCAN_WARPS * 32, 0, st>>>(ws.block_counts, nblk, E, ws.block_base, ws.offsets, expert_counts,
                                                  ea));
     CEB_CUDA_OK(cudaGetLastError());
     if (ep)
