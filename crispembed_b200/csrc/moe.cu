@@ -372,8 +372,8 @@ CEB_DEV void group_route(const float (&lgv)[RT_MAXJ], int E, int K, bool valid, 
 
 // The router over histogram blocks [blockIdx.x, nblk) step gridDim.x; rows come
 // from `rows` (activations in memory, or the fused residual + LayerNorm).
-// Q8 = true: Q8_0 router weights; false: F32 (its 32 per-lane partial sums get a
-// register budget of their own).
+// Q8 = true: Q8_0 router weights; false: F32, two tokens' rows and partial sums in
+// registers at once (hence the register budget of two CTAs per SM).
 template <int NV, bool Q8, class Rows>
 __global__ void __launch_bounds__(RT_WARPS * 32, Q8 ? RT_MIN_BLOCKS : 2)
     route_rows_kernel(Rows rows, int T_tokens, int nblk, int E, int K, const uint8_t* __restrict__ rw,
