@@ -650,6 +650,8 @@ extern "C" int ceb_attention_forward(const void* d_qkv, int n_rows, const int32_
     if (!d_qkv || !d_cu_seqlens || !d_out || n_rows < 0 || n_seqs < 0 || max_len < 0)
         return ceb_set_error(1, "attention: bad arguments");
     if (n_rows == 0 || n_seqs == 0) return 0;
+    if ((reinterpret_cast<uintptr_t>(d_qkv) | reinterpret_cast<uintptr_t>(d_out)) & 15)
+        return ceb_set_error(1, "attention: qkv and out must be 16-byte aligned");
     int* err = op_err_word();
     if (!err) return ceb_set_error(3, "attention: device error word");
     return ceb_attention(static_cast<const __half*>(d_qkv), n_rows, d_cu_seqlens, n_seqs, max_len, d, n_head,

@@ -814,7 +814,9 @@ int with_nv(int d, F&& f) {
 // combine of T tokens' K expert rows into y [T, d] (fp32)
 int launch_combine(const float* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
                    const float* bias, float* y, cudaStream_t st) {
-    const bool vec = CEB_COMBINE_ROWS && d % 128 == 0 && d <= 1024 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+    const bool vec = CEB_COMBINE_ROWS && d % 128 == 0 && d <= 1024 &&
+                     ((reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(down) |
+                       reinterpret_cast<uintptr_t>(y)) & 15) == 0;
     if (!vec) {
         CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, combine_kernel<<<T, 256, 0, st>>>(down, slot_pos, wts, T, d, K, bias, y));
         CEB_CUDA_OK(cudaGetLastError());
@@ -851,6 +853,8 @@ int ceb_moe_permute(const ceb_moe_weights& mw, const void* x, int x_dtype, const
                     cudaStream_t st) {
     const int d = mw.d, E = mw.n_experts, K = mw.top_k;
     const int nblk = (T + CHUNK - 1) / CHUNK;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(x16)) & 15)
+        return ceb_set_error(1, "moe: activations must be 16-byte aligned");
     const ceb_ep_args none;
     const ceb_ep_args& ea = ep ? *ep : none;
     CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
@@ -917,6 +921,8 @@ int ceb_moe_route(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, 
     if (int rc = moe_shape_check(mw)) return rc;
     const int d = mw.d, E = mw.n_experts, K = mw.top_k;
     if (T <= 0) return 0;
+    // rows are read as 16-byte (f32) or 8-byte (bf16 / f16) vectors
+    if (reinterpret_cast<uintptr_t>(x) & 15) return ceb_set_error(1, "moe: activations must be 16-byte aligned");
     return with_nv(d, [&](auto nvc) {
         constexpr int NV = decltype(nvc)::value;
         if (x_dtype == CEB_ACT_F32)

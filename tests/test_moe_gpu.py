@@ -168,3 +168,27 @@ def test_route_ln_matches_oracle(cuda, oracle, name):
     binding.sync_check()
     assert np.array_equal(alias.cpu().numpy(), o)
     layer.close()
+
+
+def test_misaligned_activations_rejected_before_any_launch(cuda):
+    """Rows are read as 16-byte vectors: an activation pointer off a 16-byte boundary
+    is refused on the host with an error, and the next aligned call still works."""
+    import torch
+    from crispembed_b200 import binding
+    inp = synth.make_moe_op_inputs(64, d=256, n_experts=4, top_k=2, ffn=256, wtype=GGML_Q8_0,
+                                   router_wtype=GGML_F32, seed=5)
+    layer = binding.MoELayer(inp.d, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
+                             inp.fc1_raw, inp.fc2_raw, inp.bias)
+    T = inp.x.shape[0]
+    ws = torch.empty(layer.workspace_size(T), dtype=torch.uint8, device=cuda)
+    y = torch.empty((T, inp.d), dtype=torch.float32, device=cuda)
+    flat = torch.zeros(T * inp.d + 4, dtype=torch.float32, device=cuda)
+    x_bad = flat[1:1 + T * inp.d].view(T, inp.d)      # 4 bytes past a 16-byte boundary
+    assert x_bad.data_ptr() % 16 != 0
+    with pytest.raises(binding.CrispEmbedError):
+        layer.forward(x_bad, y, ws)
+    x = torch.from_numpy(inp.x).to(cuda)
+    layer.forward(x, y, ws)
+    binding.sync_check()
+    assert torch.isfinite(y).all()
+    layer.close()
