@@ -65,7 +65,8 @@ CEB_API size_t ceb_moe_workspace_size(const ceb_moe_layer* layer, int max_tokens
  * build_encoder_graph at src/crispembed.cpp:1327-1381:
  *   y[t] = sum_j w[t,j] * fc2_{e_j}( gelu_erf( fc1_{e_j}( x[t] ) ) ) + bias,
  *   (e_j, w[t,j]) = top_k(softmax(router x[t])), weights not renormalised.
- * d_x: [n_tokens x d] activations of type x_dtype.  d_y: [n_tokens x d] floats.
+ * d_x: [n_tokens x d] activations of type x_dtype, 16-byte aligned (status 1
+ * otherwise, nothing launched).  d_y: [n_tokens x d] floats.
  * Optional outputs (may be NULL): d_ids / d_weights [n_tokens x top_k] (slot j =
  * j-th largest probability), d_expert_counts [n_experts], d_logits
  * [n_tokens x n_experts] router logits.  d_workspace: at least
@@ -205,9 +206,11 @@ CEB_API void ceb_tokenizer_free(ceb_text_tokenizer* tok);
  * cu[s] .. cu[s+1]-1) and head h, softmax(Q K^T / sqrt(head_dim)) V, no mask
  * beyond the sequence bounds.  d_qkv [n_rows x 3d] fp16 holds Q | K | V per row
  * (head h at columns h*64 .. h*64+63 of each third); d_out [n_rows x d] fp16.
- * head_dim must be 64.  Sequences of up to 512 tokens run on the tcgen05
- * CTA-pair kernel, longer ones on an mma.sync kernel.  Asynchronous on
- * `stream`; device-side failures surface through ceb_sync_check.
+ * head_dim must be 64; d_qkv and d_out 16-byte aligned (status 1 otherwise).
+ * The default kernel is mma.sync with an online softmax; CEB_ATTN_TC=1 in the
+ * environment selects the tcgen05 CTA-pair kernel for sequences of up to 512
+ * tokens.  Asynchronous on `stream`; device-side failures surface through
+ * ceb_sync_check.
  */
 CEB_API int ceb_attention_forward(const void* d_qkv, int n_rows, const int32_t* d_cu_seqlens, int n_seqs, int max_len,
                                   int d, int n_head, void* d_out, void* stream);
