@@ -30,6 +30,13 @@
 // Tiles (group, token tile, feature tile) are distributed round-robin; the
 // group table is read from device memory, so no host synchronisation is
 // needed between routing and the expert GEMMs.
+//
+// The description above is the single-CTA kernel (ceb_gemm_kernel: other
+// widths).  Layers whose width is a multiple of 256 run ceb_gemm_pair_kernel
+// further down: CTA pairs with tokens as the MMA's M (256 per pair) and 256
+// features as N.  Its weights are usually fp16 planes expanded once at load
+// (ceb_wplane_expand_f16), which both CTAs TMA-load straight into the operand
+// stage; quantized planes are dequantized in shared memory as here.
 #include <cstdio>
 #include <cstdlib>
 
