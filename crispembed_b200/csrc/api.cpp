@@ -5,7 +5,9 @@
 #include <algorithm>
 #include <cctype>
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -54,9 +56,19 @@ struct crispembed_context {
     long long graph_clock = 0;
     // pinned staging for host-buffer calls
     int32_t* h_ids = nullptr;
-    int32_t* h_cu = nullptr;
     float* h_out = nullptr;
-    size_t h_ids_cap = 0, h_cu_cap = 0, h_out_cap = 0;
+    size_t h_ids_cap = 0, h_out_cap = 0;
+    // pinned staging of cu_seqlens, one slot per call in flight: a slot is written again
+    // only after the event recorded behind its copy has completed
+    struct CuSlot {
+        int32_t* h = nullptr;
+        size_t cap = 0;
+        cudaEvent_t ev = nullptr;
+    };
+    static constexpr int N_CU_SLOTS = 4;
+    CuSlot cu_slots[N_CU_SLOTS];
+    unsigned cu_next = 0;
+    cudaEvent_t ev_last = nullptr;  // end of the previous call's work: the workspace is shared
 };
 
 namespace {
@@ -203,18 +215,22 @@ int forward_maybe_graph(crispembed_context* ctx, const int32_t* d_ids, int n_seq
 int run_device(crispembed_context* ctx, const int32_t* d_ids, const int32_t* h_lens, int n_seqs, float* d_out,
                cudaStream_t st) {
     if (n_seqs <= 0) return ceb_set_error(1, "no sequences");
-    int rc = grow_pinned(&ctx->h_cu, &ctx->h_cu_cap, (size_t)n_seqs + 1);
+    auto& slot = ctx->cu_slots[ctx->cu_next++ % crispembed_context::N_CU_SLOTS];
+    if (!slot.ev && cudaEventCreateWithFlags(&slot.ev, cudaEventDisableTiming) != cudaSuccess)
+        return ceb_set_error(3, "event creation failed");
+    if (cudaEventSynchronize(slot.ev) != cudaSuccess) return ceb_set_error(3, "cu_seqlens staging wait failed");
+    int rc = grow_pinned(&slot.h, &slot.cap, (size_t)n_seqs + 1);
     if (rc) return rc;
     int64_t M = 0;
     int max_len = 0;
-    ctx->h_cu[0] = 0;
+    slot.h[0] = 0;
     for (int i = 0; i < n_seqs; ++i) {
         const int n = h_lens[i];
         if (n <= 0 || n > ctx->model.hp.n_max_tokens)
             return ceb_set_error(1, "sequence %d has %d tokens (allowed 1..%d)", i, n, ctx->model.hp.n_max_tokens);
         M += n;
         max_len = std::max(max_len, n);
-        ctx->h_cu[i + 1] = (int32_t)M;
+        slot.h[i + 1] = (int32_t)M;
     }
     if (M > (1 << 30)) return ceb_set_error(1, "too many tokens");
     if ((rc = ceb_workspace_reserve(&ctx->ws, ctx->model, (int)M, n_seqs))) return rc;
@@ -224,12 +240,30 @@ int run_device(crispembed_context* ctx, const int32_t* d_ids, const int32_t* h_l
     cudaStream_t run = legacy ? ctx->stream : st;
     if (legacy && (cudaEventRecord(ctx->ev_in, st) != cudaSuccess || cudaStreamWaitEvent(run, ctx->ev_in, 0) != cudaSuccess))
         return ceb_set_error(3, "stream fence failed");
-    cudaError_t e = cudaMemcpyAsync(ctx->ws.cu, ctx->h_cu, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, run);
+    // calls on other streams share the workspace: this one starts after the previous one
+    if (cudaStreamWaitEvent(run, ctx->ev_last, 0) != cudaSuccess) return ceb_set_error(3, "stream fence failed");
+    cudaError_t e = cudaMemcpyAsync(ctx->ws.cu, slot.h, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, run);
+    if (e == cudaSuccess) e = cudaEventRecord(slot.ev, run);
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "cu_seqlens upload", __FILE__, __LINE__);
     rc = forward_maybe_graph(ctx, d_ids, n_seqs, (int)M, max_len, d_out, run);
+    if (cudaEventRecord(ctx->ev_last, run) != cudaSuccess) return rc ? rc : ceb_set_error(3, "stream fence failed");
     if (legacy && (cudaEventRecord(ctx->ev_out, run) != cudaSuccess || cudaStreamWaitEvent(st, ctx->ev_out, 0) != cudaSuccess))
         return rc ? rc : ceb_set_error(3, "stream fence failed");
     return rc;
+}
+
+// Batches above CEB_MAX_BATCH_TOKENS tokens (default 262144, at least the model's
+// longest sequence) run as consecutive groups of whole sequences, so the
+// activation workspace stays bounded; a sequence's embedding does not depend on
+// the rest of its batch, so the result is that of one call.  Expert-parallel
+// contexts run every call whole: all ranks take the same exchange steps.
+int64_t max_batch_tokens(const crispembed_context* ctx) {
+    int64_t cap = 262144;
+    if (const char* e = getenv("CEB_MAX_BATCH_TOKENS")) {
+        const long long v = atoll(e);
+        if (v > 0) cap = v;
+    }
+    return std::max<int64_t>(cap, ctx->model.hp.n_max_tokens);
 }
 
 const float* encode_ids_host(crispembed_context* ctx, const int32_t* ids, const int32_t* lens, int n_seqs,
@@ -241,24 +275,54 @@ const float* encode_ids_host(crispembed_context* ctx, const int32_t* ids, const 
     if (grow_pinned(&ctx->h_ids, &ctx->h_ids_cap, (size_t)std::max<int64_t>(M, 1)) ||
         grow_pinned(&ctx->h_out, &ctx->h_out_cap, (size_t)n_seqs * dim))
         return nullptr;
-    // the workspace must exist before the id upload targets it
     int max_len = 0;
     for (int i = 0; i < n_seqs; ++i) max_len = std::max(max_len, lens[i]);
     if (max_len <= 0 || max_len > ctx->model.hp.n_max_tokens) {
         ceb_set_error(1, "sequence lengths must lie in 1..%d", ctx->model.hp.n_max_tokens);
         return nullptr;
     }
-    if (ceb_workspace_reserve(&ctx->ws, ctx->model, (int)M, n_seqs)) return nullptr;
-    memcpy(ctx->h_ids, ids, (size_t)M * 4);
-    cudaStream_t st = ctx->stream;
-    if (cudaMemcpyAsync(ctx->ws.ids, ctx->h_ids, (size_t)M * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) {
-        ceb_set_error(3, "id upload failed");
+    // groups [first sequence, end) of at most `cap` tokens (one group unless the batch is larger)
+    const int64_t cap = ctx->model.ep ? INT64_MAX : max_batch_tokens(ctx);
+    std::vector<int> cut{0};
+    int64_t g_tokens = 0, max_g_tokens = 0;
+    int max_g_seqs = 0;
+    for (int i = 0; i < n_seqs; ++i) {
+        const int64_t n = std::max(lens[i], 0);
+        if (i > cut.back() && g_tokens + n > cap) {
+            cut.push_back(i);
+            g_tokens = 0;
+        }
+        g_tokens += n;
+        max_g_tokens = std::max(max_g_tokens, g_tokens);
+        max_g_seqs = std::max(max_g_seqs, i + 1 - cut.back());
+    }
+    cut.push_back(n_seqs);
+    if (max_g_tokens > (1 << 30)) {
+        ceb_set_error(1, "too many tokens");
         return nullptr;
     }
-    if (run_device(ctx, ctx->ws.ids, lens, n_seqs, ctx->ws.out, st)) return nullptr;
-    if (cudaMemcpyAsync(ctx->h_out, ctx->ws.out, (size_t)n_seqs * dim * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
-        ceb_set_error(3, "embedding download failed");
-        return nullptr;
+    // the workspace must exist before the id uploads target it, sized for the largest group
+    if (ceb_workspace_reserve(&ctx->ws, ctx->model, (int)max_g_tokens, max_g_seqs)) return nullptr;
+    memcpy(ctx->h_ids, ids, (size_t)M * 4);
+    cudaStream_t st = ctx->stream;
+    int64_t t0 = 0;
+    for (size_t g = 0; g + 1 < cut.size(); ++g) {
+        const int s0 = cut[g], ns = cut[g + 1] - cut[g];
+        int64_t m = 0;
+        for (int i = s0; i < s0 + ns; ++i) m += std::max(lens[i], 0);
+        // each group's ids come from their own part of the pinned buffer, its embeddings
+        // land in their own rows: stream order alone separates the groups
+        if (cudaMemcpyAsync(ctx->ws.ids, ctx->h_ids + t0, (size_t)m * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            ceb_set_error(3, "id upload failed");
+            return nullptr;
+        }
+        if (run_device(ctx, ctx->ws.ids, lens + s0, ns, ctx->ws.out, st)) return nullptr;
+        if (cudaMemcpyAsync(ctx->h_out + (size_t)s0 * dim, ctx->ws.out, (size_t)ns * dim * 4, cudaMemcpyDeviceToHost,
+                            st) != cudaSuccess) {
+            ceb_set_error(3, "embedding download failed");
+            return nullptr;
+        }
+        t0 += m;
     }
     if (check_device(ctx, st)) return nullptr;
     if (out_n_dim) *out_n_dim = dim;
@@ -344,7 +408,8 @@ extern "C" crispembed_context* crispembed_init(const char* model_path, int n_thr
         cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess ||
         cudaMallocHost((void**)&ctx->h_err, sizeof(int)) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->ev_in, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ctx->ev_out, cudaEventDisableTiming) != cudaSuccess) {
+        cudaEventCreateWithFlags(&ctx->ev_out, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_last, cudaEventDisableTiming) != cudaSuccess) {
         ceb_set_error(3, "context setup failed");
         crispembed_free(ctx);
         return nullptr;
@@ -410,7 +475,11 @@ extern "C" void crispembed_free(crispembed_context* ctx) {
     ceb_model_free(&ctx->model);
     if (ctx->d_err) cudaFree(ctx->d_err);
     if (ctx->h_ids) cudaFreeHost(ctx->h_ids);
-    if (ctx->h_cu) cudaFreeHost(ctx->h_cu);
+    for (auto& slot : ctx->cu_slots) {
+        if (slot.h) cudaFreeHost(slot.h);
+        if (slot.ev) cudaEventDestroy(slot.ev);
+    }
+    if (ctx->ev_last) cudaEventDestroy(ctx->ev_last);
     if (ctx->h_out) cudaFreeHost(ctx->h_out);
     if (ctx->h_err) cudaFreeHost(ctx->h_err);
     if (ctx->ev_in) cudaEventDestroy(ctx->ev_in);

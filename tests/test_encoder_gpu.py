@@ -243,3 +243,41 @@ def test_expanded_and_quantized_planes_give_identical_embeddings(cuda, tmp_path,
     streamed = m.encode_ids(ids, lens)
     m.close()
     assert np.array_equal(expanded, streamed)
+
+
+def test_large_host_batches_run_in_sequence_groups(cuda, tiny_model, monkeypatch):
+    """A host batch above CEB_MAX_BATCH_TOKENS runs as consecutive groups of whole
+    sequences through one workspace; every sequence's embedding is independent of
+    its batch, so the grouped result equals the single call bit for bit."""
+    from crispembed_b200 import binding
+    m = binding.CrispEmbed(tiny_model)
+    ids, lens = synth.ids_ragged(40, 2, 100, seed=61, hi=1000)
+    whole = m.encode_ids(ids, lens)
+    monkeypatch.setenv("CEB_MAX_BATCH_TOKENS", "300")
+    grouped = m.encode_ids(ids, lens)
+    again = m.encode_ids(ids, lens)
+    m.close()
+    assert int(lens.sum()) > 3 * 300
+    assert np.array_equal(whole, grouped)
+    assert np.array_equal(whole, again)
+
+
+def test_device_calls_queued_back_to_back(cuda, tiny_model):
+    """Device-buffer calls with different batches queued without a host synchronisation
+    in between (more calls than row-offset staging slots): each output equals the
+    host call on the same batch."""
+    import torch
+    from crispembed_b200 import binding
+    m = binding.CrispEmbed(tiny_model)
+    batches = [synth.ids_ragged(n, 2, 90, seed=70 + n, hi=1000) for n in (3, 9, 5, 12, 7, 4)]
+    refs = [m.encode_ids(i, l) for i, l in batches]
+    outs = []
+    for i, l in batches:
+        d_ids = torch.from_numpy(i).to(cuda)
+        out = torch.empty((len(l), m.dim), dtype=torch.float32, device=cuda)
+        m.encode_ids_device(d_ids, l, out)
+        outs.append((d_ids, out))
+    torch.cuda.synchronize()
+    for (_, o), r in zip(outs, refs):
+        assert np.array_equal(o.cpu().numpy(), r)
+    m.close()
