@@ -625,9 +625,6 @@ struct Lay {
 #ifndef CEB_PAIR_SLOTS_F16
 #define CEB_PAIR_SLOTS_F16 2
 #endif
-#ifndef CEB_PAIR_DIRECT_STORE
-#define CEB_PAIR_DIRECT_STORE 0  // 1: every output row stored from registers (no staging, no TMA store)
-#endif
 // quantized weights: 4 A+B stages + 4 raw stages; fp16 weights: the raw bytes become more A+B stages
 template <int FMT>
 using LayOf = Lay<FMT == CEB_W_F16 ? CEB_PAIR_PS_F16 : 4, FMT == CEB_W_F16 ? 0 : 4, FMT == CEB_W_F16 ? CEB_PAIR_SLOTS_F16 : 1>;
@@ -936,7 +933,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             const int chunk_cols = f16 ? 64 : 32;
             for (int c0 = 0; c0 < 128; c0 += chunk_cols) {
                 if (lim <= 0) break;
-                const bool full = !CEB_PAIR_DIRECT_STORE && lim >= 32;
+                const bool full = lim >= 32;
                 // slots are used in turn; the store that last used this one has finished reading it
                 uint8_t* slot = SH.staging + (size_t)(ew * NSLOT + (int)(nstore % NSLOT)) * SLOT;
                 const uint32_t slot_u32 = smem_u32(slot);
