@@ -136,21 +136,22 @@ bool ceb_gguf::open(const std::string& path, std::string* err) {
         } else if (v.type == GT_ARR) {
             v.arr_type = (int)c.rd<uint32_t>();
             const uint64_t n = c.rd<uint64_t>();
+            const size_t left = (size_t)(c.end - c.p);
             if (v.arr_type == GT_STR) {
-                if (n > size_) { c.ok = false; break; }
+                if (n > left / 8) { c.ok = false; break; }  // every string needs at least its 8-byte length
                 v.arr_str.reserve(n);
                 for (uint64_t j = 0; j < n && c.ok; ++j) v.arr_str.push_back(c.str());
             } else {
                 const size_t es = scalar_size(v.arr_type);
-                if (!es || !c.need(n * es)) { c.ok = false; break; }
+                if (!es || n > left / es) { c.ok = false; break; }
                 v.arr_num.resize(n);
                 for (uint64_t j = 0; j < n; ++j) v.arr_num[j] = read_num(c, v.arr_type);
             }
         } else {
             const double x = read_num(c, v.type);
-            v.f = x;
-            v.u = (uint64_t)x;
-            v.i = (int64_t)x;
+            v.f = x;  // integer views only where the conversion is defined
+            v.u = (x >= 0.0 && x < 18446744073709551616.0) ? (uint64_t)x : 0;
+            v.i = (x >= -9223372036854775808.0 && x < 9223372036854775808.0) ? (int64_t)x : 0;
         }
         kv_[key] = std::move(v);
     }
@@ -160,7 +161,11 @@ bool ceb_gguf::open(const std::string& path, std::string* err) {
         t.name = c.str();
         const uint32_t nd = c.rd<uint32_t>();
         if (nd == 0 || nd > 4) { c.ok = false; break; }
-        for (uint32_t j = 0; j < nd; ++j) t.ne.push_back((int64_t)c.rd<uint64_t>());
+        for (uint32_t j = 0; j < nd; ++j) {
+            const uint64_t ne = c.rd<uint64_t>();
+            if (ne == 0 || ne > ((uint64_t)1 << 40)) { c.ok = false; break; }  // no tensor of a model file is near
+            t.ne.push_back((int64_t)ne);
+        }
         t.type = (int)c.rd<uint32_t>();
         t.offset = c.rd<uint64_t>();
         infos.push_back(t);
@@ -176,11 +181,17 @@ bool ceb_gguf::open(const std::string& path, std::string* err) {
     const uint64_t data0 = (hdr + align - 1) / align * align;
     for (auto& t : infos) {
         bool ok = true;
-        uint64_t rows = 1;
-        for (size_t j = 1; j < t.ne.size(); ++j) rows *= (uint64_t)t.ne[j];
-        t.nbytes = type_row_bytes(t.type, t.ne[0], &ok) * rows;
-        t.offset += data0;
-        if (!ok || t.offset + t.nbytes > size_) {
+        uint64_t rows = 1;  // overflow-checked: a tensor larger than the file is malformed anyway
+        for (size_t j = 1; j < t.ne.size() && ok; ++j) {
+            if ((uint64_t)t.ne[j] > size_ || rows > size_ / (uint64_t)t.ne[j]) ok = false;
+            else rows *= (uint64_t)t.ne[j];
+        }
+        const uint64_t row_bytes = ok ? type_row_bytes(t.type, t.ne[0], &ok) : 0;
+        if (ok && row_bytes && rows > size_ / row_bytes) ok = false;
+        t.nbytes = row_bytes * rows;
+        if (ok && (t.offset > size_ || data0 > size_ - t.offset)) ok = false;
+        if (ok) t.offset += data0;
+        if (!ok || t.nbytes > size_ || t.offset > size_ - t.nbytes) {
             *err = "tensor '" + t.name + "' has an unsupported type or lies outside the file";
             return false;
         }

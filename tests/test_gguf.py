@@ -39,3 +39,57 @@ def test_synthetic_model_layout(tiny_model):
     assert g.tensors["enc.0.ffn.fc1.weight"].ne == (spec.d, spec.ffn)
     assert g.kv["general.fixture_order"].split(",")[0] == "token_embd.weight"
     assert synth.vocab_word(5) == "aaaa" and synth.vocab_word(6) == "aaab"
+
+
+# ---- the library's own GGUF parser on hostile files (no device: ceb_tokenizer_load
+# parses the file before anything else).  Every count, length and offset of a model
+# file is untrusted; each case must be refused with the parser's own message, never
+# crash or allocate what the file claims.
+import struct
+
+import pytest
+
+GT_U32, GT_STR, GT_ARR, GT_U64 = 4, 8, 9, 10
+
+
+def _s(text):
+    b = text.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def _file(n_tensors=0, n_kv=0, body=b"", version=3, pad=64):
+    return b"GGUF" + struct.pack("<IQQ", version, n_tensors, n_kv) + body + b"\0" * pad
+
+
+def _tensor(name, dims, ggml_type=0, offset=0):
+    return _s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", n) for n in dims) + \
+        struct.pack("<IQ", ggml_type, offset)
+
+
+HOSTILE = {
+    "too_small": (b"GGUF\3\0\0\0", "not a GGUF file"),
+    "no_magic": (b"NOPE" + b"\0" * 60, "no GGUF magic"),
+    "version": (_file(version=7), "unsupported GGUF version"),
+    "kv_past_end": (b"GGUF" + struct.pack("<IQQ", 3, 0, 5) + _s("a") + struct.pack("<I", GT_U32), "malformed"),
+    "string_longer_than_file": (_file(n_kv=1, body=struct.pack("<Q", 1 << 62) + b"k"), "malformed"),
+    "u64_array_count_overflows": (_file(n_kv=1, body=_s("a") + struct.pack("<IIQ", GT_ARR, GT_U64, 1 << 61)),
+                                  "malformed"),
+    "string_array_count_huge": (_file(n_kv=1, body=_s("a") + struct.pack("<IIQ", GT_ARR, GT_STR, 1 << 40)),
+                                "malformed"),
+    "tensor_dim_huge": (_file(n_tensors=1, body=_tensor("t", [1 << 62])), "malformed"),
+    "tensor_dim_zero": (_file(n_tensors=1, body=_tensor("t", [4, 0])), "malformed"),
+    "tensor_rows_overflow": (_file(n_tensors=1, body=_tensor("t", [1 << 39, 1 << 39, 1 << 39])), "outside the file"),
+    "tensor_offset_past_end": (_file(n_tensors=1, body=_tensor("t", [4], offset=(1 << 63) + 7)), "outside the file"),
+    "tensor_offset_wraps": (_file(n_tensors=1, body=_tensor("t", [4], offset=(1 << 64) - 16)), "outside the file"),
+    "tensor_bytes_past_end": (_file(n_tensors=1, body=_tensor("t", [1 << 20])), "outside the file"),
+}
+
+
+@pytest.mark.parametrize("case", sorted(HOSTILE))
+def test_hostile_gguf_refused_with_message(tmp_path, case):
+    from crispembed_b200 import binding
+    blob, msg = HOSTILE[case]
+    p = tmp_path / f"{case}.gguf"
+    p.write_bytes(blob)
+    with pytest.raises(binding.CrispEmbedError, match=msg):
+        binding.Tokenizer(str(p), 128)
