@@ -132,6 +132,21 @@ int ceb_tokenizer::load(const ceb_gguf& g, int max_tok) {
                 break;
             }
     }
+    // every id the encoder can emit must name a piece: the ids index the token table
+    const int n = (int)pieces.size();
+    auto bad = [n](int id) { return id < 0 || id >= n; };
+    const char* which = nullptr;
+    int id = 0;
+    if (family == 2) {
+        if (add_bos && bad(bos_id)) which = "bos", id = bos_id;
+        else if (add_eos && bad(eos_id)) which = "eos", id = eos_id;
+        else if (bad(unk_id)) which = "unknown", id = unk_id;
+    } else if (family == 0) {
+        if (bad(cls_id)) which = "cls", id = cls_id;
+        else if (bad(sep_id)) which = "sep", id = sep_id;
+        else if (bad(unk_id)) which = "unknown", id = unk_id;
+    }
+    if (which) return ceb_set_error(1, "tokenizer: %s token id %d outside the vocabulary of %d pieces", which, id, n);
     return 0;
 }
 

@@ -181,3 +181,39 @@ def test_sentencepiece_nmt_nfkc_normalisation_matches_sentencepiece(spm_nfkc_mod
     tok = binding.Tokenizer(path, max_tokens=512)
     ids = tok.encode(text)
     assert ids[1:-1] == sp.encode(text), (text, ids, sp.encode(text))
+
+
+def _vocab_gguf(path, model, tokens, extra=b""):
+    import struct
+
+    def s(t):
+        b = t.encode()
+        return struct.pack("<Q", len(b)) + b
+    kvs = [s("tokenizer.ggml.model") + struct.pack("<I", 8) + s(model),
+           s("tokenizer.ggml.tokens") + struct.pack("<IIQ", 9, 8, len(tokens)) + b"".join(s(t) for t in tokens)]
+    n_kv = len(kvs)
+    if extra:
+        kvs.append(extra)
+        n_kv += 1
+    path.write_bytes(b"GGUF" + struct.pack("<IQQ", 3, 0, n_kv) + b"".join(kvs) + b"\0" * 64)
+
+
+def test_special_ids_outside_the_vocabulary_refused(tmp_path):
+    """A special id the encoder would emit must name a piece (ids index the token
+    table): SentencePiece bos / unknown and WordPiece cls / sep / unknown ids past
+    the vocabulary are refused when the tokenizer loads."""
+    import struct
+
+    from crispembed_b200 import binding
+    p = tmp_path / "spm.gguf"
+    key = b"".join([struct.pack("<Q", len(b"tokenizer.ggml.bos_token_id")), b"tokenizer.ggml.bos_token_id"])
+    _vocab_gguf(p, "llama", ["<unk>", "<s>", "</s>", "▁h"], extra=key + struct.pack("<II", 4, 77777))
+    with pytest.raises(binding.CrispEmbedError, match="bos token id 77777"):
+        binding.Tokenizer(str(p), 128)
+    p2 = tmp_path / "wpm.gguf"  # WordPiece defaults cls 101 / sep 102 / unk 100 on a 5-piece vocabulary
+    _vocab_gguf(p2, "bert", ["[PAD]", "a", "[UNK]", "[CLS]", "[SEP]"])
+    with pytest.raises(binding.CrispEmbedError, match="cls token id 101"):
+        binding.Tokenizer(str(p2), 128)
+    p3 = tmp_path / "spm_ok.gguf"  # defaults bos 0 / eos 2 / unk 3 all name pieces
+    _vocab_gguf(p3, "llama", ["<unk>", "<s>", "</s>", "▁h"])
+    binding.Tokenizer(str(p3), 128)  # loads
