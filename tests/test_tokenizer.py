@@ -217,3 +217,37 @@ def test_special_ids_outside_the_vocabulary_refused(tmp_path):
     p3 = tmp_path / "spm_ok.gguf"  # defaults bos 0 / eos 2 / unk 3 all name pieces
     _vocab_gguf(p3, "llama", ["<unk>", "<s>", "</s>", "▁h"])
     binding.Tokenizer(str(p3), 128)  # loads
+
+
+@pytest.mark.parametrize("family", ["sentencepiece", "wordpiece"])
+def test_tokenizers_on_arbitrary_bytes(tmp_path, spm_model, family):
+    """Seeded random byte strings (broken UTF-8, control bytes, long runs) through the
+    C entry point: every call returns, truncates to max_tokens and emits only ids
+    of the vocabulary."""
+    import ctypes
+    if family == "sentencepiece":
+        sp, path = spm_model
+        n_vocab = sp.get_piece_size()
+    else:
+        vocab = ["[PAD]", "[CLS]", "[SEP]", "[UNK]", "un", "##aff", "##able", "aff", ",", "hello", "##s"]
+
+        def fill(w):
+            w.add_u32("tokenizer.ggml.type", 0)
+            w.add_str_array("tokenizer.ggml.tokens", vocab)
+            w.add_u32("tokenizer.ggml.cls_token_id", 1)
+            w.add_u32("tokenizer.ggml.sep_token_id", 2)
+            w.add_u32("tokenizer.ggml.unknown_token_id", 3)
+        path = _gguf(tmp_path / "w.gguf", fill)
+        n_vocab = len(vocab)
+    cap = 64
+    tok = binding.Tokenizer(path, max_tokens=cap)
+    buf = (ctypes.c_int32 * cap)()
+    rng = np.random.default_rng(7)
+    for trial in range(400):
+        size = int(rng.integers(0, 300))
+        raw = bytes(rng.integers(1, 256, size=size, dtype=np.uint8))  # no NUL: a C string
+        if trial % 4 == 0:
+            raw = (b"\xe2\x96\x81" * size)[:size] + raw  # runs of the space marker's bytes
+        n = tok._lib.ceb_tokenizer_encode(tok._h, raw, buf, cap)
+        assert 0 < n <= cap, (trial, n)
+        assert all(0 <= buf[i] < n_vocab for i in range(n)), trial
