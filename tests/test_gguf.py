@@ -93,3 +93,43 @@ def test_hostile_gguf_refused_with_message(tmp_path, case):
     p.write_bytes(blob)
     with pytest.raises(binding.CrispEmbedError, match=msg):
         binding.Tokenizer(str(p), 128)
+
+
+def test_mutated_gguf_files_load_or_are_refused(tmp_path):
+    """Seeded byte mutations of a small valid GGUF (tokenizer keys and two tensors):
+    the parser either loads the file or refuses it with an error; it never crashes
+    the process or follows a count, length or offset past the file."""
+    import ctypes
+
+    from crispembed_b200 import binding
+    src = tmp_path / "base.gguf"
+    w = G.GGUFWriter(str(src))
+    w.add_u32("tokenizer.ggml.type", 0)
+    w.add_str_array("tokenizer.ggml.tokens", ["[PAD]", "[CLS]", "[SEP]", "[UNK]", "a", "##b"])
+    w.add_u32("tokenizer.ggml.cls_token_id", 1)
+    w.add_u32("tokenizer.ggml.sep_token_id", 2)
+    w.add_u32("tokenizer.ggml.unknown_token_id", 3)
+    w.add_f32_array("tokenizer.ggml.scores", np.zeros(6, np.float32))
+    w.add_tensor("a.weight", (64, 2), G.GGML_F32, np.zeros((2, 64), np.float32))
+    w.add_tensor("b.weight", (32, 4), G.GGML_Q8_0, quant.quantize(np.ones((4, 32), np.float32), G.GGML_Q8_0))
+    w.write()
+    base = bytearray(src.read_bytes())
+    lib = binding.load_library()
+    rng = np.random.default_rng(11)
+    p = tmp_path / "m.gguf"
+    loaded = refused = 0
+    for trial in range(500):
+        blob = bytearray(base)
+        for _ in range(int(rng.integers(1, 6))):
+            pos = int(rng.integers(0, min(len(blob), 512)))  # the header, key-value and tensor-info region
+            blob[pos] = int(rng.integers(0, 256))
+        if trial % 5 == 0:
+            blob = blob[:int(rng.integers(0, len(blob)))]  # truncated
+        p.write_bytes(bytes(blob))
+        h = lib.ceb_tokenizer_load(str(p).encode(), 64)
+        if h:
+            loaded += 1
+            lib.ceb_tokenizer_free(ctypes.c_void_p(h))
+        else:
+            refused += 1
+    assert loaded + refused == 500 and refused > 0
