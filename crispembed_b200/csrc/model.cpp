@@ -111,8 +111,7 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
     ceb_gguf g;
     std::string err;
     if (!g.open(path, &err)) return ceb_set_error(1, "failed to open '%s': %s", path.c_str(), err.c_str());
-    Loader L{g, m};
-    L.arch = g.get_str("general.architecture");
+    Loader L{g, m, g.get_str("general.architecture")};
     if (g.find("decoder.hidden_size"))
         return ceb_set_error(1, "'%s' is a decoder-embedding model; this library implements the encoder path",
                              path.c_str());
