@@ -44,15 +44,6 @@ constexpr int MAXE = 64;
 constexpr int MAXD = 128 * LN_MAXV;  // rows live in registers, 4 values per lane per 128 columns
 
 template <typename T>
-CEB_DEV float ld_act(const T* p, size_t i);
-template <>
-CEB_DEV float ld_act<float>(const float* p, size_t i) { return p[i]; }
-template <>
-CEB_DEV float ld_act<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) { return __bfloat162float(p[i]); }
-template <>
-CEB_DEV float ld_act<__half>(const __half* p, size_t i) { return __half2float(p[i]); }
-
-template <typename T>
 CEB_DEV float4 ld_act4(const T* p, size_t i);
 template <>
 CEB_DEV float4 ld_act4<float>(const float* p, size_t i) { return *reinterpret_cast<const float4*>(p + i); }
@@ -69,17 +60,6 @@ CEB_DEV float4 ld_act4<__half>(const __half* p, size_t i) {
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
     return make_float4(a.x, a.y, b.x, b.y);
-}
-
-CEB_DEV float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-CEB_DEV float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
 }
 
 // ---------------------------------------------------------------------------
