@@ -51,6 +51,7 @@ def load_library(path: Optional[str] = None):
     i32p = ctypes.POINTER(ctypes.c_int32)
     sig = {
         "crispembed_init": ([cp, ctypes.c_int], vp),
+        "ceb_init_ex": ([cp, ctypes.c_int, ctypes.c_int], vp),
         "crispembed_free": ([vp], None),
         "crispembed_set_dim": ([vp, ctypes.c_int], None),
         "crispembed_set_prefix": ([vp, cp], None),
@@ -62,6 +63,8 @@ def load_library(path: Optional[str] = None):
         "crispembed_encode_ids_batch": ([vp, i32p, i32p, ctypes.c_int, ip], fp),
         "crispembed_encode_ids_device": ([vp, vp, i32p, ctypes.c_int, vp, ip, vp], ctypes.c_int),
         "crispembed_stream": ([vp], vp),
+        "ceb_encode_ids_routes": ([vp, i32p, i32p, ctypes.c_int, vp, vp, vp], ctypes.c_int),
+        "ceb_moe_block_count": ([vp], ctypes.c_int),
         "crispembed_has_sparse": ([vp], ctypes.c_int),
         "crispembed_has_colbert": ([vp], ctypes.c_int),
         "crispembed_is_reranker": ([vp], ctypes.c_int),
@@ -139,9 +142,15 @@ def _ptr(t) -> Optional[int]:
 class CrispEmbed:
     """Text/ids -> L2-normalised embeddings through libcrispembed.so."""
 
-    def __init__(self, model_path: str, n_threads: int = 4, lib_path: Optional[str] = None):
+    def __init__(self, model_path: str, n_threads: int = 4, lib_path: Optional[str] = None,
+                 reference_arithmetic: bool = False):
+        """reference_arithmetic: encode in the reference's CPU arithmetic bit for bit
+        (ceb_init_ex with CEB_INIT_REFERENCE_ARITHMETIC; CUDA cores, slow)."""
         self._lib = load_library(lib_path)
-        self._ctx = self._lib.crispembed_init(model_path.encode(), n_threads)
+        if reference_arithmetic:
+            self._ctx = self._lib.ceb_init_ex(model_path.encode(), n_threads, 1)
+        else:
+            self._ctx = self._lib.crispembed_init(model_path.encode(), n_threads)
         if not self._ctx:
             raise CrispEmbedError(f"Failed to load model: {model_path}: {last_error()}")
 
@@ -159,6 +168,10 @@ class CrispEmbed:
     @property
     def hparams(self) -> _Hparams:
         return self._lib.crispembed_get_hparams(self._ctx).contents
+
+    @property
+    def n_moe_blocks(self) -> int:
+        return int(self._lib.ceb_moe_block_count(self._ctx))
 
     @property
     def dim(self) -> int:
@@ -229,6 +242,23 @@ class CrispEmbed:
         if not ptr:
             raise CrispEmbedError(f"encode_ids failed: {last_error()}")
         return np.ctypeslib.as_array(ptr, shape=(len(lens) * dim.value,)).copy().reshape(len(lens), dim.value)
+
+    def encode_ids_routes(self, ids: np.ndarray, lens: Sequence[int]):
+        """(embeddings [n_seqs, dim], expert ids [n_moe, M, top_k], router logits
+        [n_moe, M, n_experts]) of one synchronous encode (ceb_encode_ids_routes)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        lens = np.ascontiguousarray(lens, dtype=np.int32)
+        hp = self.hparams
+        M, E, K = int(lens.sum()), int(hp.n_experts), int(hp.n_experts_per_tok)
+        n_moe = self.n_moe_blocks
+        emb = np.empty((len(lens), self.dim), dtype=np.float32)
+        rid = np.empty((n_moe, M, max(K, 1)), dtype=np.int32)
+        lg = np.empty((n_moe, M, max(E, 1)), dtype=np.float32)
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        rc = self._lib.ceb_encode_ids_routes(self._ctx, ids.ctypes.data_as(i32p), lens.ctypes.data_as(i32p), len(lens),
+                                             emb.ctypes.data, rid.ctypes.data, lg.ctypes.data)
+        _check(rc, "encode_ids_routes")
+        return emb, rid, lg
 
     def encode_ids_device(self, d_ids, lens: np.ndarray, d_out, stream=None) -> int:
         """d_ids: int32 CUDA tensor, d_out: float32 CUDA tensor [n_seqs, dim]."""

@@ -21,8 +21,9 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libcrispembed.so")
 
-SOURCES = ["gemm_tc.cu", "attn_tc.cu", "moe.cu", "moe_static.cu", "ep.cu", "encoder_kernels.cu", "runtime.cpp", "gguf_quants.cpp", "gguf.cpp", "tokenizer.cpp", "model.cpp", "api.cpp"]
-HEADERS = ["common.cuh", "rowwise.cuh", "ceb_internal.h", "ceb_moe_internal.h", "ceb_ep_internal.h", "ceb_encoder_internal.h", "gguf.h", "tokenizer.h", "spm_norm_table.inc"]
+SOURCES = ["gemm_tc.cu", "attn_tc.cu", "moe.cu", "moe_static.cu", "ep.cu", "encoder_kernels.cu", "ref_arith.cu", "runtime.cpp", "gguf_quants.cpp", "gguf.cpp", "tokenizer.cpp", "model.cpp", "api.cpp"]
+HEADERS = ["common.cuh", "rowwise.cuh", "ceb_internal.h", "ceb_moe_internal.h", "ceb_ep_internal.h", "ceb_encoder_internal.h", "gguf.h", "tokenizer.h", "spm_norm_table.inc",
+           "ceb_portable_math.h"]
 PUBLIC_HEADERS = [os.path.join(ROOT, "include", h) for h in ("crispembed.h", "ceb_ops.h")]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -39,7 +40,9 @@ def _flags(src: str):
     common = ["-O3", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", CSRC,
               "-I", os.path.join(ROOT, "include"), "-DCRISPEMBED_BUILD=1"]
     if src.endswith(".cu"):
-        return ARCH + ["-lineinfo", "-Xptxas", "-warn-spills"] + common
+        # the reference-arithmetic kernels fuse only the multiply-adds written as fmaf
+        exact = ["-fmad=false"] if src == "ref_arith.cu" else []
+        return ARCH + ["-lineinfo", "-Xptxas", "-warn-spills"] + exact + common
     return ["-x", "cu"] + ARCH + common if src == "api.cpp" else common
 
 

@@ -382,8 +382,18 @@ std::string g_str;  // backing store for the registry helpers
 
 // =========================================================== crispembed.h ===
 extern "C" crispembed_context* crispembed_init(const char* model_path, int n_threads) {
+    const char* ra = getenv("CEB_REFERENCE_ARITHMETIC");
+    return ceb_init_ex(model_path, n_threads, (ra && ra[0] == '1') ? CEB_INIT_REFERENCE_ARITHMETIC : 0);
+}
+
+extern "C" crispembed_context* ceb_init_ex(const char* model_path, int n_threads, int flags) {
     if (!model_path) return nullptr;
+    if (flags & ~CEB_INIT_REFERENCE_ARITHMETIC) {
+        ceb_set_error(1, "init: unknown flags 0x%x", flags);
+        return nullptr;
+    }
     auto* ctx = new crispembed_context;
+    ctx->model.ref_arith = (flags & CEB_INIT_REFERENCE_ARITHMETIC) != 0;
     ctx->n_threads = resolve_threads(n_threads);
     if (cudaGetDevice(&ctx->device) != cudaSuccess || cudaFree(nullptr) != cudaSuccess) {
         ceb_set_error(3, "no CUDA device available");
@@ -416,9 +426,10 @@ extern "C" crispembed_context* crispembed_init(const char* model_path, int n_thr
     }
     int moe = 0;
     for (const auto& Ly : ctx->model.layers) moe += Ly.moe;
-    fprintf(stderr, "crispembed-b200: loaded %d layers (%d MoE, %d experts top-%d), %d dims, %d vocab, %.1f MB weights\n",
+    fprintf(stderr, "crispembed-b200: loaded %d layers (%d MoE, %d experts top-%d), %d dims, %d vocab, %.1f MB weights%s\n",
             ctx->model.hp.n_layer, moe, ctx->model.hp.n_experts, ctx->model.hp.n_experts_per_tok,
-            ctx->model.hp.n_embd, ctx->model.hp.n_vocab, ctx->model.weight_bytes / 1e6);
+            ctx->model.hp.n_embd, ctx->model.hp.n_vocab, ctx->model.weight_bytes / 1e6,
+            ctx->model.ref_arith ? ", reference arithmetic" : "");
     return ctx;
 }
 
@@ -463,6 +474,63 @@ extern "C" int crispembed_encode_ids_device(crispembed_context* ctx, const int32
     if (!ctx || !d_ids || !h_lens || !d_out) return ceb_set_error(1, "null argument");
     if (out_n_dim) *out_n_dim = out_dim_of(ctx);
     return run_device(ctx, d_ids, h_lens, n_seqs, d_out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ceb_moe_block_count(const crispembed_context* ctx) {
+    int n = 0;
+    if (ctx)
+        for (const auto& Ly : ctx->model.layers) n += Ly.moe;
+    return n;
+}
+
+extern "C" int ceb_encode_ids_routes(crispembed_context* ctx, const int32_t* h_ids, const int32_t* h_lens, int n_seqs,
+                                     float* h_out, int32_t* h_route_ids, float* h_route_logits) {
+    if (!ctx || !h_ids || !h_lens || n_seqs <= 0) return ceb_set_error(1, "encode_ids_routes: bad arguments");
+    if (ctx->model.ep) return ceb_set_error(1, "encode_ids_routes: not available on an expert-parallel context");
+    int n_moe = 0, E = 0, K = 0;
+    for (const auto& Ly : ctx->model.layers)
+        if (Ly.moe) {
+            ++n_moe;
+            E = Ly.moew.n_experts;
+            K = Ly.moew.top_k;
+        }
+    std::vector<int32_t> cu((size_t)n_seqs + 1, 0);
+    int max_len = 0;
+    for (int i = 0; i < n_seqs; ++i) {
+        if (h_lens[i] <= 0 || h_lens[i] > ctx->model.hp.n_max_tokens)
+            return ceb_set_error(1, "sequence %d has %d tokens (allowed 1..%d)", i, h_lens[i], ctx->model.hp.n_max_tokens);
+        cu[(size_t)i + 1] = cu[(size_t)i] + h_lens[i];
+        max_len = std::max(max_len, (int)h_lens[i]);
+    }
+    const int M = cu[(size_t)n_seqs];
+    int rc = ceb_workspace_reserve(&ctx->ws, ctx->model, M, n_seqs);
+    if (rc) return rc;
+    cudaStream_t st = ctx->stream;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return ceb_set_error(3, "stream synchronize");
+    ceb_route_capture cap;
+    const size_t ids_bytes = (size_t)n_moe * M * K * 4, lg_bytes = (size_t)n_moe * M * E * 4;
+    if (n_moe && (cudaMalloc(&cap.ids, ids_bytes) != cudaSuccess || cudaMalloc(&cap.logits, lg_bytes) != cudaSuccess)) {
+        cudaFree(cap.ids);
+        return ceb_set_error(4, "encode_ids_routes: out of device memory");
+    }
+    const int dim = out_dim_of(ctx);
+    cudaError_t e = cudaMemcpyAsync(ctx->ws.ids, h_ids, (size_t)M * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ctx->ws.cu, cu.data(), cu.size() * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) rc = ceb_set_cuda_error(e, "encode_ids_routes upload", __FILE__, __LINE__);
+    if (!rc)
+        rc = ceb_encoder_forward(ctx->model, ctx->ws, ctx->ws.ids, ctx->ws.cu, n_seqs, M, max_len, ctx->ws.out, dim,
+                                 ctx->d_err, st, &cap);
+    if (!rc && h_out) e = cudaMemcpyAsync(h_out, ctx->ws.out, (size_t)n_seqs * dim * 4, cudaMemcpyDeviceToHost, st);
+    if (!rc && n_moe && h_route_ids && e == cudaSuccess)
+        e = cudaMemcpyAsync(h_route_ids, cap.ids, ids_bytes, cudaMemcpyDeviceToHost, st);
+    if (!rc && n_moe && h_route_logits && e == cudaSuccess)
+        e = cudaMemcpyAsync(h_route_logits, cap.logits, lg_bytes, cudaMemcpyDeviceToHost, st);
+    if (!rc && e != cudaSuccess) rc = ceb_set_cuda_error(e, "encode_ids_routes download", __FILE__, __LINE__);
+    if (!rc) rc = check_device(ctx, st);
+    cudaStreamSynchronize(st);
+    cudaFree(cap.ids);
+    cudaFree(cap.logits);
+    return rc;
 }
 
 extern "C" void* crispembed_stream(crispembed_context* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
@@ -694,6 +762,7 @@ extern "C" int ceb_moe_route_ln(const ceb_moe_layer* L, const float* d_res, cons
 
 extern "C" int ceb_ep_attach(crispembed_context* ctx, ceb_ep* ep) {
     if (!ctx || !ep) return ceb_set_error(1, "ep_attach: bad arguments");
+    if (ctx->model.ref_arith) return ceb_set_error(1, "ep_attach: not available with reference arithmetic");
     cudaSetDevice(ctx->device);
     return ceb_model_ep_attach(&ctx->model, ep);
 }

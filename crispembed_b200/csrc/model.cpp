@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -95,12 +96,22 @@ struct Loader {
         return 0;
     }
 
-    // one linear weight [n_out x k] (2-D tensor ne = {k, n_out})
-    int plane(const ceb_gguf_tensor* t, int n_out, int k, ceb_wplane* w) {
+    // one linear weight [n_out x k] (2-D tensor ne = {k, n_out}); with reference
+    // arithmetic also the form its kernels read
+    int plane(const ceb_gguf_tensor* t, int n_out, int k, ceb_wplane* w, ceb_refmat* r) {
         if (!t || t->ne.size() < 2 || t->ne[0] != k || t->ne[1] != n_out)
             return ceb_set_error(1, "weight '%s' has an unexpected shape", t ? t->name.c_str() : "?");
         int rc = ceb_repack_weights(w, t->type, g.data(*t), 1, n_out, k, st);
         if (!rc) m->weight_bytes += w->q_bytes + w->s_bytes;
+        if (!rc) rc = ref(r, t->type, g.data(*t), 1, n_out, k);
+        return rc;
+    }
+
+    int ref(ceb_refmat* r, int type, const void* data, int groups, int n_out, int k) {
+        if (!m->ref_arith) return 0;
+        const int rc = ceb_refmat_create(r, type, data, groups, n_out, k);
+        if (!rc) m->weight_bytes += (size_t)groups * n_out * k * (r->type == CEB_GGML_Q8_0 ? 1 : 4) +
+                                    (r->type == CEB_GGML_Q8_0 ? (size_t)groups * n_out * (k / 32) * 4 : 0);
         return rc;
     }
 };
@@ -209,7 +220,7 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
         const ceb_gguf_tensor* k = L.any({p + "attn.k.weight", b + "attn_k.weight"});
         const ceb_gguf_tensor* v = L.any({p + "attn.v.weight", b + "attn_v.weight"});
         if (qkv) {
-            rc = L.plane(qkv, 3 * d, d, &Ly.qkv);
+            rc = L.plane(qkv, 3 * d, d, &Ly.qkv, &Ly.r_qkv);
         } else if (q && k && v && q->type == k->type && k->type == v->type) {
             const int64_t rbytes = (int64_t)q->nbytes;
             std::vector<uint8_t> cat((size_t)(3 * rbytes));
@@ -217,6 +228,7 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
             memcpy(cat.data() + rbytes, g.data(*k), (size_t)rbytes);
             memcpy(cat.data() + 2 * rbytes, g.data(*v), (size_t)rbytes);
             rc = ceb_repack_weights(&Ly.qkv, q->type, cat.data(), 1, 3 * d, d, st);
+            if (!rc) rc = L.ref(&Ly.r_qkv, q->type, cat.data(), 1, 3 * d, d);
         } else if (q && k && v) {
             // mixed formats (llama.cpp's K-quant mixes give attn_v its own type): rows
             // re-encoded as Q8_0 blocks when every part allows it, else decoded to fp32
@@ -243,6 +255,11 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
             }
             if (!rc)
                 rc = ceb_repack_weights(&Ly.qkv, as_q8 ? CEB_GGML_Q8_0 : CEB_GGML_F32, cat.data(), 1, 3 * d, d, st);
+            // the reference multiplies each part in its own format: the common form is exact only for floats
+            auto flt = [](int t) { return t == CEB_GGML_F32 || t == CEB_GGML_F16 || t == CEB_GGML_BF16; };
+            if (!rc && m->ref_arith && !(flt(q->type) && flt(k->type) && flt(v->type)))
+                rc = ceb_set_error(2, "reference arithmetic: layer %d mixes attention weight formats", il);
+            if (!rc) rc = L.ref(&Ly.r_qkv, CEB_GGML_F32, cat.data(), 1, 3 * d, d);
         } else {
             rc = ceb_set_error(1, "layer %d: missing attention q/k/v weights", il);
         }
@@ -268,7 +285,7 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
                 if (!rc) rc = L.upload_raw(cat.data(), cat.size() * 4, reinterpret_cast<uint8_t**>(&Ly.qkv_b));
             }
         }
-        if (!rc) rc = L.plane(L.any({p + "attn.o.weight", b + "attn_output.weight"}), d, d, &Ly.o);
+        if (!rc) rc = L.plane(L.any({p + "attn.o.weight", b + "attn_output.weight"}), d, d, &Ly.o, &Ly.r_o);
         if (!rc) rc = L.upload_f32(L.any({p + "attn.o.bias", b + "attn_output.bias"}), &Ly.o_b, d);
         if (!rc) rc = L.upload_f32(L.any({p + "ln1.weight", b + "attn_output_norm.weight", b + "attn_norm.weight"}),
                                    &Ly.ln1_w, d);
@@ -309,6 +326,9 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
             rc = L.upload_raw(g.data(*gate), gate->nbytes, &mw.router);
             if (!rc) rc = ceb_repack_weights(&mw.fc1, e1->type, g.data(*e1), E, F, d, st);
             if (!rc) rc = ceb_repack_weights(&mw.fc2, e2->type, g.data(*e2), E, d, F, st);
+            if (!rc) rc = L.ref(&Ly.r_router, gate->type, g.data(*gate), 1, E, d);
+            if (!rc) rc = L.ref(&Ly.r_e1, e1->type, g.data(*e1), E, F, d);
+            if (!rc) rc = L.ref(&Ly.r_e2, e2->type, g.data(*e2), E, d, F);
             if (!rc) m->weight_bytes += mw.fc1.q_bytes + mw.fc1.s_bytes + mw.fc2.q_bytes + mw.fc2.s_bytes;
             if (!rc) rc = L.upload_f32(g.tensor(p + "ffn.moe_bias"), &mw.bias, d);
         } else {
@@ -323,11 +343,16 @@ int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out) 
                 break;
             }
             const int F = (int)f1->ne[1];
-            rc = L.plane(f1, F, d, &Ly.fc1);
+            rc = L.plane(f1, F, d, &Ly.fc1, &Ly.r_fc1);
             if (!rc) rc = L.upload_f32(L.any({p + "ffn.fc1.bias", b + "ffn_up.bias"}), &Ly.fc1_b, F);
-            if (!rc) rc = L.plane(f2, d, F, &Ly.fc2);
+            if (!rc) rc = L.plane(f2, d, F, &Ly.fc2, &Ly.r_fc2);
             if (!rc) rc = L.upload_f32(L.any({p + "ffn.fc2.bias", b + "ffn_down.bias"}), &Ly.fc2_b, d);
         }
+    }
+    if (!rc && m->ref_arith) {
+        if (m->use_rope) rc = ceb_set_error(2, "reference arithmetic covers encoders with learned positions");
+        else if (m->pool_method != 0) rc = ceb_set_error(2, "reference arithmetic covers mean pooling");
+        else if ((size_t)d * 4 * 8 > 48 * 1024) rc = ceb_set_error(2, "reference arithmetic: width %d too large", d);
     }
     cudaStreamDestroy(st);
     if (rc) ceb_model_free(m);
@@ -369,6 +394,8 @@ int ceb_model_ep_attach(ceb_model* m, ceb_ep* ep) {
 
 void ceb_model_free(ceb_model* m) {
     for (auto& Ly : m->layers) {
+        for (ceb_refmat* r : {&Ly.r_qkv, &Ly.r_o, &Ly.r_fc1, &Ly.r_fc2, &Ly.r_router, &Ly.r_e1, &Ly.r_e2})
+            ceb_refmat_free(r);
         ceb_wplane_free(&Ly.qkv);
         ceb_wplane_free(&Ly.o);
         ceb_wplane_free(&Ly.fc1);
@@ -410,6 +437,30 @@ int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int
     const size_t moe_bytes = ceb_moe_ws_layout(T, d, E, K, Fm, nullptr, nullptr);
     const size_t o_moe = take(moe_bytes);
     const size_t o_ids = take((size_t)T * 4), o_cu = take((size_t)(S + 1) * 4), o_out = take((size_t)S * d * 4);
+    // reference arithmetic: fp32 activations, Q8_0 copies of every matrix input, expert rows
+    // padded to whole 32-row tiles per expert
+    size_t r_qkv = 0, r_attn = 0, r_h = 0, r_xp = 0, r_down = 0, r_lg = 0, r_wts = 0, r_xq = 0, r_xd = 0, r_ids = 0,
+           r_pos = 0, r_src = 0, r_tg = 0;
+    int n_tiles = 0;
+    if (m.ref_arith) {
+        n_tiles = (int)(((int64_t)T * K + (int64_t)E * 31 + 31) / 32);
+        const size_t rows_pad = (size_t)n_tiles * 32;
+        const size_t wmax = (size_t)std::max(std::max(d, F), Fm);
+        const size_t qrows = std::max((size_t)T, rows_pad);
+        r_qkv = take((size_t)T * 3 * d * 4);
+        r_attn = take((size_t)T * d * 4);
+        r_h = take(std::max((size_t)T * (F > 0 ? F : 128), rows_pad * Fm) * 4);
+        r_xp = take(rows_pad * d * 4);
+        r_down = take(rows_pad * d * 4);
+        r_lg = take((size_t)T * E * 4);
+        r_wts = take((size_t)T * K * 4);
+        r_xq = take(qrows * wmax);
+        r_xd = take(qrows * (wmax / 32) * 4);
+        r_ids = take((size_t)T * K * 4);
+        r_pos = take((size_t)T * K * 4);
+        r_src = take(rows_pad * 4);
+        r_tg = take((size_t)n_tiles * 4);
+    }
     void* base = nullptr;
     if (cudaMalloc(&base, off) != cudaSuccess)
         return ceb_set_error(4, "out of device memory for a %d-token workspace (%.2f GB)", T, off / 1e9);
@@ -431,6 +482,23 @@ int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int
     ws->ids = reinterpret_cast<int32_t*>(b + o_ids);
     ws->cu = reinterpret_cast<int32_t*>(b + o_cu);
     ws->out = reinterpret_cast<float*>(b + o_out);
+    if (m.ref_arith) {
+        ceb_ref_ws& r = ws->ref;
+        r.qkv = reinterpret_cast<float*>(b + r_qkv);
+        r.attn = reinterpret_cast<float*>(b + r_attn);
+        r.h = reinterpret_cast<float*>(b + r_h);
+        r.xp = reinterpret_cast<float*>(b + r_xp);
+        r.down = reinterpret_cast<float*>(b + r_down);
+        r.logits = reinterpret_cast<float*>(b + r_lg);
+        r.wts = reinterpret_cast<float*>(b + r_wts);
+        r.xq = reinterpret_cast<int8_t*>(b + r_xq);
+        r.xd = reinterpret_cast<float*>(b + r_xd);
+        r.ids = reinterpret_cast<int32_t*>(b + r_ids);
+        r.pos = reinterpret_cast<int32_t*>(b + r_pos);
+        r.src = reinterpret_cast<int32_t*>(b + r_src);
+        r.tile_group = reinterpret_cast<int32_t*>(b + r_tg);
+        r.n_tiles_max = n_tiles;
+    }
     return 0;
 }
 
@@ -439,18 +507,93 @@ void ceb_workspace_free(ceb_workspace* ws) {
     *ws = ceb_workspace();
 }
 
+// ------------------------------------------------------------------ forward, reference arithmetic
+namespace {
+
+// The encoder in the reference's CPU arithmetic (ref_arith.cu), in the order of
+// build_encoder_graph (src/crispembed.cpp:1068-1428): every matrix input that
+// meets a Q8_0 weight is re-quantized to Q8_0 first, as ggml's mul_mat does for
+// vec_dot_type Q8_0; everything stays fp32 between the products.
+int encoder_forward_ref(const ceb_model& m, ceb_workspace& ws, const int32_t* d_ids, const int32_t* d_cu, int n_seqs,
+                        int M, int max_len, float* d_out, int out_dim, int* d_err, cudaStream_t st,
+                        const ceb_route_capture* cap) {
+    const auto& hp = m.hp;
+    const int d = hp.n_embd;
+    const float eps = hp.layer_norm_eps;
+    const ceb_ref_ws& r = ws.ref;
+    int rc = ceb_ref_embed(d_ids, d_cu, n_seqs, d, hp.n_vocab, m.tok, m.pos, m.n_pos, m.pos_offset, m.type0, ws.t32,
+                           d_err, st);
+    if (rc) return rc;
+    if (m.embd_ln_w) {  // the graph normalises the embeddings when the model has embd_ln
+        if ((rc = ceb_ref_ln(ws.t32, nullptr, M, d, m.embd_ln_w, m.embd_ln_b, eps, ws.x32, st))) return rc;
+    } else if (cudaMemcpyAsync(ws.x32, ws.t32, (size_t)M * d * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+        return ceb_set_error(3, "embedding copy");
+    }
+    // y = W x (+ bias) for `rows` rows of x (k values each), x re-quantized first for Q8_0 weights
+    auto linear = [&](const ceb_refmat& w, const float* x, int rows, const int32_t* tile_group, const float* bias,
+                      float* y) {
+        if (w.type == CEB_GGML_Q8_0)
+            if (int e = ceb_ref_quant(x, rows, w.k, r.xq, r.xd, st)) return e;
+        return ceb_ref_matmul(w, x, r.xq, r.xd, rows, tile_group, bias, 0, y, w.n_out, st);
+    };
+    int moe_block = 0;
+    for (const ceb_layer& Ly : m.layers) {
+        if ((rc = linear(Ly.r_qkv, ws.x32, M, nullptr, Ly.qkv_b, r.qkv))) return rc;
+        if ((rc = ceb_ref_attention(r.qkv, d_cu, n_seqs, max_len, d, hp.n_head, r.attn, st))) return rc;
+        if ((rc = linear(Ly.r_o, r.attn, M, nullptr, Ly.o_b, ws.t32))) return rc;
+        if ((rc = ceb_ref_ln(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, st))) return rc;
+        if (Ly.moe) {
+            const ceb_moe_weights& mw = Ly.moew;
+            const int E = mw.n_experts, K = mw.top_k, F = mw.ffn;
+            // router logits (no bias), softmax, top-k (src/crispembed.cpp:1333-1345)
+            if ((rc = linear(Ly.r_router, ws.c32, M, nullptr, nullptr, r.logits))) return rc;
+            if ((rc = ceb_ref_route(r.logits, M, E, K, r.ids, r.wts, st))) return rc;
+            if (cap && cap->logits &&
+                cudaMemcpyAsync(cap->logits + (size_t)moe_block * M * E, r.logits, (size_t)M * E * 4,
+                                cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+                return ceb_set_error(3, "route capture");
+            if (cap && cap->ids &&
+                cudaMemcpyAsync(cap->ids + (size_t)moe_block * M * K, r.ids, (size_t)M * K * 4,
+                                cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+                return ceb_set_error(3, "route capture");
+            ++moe_block;
+            // expert rows grouped per expert (ggml_mul_mat_id), fc1 -> erf-GELU -> fc2 (:1365-1371)
+            const int rows_pad = r.n_tiles_max * 32;
+            if ((rc = ceb_ref_group(r.ids, M, K, E, r.n_tiles_max, r.pos, r.src, r.tile_group, st))) return rc;
+            if ((rc = ceb_ref_gather(ws.c32, r.src, rows_pad, d, r.xp, st))) return rc;
+            if ((rc = linear(Ly.r_e1, r.xp, rows_pad, r.tile_group, nullptr, r.h))) return rc;
+            if ((rc = ceb_ref_gelu(r.h, (int64_t)rows_pad * F, st))) return rc;
+            if ((rc = linear(Ly.r_e2, r.h, rows_pad, r.tile_group, nullptr, r.down))) return rc;
+            // gate-weighted combine + MoE bias (:1375-1381)
+            if ((rc = ceb_ref_combine(r.down, r.pos, r.wts, M, K, d, mw.bias, ws.t32, st))) return rc;
+        } else {
+            const int F = Ly.r_fc1.n_out;
+            if ((rc = linear(Ly.r_fc1, ws.c32, M, nullptr, Ly.fc1_b, r.h))) return rc;
+            if ((rc = ceb_ref_gelu(r.h, (int64_t)M * F, st))) return rc;
+            if ((rc = linear(Ly.r_fc2, r.h, M, nullptr, Ly.fc2_b, ws.t32))) return rc;
+        }
+        if ((rc = ceb_ref_ln(ws.c32, ws.t32, M, d, Ly.ln2_w, Ly.ln2_b, eps, ws.x32, st))) return rc;
+    }
+    return ceb_ref_pool(ws.x32, d_cu, n_seqs, d, out_dim, d_out, st);
+}
+
+}  // namespace
+
 // ------------------------------------------------------------------ forward
 int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_ids, const int32_t* d_cu, int n_seqs,
-                        int M, int max_len, float* d_out, int out_dim, int* d_err, cudaStream_t st) {
+                        int M, int max_len, float* d_out, int out_dim, int* d_err, cudaStream_t st,
+                        const ceb_route_capture* cap) {
     const auto& hp = m.hp;
     const int d = hp.n_embd;
     const float eps = hp.layer_norm_eps;
     if (M > ws.cap_tokens) return ceb_set_error(1, "forward: %d tokens exceed the workspace (%d)", M, ws.cap_tokens);
     if (max_len > m.n_pos - m.pos_offset)
         return ceb_set_error(1, "sequence of %d tokens exceeds the model's %d positions", max_len, m.n_pos);
+    if (m.ref_arith) return encoder_forward_ref(m, ws, d_ids, d_cu, n_seqs, M, max_len, d_out, out_dim, d_err, st, cap);
     int rc = ceb_embed_ln(d_ids, d_cu, n_seqs, M, d, hp.n_vocab, m.tok, m.pos, m.n_pos, m.pos_offset, m.type0,
                           m.embd_ln_w, m.embd_ln_b, eps, ws.x32, ws.x16, d_err, st);
     if (rc) return rc;
+    int moe_block = 0;
     for (const ceb_layer& Ly : m.layers) {
         ceb_gemm_args a;
         a.m_rows = M;
@@ -473,9 +616,16 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
         if ((rc = ceb_gemm_launch(Ly.o, ws.a16, M, a, st))) return rc;
         if (Ly.moe) {
             const ceb_moe_weights& mw = Ly.moew;
+            float* cap_logits = cap && cap->logits ? cap->logits + (size_t)moe_block * M * mw.n_experts : nullptr;
             if ((rc = ceb_add_ln_route(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, mw, ws.moe,
-                                       nullptr, st)))
+                                       cap_logits, st)))
                 return rc;
+            if (cap && cap->ids) {
+                const cudaError_t e = cudaMemcpyAsync(cap->ids + (size_t)moe_block * M * mw.top_k, ws.moe.ids,
+                                                      (size_t)M * mw.top_k * 4, cudaMemcpyDeviceToDevice, st);
+                if (e != cudaSuccess) return ceb_set_cuda_error(e, "route capture", __FILE__, __LINE__);
+            }
+            ++moe_block;
             const float* down = ws.moe.down;
             if (m.ep) {
                 if ((rc = ceb_ep_moe(m.ep, mw, ws.c32, CEB_ACT_F32, ws.c16, M, ws.moe, d_err, st))) return rc;

@@ -40,6 +40,7 @@ extern "C" {
 #define CEB_ACT_F16 2
 
 typedef struct ceb_moe_layer ceb_moe_layer;
+typedef struct crispembed_context crispembed_context;
 
 /*
  * Upload one MoE feed-forward block.  Host buffers hold ggml tensor bytes as a
@@ -119,6 +120,43 @@ CEB_API int ceb_moe_ffn_static(const ceb_moe_layer* layer, const void* d_x, int 
                                void* stream);
 
 /*
+ * crispembed_init with options (no counterpart in the reference).  flags:
+ *
+ * CEB_INIT_REFERENCE_ARITHMETIC -- run the encoder in the arithmetic of the
+ *   reference's ggml CPU path, bit for bit: every activation that meets a Q8_0
+ *   weight is re-quantized to Q8_0 and dotted in integers with ggml's x86 lane
+ *   order, float weights accumulate with one fma per element in index order,
+ *   attention, LayerNorm, softmax and pooling sum in the reference's sequential
+ *   orders, and exp / erf are shared double-precision routines that round
+ *   correctly.  The expert choice of every MoE block then equals the reference
+ *   arithmetic's, which the default fp16 tensor-core path cannot promise: there a
+ *   token whose 2nd and 3rd router logits lie closer than the Q8_0 rounding noise
+ *   (~1e-2 after a few layers) may take the other expert.  CUDA cores only, far
+ *   slower than the default; F32/F16/BF16/Q8_0 weights, learned positions and
+ *   mean pooling; no expert parallelism.  crispembed_init selects it when the
+ *   environment variable CEB_REFERENCE_ARITHMETIC is 1.
+ * Returns NULL on failure (message in ceb_last_error()).
+ */
+#define CEB_INIT_REFERENCE_ARITHMETIC 1
+CEB_API crispembed_context* ceb_init_ex(const char* model_path, int n_threads, int flags);
+
+/*
+ * Diagnostic encode that also returns every MoE block's routing (no counterpart in
+ * the reference, whose expert choice stays inside its graph at
+ * src/crispembed.cpp:1333-1345).  Encodes the packed ids (h_lens[i] tokens per
+ * sequence, M tokens in all) like crispembed_encode_ids_batch, synchronously and
+ * without graph capture, and copies to host memory: h_out [n_seqs x dim]
+ * embeddings (may be NULL), h_route_ids [n_moe x M x top_k] expert ids (slot j =
+ * j-th largest probability) and h_route_logits [n_moe x M x n_experts] router
+ * logits, n_moe = the number of MoE blocks in layer order (either may be NULL).
+ * Allocates its capture buffers for the call.  Returns 0 or a status.
+ */
+CEB_API int ceb_encode_ids_routes(crispembed_context* ctx, const int32_t* h_ids, const int32_t* h_lens, int n_seqs,
+                                  float* h_out, int32_t* h_route_ids, float* h_route_logits);
+/* Number of MoE blocks of the context's model (the n_moe above). */
+CEB_API int ceb_moe_block_count(const crispembed_context* ctx);
+
+/*
  * Mean pool + L2 normalise, replacing the host loops of encode_tokens
  * (src/crispembed.cpp:1822-1846) and pool_and_norm (:2024-2045):
  *   p = mean over the rows of each sequence; out = p / sqrt(max(sum p^2, 1e-12)).
@@ -165,7 +203,6 @@ CEB_API void ceb_ep_free(ceb_ep* ep);
  * context keeps only this rank's experts; the other experts' weights are freed.
  * The exchange must outlive the context's use of it.
  */
-typedef struct crispembed_context crispembed_context;
 CEB_API int ceb_ep_attach(crispembed_context* ctx, ceb_ep* ep);
 
 /*

@@ -34,6 +34,10 @@
 #include <omp.h>
 #endif
 
+/* exp / erf shared bit for bit with the device kernels (the C library's expf and
+ * erff stand in for the reference's; see the header) */
+#include "ceb_portable_math.h"
+
 enum { CEO_EXACT = 0, CEO_GGML = 1, CEO_F16 = 2 };
 enum {
     T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13,
@@ -459,11 +463,15 @@ void ceo_matmul(int type, const uint8_t *w, int64_t n_out, int64_t k, const floa
     free(wf);
 }
 
+/* the shared exp / erf, exported for their accuracy test */
+float ceo_expf(float x) { return ceb_expf(x); }
+float ceo_erff(float x) { return ceb_erff(x); }
+
 /* ------------------------------------------------------------ elementwise */
 /* exact erf GELU, as ggml_vec_gelu_erf_f32 computes it: 0.5x(1+erf(x/sqrt2)) */
 void ceo_gelu_erf(float *x, int64_t n) {
     const float s2 = 0.70710678118654752440f;
-    for (int64_t i = 0; i < n; i++) x[i] = 0.5f * x[i] * (1.0f + erff(x[i] * s2));
+    for (int64_t i = 0; i < n; i++) x[i] = 0.5f * x[i] * (1.0f + ceb_erff(x[i] * s2));
 }
 
 /* ggml_norm_f32 then ggml_mul(gamma) and ggml_add(beta): mean and variance
@@ -520,10 +528,10 @@ void ceo_attention(const float *q, const float *k, const float *v, int64_t ld, c
                     if (sc > M) {
                         float Mold = M;
                         M = sc;
-                        ms = expf(Mold - M);
+                        ms = ceb_expf(Mold - M);
                         for (int c = 0; c < hd; c++) acc[c] *= ms;
                     } else {
-                        vs = expf(sc - M);
+                        vs = ceb_expf(sc - M);
                     }
                     for (int c = 0; c < hd; c++) acc[c] = fmaf(vj[c], vs, acc[c]);
                     S = S * ms + vs;
@@ -549,7 +557,7 @@ void ceo_route(const float *logits, int64_t T, int E, int k, int32_t *ids, float
         float p[256];
         double sum = 0.0;
         for (int e = 0; e < E; e++) {
-            p[e] = expf(lg[e] - mx);
+            p[e] = ceb_expf(lg[e] - mx);
             sum += (double)p[e];
         }
         float inv = (float)(1.0 / sum);

@@ -37,9 +37,13 @@ _ip = ctypes.POINTER(ctypes.c_int32)
 _up = ctypes.POINTER(ctypes.c_uint8)
 
 
+_SOURCES = [os.path.join(HERE, "ceb_oracle.c"),
+            os.path.join(os.path.dirname(HERE), "crispembed_b200", "csrc", "ceb_portable_math.h")]
+
+
 def build(force: bool = False) -> str:
-    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(
-            os.path.join(HERE, "ceb_oracle.c")):
+    if force or not os.path.exists(LIB_PATH) or any(
+            os.path.exists(p) and os.path.getmtime(LIB_PATH) < os.path.getmtime(p) for p in _SOURCES):
         subprocess.run(["make", "-C", HERE, "-s"], check=True)
     return LIB_PATH
 
@@ -75,6 +79,10 @@ def lib():
                                    _fp, _fp, _ip, _fp, _fp]
         L.ceo_pool_l2.argtypes = [_fp, _ip, ctypes.c_int, ctypes.c_int, _fp]
         L.ceo_truncate_renorm.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp]
+        L.ceo_expf.argtypes = [ctypes.c_float]
+        L.ceo_expf.restype = ctypes.c_float
+        L.ceo_erff.argtypes = [ctypes.c_float]
+        L.ceo_erff.restype = ctypes.c_float
         L.ceo_set_threads.argtypes = [ctypes.c_int]
         L.ceo_set_threads.restype = ctypes.c_int
         _lib = L
