@@ -2,7 +2,7 @@
 """MoE-encoder throughput on B200 -- one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c3|c4|c5] [--no-ep] [--no-cpu-baseline]
+                    [--workload c2|c3|c4|c5] [--no-ep] [--no-ops] [--no-cpu-baseline]
 
 Workloads (inputs synthetic and seeded, weights random-init
 of the nomic-embed-text-v2-moe architecture, see crispembed_b200/synth.py):
@@ -25,6 +25,12 @@ carries "expert_parallel": BASELINE config 4 (512 x 512 tokens per step for the
 whole job, sequences sharded over the ranks and the MoE experts split over them,
 exchange by the library's own peer-memory kernels), at every N (N=1 runs the
 exchange with itself).  --workload c4 prints that measurement as the main line.
+At N=1 the line also carries "moe_operator": the c3 and c5 workloads (every case
+of each: c3 at T = 65536, 512, 8192; c5 balanced and Zipf 1.5), each with its
+own e2e, roofline and CPU baseline; --workload c3|c5 prints one as the main line.
+Rooflines: "roofline" covers every launch of the dominant kernel (the tcgen05 GEMM
+of all linear layers), "roofline_moe_grouped_gemm" the grouped expert GEMMs alone;
+all use the measured sustained bf16 peak, with the burst fraction beside it.
 --impl reference: the CPU restatement of the reference's ggml CPU path (oracle/,
 the reference itself cannot be built here) on all host threads, bounded sample.
 """
@@ -293,6 +299,22 @@ def bench_ep(args, rank, world, local, path, dist):
                 k: [min(b[k] for b in per_rank), max(b[k] for b in per_rank)] for k in brk}}
 
 
+def gemm_roofline(g, pk, pk_src, kernel, traffic, traffic_source):
+    """Tensor roofline of a set of GEMM launches: algorithmic FLOPs per launch over the
+    mean CUDA-event duration, against the measured sustained bf16 peak (every line of
+    this file uses that peak; the fraction of the burst peak is given beside it)."""
+    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
+    peak = float(pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    burst = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    return {"kernel": kernel, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "peak_source": f"{pk_src} bf16_tflops_sustained",
+            "frac_of_burst_peak": achieved / burst, "launches": g["launches"],
+            "flops_per_launch": g["flops"] / max(1, g["launches"]), "avg_launch_ms": g["ms"] / max(1, g["launches"]),
+            "traffic": traffic, "traffic_source": traffic_source,
+            "measured": "kernel time from CUDA events around each GEMM launch on its stream, in a pass of the "
+                        "same steps right after the timed region"}
+
+
 def traffic_from_profile(workload):
     p = os.path.join(ROOT, "profiles", f"gemm_traffic_{workload}.json")
     if os.path.exists(p):
@@ -310,6 +332,7 @@ def main():
     ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel (config 4) block of the c2 line")
+    ap.add_argument("--no-ops", action="store_true", help="skip the MoE-operator (configs 3, 5) blocks of the c2 line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -403,11 +426,11 @@ def main():
     m.close()
 
     pk, pk_src = peaks()
-    g = prof["gemm"]
-    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
-    peak = float(pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    g = {k: prof["gemm"][k] + prof["moe_gemm"][k] for k in ("launches", "ms", "flops", "bytes")}
     tr = traffic_from_profile("c2")
-    per_launch_flops = g["flops"] / max(1, g["launches"])
+    moe_shapes = [sh for sh in (tr or {}).get("shapes", []) if sh["shape"].startswith("MoE")]
+    moe_traffic = (sum(sh["dram_read"] + sh["dram_write"] for sh in moe_shapes) / len(moe_shapes)
+                   if moe_shapes else None)
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * t / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -418,14 +441,13 @@ def main():
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(ids.nbytes),
                 "d2h_bytes_per_step": int(n_seqs * dim * 4)},
         "gpu_launches": int(launches),
-        "roofline": {"kernel": "ceb_gemm_pair_kernel (grouped tcgen05 CTA-pair GEMM, all linear layers)", "bound": "tensor",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": f"{pk_src} bf16_tflops_sustained", "launches": g["launches"],
-                     "flops_per_launch": per_launch_flops, "avg_launch_ms": g["ms"] / max(1, g["launches"]),
-                     "traffic": (tr or {}).get("bytes_per_launch"),
-                     "traffic_source": (tr or {}).get("source"),
-                     "measured": "kernel time from CUDA events around each GEMM launch on its stream, in a pass "
-                                 "of the same steps right after the timed region"},
+        "roofline": gemm_roofline(g, pk, pk_src, "ceb_gemm_pair_kernel (tcgen05 CTA-pair GEMM), every launch of "
+                                  "the step: dense linear layers and grouped expert GEMMs",
+                                  (tr or {}).get("bytes_per_launch"), (tr or {}).get("source")),
+        "roofline_moe_grouped_gemm": gemm_roofline(
+            prof["moe_gemm"], pk, pk_src, "ceb_gemm_pair_kernel, the grouped expert GEMMs of the MoE blocks only "
+            "(fc1 + GELU and fc2, 8 experts per launch)", moe_traffic,
+            "mean of the MoE fc1 and fc2 shapes of the same ncu capture (profiles/gemm_traffic_c2.json)"),
         "breakdown_ms_per_step": {k: v["ms"] / args.steps for k, v in prof.items()},
         "clocks": clk.summary(),
     }
@@ -435,6 +457,8 @@ def main():
         result["expert_parallel"] = bench_ep(args, rank, world, local, path, dist)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(path, ids, lens)
+    if world == 1 and not args.no_ops:
+        result["moe_operator"] = {w: moe_op_block(args, w, local) for w in ("c3", "c5")}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if dist:
@@ -501,14 +525,58 @@ def _time_moe_op(args, cfg, T, zipf, local, with_clocks=False):
     torch.cuda.synchronize()
     te = (time.perf_counter() - t0) / steps
     loads = cnt.cpu().numpy()
-    g = prof["gemm"]
+    g = prof["moe_gemm"]
     r = {"T": T, "zipf": zipf, "ms": 1000 * t, "tokens_per_s": T / t, "e2e_tokens_per_s": T / te,
          "h2d_bytes": int(hx.numel() * hx.element_size()), "d2h_bytes": int(hy.numel() * 4),
          "gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
-         "gemm_ms": g["ms"] / steps, "launches": int(launches), "max_over_mean_expert_load": float(loads.max() / loads.mean()),
+         "gemm_ms": g["ms"] / steps, "gemm": g, "launches": int(launches),
+         "max_over_mean_expert_load": float(loads.max() / loads.mean()),
          "breakdown_ms": {k: v["ms"] / steps for k, v in prof.items()}, "clocks": clk.summary() if clk else None}
     layer.close()
     return r, inp
+
+
+def op_cases(cfg):
+    """(T, zipf) of every measured case of an operator workload, the main case first."""
+    return [(cfg["T"], cfg["zipf"])] + [(T, cfg["zipf"]) for T in cfg["sweep"]] + [(cfg["T"], z) for z in cfg["variants"]]
+
+
+def op_metric(cfg):
+    skew = f"Zipf {cfg['zipf']}" if cfg["zipf"] else "balanced"
+    return (f"MoE FFN operator tokens/s (Q4_K, d={cfg['d']} E={cfg['n_experts']} top-{cfg['top_k']} "
+            f"F={cfg['ffn']}, T={cfg['T']}, {skew})"), skew
+
+
+def moe_op_block(args, workload, local, cpu_budget_s=5.0):
+    """One operator workload (BASELINE config 3 or 5) as a block of the default line:
+    its main case with e2e, the tensor roofline of its grouped GEMMs, clocks, the
+    other cases of the config and the CPU restatement on a bounded sample."""
+    cfg = OP_WORKLOADS[workload]
+    pk, pk_src = peaks()
+    cases = []
+    inp = None
+    for i, (T, z) in enumerate(op_cases(cfg)):
+        r, got = _time_moe_op(args, cfg, T, z, local, with_clocks=(i == 0))
+        if i == 0:
+            main_r, inp = r, got
+        cases.append({k: r[k] for k in ("T", "zipf", "ms", "tokens_per_s", "e2e_tokens_per_s", "gemm_tflops",
+                                        "max_over_mean_expert_load")})
+    metric, skew = op_metric(cfg)
+    tr = traffic_from_profile(workload)
+    block = {"metric": metric, "value": main_r["tokens_per_s"], "unit": "tokens/s", "ms_per_step": main_r["ms"],
+             "steps": args.steps,
+             "config": {"workload": f"{workload}: MoE op, x bf16 N(0,1), router F32, experts Q4_K, {skew}",
+                        "tokens": cfg["T"], "l2": "inputs larger than L2"},
+             "e2e": {"value": main_r["e2e_tokens_per_s"], "unit": "tokens/s",
+                     "h2d_bytes_per_step": main_r["h2d_bytes"], "d2h_bytes_per_step": main_r["d2h_bytes"]},
+             "gpu_launches": main_r["launches"],
+             "roofline": gemm_roofline(main_r["gemm"], pk, pk_src, "ceb_gemm_pair_kernel, grouped expert GEMMs "
+                                       "(fc1 + GELU, fc2) on Q4_K weights expanded to fp16 at load",
+                                       (tr or {}).get("bytes_per_launch"), (tr or {}).get("source")),
+             "breakdown_ms_per_step": main_r["breakdown_ms"], "clocks": main_r["clocks"], "cases": cases}
+    if not args.no_cpu_baseline:
+        block["cpu_baseline"] = op_cpu_baseline(inp, budget_s=cpu_budget_s)
+    return block
 
 
 def op_cpu_baseline(inp, budget_s=10.0, n=256):
@@ -532,11 +600,13 @@ def bench_moe_op(args, rank, world, local):
     cfg = OP_WORKLOADS[args.workload]
     main_r, inp = _time_moe_op(args, cfg, cfg["T"], cfg["zipf"], local, with_clocks=True)
     pk, pk_src = peaks()
-    peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     flops_tok = 2.0 * 2 * cfg["top_k"] * cfg["d"] * cfg["ffn"]
-    skew = f"Zipf {cfg['zipf']}" if cfg["zipf"] else "balanced"
-    result = {"metric": f"MoE FFN operator tokens/s (Q4_K, d={cfg['d']} E={cfg['n_experts']} top-{cfg['top_k']} "
-                        f"F={cfg['ffn']}, T={cfg['T']}, {skew})",
+    metric, skew = op_metric(cfg)
+    tr = traffic_from_profile(args.workload)
+    rl = gemm_roofline(main_r["gemm"], pk, pk_src, "ceb_gemm_pair_kernel, grouped expert GEMMs (fc1 + GELU, fc2)",
+                       (tr or {}).get("bytes_per_launch"), (tr or {}).get("source"))
+    rl["op_tflops"] = main_r["tokens_per_s"] * flops_tok / 1e12
+    result = {"metric": metric,
               "value": main_r["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
               "warmup": args.warmup, "ms_per_step": main_r["ms"], "higher_is_better": True, "scaling": "weak",
               "vs_baseline": None, "dtype": "fp16 (Q4_K dequant, fp32 accumulate)", "data": "synthetic",
@@ -545,10 +615,7 @@ def bench_moe_op(args, rank, world, local):
               "e2e": {"value": main_r["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": main_r["h2d_bytes"],
                       "d2h_bytes_per_step": main_r["d2h_bytes"]},
               "gpu_launches": main_r["launches"],
-              "roofline": {"bound": "tensor", "kernel": "grouped tcgen05 GEMM (fc1+GELU, fc2)",
-                           "achieved": main_r["gemm_tflops"], "peak": peak, "unit": "TFLOP/s",
-                           "frac": main_r["gemm_tflops"] / peak, "peak_source": f"{pk_src} bf16_tflops (burst)",
-                           "op_tflops": main_r["tokens_per_s"] * flops_tok / 1e12, "traffic": None},
+              "roofline": rl,
               "max_over_mean_expert_load": main_r["max_over_mean_expert_load"],
               "breakdown_ms_per_step": main_r["breakdown_ms"], "clocks": main_r["clocks"]}
     others = []

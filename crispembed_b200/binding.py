@@ -75,6 +75,8 @@ def load_library(path: Optional[str] = None):
         "ceb_moe_ffn": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp, ctypes.c_size_t, vp],
                         ctypes.c_int),
         "ceb_moe_ffn_static": ([vp, vp, ctypes.c_int, ctypes.c_int, vp, vp], ctypes.c_int),
+        "ceb_moe_workspace_routing": ([vp, ctypes.c_int, vp, ctypes.POINTER(vp), ctypes.POINTER(vp),
+                                       ctypes.POINTER(vp), ctypes.POINTER(vp)], ctypes.c_int),
         "ceb_gguf_dequantize": ([ctypes.c_int, vp, ctypes.c_int64, ctypes.c_int64, vp], ctypes.c_int),
         "ceb_ep_create": ([ctypes.c_int] * 7, vp),
         "ceb_ep_ipc_handle": ([vp, vp], ctypes.c_int),
@@ -304,6 +306,22 @@ class MoELayer:
         _check(self._lib.ceb_moe_ffn_static(self._h, x.data_ptr(), act, x.shape[0], y.data_ptr(), _stream_ptr(stream)),
                "ceb_moe_ffn_static")
 
+    def routing(self, workspace, n_tokens: int):
+        """(ids, weights, slot_pos, offsets) of the last call on `workspace` (a uint8
+        CUDA tensor), as host numpy arrays (ceb_moe_workspace_routing)."""
+        import torch
+        ptrs = [ctypes.c_void_p() for _ in range(4)]
+        _check(self._lib.ceb_moe_workspace_routing(self._h, n_tokens, workspace.data_ptr(),
+                                                   *[ctypes.byref(p) for p in ptrs]), "ceb_moe_workspace_routing")
+        K, E = self.top_k, self.n_experts
+        out = []
+        for p, n, dt in ((ptrs[0], n_tokens * K, torch.int32), (ptrs[1], n_tokens * K, torch.float32),
+                         (ptrs[2], n_tokens * K, torch.int32), (ptrs[3], E + 1, torch.int32)):
+            off = p.value - workspace.data_ptr()
+            out.append(workspace[off:off + 4 * n].view(dt).cpu().numpy())
+        ids, w, sp, offsets = out
+        return ids.reshape(n_tokens, K), w.reshape(n_tokens, K), sp.reshape(n_tokens, K), offsets
+
     def workspace_size(self, n_tokens: int) -> int:
         return int(self._lib.ceb_moe_workspace_size(self._h, n_tokens))
 
@@ -491,7 +509,7 @@ def sync_check(stream=None):
     _check(load_library().ceb_sync_check(_stream_ptr(stream)), "device check")
 
 
-PROFILE_CATEGORIES = ("gemm", "attention", "routing", "rowwise", "exchange", "exchange_wait")
+PROFILE_CATEGORIES = ("gemm", "attention", "routing", "rowwise", "exchange", "exchange_wait", "moe_gemm")
 
 
 def launch_count() -> int:

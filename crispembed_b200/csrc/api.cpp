@@ -24,7 +24,7 @@
 
 static_assert(sizeof(crispembed_hparams) == sizeof(ceb_hparams_c), "hparams layout");
 
-int ceb_moe_static_take_error();  // moe_static.cu
+int ceb_moe_static_take_error(int* code);  // moe_static.cu
 
 struct crispembed_context {
     ceb_model model;
@@ -688,16 +688,39 @@ extern "C" size_t ceb_moe_workspace_size(const ceb_moe_layer* L, int max_tokens)
     return ceb_moe_ws_layout(max_tokens, L->w.d, L->w.n_experts, L->w.top_k, L->w.ffn, nullptr, nullptr);
 }
 
+extern "C" int ceb_moe_workspace_routing(const ceb_moe_layer* L, int n_tokens, void* d_workspace, int32_t** d_ids,
+                                         float** d_weights, int32_t** d_slot_pos, int32_t** d_offsets) {
+    if (!L || n_tokens <= 0 || !d_workspace) return ceb_set_error(1, "moe_workspace_routing: bad arguments");
+    ceb_moe_ws ws;
+    ceb_moe_ws_layout(n_tokens, L->w.d, L->w.n_experts, L->w.top_k, L->w.ffn, &ws, static_cast<uint8_t*>(d_workspace));
+    if (d_ids) *d_ids = ws.ids;
+    if (d_weights) *d_weights = ws.wts;
+    if (d_slot_pos) *d_slot_pos = ws.slot_pos;
+    if (d_offsets) *d_offsets = ws.offsets;
+    return 0;
+}
+
 namespace {
-int* g_op_err = nullptr;  // device error word for operator-level calls
+// Device error words of the operator-level calls, one per device: kernels write
+// the word of the device they run on, and ceb_sync_check reads the current
+// device's (a process may drive several GPUs).
+constexpr int OP_MAX_DEVICES = 64;
+int* g_op_err[OP_MAX_DEVICES] = {};
 std::mutex g_op_mu;
 int* op_err_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= OP_MAX_DEVICES) return nullptr;
     std::lock_guard<std::mutex> lk(g_op_mu);
-    if (!g_op_err) {
-        if (cudaMalloc(&g_op_err, sizeof(int)) != cudaSuccess) return nullptr;
-        cudaMemset(g_op_err, 0, sizeof(int));
+    if (!g_op_err[dev]) {
+        int* p = nullptr;
+        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
+            cudaFree(p);
+            return nullptr;
+        }
+        g_op_err[dev] = p;
     }
-    return g_op_err;
+    return g_op_err[dev];
 }
 }  // namespace
 
@@ -867,16 +890,22 @@ extern "C" int ceb_sync_check(void* stream) {
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "stream synchronize", __FILE__, __LINE__);
     e = cudaGetLastError();
     if (e != cudaSuccess) return ceb_set_cuda_error(e, "pending error", __FILE__, __LINE__);
-    const int hs = ceb_moe_static_take_error();
-    if (hs) return ceb_set_error(5, "device-side check failed in ceb_moe_ffn_static (code 0x%x)", hs);
-    int* err = op_err_word();
-    if (!err) return 0;
-    int h = 0;
-    if (cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return ceb_set_error(3, "error word");
-    if (h) {
-        cudaMemset(err, 0, sizeof(int));
-        return ceb_set_error(5, "device-side check failed (code 0x%x)", h);
+    // both device error words of the current device are read and cleared, so a pending
+    // error is reported once, by this call
+    int hs = 0, h = 0;
+    const int rs = ceb_moe_static_take_error(&hs);
+    int ro = 0;
+    if (int* err = op_err_word()) {
+        if (cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) ro = 3;
+        else if (h && cudaMemset(err, 0, sizeof(int)) != cudaSuccess) ro = 3;
+    } else {
+        ro = 3;
     }
+    if (hs && h)
+        return ceb_set_error(5, "device-side checks failed: operator code 0x%x, ceb_moe_ffn_static code 0x%x", h, hs);
+    if (h) return ceb_set_error(5, "device-side check failed (code 0x%x)", h);
+    if (hs) return ceb_set_error(5, "device-side check failed in ceb_moe_ffn_static (code 0x%x)", hs);
+    if (rs || ro) return ceb_set_error(3, "device error word could not be read");
     return 0;
 }
 

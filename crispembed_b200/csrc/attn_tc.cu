@@ -85,9 +85,15 @@ CEB_DEV float ex2f(float x) {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                      const __grid_constant__ CUtensorMap v_map, const int32_t* __restrict__ cu, int d, float scale_log2,
-                     __half* __restrict__ out, int* err) {
+                     __half* __restrict__ out, int* err, int total_rows, int max_len) {
     const int seq = blockIdx.z, head0 = HPC * blockIdx.y;
     const int start = cu[seq], len = cu[seq + 1] - start;
+    // row offsets that leave the rows or disagree with max_len: report, touch nothing
+    // (both CTAs of the pair read the same offsets and return together)
+    if (start < 0 || len < 0 || len > total_rows - start || len > max_len) {
+        if (blockIdx.x == 0 && head0 == 0 && threadIdx.x == 0 && err) atomicCAS(err, 0, (int)CEB_DEVERR_BAD_INDEX);
+        return;
+    }
     const int q0 = (blockIdx.x >> 1) * 2 * QT;
     if (q0 >= len || len > LMAX) return;  // both CTAs of the pair take the same branch
 
@@ -363,7 +369,8 @@ int ceb_attention_tc(const __half* qkv, int total_rows, const int32_t* cu, int n
     const int n_qpairs = (max_len + 2 * QT - 1) / (2 * QT);
     dim3 grid(2 * n_qpairs, n_head / HPC, n_seqs);
     CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0,
-               attn_pair_kernel<<<grid, NTHR, SMEM_LAUNCH, st>>>(q_map, k_map, v_map, cu, d, scale_log2, out, d_err));
+               attn_pair_kernel<<<grid, NTHR, SMEM_LAUNCH, st>>>(q_map, k_map, v_map, cu, d, scale_log2, out, d_err,
+                                                                  total_rows, max_len));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }

@@ -60,6 +60,18 @@ enum : int {
     CEB_EPI_GELU = 4,     // erf-GELU after bias
 };
 
+// ---- launch accounting and optional per-category CUDA-event timing ---------
+enum ceb_prof_cat : int {
+    CEB_PROF_GEMM = 0,
+    CEB_PROF_ATTN = 1,
+    CEB_PROF_ROUTE = 2,   // router + histogram/scan + permutation
+    CEB_PROF_ROWWISE = 3, // embedding, residual+LN, combine+LN, pooling
+    CEB_PROF_EXCHANGE = 4, // expert-parallel peer copies (dispatching permutation, return)
+    CEB_PROF_EP_WAIT = 5,  // expert-parallel waits for peers' flags
+    CEB_PROF_MOE_GEMM = 6, // the grouped expert GEMMs of MoE blocks (fc1 + GELU, fc2)
+    CEB_PROF_NCAT = 7,
+};
+
 struct ceb_gemm_args {
     const int* offsets = nullptr;  // device [n_groups+1] activation-row ranges per group; null = dense
     int m_rows = 0;                // dense: activation rows; grouped: capacity of the activation buffer
@@ -69,6 +81,7 @@ struct ceb_gemm_args {
     const float* bias = nullptr;
     int64_t bias_group_stride = 0;
     int* err = nullptr;            // device error word
+    int prof_cat = CEB_PROF_GEMM;  // profiling category of the launch
 };
 
 // status / errors
@@ -99,16 +112,7 @@ int ceb_num_sms();
 // device error word shared by the operator-level entry points (api.cpp)
 int* ceb_op_error_word();
 
-// ---- launch accounting and optional per-category CUDA-event timing ---------
-enum ceb_prof_cat : int {
-    CEB_PROF_GEMM = 0,
-    CEB_PROF_ATTN = 1,
-    CEB_PROF_ROUTE = 2,   // router + histogram/scan + permutation
-    CEB_PROF_ROWWISE = 3, // embedding, residual+LN, combine+LN, pooling
-    CEB_PROF_EXCHANGE = 4, // expert-parallel peer copies (dispatching permutation, return)
-    CEB_PROF_EP_WAIT = 5,  // expert-parallel waits for peers' flags
-    CEB_PROF_NCAT = 6,
-};
+
 // Counts one kernel launch; when profiling is on, records a start event on `st`.
 int ceb_prof_begin(cudaStream_t st, int cat);
 // Records the stop event of the token returned by ceb_prof_begin (no-op for -1)

@@ -232,12 +232,18 @@ CEB_DEV void load_tile(__half* s, const __half* g, size_t g_ld, int n_valid, int
 }
 
 __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ cu,
-                                                        int d, float scale_log2, __half* __restrict__ out) {
+                                                        int d, float scale_log2, __half* __restrict__ out,
+                                                        int total_rows, int max_len, int* __restrict__ err) {
     __shared__ __align__(128) __half sQ[AT_Q * AT_LD];
     __shared__ __align__(128) __half sK[2][AT_K * AT_LD];
     __shared__ __align__(128) __half sV[2][AT_K * AT_LD];
     const int seq = blockIdx.z, head = blockIdx.y;
     const int start = cu[seq], len = cu[seq + 1] - start;
+    // row offsets that leave the rows or disagree with max_len: report, touch nothing
+    if (start < 0 || len < 0 || len > total_rows - start || len > max_len) {
+        if (blockIdx.x == 0 && head == 0 && threadIdx.x == 0 && err) atomicCAS(err, 0, (int)CEB_DEVERR_BAD_INDEX);
+        return;
+    }
     const int q0 = blockIdx.x * AT_Q;
     if (q0 >= len) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -498,7 +504,8 @@ int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_se
     }
     const float scale_log2 = (1.0f / sqrtf((float)AT_HD)) * 1.4426950408889634f;
     dim3 grid((max_len + AT_Q - 1) / AT_Q, n_head, n_seqs);
-    CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_kernel<<<grid, 128, 0, st>>>(qkv, cu, d, scale_log2, out));
+    CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_kernel<<<grid, 128, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len,
+                                                                             d_err));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }

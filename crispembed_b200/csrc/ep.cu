@@ -216,6 +216,7 @@ int ceb_ep_moe(ceb_ep* ep, const ceb_moe_weights& mwl, const void* x, int x_dtyp
     a1.ldo = ep->F;
     a1.epi = CEB_EPI_F16_OUT | CEB_EPI_GELU;
     a1.err = dev_err;
+    a1.prof_cat = CEB_PROF_MOE_GEMM;
     if ((rc = ceb_gemm_launch(mwl.fc1, ep->self.recv, rows, a1, st))) return rc;
     ceb_gemm_args a2;
     a2.offsets = ep->offsets_recv;
@@ -224,6 +225,7 @@ int ceb_ep_moe(ceb_ep* ep, const ceb_moe_weights& mwl, const void* x, int x_dtyp
     a2.ldo = ep->d;
     a2.epi = 0;
     a2.err = dev_err;
+    a2.prof_cat = CEB_PROF_MOE_GEMM;
     if ((rc = ceb_gemm_launch(mwl.fc2, ep->h, rows, a2, st))) return rc;
     const int grid = 2 * ceb_num_sms();
     CEB_LAUNCH(CEB_PROF_EXCHANGE, st, 0.0, 0.0,

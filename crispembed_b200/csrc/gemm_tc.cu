@@ -1138,9 +1138,9 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
         }
         int rc = 0;
         switch (w.format) {
-            case CEB_W_Q8_0: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q8_0>(map, omap, wmap, w, a, max_pairs, stream)); break;
-            case CEB_W_Q4_K: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_Q4_K>(map, omap, wmap, w, a, max_pairs, stream)); break;
-            case CEB_W_F16: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_pair<CEB_W_F16>(map, omap, wmap, w, a, max_pairs, stream)); break;
+            case CEB_W_Q8_0: CEB_LAUNCH(a.prof_cat, stream, flops, bytes, rc = launch_pair<CEB_W_Q8_0>(map, omap, wmap, w, a, max_pairs, stream)); break;
+            case CEB_W_Q4_K: CEB_LAUNCH(a.prof_cat, stream, flops, bytes, rc = launch_pair<CEB_W_Q4_K>(map, omap, wmap, w, a, max_pairs, stream)); break;
+            case CEB_W_F16: CEB_LAUNCH(a.prof_cat, stream, flops, bytes, rc = launch_pair<CEB_W_F16>(map, omap, wmap, w, a, max_pairs, stream)); break;
             default: return ceb_set_error(2, "gemm: unknown weight format %d", w.format);
         }
         return rc;
@@ -1157,9 +1157,9 @@ int ceb_gemm_launch(const ceb_wplane& w, const void* act_f16, int act_rows, cons
     if (bound < grid) grid = (int)bound;
     int rc = 0;
     switch (w.format) {
-        case CEB_W_Q8_0: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q8_0>(map, omap, w, a, grid, stream)); break;
-        case CEB_W_Q4_K: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_Q4_K>(map, omap, w, a, grid, stream)); break;
-        case CEB_W_F16: CEB_LAUNCH(CEB_PROF_GEMM, stream, flops, bytes, rc = launch_fmt<CEB_W_F16>(map, omap, w, a, grid, stream)); break;
+        case CEB_W_Q8_0: CEB_LAUNCH(a.prof_cat, stream, flops, bytes, rc = launch_fmt<CEB_W_Q8_0>(map, omap, w, a, grid, stream)); break;
+        case CEB_W_Q4_K: CEB_LAUNCH(a.prof_cat, stream, flops, bytes, rc = launch_fmt<CEB_W_Q4_K>(map, omap, w, a, grid, stream)); break;
+        case CEB_W_F16: CEB_LAUNCH(a.prof_cat, stream, flops, bytes, rc = launch_fmt<CEB_W_F16>(map, omap, w, a, grid, stream)); break;
         default: return ceb_set_error(2, "gemm: unknown weight format %d", w.format);
     }
     return rc;

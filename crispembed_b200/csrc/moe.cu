@@ -878,6 +878,7 @@ int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, cons
     a1.ldo = F;
     a1.epi = CEB_EPI_F16_OUT | CEB_EPI_GELU;
     a1.err = dev_err;
+    a1.prof_cat = CEB_PROF_MOE_GEMM;
     int rc = ceb_gemm_launch(mw.fc1, ws.x_perm, rows, a1, st);
     if (rc) return rc;
     ceb_gemm_args a2;
@@ -887,6 +888,7 @@ int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, cons
     a2.ldo = d;
     a2.epi = 0;
     a2.err = dev_err;
+    a2.prof_cat = CEB_PROF_MOE_GEMM;
     rc = ceb_gemm_launch(mw.fc2, ws.h_perm, rows, a2, st);
     if (rc) return rc;
     if (y) {

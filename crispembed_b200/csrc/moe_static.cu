@@ -69,19 +69,24 @@ extern "C" int ceb_moe_ffn_static(const ceb_moe_layer* layer, const void* d_x, i
     int* err = nullptr;
     int rc = static_addresses(&scratch, &err);
     if (rc) return rc;
-    // Every word of scratch this call reads is written earlier in the same call
-    // (histograms, offsets, permutation, permuted rows), so nothing needs clearing.
+    // Nothing needs clearing.  The routing words this call reads (histograms,
+    // offsets, permutation) are all written earlier in the same call.  The grouped
+    // GEMMs load whole 128-row tiles, so the tail rows of an expert's last tile in
+    // x_perm / h_perm can hold another expert's rows or rows left from an earlier
+    // call; the products of those rows are never stored.
     ceb_moe_ws ws;
     ceb_moe_ws_layout(n_tokens, w.d, w.n_experts, w.top_k, w.ffn, &ws, scratch);
     return ceb_moe_run(w, d_x, x_dtype, nullptr, n_tokens, d_y, ws, nullptr, nullptr, err,
                        static_cast<cudaStream_t>(stream));
 }
 
-// Reads and clears the static path's device error word on the current device
-// (0 when the path was never used there); called by ceb_sync_check.
-int ceb_moe_static_take_error() {
+// Reads and clears the static path's device error word on the current device into
+// *code (0 when the path was never used there); returns 0, or 3 when the word
+// could not be read or cleared.  Called by ceb_sync_check.
+int ceb_moe_static_take_error(int* code) {
+    *code = 0;
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return 3;
     int* err = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
@@ -89,7 +94,8 @@ int ceb_moe_static_take_error() {
     }
     if (!err) return 0;
     int h = 0;
-    if (cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
-    if (h) cudaMemset(err, 0, sizeof(int));
-    return h;
+    if (cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return 3;
+    if (h && cudaMemset(err, 0, sizeof(int)) != cudaSuccess) return 3;
+    *code = h;
+    return 0;
 }

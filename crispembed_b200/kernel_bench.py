@@ -4,6 +4,9 @@
     python -m crispembed_b200.kernel_bench moe --T 65536 --type q4_k --zipf 1.2
     python -m crispembed_b200.kernel_bench route_ln --T 70825 --router-type q8_0
     python -m crispembed_b200.kernel_bench attn --seqs 256 [--impl mma|tc]
+    python -m crispembed_b200.kernel_bench pool --seqs 256
+    python -m crispembed_b200.kernel_bench encode --seqs 256
+    python -m crispembed_b200.kernel_bench cublas --m 70825 --n 3072 --k 768
 
 Used for the roofline numbers of single kernels and as the command that ncu
 captures (small cases: a few launches, a few GB at most).  Prints one JSON line.
@@ -164,6 +167,102 @@ def bench_attn(a):
             "tflops": flops / (ms / 1e3) / 1e12}
 
 
+def _c2_lens(n_seqs):
+    from . import synth
+    _, lens = synth.config_ids(2)
+    return lens[:n_seqs]
+
+
+def bench_pool(a):
+    """Mean pool + L2 (ceb_pool_l2) over config-2 lengths: hidden [M, d] fp32.
+    Algorithmic bytes: every hidden value read once (d*4 per token), rows written."""
+    import torch
+
+    from . import binding
+    lens = _c2_lens(a.seqs)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).cuda()
+    M = int(lens.sum())
+    g = torch.Generator(device="cuda").manual_seed(0)
+    hidden = torch.randn((M, a.d), device="cuda", generator=g)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # larger than L2
+    for _ in range(a.warmup):
+        binding.pool_l2(hidden, cu)
+    torch.cuda.synchronize()
+    ms_all = []
+    for _ in range(a.iters):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        binding.pool_l2(hidden, cu)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_all.append(e0.elapsed_time(e1))
+    binding.sync_check()
+    ms = float(np.median(ms_all))
+    nbytes = (M + len(lens)) * a.d * 4
+    pk, src = _peaks()
+    return {"kernel": "pool_l2", "seqs": len(lens), "tokens": M, "ms": ms, "gbs": nbytes / (ms / 1e3) / 1e9,
+            "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"], "peak_source": src}
+
+
+def bench_encode(a):
+    """The whole config-2 encoder on the first n_seqs sequences (device ids), the
+    command ncu captures the encoder's row-wise kernels from."""
+    import os
+    import sys as _sys
+
+    import torch
+
+    from . import binding, synth
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    _sys.path.insert(0, root)
+    import bench
+    ids, lens = synth.config_ids(2)
+    lens = lens[:a.seqs]
+    ids = np.ascontiguousarray(ids[:int(lens.sum())])
+    m = binding.CrispEmbed(bench.model_path(0))
+    d_ids = torch.from_numpy(ids).cuda()
+    out = torch.empty((len(lens), m.dim), dtype=torch.float32, device="cuda")
+    for _ in range(a.warmup):
+        m.encode_ids_device(d_ids, lens, out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        m.encode_ids_device(d_ids, lens, out)
+    e1.record()
+    torch.cuda.synchronize()
+    binding.sync_check()
+    ms = e0.elapsed_time(e1) / a.iters
+    m.close()
+    return {"kernel": "encode", "seqs": len(lens), "tokens": int(lens.sum()), "ms": ms,
+            "tokens_per_s": int(lens.sum()) / (ms / 1e3)}
+
+
+def bench_cublas(a):
+    """torch.matmul (cuBLAS) on the same shape as a linear layer: fp16 operands, fp32
+    accumulation, fp16 output -- the library-GEMM bar for ceb_gemm_pair_kernel."""
+    import torch
+    x = torch.randn((a.m, a.k), device="cuda", dtype=torch.float16)
+    w = torch.randn((a.n, a.k), device="cuda", dtype=torch.float16) * 0.02
+    for _ in range(a.warmup):
+        y = torch.matmul(x, w.t())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        y = torch.matmul(x, w.t())
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.iters
+    flops = 2.0 * a.m * a.n * a.k
+    pk, src = _peaks()
+    tf = flops / (ms / 1e3) / 1e12
+    del y
+    return {"kernel": "cublas_fp16", "m": a.m, "n": a.n, "k": a.k, "ms": ms, "tflops": tf,
+            "frac_of_peak": tf / pk["bf16_tflops"], "peak_source": src}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -207,8 +306,24 @@ def main(argv=None):
     t.add_argument("--impl", choices=["mma", "tc"], default="mma")
     t.add_argument("--iters", type=int, default=20)
     t.add_argument("--warmup", type=int, default=3)
+    p = sub.add_parser("pool")
+    p.add_argument("--seqs", type=int, default=256)
+    p.add_argument("--d", type=int, default=768)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    e = sub.add_parser("encode")
+    e.add_argument("--seqs", type=int, default=256)
+    e.add_argument("--iters", type=int, default=3)
+    e.add_argument("--warmup", type=int, default=1)
+    c = sub.add_parser("cublas")
+    c.add_argument("--m", type=int, default=70825)
+    c.add_argument("--n", type=int, default=3072)
+    c.add_argument("--k", type=int, default=768)
+    c.add_argument("--iters", type=int, default=20)
+    c.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
-    r = {"gemm": bench_gemm, "moe": bench_moe, "route_ln": bench_route_ln, "attn": bench_attn}[a.what](a)
+    r = {"gemm": bench_gemm, "moe": bench_moe, "route_ln": bench_route_ln, "attn": bench_attn, "pool": bench_pool,
+         "encode": bench_encode, "cublas": bench_cublas}[a.what](a)
     print(json.dumps(r), flush=True)
     return 0
 

@@ -343,14 +343,36 @@ def zipf_shift(router_w: np.ndarray, top_k: int, s: float, rng: np.random.Genera
     return b.astype(np.float32)
 
 
+_OP_WEIGHTS: Dict[tuple, tuple] = {}  # quantized operator weights of the last few parameter sets
+
+
 def make_moe_op_inputs(T: int, d: int = 768, n_experts: int = 8, top_k: int = 2, ffn: int = 3072,
                        wtype: int = G.GGML_Q4_K, router_wtype: int = G.GGML_F32, zipf_s: Optional[float] = 1.2,
                        seed: int = 0, with_bias: bool = False) -> MoEOpInputs:
-    rng = np.random.default_rng(seed)
-    router = (rng.standard_normal((n_experts, d), dtype=np.float32) * np.float32(0.02))
-    fc1 = (rng.standard_normal((n_experts, ffn, d), dtype=np.float32) * np.float32(0.02))
-    fc2 = (rng.standard_normal((n_experts, d, ffn), dtype=np.float32) * np.float32(0.02))
-    bias = (rng.standard_normal((d,), dtype=np.float32) * np.float32(0.02)) if with_bias else None
+    """Seeded operator inputs: router / expert weights N(0, 0.02) drawn first from
+    default_rng(seed), then the activations z ~ N(0, 1) from the same stream.  The
+    quantized weights of a parameter set are kept for the next call with the same
+    weights (the balanced and Zipf variants of a config share them); the stream is
+    resumed from its state after the weights, so every call returns the same
+    arrays as a fresh draw."""
+    key = (d, n_experts, ffn, wtype, router_wtype, seed, with_bias)
+    if key in _OP_WEIGHTS:
+        router, router_raw, fc1_raw, fc2_raw, bias, state = _OP_WEIGHTS[key]
+        rng = np.random.default_rng(seed)
+        rng.bit_generator.state = state
+    else:
+        rng = np.random.default_rng(seed)
+        router = (rng.standard_normal((n_experts, d), dtype=np.float32) * np.float32(0.02))
+        fc1 = (rng.standard_normal((n_experts, ffn, d), dtype=np.float32) * np.float32(0.02))
+        fc2 = (rng.standard_normal((n_experts, d, ffn), dtype=np.float32) * np.float32(0.02))
+        bias = (rng.standard_normal((d,), dtype=np.float32) * np.float32(0.02)) if with_bias else None
+        router_raw = quantize(router, router_wtype).view(np.uint8).reshape(n_experts, -1)
+        fc1_raw = quantize(fc1, wtype).view(np.uint8).reshape(n_experts, ffn, -1)
+        fc2_raw = quantize(fc2, wtype).view(np.uint8).reshape(n_experts, d, -1)
+        del fc1, fc2
+        if len(_OP_WEIGHTS) >= 2:
+            _OP_WEIGHTS.pop(next(iter(_OP_WEIGHTS)))
+        _OP_WEIGHTS[key] = (router, router_raw, fc1_raw, fc2_raw, bias, rng.bit_generator.state)
     z = rng.standard_normal((T, d), dtype=np.float32)
     if zipf_s:
         b = zipf_shift(router, top_k, zipf_s, np.random.default_rng(seed + 1))
@@ -361,8 +383,6 @@ def make_moe_op_inputs(T: int, d: int = 768, n_experts: int = 8, top_k: int = 2,
         x = z
     x = _round_bf16(x)
     return MoEOpInputs(d=d, n_experts=n_experts, top_k=top_k, ffn=ffn, wtype=wtype, router_wtype=router_wtype,
-                       x=x, router_raw=quantize(router, router_wtype).view(np.uint8).reshape(n_experts, -1),
-                       fc1_raw=quantize(fc1, wtype).view(np.uint8).reshape(n_experts, ffn, -1),
-                       fc2_raw=quantize(fc2, wtype).view(np.uint8).reshape(n_experts, d, -1),
+                       x=x, router_raw=router_raw, fc1_raw=fc1_raw, fc2_raw=fc2_raw,
                        bias=bias, router_bias_logits=b,
                        meta=dict(T=T, seed=seed, zipf_s=zipf_s, init="N(0,0.02) weights, x=bf16(N(0,1)+W^+ b)"))

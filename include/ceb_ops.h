@@ -78,6 +78,20 @@ CEB_API int ceb_moe_ffn(const ceb_moe_layer* layer, const void* d_x, int x_dtype
                         size_t workspace_bytes, void* stream);
 
 /*
+ * Where the routing of the last ceb_moe_ffn / ceb_moe_route_ln call on a workspace
+ * lives inside it (device pointers into d_workspace, valid until the next call on
+ * it; no counterpart in the reference, where the grouping stays inside
+ * ggml_mul_mat_id, src/crispembed.cpp:1365,1371): ids / weights [n_tokens x
+ * top_k], slot_pos [n_tokens x top_k] = row of (token, slot) in the permuted
+ * expert matrices, offsets [n_experts + 1] = first row of each expert.  Rows are
+ * ordered by expert, then token, then slot -- ggml_mul_mat_id's grouping.
+ * offsets and slot_pos are written by the expert dispatch (ceb_moe_ffn), not by
+ * ceb_moe_route_ln alone.  Any output pointer may be NULL.
+ */
+CEB_API int ceb_moe_workspace_routing(const ceb_moe_layer* layer, int n_tokens, void* d_workspace, int32_t** d_ids,
+                                      float** d_weights, int32_t** d_slot_pos, int32_t** d_offsets);
+
+/*
  * The residual + LayerNorm that feeds the MoE block and the block's router in
  * one pass (src/crispembed.cpp:1316-1323 post-attention LN, then :1333-1345
  * router, softmax, top_k, gate weights): d_out = LN(d_res + d_y) * gamma + beta
@@ -281,10 +295,11 @@ CEB_API int ceb_matmul(int w_type, const void* h_w, int n_out, int k, const void
  * CRISPEMBED_CRISPEMBED_BENCH wall-clock prints, src/crispembed.cpp:1707-1712).
  * ceb_launch_count: kernels this library has launched since it was loaded.
  * ceb_profile_enable(1): from now on record CUDA events around every launch,
- * on the launch's own stream.  ceb_profile_read: per category (0 grouped GEMM,
- * 1 attention, 2 routing + permutation, 3 row-wise: embedding / LayerNorm /
- * combine / pooling, 4 expert-parallel peer copies, 5 expert-parallel waits for
- * peers) the number of launches, summed kernel milliseconds and
+ * on the launch's own stream.  ceb_profile_read: per category (0 dense GEMMs of
+ * the encoder and the linear entry points, 1 attention, 2 routing + permutation,
+ * 3 row-wise: embedding / LayerNorm / combine / pooling, 4 expert-parallel peer
+ * copies, 5 expert-parallel waits for peers, 6 grouped expert GEMMs of MoE
+ * blocks) the number of launches, summed kernel milliseconds and
  * algorithmic flops / bytes; synchronises on the recorded events and clears
  * them.  Returns 0 on success.
  */

@@ -578,6 +578,33 @@ void ceo_route(const float *logits, int64_t T, int E, int k, int32_t *ids, float
 }
 
 /* ------------------------------------------------------------ MoE FFN --- */
+/* The (token, slot) rows routed to expert e, in token order then slot order: the
+ * grouping ggml_mul_mat_id builds for each expert (src/crispembed.cpp:1365,1371).
+ * rows[i] = t*k + j; returns the count. */
+static int64_t expert_rows(const int32_t *ids, int64_t T, int k, int e, int64_t *rows) {
+    int64_t n = 0;
+    for (int64_t t = 0; t < T; t++)
+        for (int j = 0; j < k; j++)
+            if (ids[t * k + j] == e) rows[n++] = t * k + j;
+    return n;
+}
+
+/* The permutation of all experts' rows stacked in expert order: offsets[e] = first
+ * permuted row of expert e (offsets[E] = T*k), slot_pos[t*k + j] = permuted row of
+ * (token t, slot j). */
+void ceo_moe_permutation(const int32_t *ids, int64_t T, int k, int E, int32_t *slot_pos, int32_t *offsets) {
+    int64_t *rows = (int64_t *)malloc((size_t)(T * k + 1) * sizeof(int64_t));
+    int64_t base = 0;
+    for (int e = 0; e < E; e++) {
+        offsets[e] = (int32_t)base;
+        const int64_t n = expert_rows(ids, T, k, e, rows);
+        for (int64_t i = 0; i < n; i++) slot_pos[rows[i]] = (int32_t)(base + i);
+        base += n;
+    }
+    offsets[E] = (int32_t)base;
+    free(rows);
+}
+
 /* The MoE branch of build_encoder_graph (src/crispembed.cpp:1327-1381):
  * router -> softmax -> top-k -> per-slot fc1 (ggml_mul_mat_id) -> erf-GELU
  * -> fc2 -> y[t] = sum_j w[t,j]*down[t,j] (+ bias).  Expert rows are
@@ -611,10 +638,7 @@ void ceo_moe_ffn2(const float *x, int64_t T, int d, int E, int k, int F, int rou
     /* gather rows per expert (stable in token order) */
     int64_t *rows = (int64_t *)malloc((size_t)(T * k) * sizeof(int64_t));
     for (int e = 0; e < E; e++) {
-        int64_t n = 0;
-        for (int64_t t = 0; t < T; t++)
-            for (int j = 0; j < k; j++)
-                if (ids[t * k + j] == e) rows[n++] = t * k + j;
+        int64_t n = expert_rows(ids, T, k, e, rows);
         if (!n) continue;
         float *xe = (float *)malloc((size_t)(n * d) * sizeof(float));
         float *he = (float *)malloc((size_t)(n * F) * sizeof(float));

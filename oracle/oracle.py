@@ -77,6 +77,7 @@ def lib():
         L.ceo_moe_ffn2.argtypes = [_fp, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                    ctypes.c_int, _up, ctypes.c_int, _up, ctypes.c_int, _up, _fp, ctypes.c_int, _ip,
                                    _fp, _fp, _ip, _fp, _fp]
+        L.ceo_moe_permutation.argtypes = [_ip, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _ip, _ip]
         L.ceo_pool_l2.argtypes = [_fp, _ip, ctypes.c_int, ctypes.c_int, _fp]
         L.ceo_truncate_renorm.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp]
         L.ceo_expf.argtypes = [ctypes.c_float]
@@ -192,6 +193,17 @@ def moe_ffn(x: np.ndarray, E: int, k: int, F: int, router_type: int, router_raw:
     lib().ceo_moe_ffn2(_f(x), T, d, E, k, F, router_type, pr, wtype, p1, wtype if wtype2 is None else wtype2, p2,
                        _f(bias), mode, _i(ids_in), _f(wts_in), _f(y), _i(ids), _f(w), _f(logits))
     return y, ids, w, logits
+
+
+def moe_permutation(ids: np.ndarray, n_experts: int):
+    """(slot_pos [T, k], offsets [E+1]) of the expert grouping of ids [T, k]: rows in
+    (expert, token, slot) order, as ggml_mul_mat_id groups them."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, k = ids.shape
+    slot_pos = np.empty((T, k), dtype=np.int32)
+    offsets = np.empty(n_experts + 1, dtype=np.int32)
+    lib().ceo_moe_permutation(_i(ids), T, k, n_experts, _i(slot_pos), _i(offsets))
+    return slot_pos, offsets
 
 
 def attention(qkv: np.ndarray, cu: np.ndarray, n_head: int, d: int) -> np.ndarray:

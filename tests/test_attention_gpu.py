@@ -74,3 +74,49 @@ def test_attention_repeatable(cuda, attn_impl):
     a = binding.attention(q, c, 2).cpu().numpy()
     b = binding.attention(q, c, 2).cpu().numpy()
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("cu_list,rows,max_len", [
+    ([0, 64], 64, 32),      # a sequence longer than max_len
+    ([0, 40, 100], 64, 64),  # offsets past the last row
+])
+def test_inconsistent_row_offsets_reported(cuda, attn_impl, cu_list, rows, max_len):
+    """Offsets that disagree with max_len or leave the rows set the device error word
+    (status 5 from ceb_sync_check) and write nothing; the context stays usable."""
+    import torch
+    from crispembed_b200 import binding
+    qkv, _, _ = _qkv([rows], 2, seed=4)
+    q = torch.from_numpy(qkv).to(cuda)
+    cu = torch.tensor(cu_list, dtype=torch.int32, device=cuda)
+    out = binding.attention(q, cu, 2, max_len=max_len)
+    with pytest.raises(binding.CrispEmbedError, match=r"\(5\).*0x106"):
+        binding.sync_check()
+    binding.sync_check()  # reported once, then clear
+    good = binding.attention(q, torch.tensor([0, rows], dtype=torch.int32, device=cuda), 2)
+    binding.sync_check()
+    assert torch.isfinite(good.float()).all()
+    del out
+
+
+def test_error_words_are_per_device(attn_impl):
+    """A device-side check raised by an operator on GPU 1 is reported by ceb_sync_check
+    on GPU 1 only; GPU 0's word stays clear (one error word per device)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from crispembed_b200 import binding
+    binding.load_library()
+    qkv, _, _ = _qkv([64], 2, seed=4)
+    for dev in (0, 1):  # both devices have an error word before the fault is raised
+        with torch.cuda.device(dev):
+            binding.sync_check()
+    with torch.cuda.device(1):
+        q = torch.from_numpy(qkv).to("cuda:1")
+        binding.attention(q, torch.tensor([0, 64], dtype=torch.int32, device="cuda:1"), 2, max_len=32)
+        torch.cuda.synchronize()
+    with torch.cuda.device(0):
+        binding.sync_check()
+    with torch.cuda.device(1):
+        with pytest.raises(binding.CrispEmbedError, match=r"\(5\)"):
+            binding.sync_check()
+        binding.sync_check()

@@ -5,6 +5,8 @@ Checks, per BASELINE's bar:
   * router logits bit-identical to the ggml-faithful oracle for Q8_0 routers
     (x re-quantized to Q8_0, integer block dots in ggml's lane order);
   * expert ids bit-exact wherever the k-th/(k+1)-th logit gap exceeds 1e-4;
+  * the expert permutation (row of every (token, slot) in the grouped matrices,
+    expert row offsets) bit-identical to ggml_mul_mat_id's grouping;
   * expert math within 1e-3 (of max-abs) of the oracle computed with the same
     routing and the kernels' operand precision (F16 mode), and cos >= 0.999 per
     token against the ggml-faithful oracle;
@@ -54,7 +56,8 @@ def _run(cuda, inp, x_dtype="bf16", repeat=1):
         lg = torch.empty((T, inp.n_experts), dtype=torch.float32, device=cuda)
         layer.forward(x, y, ws, ids=ids, weights=w, counts=cnt, logits=lg)
         binding.sync_check()
-        outs.append(tuple(t.cpu().numpy() for t in (y, ids, w, cnt, lg)))
+        _, _, slot_pos, offsets = layer.routing(ws, T)
+        outs.append(tuple(t.cpu().numpy() for t in (y, ids, w, cnt, lg)) + (slot_pos, offsets))
     layer.close()
     return outs
 
@@ -69,7 +72,7 @@ def test_moe_matches_oracle(cuda, oracle, name):
     cfg = dict(CONFIGS[name])
     T = cfg.pop("T")
     inp = synth.make_moe_op_inputs(T, seed=11, **cfg)
-    (y, ids, w, cnt, lg), = _run(cuda, inp)
+    (y, ids, w, cnt, lg, slot_pos, offsets), = _run(cuda, inp)
     x = inp.x
     ry, rids, rw, rlg = oracle.moe_ffn(x, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw,
                                        inp.wtype, inp.fc1_raw, inp.fc2_raw, inp.bias, oracle.GGML)
@@ -84,6 +87,11 @@ def test_moe_matches_oracle(cuda, oracle, name):
     assert np.array_equal(ids[sure], rids[sure])
     assert np.allclose(w[sure], rw[sure], rtol=1e-5, atol=1e-7)
     assert np.array_equal(cnt, np.bincount(ids.reshape(-1), minlength=inp.n_experts))
+    # permutation: ggml_mul_mat_id's (expert, token, slot) grouping of the same ids, bit for bit
+    osp, ooff = oracle.moe_permutation(ids, inp.n_experts)
+    assert np.array_equal(offsets, ooff) and np.array_equal(slot_pos, osp)
+    if np.array_equal(ids, rids):
+        assert np.array_equal(slot_pos, oracle.moe_permutation(rids, inp.n_experts)[0])
     # expert math at kernel precision on the kernel's own routing
     fy, _, _, _ = oracle.moe_ffn(x, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw, inp.wtype,
                                  inp.fc1_raw, inp.fc2_raw, inp.bias, oracle.F16, ids_in=ids, wts_in=w)
@@ -108,8 +116,8 @@ def test_moe_repeat_bit_identical(cuda):
 def test_moe_input_dtypes(cuda, oracle, dtype):
     inp = synth.make_moe_op_inputs(96, d=256, n_experts=4, top_k=2, ffn=512, wtype=GGML_Q8_0,
                                    router_wtype=GGML_Q8_0, zipf_s=None, seed=2, with_bias=True)
-    (y, ids, w, cnt, lg), = _run(cuda, inp, x_dtype=dtype)
-    (yb, idsb, _, _, _), = _run(cuda, inp, x_dtype="bf16")
+    (y, ids, w, cnt, lg, _, _), = _run(cuda, inp, x_dtype=dtype)
+    (yb, idsb, _, _, _, _, _), = _run(cuda, inp, x_dtype="bf16")
     # x holds bf16-representable values, exactly representable in f32 and (at this range) f16
     assert np.array_equal(ids, idsb)
     assert np.abs(y - yb).max() <= 1e-6 * max(1.0, np.abs(yb).max())
