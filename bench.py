@@ -31,7 +31,8 @@ own e2e, roofline and CPU baseline; --workload c3|c5 prints one as the main line
 Rooflines: "roofline" covers every launch of the dominant kernel (the tcgen05 GEMM
 of all linear layers), "roofline_moe_grouped_gemm" the grouped expert GEMMs alone;
 all use the measured sustained bf16 peak, with the burst fraction beside it.
---impl reference: the CPU restatement of the reference's ggml CPU path (oracle/,
+--impl reference: the CPU restatement of the reference's ggml CPU path (oracle/, its
+timing build: the C library's expf / erff as ggml calls them,
 the reference itself cannot be built here) on all host threads, bounded sample.
 """
 from __future__ import annotations
@@ -155,6 +156,7 @@ def cpu_baseline(path, ids, lens, budget_s=15.0):
     """Oracle (CPU restatement of ggml's CPU path) on the first sequences of the batch."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    O.use_timing_build()
     cores = O.set_threads(os.cpu_count() or 1)
     m = O.load_model(path)
     cu = np.concatenate([[0], np.cumsum(lens)])
@@ -166,7 +168,7 @@ def cpu_baseline(path, ids, lens, budget_s=15.0):
     dt = time.perf_counter() - t0
     return {"value": done_tok / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"first {n} sequences ({done_tok} tokens) of the config-2 batch, one encode per sequence "
-                      f"as the reference's sequential path does, ggml-faithful mode, {dt:.1f}s"}
+                      f"as the reference's sequential path does, ggml-faithful mode (C library expf/erff), {dt:.1f}s"}
 
 
 def c2_config(n_seqs, tokens, world):
@@ -183,6 +185,7 @@ def run_reference(args, rank):
     ids, lens = synth.config_ids(2)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    O.use_timing_build()
     cores = O.set_threads(os.cpu_count() or 1)
     m = O.load_model(path)
     cu = np.concatenate([[0], np.cumsum(lens)])
@@ -200,7 +203,8 @@ def run_reference(args, rank):
             toks.append(int(lens[a:b].sum()))
     value = sum(toks) / sum(times)
     sample = (f"{per_step} sequences per step of the config-2 batch (lens U[32,512] seed 2), encoded one by one "
-              f"(the reference's sequential encode_tokens path), oracle ggml-faithful CPU restatement")
+              f"(the reference's sequential encode_tokens path), oracle ggml-faithful CPU restatement with the C "
+              f"library's expf/erff")
     out = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8 blocks / f32",
@@ -583,6 +587,7 @@ def op_cpu_baseline(inp, budget_s=10.0, n=256):
     """Oracle MoE op (ggml-faithful CPU restatement) on the first n tokens, repeated for ~budget_s."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    O.use_timing_build()
     cores = O.set_threads(os.cpu_count() or 1)
     x = inp.x[:n]
     done, t0 = 0, time.perf_counter()
@@ -592,7 +597,8 @@ def op_cpu_baseline(inp, budget_s=10.0, n=256):
         done += len(x)
     dt = time.perf_counter() - t0
     return {"value": done / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"the first {n} tokens of the workload, MoE op repeated for {dt:.1f}s, ggml-faithful mode"}
+            "sample": f"the first {n} tokens of the workload, MoE op repeated for {dt:.1f}s, ggml-faithful mode "
+                      f"(C library expf/erff)"}
 
 
 def bench_moe_op(args, rank, world, local):

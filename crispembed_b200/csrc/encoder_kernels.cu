@@ -192,6 +192,16 @@ CEB_DEV float ex2_approx(float x) {  // MUFU 2^x (ex2(-inf) = 0)
 #ifndef CEB_ATTN_POLY_J
 #define CEB_ATTN_POLY_J 0xC0  // key n-tiles (bit j) whose exponentials use ex2_poly instead of MUFU
 #endif
+#ifndef CEB_ATTN_EXP_F16X2
+#define CEB_ATTN_EXP_F16X2 1  // exponentials two at a time in fp16 (ex2.approx.f16x2), row sums by the MMA
+#endif
+// 2^t for two exponents: the pair rounded to fp16 (one conversion), then one MUFU
+// op for both; the result is the packed fp16 pair the P V product consumes.
+CEB_DEV uint32_t ex2_h2(float t0, float t1) {
+    uint32_t in = h2_as_u32(__floats2half2_rn(t0, t1)), r;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(in));
+    return r;
+}
 
 CEB_DEV void cp_async16(uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -264,6 +274,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
     float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+    float o_sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row sums of P (fp16 pairs path): c0 row g, c2 row g + 8
     const int g = lane >> 2, tq = lane & 3;
 
     for (int kt = 0; kt < n_kt; ++kt) {
@@ -329,6 +340,32 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
             corr[r] = ex2_approx(fmaf(m_r[r], scale_log2, nm[r]));
         }
         uint32_t pf[4][4];
+#if CEB_ATTN_EXP_F16X2
+        // P in fp16 pairs straight from the exponent unit; the row sums come from the
+        // P V product against an all-ones column tile (o_sum), so no float adds here
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int kk = j >> 1, hi = j & 1;
+            pf[kk][hi * 2 + 0] = ex2_h2(fmaf(s[j][0], scale_log2, nm[0]), fmaf(s[j][1], scale_log2, nm[0]));
+            pf[kk][hi * 2 + 1] = ex2_h2(fmaf(s[j][2], scale_log2, nm[1]), fmaf(s[j][3], scale_log2, nm[1]));
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) m_r[r] = mx[r];
+        if (__any_sync(0xffffffffu, corr[0] != 1.0f || corr[1] != 1.0f)) {  // the running max moved
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                o[i][0] *= corr[0];
+                o[i][1] *= corr[0];
+                o[i][2] *= corr[1];
+                o[i][3] *= corr[1];
+            }
+            o_sum[0] *= corr[0];
+            o_sum[1] *= corr[0];
+            o_sum[2] *= corr[1];
+            o_sum[3] *= corr[1];
+        }
+        (void)rs;
+#else
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             float p0, p1, p2, p3;
@@ -365,10 +402,14 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
                 o[i][3] *= corr[1];
             }
         }
+#endif
         // O += P V : k = 64 keys (4 steps of 16), n = 64 dims (8 tiles of 8)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
+#if CEB_ATTN_EXP_F16X2
+            mma16816(o_sum, a, 0x3C003C00u, 0x3C003C00u);  // P times a tile of fp16 ones: row sums
+#endif
 #pragma unroll
             for (int np = 0; np < 4; ++np) {
                 const int key = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
@@ -382,6 +423,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         __syncthreads();
     }
     // normalise and store fp16
+#if CEB_ATTN_EXP_F16X2
+    l_r[0] = o_sum[0];
+    l_r[1] = o_sum[2];
+#endif
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int q = q0 + warp * 16 + g + 8 * r;
@@ -429,6 +474,80 @@ __global__ void pool_l2_kernel(const float* __restrict__ hidden, const int32_t* 
     __syncthreads();
     const float norm = red[31];
     for (int c = threadIdx.x; c < out_dim; c += blockDim.x) out[(size_t)s * out_dim + c] = sp[c] / norm;
+}
+
+// Mean pool + L2 for mode 0, one cluster of POOL_SPLIT CTAs per sequence: CTA x sums
+// the sequence's 8-row blocks x, x + POOL_SPLIT, ... (float4 columns, the block's rows
+// loaded together, added in row order), the cluster's rank 0 then adds the partials of
+// ranks 0..POOL_SPLIT-1 in rank order from their shared memory, divides by the row
+// count and normalises.  Fixed orders: results identical run to run and independent
+// of the rest of the batch.  d / 4 threads (one float4 column each).
+constexpr int POOL_SPLIT = 8, POOL_ROWS = 8;
+__global__ void __cluster_dims__(POOL_SPLIT, 1, 1) pool_mean_cluster_kernel(const float* __restrict__ hidden,
+                                                                            const int32_t* __restrict__ cu, int d,
+                                                                            int out_dim, float* __restrict__ out) {
+    extern __shared__ float4 pp[];  // [d/4] partial + [32] scratch
+    const int s = blockIdx.y;
+    const uint32_t x = cluster_ctarank();
+    const int r0 = cu[s], n = cu[s + 1] - cu[s];
+    const int c4 = threadIdx.x, nc4 = d >> 2;
+    const float4* h = reinterpret_cast<const float4*>(hidden) + (size_t)r0 * nc4 + c4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int b = (int)x * POOL_ROWS; b < n; b += POOL_SPLIT * POOL_ROWS) {
+        float4 v[POOL_ROWS];
+#pragma unroll
+        for (int i = 0; i < POOL_ROWS; ++i)
+            v[i] = b + i < n ? __ldcs(h + (size_t)(b + i) * nc4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < POOL_ROWS; ++i) {
+            acc.x += v[i].x;
+            acc.y += v[i].y;
+            acc.z += v[i].z;
+            acc.w += v[i].w;
+        }
+    }
+    pp[c4] = acc;
+    cluster_sync();  // every partial written
+    if (x == 0) {
+        float4 t = acc;
+        for (uint32_t r = 1; r < POOL_SPLIT; ++r) {
+            const uint32_t a = mapa_shared(smem_u32(&pp[c4]), r);
+            float4 q;
+            asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(q.x), "=f"(q.y), "=f"(q.z), "=f"(q.w)
+                         : "r"(a));
+            t.x += q.x;
+            t.y += q.y;
+            t.z += q.z;
+            t.w += q.w;
+        }
+        const float inv_n = 1.0f / (float)(n > 0 ? n : 1);
+        t = n > 0 ? make_float4(t.x * inv_n, t.y * inv_n, t.z * inv_n, t.w * inv_n) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float part = 0.0f;
+        const int base = 4 * c4;
+        if (base < out_dim) part += t.x * t.x;
+        if (base + 1 < out_dim) part += t.y * t.y;
+        if (base + 2 < out_dim) part += t.z * t.z;
+        if (base + 3 < out_dim) part += t.w * t.w;
+        part = wsum(part);
+        float* red = reinterpret_cast<float*>(pp + nc4);
+        __syncthreads();  // rank 0 only: all its threads take this branch
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float tot = 0.0f;
+            for (int w = 0; w < (int)((blockDim.x + 31) >> 5); ++w) tot += red[w];
+            red[31] = sqrtf(fmaxf(tot, 1e-12f));
+        }
+        __syncthreads();
+        const float norm = red[31];
+        float* o = out + (size_t)s * out_dim + base;
+        if (base < out_dim) o[0] = t.x / norm;
+        if (base + 1 < out_dim) o[1] = t.y / norm;
+        if (base + 2 < out_dim) o[2] = t.z / norm;
+        if (base + 3 < out_dim) o[3] = t.w / norm;
+    }
+    cluster_sync();  // rank 0 has read every partial before any CTA of the cluster exits
 }
 
 }  // namespace
@@ -514,6 +633,14 @@ int ceb_pool_l2_launch(const float* hidden, const int32_t* cu, int n_seqs, int d
                        cudaStream_t st, int mode) {
     if (n_seqs <= 0) return 0;
     if (out_dim <= 0 || out_dim > d) return ceb_set_error(1, "pool: out_dim %d outside (0, %d]", out_dim, d);
+    if (mode == 0 && d % 128 == 0 && d <= 4096 && (reinterpret_cast<uintptr_t>(hidden) & 15) == 0) {
+        const size_t smem = (size_t)d * sizeof(float) + 32 * sizeof(float4);
+        CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0,
+                   pool_mean_cluster_kernel<<<dim3(POOL_SPLIT, n_seqs), d / 4, smem, st>>>(hidden, cu, d, out_dim,
+                                                                                            out));
+        CEB_CUDA_OK(cudaGetLastError());
+        return 0;
+    }
     const size_t smem = (size_t)(d + 32) * sizeof(float);
     CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, pool_l2_kernel<<<n_seqs, 256, smem, st>>>(hidden, cu, d, out_dim, out, mode));
     CEB_CUDA_OK(cudaGetLastError());

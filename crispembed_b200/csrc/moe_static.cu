@@ -6,7 +6,9 @@
 // allocate, or latency-critical callers that cannot afford the device-wide
 // synchronisation cudaMalloc/cudaFree may cause.  ceb_moe_ffn_static serves
 // them: its scratch is the file-scope array below, which the CUDA runtime sets
-// aside on every GPU that loads this library and keeps until the process exits.
+// aside on a GPU when this library's device code is loaded there (at its first use
+// on that GPU under lazy module loading, the default; on every GPU the process
+// initialises under CUDA_MODULE_LOADING=EAGER) and keeps until the process exits.
 #include <cuda_runtime.h>
 
 #include <mutex>

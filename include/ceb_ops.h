@@ -115,9 +115,12 @@ CEB_API int ceb_moe_route_ln(const ceb_moe_layer* layer, const float* d_res, con
  * GPU memory belongs to another allocator, a plugin handed only a stream, or a
  * latency-critical path that cannot take the device-wide synchronisation of
  * cudaMalloc/cudaFree.  The scratch is a fixed CEB_MOE_STATIC_SCRATCH_BYTES
- * array inside this library, held on every GPU that loads it until the process
- * exits; the call itself allocates nothing (with instrumentation off, the
- * default).  Computes what ceb_moe_ffn computes (y only).
+ * array inside this library, reserved on a device when the library's device code
+ * is loaded there -- with lazy module loading (CUDA_MODULE_LOADING=LAZY, the
+ * default since CUDA 12.2) at the first use of that code on the device, with
+ * EAGER on every device the process initialises, callers of this entry or not --
+ * and held until the process exits; the call itself allocates nothing (with
+ * instrumentation off, the default).  Computes what ceb_moe_ffn computes (y only).
  *
  * Limits and rules:
  *  - n_tokens is limited by the scratch: ceb_moe_workspace_size(layer, n_tokens)

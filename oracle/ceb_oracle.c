@@ -34,9 +34,18 @@
 #include <omp.h>
 #endif
 
-/* exp / erf shared bit for bit with the device kernels (the C library's expf and
- * erff stand in for the reference's; see the header) */
+/* exp / erf shared bit for bit with the device kernels (see the header).  The
+ * build that times the CPU path (CEO_LIBM_MATH) calls the C library's expf / erff
+ * instead, as ggml does: the shared routines compute in double precision and cost
+ * several times more on the CPU; the two differ by at most one ulp. */
 #include "ceb_portable_math.h"
+#ifdef CEO_LIBM_MATH
+#define ceo_expf_ expf
+#define ceo_erff_ erff
+#else
+#define ceo_expf_ ceb_expf
+#define ceo_erff_ ceb_erff
+#endif
 
 enum { CEO_EXACT = 0, CEO_GGML = 1, CEO_F16 = 2 };
 enum {
@@ -471,7 +480,7 @@ float ceo_erff(float x) { return ceb_erff(x); }
 /* exact erf GELU, as ggml_vec_gelu_erf_f32 computes it: 0.5x(1+erf(x/sqrt2)) */
 void ceo_gelu_erf(float *x, int64_t n) {
     const float s2 = 0.70710678118654752440f;
-    for (int64_t i = 0; i < n; i++) x[i] = 0.5f * x[i] * (1.0f + ceb_erff(x[i] * s2));
+    for (int64_t i = 0; i < n; i++) x[i] = 0.5f * x[i] * (1.0f + ceo_erff_(x[i] * s2));
 }
 
 /* ggml_norm_f32 then ggml_mul(gamma) and ggml_add(beta): mean and variance
@@ -528,10 +537,10 @@ void ceo_attention(const float *q, const float *k, const float *v, int64_t ld, c
                     if (sc > M) {
                         float Mold = M;
                         M = sc;
-                        ms = ceb_expf(Mold - M);
+                        ms = ceo_expf_(Mold - M);
                         for (int c = 0; c < hd; c++) acc[c] *= ms;
                     } else {
-                        vs = ceb_expf(sc - M);
+                        vs = ceo_expf_(sc - M);
                     }
                     for (int c = 0; c < hd; c++) acc[c] = fmaf(vj[c], vs, acc[c]);
                     S = S * ms + vs;
@@ -557,7 +566,7 @@ void ceo_route(const float *logits, int64_t T, int E, int k, int32_t *ids, float
         float p[256];
         double sum = 0.0;
         for (int e = 0; e < E; e++) {
-            p[e] = ceb_expf(lg[e] - mx);
+            p[e] = ceo_expf_(lg[e] - mx);
             sum += (double)p[e];
         }
         float inv = (float)(1.0 / sum);

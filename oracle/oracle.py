@@ -22,6 +22,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libceb_oracle.so")
+# the timing build (C library expf / erff, as the reference's CPU path calls them):
+# select it with use_timing_build() before the first call, for CPU-baseline timings only
+TIMING_LIB_PATH = os.path.join(HERE, "libceb_oracle_timing.so")
+_lib_path = LIB_PATH
 
 EXACT, GGML, F16 = 0, 1, 2
 T_F32, T_F16, T_Q8_0, T_Q4_K = 0, 1, 8, 12
@@ -42,17 +46,26 @@ _SOURCES = [os.path.join(HERE, "ceb_oracle.c"),
 
 
 def build(force: bool = False) -> str:
-    if force or not os.path.exists(LIB_PATH) or any(
-            os.path.exists(p) and os.path.getmtime(LIB_PATH) < os.path.getmtime(p) for p in _SOURCES):
+    if force or any(not os.path.exists(t) or any(os.path.exists(p) and os.path.getmtime(t) < os.path.getmtime(p)
+                                                 for p in _SOURCES) for t in (LIB_PATH, TIMING_LIB_PATH)):
         subprocess.run(["make", "-C", HERE, "-s"], check=True)
-    return LIB_PATH
+    return _lib_path
+
+
+def use_timing_build():
+    """Load the timing build (the C library's expf / erff) instead of the parity build;
+    call before any other function of this module (CPU-baseline timings only)."""
+    global _lib_path
+    if _lib is not None and _lib_path != TIMING_LIB_PATH:
+        raise RuntimeError("the parity build is already loaded in this process")
+    _lib_path = TIMING_LIB_PATH
 
 
 def lib():
     global _lib
     if _lib is None:
         build()
-        L = ctypes.CDLL(LIB_PATH)
+        L = ctypes.CDLL(_lib_path)
         L.ceo_f16_to_f32.argtypes = [ctypes.c_uint16]
         L.ceo_f16_to_f32.restype = ctypes.c_float
         L.ceo_f32_to_f16.argtypes = [ctypes.c_float]

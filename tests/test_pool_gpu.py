@@ -43,6 +43,26 @@ def test_pool_matryoshka(cuda, oracle):
     assert np.abs(out - ref).max() <= 2e-6
 
 
+def test_pool_empty_sequence_and_unaligned_rows(cuda, oracle):
+    """A sequence without rows pools to zeros; hidden rows off a 16-byte boundary take
+    the scalar path and give the same result."""
+    import torch
+    from crispembed_b200 import binding
+    rng = np.random.default_rng(3)
+    lens = np.array([0, 3, 64, 0, 9], dtype=np.int32)
+    cu = _cu(lens)
+    h = rng.standard_normal((int(cu[-1]), 256), dtype=np.float32)
+    out = binding.pool_l2(torch.from_numpy(h).to(cuda), torch.from_numpy(cu).to(cuda)).cpu().numpy()
+    ref = oracle.pool_l2(h, cu)
+    assert np.all(out[0] == 0.0) and np.all(out[3] == 0.0)
+    assert np.abs(out - ref).max() <= 2e-6
+    buf = torch.empty(int(cu[-1]) * 256 + 1, dtype=torch.float32, device=cuda)
+    shifted = buf[1:].view(int(cu[-1]), 256)  # 4-byte offset
+    shifted.copy_(torch.from_numpy(h))
+    out2 = binding.pool_l2(shifted, torch.from_numpy(cu).to(cuda)).cpu().numpy()
+    assert np.abs(out2 - ref).max() <= 2e-6
+
+
 def test_pool_zero_vector_epsilon(cuda):
     import torch
     from crispembed_b200 import binding
