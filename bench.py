@@ -221,7 +221,7 @@ def c4_config(world, tokens):
                         "sequences sharded over the ranks, MoE experts split over the ranks",
             "tokens_per_step": tokens, "global_batch": 512, "seq_len": 512,
             "parallelism": f"ep{world} (experts {8 // world} per GPU) x dp{world} sequence shards",
-            "exchange": "per MoE block: counts, dispatch rows (fp16) and expert outputs (fp32) stored into peer "
+            "exchange": "per MoE block: counts, dispatch rows (fp16) and expert outputs (fp16) stored into peer "
                         "memory by the permutation / return kernels over NVLink, bounded flag waits",
             "l2": "inputs larger than L2"}
 

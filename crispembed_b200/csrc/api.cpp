@@ -772,7 +772,7 @@ extern "C" int ceb_moe_route_ln(const ceb_moe_layer* L, const float* d_res, cons
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     ceb_moe_ws ws;
     ceb_moe_ws_layout(n_tokens, L->w.d, L->w.n_experts, L->w.top_k, L->w.ffn, &ws, static_cast<uint8_t*>(d_workspace));
-    int rc = ceb_add_ln_route(d_res, d_y, n_tokens, L->w.d, d_gamma, d_beta, eps, d_out, static_cast<__half*>(d_out16),
+    int rc = ceb_add_ln_route(d_res, d_y, false, n_tokens, L->w.d, d_gamma, d_beta, eps, d_out, static_cast<__half*>(d_out16),
                               L->w, ws, d_logits, st);
     if (rc) return rc;
     const size_t S = (size_t)n_tokens * L->w.top_k;

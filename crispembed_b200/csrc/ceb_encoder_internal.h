@@ -14,9 +14,11 @@
 int ceb_embed_ln(const int32_t* ids, const int32_t* cu, int n_seqs, int M, int d, int n_vocab, const float* tok,
                  const float* pos, int n_pos, int pos_offset, const float* type0, const float* gamma,
                  const float* beta, float eps, float* out32, __half* out16, int* err, cudaStream_t st);
-int ceb_add_ln(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
+// y: the fp16 output of the GEMM in front of the residual
+int ceb_add_ln(const float* res, const __half* y, int M, int d, const float* gamma, const float* beta, float eps,
                float* out32, __half* out16, cudaStream_t st);
-int ceb_moe_combine_ln(const float* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
+// down: the fp16 expert rows of the MoE block (fc2 output, permuted order)
+int ceb_moe_combine_ln(const __half* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
                        const float* cur, int M, int d, const float* gamma, const float* beta, float eps, float* out32,
                        __half* out16, cudaStream_t st);
 int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
@@ -120,6 +122,7 @@ struct ceb_workspace {
     size_t bytes = 0;
     float *x32 = nullptr, *c32 = nullptr, *t32 = nullptr;
     __half *x16 = nullptr, *c16 = nullptr, *qkv16 = nullptr, *a16 = nullptr, *h16 = nullptr;
+    __half* t16 = nullptr;     // fp16 output of the GEMMs in front of a residual (attn-out, dense fc2)
     ceb_moe_ws moe;
     ceb_ref_ws ref;            // reference-arithmetic models only
     int32_t* ids = nullptr;    // [cap_tokens]

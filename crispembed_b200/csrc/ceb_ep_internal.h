@@ -11,7 +11,7 @@
 //   header  : ceb_ep_header (shape check at connect time)
 //   recv    : [recv_rows x d] fp16  rows of r's experts, expert-major, then by
 //             source rank, then in the source's stable (token, slot) order
-//   ret     : [T_cap*K x d] fp32    expert outputs of r's own (token, slot)s,
+//   ret     : [T_cap*K x d] fp16    expert outputs of r's own (token, slot)s,
 //             in r's local expert-major order (the single-GPU permutation)
 //   counts  : [2][world][E] int32   per-source expert counts (epoch parity)
 //   flags   : [3][world] uint32     counts / dispatch / return done, by source
@@ -26,7 +26,7 @@
 
 struct ceb_ep_peer {
     __half* recv;
-    float* ret;
+    __half* ret;
     int32_t* counts;
     uint32_t* flags;
 };
@@ -53,7 +53,7 @@ struct ceb_ep {
     ceb_ep_peer* d_peers = nullptr;   // device [world]
     // local (not exported) buffers
     __half* h = nullptr;              // [recv_rows x F] fc1 output
-    float* down = nullptr;            // [recv_rows x d] fc2 output
+    __half* down = nullptr;           // [recv_rows x d] fc2 output
     int32_t* offsets_recv = nullptr;  // [E_loc + 1] row ranges of the local experts in recv
     int* done = nullptr;              // [2] completion counters of the dispatch / return kernels
 };
@@ -94,5 +94,5 @@ int ceb_moe_route(const ceb_moe_weights& mw, const void* x, int x_dtype, int T, 
 int ceb_moe_permute(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T,
                     const ceb_moe_ws& ws, int32_t* expert_counts, const ceb_ep_args* ep, int* dev_err,
                     cudaStream_t st);
-int ceb_moe_combine(const float* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
+int ceb_moe_combine(const __half* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
                     const float* bias, float* y, cudaStream_t st);

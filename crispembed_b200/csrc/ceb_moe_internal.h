@@ -34,7 +34,7 @@ struct ceb_moe_ws {
     int32_t* slot_pos = nullptr;      // [T*K] permuted row of each (token, slot)
     __half* x_perm = nullptr;         // [T*K x d]
     __half* h_perm = nullptr;         // [T*K x ffn]
-    float* down = nullptr;            // [T*K x d]
+    __half* down = nullptr;           // [T*K x d] fc2 outputs (fp16)
 };
 
 size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint8_t* base);
@@ -47,9 +47,10 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __h
 // and routes the normalised rows in the same pass (ids, wts, block_counts of
 // ws), then ceb_moe_dispatch (scan, scatter, expert GEMMs, optional combine)
 // runs on those routes with x = out32 (x_dtype F32) and x16 = out16.
-int ceb_add_ln_route(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
-                     float* out32, __half* out16, const ceb_moe_weights& mw, const ceb_moe_ws& ws, float* logits_out,
-                     cudaStream_t st);
+// y is fp16 when y_f16 (the encoder's GEMM output), else float (the operator entry point).
+int ceb_add_ln_route(const float* res, const void* y, bool y_f16, int M, int d, const float* gamma, const float* beta,
+                     float eps, float* out32, __half* out16, const ceb_moe_weights& mw, const ceb_moe_ws& ws,
+                     float* logits_out, cudaStream_t st);
 int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, const __half* x16, int T, float* y,
                      const ceb_moe_ws& ws, int32_t* expert_counts, int* dev_err, cudaStream_t st);
 

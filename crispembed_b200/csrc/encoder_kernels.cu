@@ -78,8 +78,9 @@ __global__ void embed_ln_kernel(const int32_t* __restrict__ ids, const int32_t* 
     }
 }
 
-// out = LN(res + y)   (out32 may alias res)
-__global__ void add_ln_kernel(const float* res, const float* __restrict__ y, int M, int d,
+// out = LN(res + y)   (out32 may alias res); y fp16 (the GEMM outputs) or float
+template <typename TY>
+__global__ void add_ln_kernel(const float* res, const TY* __restrict__ y, int M, int d,
                               const float* __restrict__ gamma, const float* __restrict__ beta, float eps, float* out32,
                               __half* __restrict__ out16) {
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -90,18 +91,18 @@ __global__ void add_ln_kernel(const float* res, const float* __restrict__ y, int
     for (int i = 0; i < LN_MAXV; ++i)
         if (i < nv) {
             const int c = (i * 32 + lane) * 4;
-            v[i] = f4add(*reinterpret_cast<const float4*>(res + (size_t)t * d + c),
-                         *reinterpret_cast<const float4*>(y + (size_t)t * d + c));
+            v[i] = f4add(*reinterpret_cast<const float4*>(res + (size_t)t * d + c), ceb_row::ld4(y + (size_t)t * d + c));
         }
     __syncwarp();
     ceb_row::ln_row(v, nv, d, gamma, beta, eps, out32 + (size_t)t * d, out16 + (size_t)t * d, lane);
 }
 
 // ffn = sum_j w_j * down[pos_j] (fmaf in slot order) + moe_bias; out = LN(cur + ffn).
+// down: the fp16 expert rows written by the fc2 GEMM.
 // NV = d / 128 float4 registers per lane; the residual row and two slots' expert rows
 // are requested together so a warp has three rows of loads in flight.
 template <int NV>
-__global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int32_t* __restrict__ slot_pos,
+__global__ void moe_combine_ln_kernel(const __half* __restrict__ down, const int32_t* __restrict__ slot_pos,
                                       const float* __restrict__ wts, int K, const float* __restrict__ moe_bias,
                                       const float* cur, int M, const float* __restrict__ gamma,
                                       const float* __restrict__ beta, float eps, float* out32,
@@ -123,8 +124,8 @@ __global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int3
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
             const int c = (i * 32 + lane) * 4;
-            d0[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p0 * d + c));
-            d1[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p1 * d + c));
+            d0[i] = ceb_row::ldg4(down + (size_t)p0 * d + c);
+            d1[i] = ceb_row::ldg4(down + (size_t)p1 * d + c);
         }
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
@@ -139,7 +140,7 @@ __global__ void moe_combine_ln_kernel(const float* __restrict__ down, const int3
         const float w = wts[(size_t)t * K + jj];
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            const float4 dv = __ldg(reinterpret_cast<const float4*>(down + (size_t)p * d + (i * 32 + lane) * 4));
+            const float4 dv = ceb_row::ldg4(down + (size_t)p * d + (i * 32 + lane) * 4);
             acc[i].x = __fmaf_rn(w, dv.x, acc[i].x);
             acc[i].y = __fmaf_rn(w, dv.y, acc[i].y);
             acc[i].z = __fmaf_rn(w, dv.z, acc[i].z);
@@ -189,11 +190,8 @@ CEB_DEV float ex2_approx(float x) {  // MUFU 2^x (ex2(-inf) = 0)
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
-#ifndef CEB_ATTN_POLY_J
-#define CEB_ATTN_POLY_J 0xC0  // key n-tiles (bit j) whose exponentials use ex2_poly instead of MUFU
-#endif
-#ifndef CEB_ATTN_EXP_F16X2
-#define CEB_ATTN_EXP_F16X2 1  // exponentials two at a time in fp16 (ex2.approx.f16x2), row sums by the MMA
+#ifndef CEB_ATTN_TAIL_SKIP
+#define CEB_ATTN_TAIL_SKIP 1  // skip work on keys / query rows past a sequence's end
 #endif
 // 2^t for two exponents: the pair rounded to fp16 (one conversion), then one MUFU
 // op for both; the result is the packed fp16 pair the P V product consumes.
@@ -273,9 +271,12 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
     float o[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
-    float o_sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row sums of P (fp16 pairs path): c0 row g, c2 row g + 8
+    float m_r[2] = {-INFINITY, -INFINITY};
+    float o_sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row sums of P, from the MMA: c0 row g, c2 row g + 8
     const int g = lane >> 2, tq = lane & 3;
+    // a warp whose 16 query rows all lie past the sequence's end (last query tile) only
+    // takes part in the tile loads and barriers
+    const bool active = !CEB_ATTN_TAIL_SKIP || warp * 16 < nq;
 
     for (int kt = 0; kt < n_kt; ++kt) {
         const int buf = kt & 1;
@@ -287,6 +288,12 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
+        // keys of this tile inside the sequence; only the last tile has fewer than 64,
+        // and key pairs of n-tiles, 16-key P V steps and exponentials past them are skipped
+        const int kbase = kt * AT_K;
+        const int nkv_valid = min(AT_K, len - kbase);
+        const int nkv = CEB_ATTN_TAIL_SKIP ? nkv_valid : AT_K;
+        if (active) {
         if (kt == 0) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -303,6 +310,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
             for (int jp = 0; jp < 4; ++jp) {  // pairs of n-tiles
+                if (jp * 16 >= nkv) break;
                 const int key = jp * 16 + (lane & 7) + 8 * (lane >> 4);
                 const int col = ks * 16 + 8 * ((lane >> 3) & 1);
                 uint32_t b0, b1, b2, b3;
@@ -314,8 +322,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         // online softmax (rows g and g+8 of this warp).  Only the sequence's last key
         // tile holds keys past its end; the max is taken on raw scores and the
         // softmax scale folds into one FMA ahead of the exp2.
-        const int kbase = kt * AT_K;
-        if (kbase + AT_K > len) {
+        if (nkv_valid < AT_K) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
 #pragma unroll
@@ -333,19 +340,22 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
         }
-        float corr[2], rs[2] = {0.0f, 0.0f}, nm[2];
+        float corr[2], nm[2];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             nm[r] = -mx[r] * scale_log2;
             corr[r] = ex2_approx(fmaf(m_r[r], scale_log2, nm[r]));
         }
         uint32_t pf[4][4];
-#if CEB_ATTN_EXP_F16X2
         // P in fp16 pairs straight from the exponent unit; the row sums come from the
         // P V product against an all-ones column tile (o_sum), so no float adds here
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int kk = j >> 1, hi = j & 1;
+            if (kk * 16 >= nkv) {  // a 16-key step wholly past the end: never read by the P V loop
+                pf[kk][hi * 2 + 0] = pf[kk][hi * 2 + 1] = 0u;
+                continue;
+            }
             pf[kk][hi * 2 + 0] = ex2_h2(fmaf(s[j][0], scale_log2, nm[0]), fmaf(s[j][1], scale_log2, nm[0]));
             pf[kk][hi * 2 + 1] = ex2_h2(fmaf(s[j][2], scale_log2, nm[1]), fmaf(s[j][3], scale_log2, nm[1]));
         }
@@ -364,52 +374,12 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
             o_sum[2] *= corr[1];
             o_sum[3] *= corr[1];
         }
-        (void)rs;
-#else
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float p0, p1, p2, p3;
-            if ((CEB_ATTN_POLY_J >> j) & 1) {
-                p0 = ex2_poly(fmaf(s[j][0], scale_log2, nm[0]));
-                p1 = ex2_poly(fmaf(s[j][1], scale_log2, nm[0]));
-                p2 = ex2_poly(fmaf(s[j][2], scale_log2, nm[1]));
-                p3 = ex2_poly(fmaf(s[j][3], scale_log2, nm[1]));
-            } else {
-                p0 = ex2_approx(fmaf(s[j][0], scale_log2, nm[0]));
-                p1 = ex2_approx(fmaf(s[j][1], scale_log2, nm[0]));
-                p2 = ex2_approx(fmaf(s[j][2], scale_log2, nm[1]));
-                p3 = ex2_approx(fmaf(s[j][3], scale_log2, nm[1]));
-            }
-            rs[0] += p0 + p1;
-            rs[1] += p2 + p3;
-            const int kk = j >> 1, hi = j & 1;
-            pf[kk][hi * 2 + 0] = h2_as_u32(__floats2half2_rn(p0, p1));
-            pf[kk][hi * 2 + 1] = h2_as_u32(__floats2half2_rn(p2, p3));
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-            l_r[r] = l_r[r] * corr[r] + rs[r];
-            m_r[r] = mx[r];
-        }
-        if (__any_sync(0xffffffffu, corr[0] != 1.0f || corr[1] != 1.0f)) {  // the running max moved
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                o[i][0] *= corr[0];
-                o[i][1] *= corr[0];
-                o[i][2] *= corr[1];
-                o[i][3] *= corr[1];
-            }
-        }
-#endif
         // O += P V : k = 64 keys (4 steps of 16), n = 64 dims (8 tiles of 8)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
+            if (kk * 16 >= nkv) break;
             uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
-#if CEB_ATTN_EXP_F16X2
             mma16816(o_sum, a, 0x3C003C00u, 0x3C003C00u);  // P times a tile of fp16 ones: row sums
-#endif
 #pragma unroll
             for (int np = 0; np < 4; ++np) {
                 const int key = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
@@ -420,13 +390,11 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
                 mma16816(o[2 * np + 1], a, b2, b3);
             }
         }
+        }  // active
         __syncthreads();
     }
     // normalise and store fp16
-#if CEB_ATTN_EXP_F16X2
-    l_r[0] = o_sum[0];
-    l_r[1] = o_sum[2];
-#endif
+    const float l_r[2] = {o_sum[0], o_sum[2]};
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int q = q0 + warp * 16 + g + 8 * r;
@@ -573,16 +541,18 @@ int ceb_rope_neox(__half* qkv, int M, const int32_t* cu, int n_seqs, int d, int 
     return 0;
 }
 
-int ceb_add_ln(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
+int ceb_add_ln(const float* res, const __half* y, int M, int d, const float* gamma, const float* beta, float eps,
                float* out32, __half* out16, cudaStream_t st) {
     if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "add_ln: d=%d unsupported", d);
     const int threads = 256, per = threads / 32;
-    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0, add_ln_kernel<<<(M + per - 1) / per, threads, 0, st>>>(res, y, M, d, gamma, beta, eps, out32, out16));
+    CEB_LAUNCH(CEB_PROF_ROWWISE, st, 0.0, 0.0,
+               add_ln_kernel<__half><<<(M + per - 1) / per, threads, 0, st>>>(res, y, M, d, gamma, beta, eps, out32,
+                                                                             out16));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
 }
 
-int ceb_moe_combine_ln(const float* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
+int ceb_moe_combine_ln(const __half* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
                        const float* cur, int M, int d, const float* gamma, const float* beta, float eps, float* out32,
                        __half* out16, cudaStream_t st) {
     if (d % 128 || d > 128 * LN_MAXV) return ceb_set_error(2, "combine: d=%d unsupported", d);

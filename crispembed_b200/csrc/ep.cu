@@ -60,7 +60,7 @@ __global__ void ep_wait_kernel(const uint32_t* __restrict__ flags, int world, ui
 // order is segments (local expert el, source p) in increasing start; segment
 // (el, p) goes to p's ret rows from p's own offset of expert r*E_loc+el.
 __global__ void __launch_bounds__(256)
-    ep_return_kernel(const float* __restrict__ down, int d, int E, ceb_ep_args ep, int* err) {
+    ep_return_kernel(const __half* __restrict__ down, int d, int E, ceb_ep_args ep, int* err) {
     __shared__ int seg_start[EP_MAXE + 1];
     __shared__ long long seg_dst[EP_MAXE];
     __shared__ int seg_peer[EP_MAXE];
@@ -79,7 +79,6 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
     const int total = seg_start[nseg];
-    const int nv = d / 128;
     for (int r = blockIdx.x * wpb + warp; r < total; r += gridDim.x * wpb) {
         int s = 0;
         while (s + 1 < nseg && seg_start[s + 1] <= r) ++s;
@@ -88,15 +87,17 @@ __global__ void __launch_bounds__(256)
             if (lane == 0) atomicCAS(err, 0, (int)CEB_DEVERR_EP_OVERFLOW);
             continue;
         }
-        const float4* src = reinterpret_cast<const float4*>(down + (size_t)r * d);
-        float4* dst = reinterpret_cast<float4*>(ep.peers[seg_peer[s]].ret + (size_t)row * d);
-        float4 v[8];  // the whole row in flight before the peer stores (d <= 1024)
+        // fp16 rows: 16 bytes (8 values) per lane and step, d / 256 steps
+        const uint4* src = reinterpret_cast<const uint4*>(down + (size_t)r * d);
+        uint4* dst = reinterpret_cast<uint4*>(ep.peers[seg_peer[s]].ret + (size_t)row * d);
+        const int nu = d / 8;  // uint4 per row
+        uint4 v[4];            // the whole row in flight before the peer stores (d <= 1024)
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (i < nv) v[i] = __ldg(src + i * 32 + lane);
+        for (int i = 0; i < 4; ++i)
+            if (i * 32 + lane < nu) v[i] = __ldg(src + i * 32 + lane);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (i < nv) dst[i * 32 + lane] = v[i];
+        for (int i = 0; i < 4; ++i)
+            if (i * 32 + lane < nu) dst[i * 32 + lane] = v[i];
     }
     __threadfence_system();
     __syncthreads();
@@ -122,7 +123,7 @@ RegionLayout region_layout(int world, int E, int K, int d, int T_cap, int64_t re
     L.o_recv = off;
     off += align256((size_t)recv_rows * d * 2);
     L.o_ret = off;
-    off += align256((size_t)T_cap * K * d * 4);
+    off += align256((size_t)T_cap * K * d * 2);
     L.o_counts = off;
     off += align256((size_t)2 * world * E * 4);
     L.o_flags = off;
@@ -134,7 +135,7 @@ RegionLayout region_layout(int world, int E, int K, int d, int T_cap, int64_t re
 ceb_ep_peer peer_at(uint8_t* base, const RegionLayout& L) {
     ceb_ep_peer p;
     p.recv = reinterpret_cast<__half*>(base + L.o_recv);
-    p.ret = reinterpret_cast<float*>(base + L.o_ret);
+    p.ret = reinterpret_cast<__half*>(base + L.o_ret);
     p.counts = reinterpret_cast<int32_t*>(base + L.o_counts);
     p.flags = reinterpret_cast<uint32_t*>(base + L.o_flags);
     return p;
@@ -223,7 +224,7 @@ int ceb_ep_moe(ceb_ep* ep, const ceb_moe_weights& mwl, const void* x, int x_dtyp
     a2.m_rows = rows;
     a2.out = ep->down;
     a2.ldo = ep->d;
-    a2.epi = 0;
+    a2.epi = CEB_EPI_F16_OUT;
     a2.err = dev_err;
     a2.prof_cat = CEB_PROF_MOE_GEMM;
     if ((rc = ceb_gemm_launch(mwl.fc2, ep->h, rows, a2, st))) return rc;
@@ -266,7 +267,7 @@ extern "C" ceb_ep* ceb_ep_create(int rank, int world, int n_experts, int top_k, 
     ep->region_bytes = L.bytes;
     bool ok = cudaMalloc(&ep->region, L.bytes) == cudaSuccess &&
               cudaMalloc(&ep->h, (size_t)ep->recv_rows * ffn * 2) == cudaSuccess &&
-              cudaMalloc(&ep->down, (size_t)ep->recv_rows * d * 4) == cudaSuccess &&
+              cudaMalloc(&ep->down, (size_t)ep->recv_rows * d * 2) == cudaSuccess &&
               cudaMalloc(&ep->offsets_recv, (size_t)(ep->E_loc + 1) * 4) == cudaSuccess &&
               cudaMalloc(&ep->done, 4 * sizeof(int)) == cudaSuccess &&
               cudaMalloc(&ep->d_peers, (size_t)world * sizeof(ceb_ep_peer)) == cudaSuccess;

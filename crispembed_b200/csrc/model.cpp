@@ -431,7 +431,7 @@ int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int
         return o;
     };
     const size_t o_x32 = take((size_t)T * d * 4), o_c32 = take((size_t)T * d * 4), o_t32 = take((size_t)T * d * 4);
-    const size_t o_x16 = take((size_t)T * d * 2), o_c16 = take((size_t)T * d * 2);
+    const size_t o_x16 = take((size_t)T * d * 2), o_c16 = take((size_t)T * d * 2), o_t16 = take((size_t)T * d * 2);
     const size_t o_qkv = take((size_t)T * 3 * d * 2), o_a16 = take((size_t)T * d * 2);
     const size_t o_h16 = take((size_t)T * (F > 0 ? F : 128) * 2);
     const size_t moe_bytes = ceb_moe_ws_layout(T, d, E, K, Fm, nullptr, nullptr);
@@ -475,6 +475,7 @@ int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int
     ws->t32 = reinterpret_cast<float*>(b + o_t32);
     ws->x16 = reinterpret_cast<__half*>(b + o_x16);
     ws->c16 = reinterpret_cast<__half*>(b + o_c16);
+    ws->t16 = reinterpret_cast<__half*>(b + o_t16);
     ws->qkv16 = reinterpret_cast<__half*>(b + o_qkv);
     ws->a16 = reinterpret_cast<__half*>(b + o_a16);
     ws->h16 = reinterpret_cast<__half*>(b + o_h16);
@@ -608,16 +609,16 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
             (rc = ceb_rope_neox(ws.qkv16, M, d_cu, n_seqs, d, hp.n_head, m.pos_offset, m.rope_theta, st)))
             return rc;
         if ((rc = ceb_attention(ws.qkv16, M, d_cu, n_seqs, max_len, d, hp.n_head, ws.a16, d_err, st))) return rc;
-        // output projection (+bias) -> fp32, residual + LN1
-        a.out = ws.t32;
+        // output projection (+bias) -> fp16, residual + LN1
+        a.out = ws.t16;
         a.ldo = d;
-        a.epi = Ly.o_b ? CEB_EPI_BIAS : 0;
+        a.epi = CEB_EPI_F16_OUT | (Ly.o_b ? CEB_EPI_BIAS : 0);
         a.bias = Ly.o_b;
         if ((rc = ceb_gemm_launch(Ly.o, ws.a16, M, a, st))) return rc;
         if (Ly.moe) {
             const ceb_moe_weights& mw = Ly.moew;
             float* cap_logits = cap && cap->logits ? cap->logits + (size_t)moe_block * M * mw.n_experts : nullptr;
-            if ((rc = ceb_add_ln_route(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, mw, ws.moe,
+            if ((rc = ceb_add_ln_route(ws.x32, ws.t16, true, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, mw, ws.moe,
                                        cap_logits, st)))
                 return rc;
             if (cap && cap->ids) {
@@ -626,7 +627,7 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
                 if (e != cudaSuccess) return ceb_set_cuda_error(e, "route capture", __FILE__, __LINE__);
             }
             ++moe_block;
-            const float* down = ws.moe.down;
+            const __half* down = ws.moe.down;
             if (m.ep) {
                 if ((rc = ceb_ep_moe(m.ep, mw, ws.c32, CEB_ACT_F32, ws.c16, M, ws.moe, d_err, st))) return rc;
                 down = m.ep->self.ret;
@@ -638,18 +639,18 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
                                          Ly.ln2_w, Ly.ln2_b, eps, ws.x32, ws.x16, st)))
                 return rc;
         } else {
-            if ((rc = ceb_add_ln(ws.x32, ws.t32, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, st))) return rc;
+            if ((rc = ceb_add_ln(ws.x32, ws.t16, M, d, Ly.ln1_w, Ly.ln1_b, eps, ws.c32, ws.c16, st))) return rc;
             a.out = ws.h16;
             a.ldo = Ly.fc1.n_out;
             a.epi = CEB_EPI_F16_OUT | CEB_EPI_GELU | (Ly.fc1_b ? CEB_EPI_BIAS : 0);
             a.bias = Ly.fc1_b;
             if ((rc = ceb_gemm_launch(Ly.fc1, ws.c16, M, a, st))) return rc;
-            a.out = ws.t32;
+            a.out = ws.t16;
             a.ldo = d;
-            a.epi = Ly.fc2_b ? CEB_EPI_BIAS : 0;
+            a.epi = CEB_EPI_F16_OUT | (Ly.fc2_b ? CEB_EPI_BIAS : 0);
             a.bias = Ly.fc2_b;
             if ((rc = ceb_gemm_launch(Ly.fc2, ws.h16, M, a, st))) return rc;
-            if ((rc = ceb_add_ln(ws.c32, ws.t32, M, d, Ly.ln2_w, Ly.ln2_b, eps, ws.x32, ws.x16, st))) return rc;
+            if ((rc = ceb_add_ln(ws.c32, ws.t16, M, d, Ly.ln2_w, Ly.ln2_b, eps, ws.x32, ws.x16, st))) return rc;
         }
     }
     return ceb_pool_l2_launch(ws.x32, d_cu, n_seqs, d, out_dim, d_out, st, m.pool_method);

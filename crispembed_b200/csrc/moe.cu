@@ -143,20 +143,21 @@ struct ActRows {  // the activations, already in memory
     }
 };
 
-template <int NV>
+template <int NV, typename TY>
 struct AddLnRows {  // out = LN(res + y), stored, and routed from the registers
     const float* res;
-    const float* y;
+    const TY* y;
     const float* gamma;
     const float* beta;
     float eps;
     float* out32;
     __half* out16;
     CEB_DEV void prefetch(int t, int lane) const {
-        constexpr int LINES = NV * 4;  // 128-byte lines per fp32 row
-        for (int i = lane; i < 2 * LINES; i += 32) {
-            const float* base = i < LINES ? res : y;
-            prefetch_l2(base + (size_t)t * NV * 128 + (size_t)(i < LINES ? i : i - LINES) * 32);
+        constexpr int LINES = NV * 4;                   // 128-byte lines per fp32 row
+        constexpr int YLINES = LINES * sizeof(TY) / 4;  // and per y row
+        for (int i = lane; i < LINES + YLINES; i += 32) {
+            if (i < LINES) prefetch_l2(res + (size_t)t * NV * 128 + (size_t)i * 32);
+            else prefetch_l2(y + (size_t)t * NV * 128 + (size_t)(i - LINES) * (128 / sizeof(TY)));
         }
     }
     CEB_DEV void row(int t, float4 (&v)[NV], int lane) const {
@@ -164,7 +165,7 @@ struct AddLnRows {  // out = LN(res + y), stored, and routed from the registers
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
             const size_t c = (size_t)t * d + (i * 32 + lane) * 4;
-            v[i] = ceb_row::f4add(*reinterpret_cast<const float4*>(res + c), __ldg(reinterpret_cast<const float4*>(y + c)));
+            v[i] = ceb_row::f4add(*reinterpret_cast<const float4*>(res + c), ceb_row::ldg4(y + c));
         }
         ceb_row::ln_row(v, NV, d, gamma, beta, eps, out32 + (size_t)t * d, out16 ? out16 + (size_t)t * d : nullptr, lane);
     }
@@ -631,7 +632,7 @@ __global__ void __launch_bounds__(256)
 }
 
 // y[t, c] = sum_j w[t,j] * down[pos(t,j), c] (fmaf in slot order) + bias[c]
-__global__ void combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ slot_pos,
+__global__ void combine_kernel(const __half* __restrict__ down, const int32_t* __restrict__ slot_pos,
                                const float* __restrict__ wts, int T_tokens, int d, int K, const float* __restrict__ bias,
                                float* __restrict__ y) {
     const int t = blockIdx.x;
@@ -640,7 +641,7 @@ __global__ void combine_kernel(const float* __restrict__ down, const int32_t* __
         float s = 0.0f;
         for (int j = 0; j < K; ++j) {
             const int pos = slot_pos[(size_t)t * K + j];
-            s = __fmaf_rn(wts[(size_t)t * K + j], down[(size_t)pos * d + c], s);
+            s = __fmaf_rn(wts[(size_t)t * K + j], __half2float(down[(size_t)pos * d + c]), s);
         }
         y[(size_t)t * d + c] = bias ? __fadd_rn(s, bias[c]) : s;
     }
@@ -653,7 +654,7 @@ __global__ void combine_kernel(const float* __restrict__ down, const int32_t* __
 // the rows of two slots are requested whole before their FMAs (accumulated in slot
 // order), so two expert rows of every token are in flight.
 template <int NV>
-__global__ void __launch_bounds__(128) combine_rows_kernel(const float* __restrict__ down,
+__global__ void __launch_bounds__(128) combine_rows_kernel(const __half* __restrict__ down,
                                                            const int32_t* __restrict__ slot_pos,
                                                            const float* __restrict__ wts, int T_tokens, int K,
                                                            const float* __restrict__ bias, float* __restrict__ y) {
@@ -671,8 +672,8 @@ __global__ void __launch_bounds__(128) combine_rows_kernel(const float* __restri
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
             const int c = (i * 32 + lane) * 4;
-            r0[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p0 * d + c));
-            r1[i] = __ldg(reinterpret_cast<const float4*>(down + (size_t)p1 * d + c));
+            r0[i] = ceb_row::ldg4(down + (size_t)p0 * d + c);
+            r1[i] = ceb_row::ldg4(down + (size_t)p1 * d + c);
         }
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
@@ -687,7 +688,7 @@ __global__ void __launch_bounds__(128) combine_rows_kernel(const float* __restri
         const float w = wts[(size_t)t * K + j];
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            const float4 r = __ldg(reinterpret_cast<const float4*>(down + (size_t)p * d + (i * 32 + lane) * 4));
+            const float4 r = ceb_row::ldg4(down + (size_t)p * d + (i * 32 + lane) * 4);
             acc[i].x = __fmaf_rn(w, r.x, acc[i].x);
             acc[i].y = __fmaf_rn(w, r.y, acc[i].y);
             acc[i].z = __fmaf_rn(w, r.z, acc[i].z);
@@ -730,7 +731,7 @@ size_t ceb_moe_ws_layout(int T, int d, int E, int K, int F, ceb_moe_ws* ws, uint
     w.slot_pos = (int32_t*)take(S * 4);
     w.x_perm = (__half*)take(S * d * 2);
     w.h_perm = (__half*)take(S * F * 2);
-    w.down = (float*)take(S * d * 4);
+    w.down = (__half*)take(S * d * 2);
     if (ws) *ws = w;
     return off;
 }
@@ -791,8 +792,8 @@ int with_nv(int d, F&& f) {
     }
 }
 
-// combine of T tokens' K expert rows into y [T, d] (fp32)
-int launch_combine(const float* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
+// combine of T tokens' K expert rows (fp16) into y [T, d] (fp32)
+int launch_combine(const __half* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
                    const float* bias, float* y, cudaStream_t st) {
     const bool vec = CEB_COMBINE_ROWS && d % 128 == 0 && d <= 1024 &&
                      ((reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(down) |
@@ -815,15 +816,20 @@ int launch_combine(const float* down, const int32_t* slot_pos, const float* wts,
 
 }  // namespace
 
-int ceb_add_ln_route(const float* res, const float* y, int M, int d, const float* gamma, const float* beta, float eps,
-                     float* out32, __half* out16, const ceb_moe_weights& mw, const ceb_moe_ws& ws, float* logits_out,
-                     cudaStream_t st) {
+int ceb_add_ln_route(const float* res, const void* y, bool y_f16, int M, int d, const float* gamma, const float* beta,
+                     float eps, float* out32, __half* out16, const ceb_moe_weights& mw, const ceb_moe_ws& ws,
+                     float* logits_out, cudaStream_t st) {
     if (int rc = moe_shape_check(mw)) return rc;
     if (d != mw.d) return ceb_set_error(2, "add_ln_route: d=%d but the MoE block has d=%d", d, mw.d);
     if (M <= 0) return 0;
     return with_nv(d, [&](auto nvc) {
         constexpr int NV = decltype(nvc)::value;
-        const AddLnRows<NV> rows{res, y, gamma, beta, eps, out32, out16};
+        if (y_f16) {
+            const AddLnRows<NV, __half> rows{res, static_cast<const __half*>(y), gamma, beta, eps, out32, out16};
+            return launch_route_rows<NV>(rows, M, mw.n_experts, mw.top_k, mw.router_type, mw.router, ws, logits_out,
+                                         st);
+        }
+        const AddLnRows<NV, float> rows{res, static_cast<const float*>(y), gamma, beta, eps, out32, out16};
         return launch_route_rows<NV>(rows, M, mw.n_experts, mw.top_k, mw.router_type, mw.router, ws, logits_out, st);
     });
 }
@@ -886,7 +892,7 @@ int ceb_moe_dispatch(const ceb_moe_weights& mw, const void* x, int x_dtype, cons
     a2.m_rows = rows;
     a2.out = ws.down;
     a2.ldo = d;
-    a2.epi = 0;
+    a2.epi = CEB_EPI_F16_OUT;
     a2.err = dev_err;
     a2.prof_cat = CEB_PROF_MOE_GEMM;
     rc = ceb_gemm_launch(mw.fc2, ws.h_perm, rows, a2, st);
@@ -924,7 +930,7 @@ int ceb_moe_run(const ceb_moe_weights& mw, const void* x, int x_dtype, const __h
     return ceb_moe_dispatch(mw, x, x_dtype, x16, T, y, ws, expert_counts, dev_err, st);
 }
 
-int ceb_moe_combine(const float* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
+int ceb_moe_combine(const __half* down, const int32_t* slot_pos, const float* wts, int T, int d, int K,
                     const float* bias, float* y, cudaStream_t st) {
     if (T <= 0) return 0;
     if (int rc = launch_combine(down, slot_pos, wts, T, d, K, bias, y, st)) return rc;

@@ -23,6 +23,21 @@ CEB_DEV float4 f4add(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
 }
 
+// four consecutive values of a float or fp16 row as float4 (16- / 8-byte loads);
+// ldg4 reads through the read-only path
+CEB_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+CEB_DEV float4 ld4(const __half* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(u32_as_h2(u.x)), b = __half22float2(u32_as_h2(u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+CEB_DEV float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+CEB_DEV float4 ldg4(const __half* p) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 a = __half22float2(u32_as_h2(u.x)), b = __half22float2(u32_as_h2(u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // LayerNorm of one row in place (v becomes the normalised row; the first nv of
 // its N registers are used) and, where the pointers are set, its fp32 and fp16
 // stores.  ggml_norm order

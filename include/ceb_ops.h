@@ -124,7 +124,7 @@ CEB_API int ceb_moe_route_ln(const ceb_moe_layer* layer, const float* d_res, con
  *
  * Limits and rules:
  *  - n_tokens is limited by the scratch: ceb_moe_workspace_size(layer, n_tokens)
- *    must not exceed CEB_MOE_STATIC_SCRATCH_BYTES (about 3000 tokens for d=768,
+ *    must not exceed CEB_MOE_STATIC_SCRATCH_BYTES (about 3600 tokens for d=768,
  *    ffn=3072, top-2); larger batches are rejected with status 1 -- split them.
  *  - The first call on a device looks the scratch up on that device; make that
  *    first call before any stream capture.

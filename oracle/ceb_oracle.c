@@ -22,8 +22,8 @@
  *               the weight's vec_dot type (Q8_0 for Q8_0, Q8_K for Q4_K), integer
  *               block dots, float accumulation in ggml's lane order.
  *   CEO_F16   : operands rounded to fp16 (weights as fp16(dequant), activations as
- *               fp16), double accumulation -- the operand precision of the
- *               device kernels, used to check them tightly.
+ *               fp16), double accumulation, MoE expert outputs stored as fp16 --
+ *               the precision of the device kernels, used to check them tightly.
  */
 #include <math.h>
 #include <stdint.h>
@@ -656,6 +656,8 @@ void ceo_moe_ffn2(const float *x, int64_t T, int d, int E, int k, int F, int rou
         ceo_matmul(wtype, fc1 + (int64_t)e * F * rb1, F, d, xe, n, NULL, he, mode);
         ceo_gelu_erf(he, n * F);
         ceo_matmul(wtype2, fc2 + (int64_t)e * d * rb2, d, F, he, n, NULL, oe, mode);
+        if (mode == CEO_F16) /* the device stores the expert outputs as fp16 */
+            for (int64_t i = 0; i < n * d; i++) oe[i] = round_f16(oe[i]);
         for (int64_t i = 0; i < n; i++) memcpy(down + rows[i] * d, oe + i * d, (size_t)d * sizeof(float));
         free(xe);
         free(he);
