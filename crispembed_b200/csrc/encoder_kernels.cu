@@ -190,9 +190,6 @@ CEB_DEV float ex2_approx(float x) {  // MUFU 2^x (ex2(-inf) = 0)
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
-#ifndef CEB_ATTN_TAIL_SKIP
-#define CEB_ATTN_TAIL_SKIP 1  // skip work on keys / query rows past a sequence's end
-#endif
 // 2^t for two exponents: the pair rounded to fp16 (one conversion), then one MUFU
 // op for both; the result is the packed fp16 pair the P V product consumes.
 CEB_DEV uint32_t ex2_h2(float t0, float t1) {
@@ -274,9 +271,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
     float m_r[2] = {-INFINITY, -INFINITY};
     float o_sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row sums of P, from the MMA: c0 row g, c2 row g + 8
     const int g = lane >> 2, tq = lane & 3;
-    // a warp whose 16 query rows all lie past the sequence's end (last query tile) only
-    // takes part in the tile loads and barriers
-    const bool active = !CEB_ATTN_TAIL_SKIP || warp * 16 < nq;
 
     for (int kt = 0; kt < n_kt; ++kt) {
         const int buf = kt & 1;
@@ -288,12 +282,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        // keys of this tile inside the sequence; only the last tile has fewer than 64,
-        // and key pairs of n-tiles, 16-key P V steps and exponentials past them are skipped
-        const int kbase = kt * AT_K;
-        const int nkv_valid = min(AT_K, len - kbase);
-        const int nkv = CEB_ATTN_TAIL_SKIP ? nkv_valid : AT_K;
-        if (active) {
         if (kt == 0) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -310,7 +298,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
             for (int jp = 0; jp < 4; ++jp) {  // pairs of n-tiles
-                if (jp * 16 >= nkv) break;
                 const int key = jp * 16 + (lane & 7) + 8 * (lane >> 4);
                 const int col = ks * 16 + 8 * ((lane >> 3) & 1);
                 uint32_t b0, b1, b2, b3;
@@ -322,7 +309,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         // online softmax (rows g and g+8 of this warp).  Only the sequence's last key
         // tile holds keys past its end; the max is taken on raw scores and the
         // softmax scale folds into one FMA ahead of the exp2.
-        if (nkv_valid < AT_K) {
+        const int kbase = kt * AT_K;
+        if (kbase + AT_K > len) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
 #pragma unroll
@@ -352,10 +340,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int kk = j >> 1, hi = j & 1;
-            if (kk * 16 >= nkv) {  // a 16-key step wholly past the end: never read by the P V loop
-                pf[kk][hi * 2 + 0] = pf[kk][hi * 2 + 1] = 0u;
-                continue;
-            }
             pf[kk][hi * 2 + 0] = ex2_h2(fmaf(s[j][0], scale_log2, nm[0]), fmaf(s[j][1], scale_log2, nm[0]));
             pf[kk][hi * 2 + 1] = ex2_h2(fmaf(s[j][2], scale_log2, nm[1]), fmaf(s[j][3], scale_log2, nm[1]));
         }
@@ -377,7 +361,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
         // O += P V : k = 64 keys (4 steps of 16), n = 64 dims (8 tiles of 8)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            if (kk * 16 >= nkv) break;
             uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
             mma16816(o_sum, a, 0x3C003C00u, 0x3C003C00u);  // P times a tile of fp16 ones: row sums
 #pragma unroll
@@ -390,7 +373,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
                 mma16816(o[2 * np + 1], a, b2, b3);
             }
         }
-        }  // active
         __syncthreads();
     }
     // normalise and store fp16
