@@ -29,6 +29,9 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#if defined(__AVX2__) || defined(__F16C__)
+#include <immintrin.h>
+#endif
 
 #ifdef _OPENMP
 #include <omp.h>
@@ -63,6 +66,9 @@ enum {
 /* IEEE binary16 <-> binary32, round-to-nearest-even (what F16C's
  * _cvtss_sh(x, 0) and numpy's astype(float16) do). */
 float ceo_f16_to_f32(uint16_t h) {
+#if defined(__F16C__)
+    return _cvtsh_ss(h); /* the hardware conversion: exact, the same value as below */
+#endif
     uint32_t sign = (uint32_t)(h & 0x8000) << 16;
     uint32_t exp = (h >> 10) & 0x1F;
     uint32_t man = h & 0x3FF;
@@ -328,7 +334,42 @@ void ceo_quant_act_q8_k(const float *x, int64_t k, uint8_t *out) {
  * the same structure): eight float lanes, lane l holds the int sum of products
  * 4l..4l+3 of each block, scaled by d_w*d_a with an FMA per block; horizontal
  * sum ((a0+a4)+(a2+a6))+((a1+a5)+(a3+a7)). */
+#if defined(__AVX2__) && defined(__FMA__)
+/* The same lanes with AVX2 integer arithmetic, as ggml's x86 kernel forms them:
+ * |w| times sign(w)*a byte pairs summed to int16 (no saturation: |q| <= 127), pairs of
+ * those summed to the eight int32 lane sums, converted exactly to float and FMA'd
+ * with the block's d.  Bit-identical to the scalar form below (same integer lanes,
+ * same float operations in the same order); used where the host has AVX2. */
+static float dot_q8_0_avx2(int64_t k, const uint8_t *w, const uint8_t *a) {
+    __m256 acc = _mm256_setzero_ps();
+    const __m256i ones = _mm256_set1_epi16(1);
+    for (int64_t b = 0; b < k / QK8_0; b++) {
+        const uint8_t *wb = w + b * Q8_0_BYTES, *ab = a + b * Q8_0_BYTES;
+        const __m256 d = _mm256_set1_ps(ceo_f16_to_f32(rd_u16(wb)) * ceo_f16_to_f32(rd_u16(ab)));
+        const __m256i qw = _mm256_loadu_si256((const __m256i *)(wb + 2));
+        const __m256i qa = _mm256_loadu_si256((const __m256i *)(ab + 2));
+        const __m256i pairs = _mm256_maddubs_epi16(_mm256_sign_epi8(qw, qw), _mm256_sign_epi8(qa, qw));
+        const __m256i lanes = _mm256_madd_epi16(pairs, ones);
+        acc = _mm256_fmadd_ps(d, _mm256_cvtepi32_ps(lanes), acc);
+    }
+    float l[8];
+    _mm256_storeu_ps(l, acc);
+    return ((l[0] + l[4]) + (l[2] + l[6])) + ((l[1] + l[5]) + (l[3] + l[7]));
+}
+#endif
+
+float ceo_dot_q8_0_scalar(int64_t k, const uint8_t *w, const uint8_t *a);
+
 float ceo_dot_q8_0(int64_t k, const uint8_t *w, const uint8_t *a) {
+#if defined(__AVX2__) && defined(__FMA__)
+    return dot_q8_0_avx2(k, w, a);
+#else
+    return ceo_dot_q8_0_scalar(k, w, a);
+#endif
+}
+
+/* the lanes one product at a time (also the reference form the AVX2 one is tested against) */
+float ceo_dot_q8_0_scalar(int64_t k, const uint8_t *w, const uint8_t *a) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int64_t b = 0; b < k / QK8_0; b++) {
         const uint8_t *wb = w + b * Q8_0_BYTES, *ab = a + b * Q8_0_BYTES;
@@ -346,7 +387,42 @@ float ceo_dot_q8_0(int64_t k, const uint8_t *w, const uint8_t *a) {
 /* ggml generic ggml_vec_dot_q4_K_q8_K: per super-block, integer sub-block dots
  * scaled by the 6-bit scales into eight int lanes, d*lane accumulated into eight
  * float sums; the min term dmin*d_a*sum(m_j*bsum) subtracted once per block. */
-float ceo_dot_q4_k(int64_t k, const uint8_t *w, const uint8_t *a) {
+#if defined(__AVX2__)
+/* The eight int32 lanes of one Q4_K super-block with AVX2: per 32-value sub-block j,
+ * int16 products of the 4-bit quants and the Q8_K values, folded so that element i
+ * lands in lane i % 8 (the two 16-element halves, then the two 8-element halves),
+ * widened and scaled by the sub-block's 6-bit scale.  Integer sums only: the lanes
+ * equal the scalar loop's exactly (|products| <= 15 * 127, four per lane and
+ * sub-block, no int16 overflow). */
+static void q4k_lanes_avx2(const uint8_t *qs, const int8_t *q8, const int *scs, int32_t aux[8]) {
+    __m256i acc = _mm256_setzero_si256();
+    const __m128i m4 = _mm_set1_epi8(0x0F);
+    for (int j = 0; j < 8; j++) {
+        const uint8_t *src = qs + 32 * (j >> 1);
+        __m128i b0 = _mm_loadu_si128((const __m128i *)src), b1 = _mm_loadu_si128((const __m128i *)(src + 16));
+        if (j & 1) {
+            b0 = _mm_srli_epi16(b0, 4);
+            b1 = _mm_srli_epi16(b1, 4);
+        }
+        b0 = _mm_and_si128(b0, m4);
+        b1 = _mm_and_si128(b1, m4);
+        const __m256i a0 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(q8 + 32 * j)));
+        const __m256i a1 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(q8 + 32 * j + 16)));
+        const __m256i t = _mm256_add_epi16(_mm256_mullo_epi16(_mm256_cvtepu8_epi16(b0), a0),
+                                           _mm256_mullo_epi16(_mm256_cvtepu8_epi16(b1), a1));
+        const __m128i u = _mm_add_epi16(_mm256_castsi256_si128(t), _mm256_extracti128_si256(t, 1));
+        acc = _mm256_add_epi32(acc, _mm256_mullo_epi32(_mm256_cvtepi16_epi32(u), _mm256_set1_epi32(scs[j])));
+    }
+    _mm256_storeu_si256((__m256i *)aux, acc);
+}
+#endif
+
+static float dot_q4_k(int64_t k, const uint8_t *w, const uint8_t *a, int use_simd);
+
+float ceo_dot_q4_k(int64_t k, const uint8_t *w, const uint8_t *a) { return dot_q4_k(k, w, a, 1); }
+float ceo_dot_q4_k_scalar(int64_t k, const uint8_t *w, const uint8_t *a) { return dot_q4_k(k, w, a, 0); }
+
+static float dot_q4_k(int64_t k, const uint8_t *w, const uint8_t *a, int use_simd) {
     float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float sumf = 0.0f;
     for (int64_t b = 0; b < k / QK_K; b++) {
@@ -357,23 +433,31 @@ float ceo_dot_q4_k(int64_t k, const uint8_t *w, const uint8_t *a) {
         int16_t bs[16];
         memcpy(bs, ab + 4 + QK_K, sizeof bs);
         const uint8_t *sc = wb + 4, *qs = wb + 16;
-        int8_t q4[QK_K];
-        for (int c = 0; c < 4; c++)
-            for (int l = 0; l < 32; l++) {
-                q4[64 * c + l] = (int8_t)(qs[32 * c + l] & 0xF);
-                q4[64 * c + 32 + l] = (int8_t)(qs[32 * c + l] >> 4);
-            }
         int scs[8], mns[8];
         for (int j = 0; j < 8; j++) q4k_scale_min(j, sc, &scs[j], &mns[j]);
         int sumi = 0;
         for (int j = 0; j < 16; j++) sumi += bs[j] * mns[j / 2];
         int32_t aux32[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int j = 0; j < 8; j++) {
-            for (int g = 0; g < 4; g++)
-                for (int l = 0; l < 8; l++) {
-                    int idx = 32 * j + 8 * g + l;
-                    aux32[l] += scs[j] * (int)(q8[idx] * q4[idx]);
+#if defined(__AVX2__)
+        if (use_simd) {
+            q4k_lanes_avx2(qs, q8, scs, aux32);
+        } else
+#endif
+        {
+            (void)use_simd;
+            int8_t q4[QK_K];
+            for (int c = 0; c < 4; c++)
+                for (int l = 0; l < 32; l++) {
+                    q4[64 * c + l] = (int8_t)(qs[32 * c + l] & 0xF);
+                    q4[64 * c + 32 + l] = (int8_t)(qs[32 * c + l] >> 4);
                 }
+            for (int j = 0; j < 8; j++) {
+                for (int g = 0; g < 4; g++)
+                    for (int l = 0; l < 8; l++) {
+                        int idx = 32 * j + 8 * g + l;
+                        aux32[l] += scs[j] * (int)(q8[idx] * q4[idx]);
+                    }
+            }
         }
         float d = ceo_f16_to_f32(rd_u16(wb)) * ad;
         for (int l = 0; l < 8; l++) sums[l] += d * (float)aux32[l];
@@ -397,13 +481,19 @@ void ceo_matmul(int type, const uint8_t *w, int64_t n_out, int64_t k, const floa
             if (type == T_Q8_0) ceo_quant_act_q8_0(x + m * k, k, xq + m * qb);
             else ceo_quant_act_q8_k(x + m * k, k, xq + m * qb);
         }
+        /* 32 x 32 tiles of (activation row, weight row): a tile's rows stay in the core's
+         * cache while every dot of the tile is formed (each dot is computed on its own, so
+         * the tiling changes no result) */
+        const int64_t TM = 32, TN = 32, mt = (m_rows + TM - 1) / TM, nt = (n_out + TN - 1) / TN;
 #pragma omp parallel for schedule(static) collapse(2)
-        for (int64_t m = 0; m < m_rows; m++)
-            for (int64_t n = 0; n < n_out; n++) {
-                float s = type == T_Q8_0 ? ceo_dot_q8_0(k, w + n * rb, xq + m * qb)
-                                         : ceo_dot_q4_k(k, w + n * rb, xq + m * qb);
-                out[m * n_out + n] = bias ? s + bias[n] : s;
-            }
+        for (int64_t bm = 0; bm < mt; bm++)
+            for (int64_t bn = 0; bn < nt; bn++)
+                for (int64_t m = bm * TM; m < m_rows && m < (bm + 1) * TM; m++)
+                    for (int64_t n = bn * TN; n < n_out && n < (bn + 1) * TN; n++) {
+                        float s = type == T_Q8_0 ? ceo_dot_q8_0(k, w + n * rb, xq + m * qb)
+                                                 : ceo_dot_q4_k(k, w + n * rb, xq + m * qb);
+                        out[m * n_out + n] = bias ? s + bias[n] : s;
+                    }
         free(xq);
         return;
     }
@@ -480,6 +570,7 @@ float ceo_erff(float x) { return ceb_erff(x); }
 /* exact erf GELU, as ggml_vec_gelu_erf_f32 computes it: 0.5x(1+erf(x/sqrt2)) */
 void ceo_gelu_erf(float *x, int64_t n) {
     const float s2 = 0.70710678118654752440f;
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) x[i] = 0.5f * x[i] * (1.0f + ceo_erff_(x[i] * s2));
 }
 
@@ -516,6 +607,24 @@ void ceo_layernorm(const float *x, int64_t rows, int64_t d, const float *gamma, 
  * flash_attn_ext runs it for f32 K/V: one pass over keys with an online
  * softmax (running max M, running sum S, V accumulator rescaled by expf(Mold-M)).
  * q/k/v rows have stride ld (elements); head h uses columns h*hd..h*hd+hd-1. */
+/* q . k of one head.  The parity build sums in index order (one fmaf chain); the
+ * timing build (CEO_LIBM_MATH) uses eight-lane AVX2 partial sums, as ggml's SIMD
+ * vector dot does, so the CPU baseline pays ggml's cost, not a serial chain's. */
+static inline float attn_dot(const float *a, const float *b, int n) {
+#if defined(CEO_LIBM_MATH) && defined(__AVX2__) && defined(__FMA__)
+    if (n % 8 == 0) {
+        __m256 acc = _mm256_setzero_ps();
+        for (int c = 0; c < n; c += 8) acc = _mm256_fmadd_ps(_mm256_loadu_ps(a + c), _mm256_loadu_ps(b + c), acc);
+        float l[8];
+        _mm256_storeu_ps(l, acc);
+        return ((l[0] + l[4]) + (l[2] + l[6])) + ((l[1] + l[5]) + (l[3] + l[7]));
+    }
+#endif
+    float s = 0.0f;
+    for (int c = 0; c < n; c++) s = fmaf(a[c], b[c], s);
+    return s;
+}
+
 void ceo_attention(const float *q, const float *k, const float *v, int64_t ld, const int32_t *cu_seqlens,
                    int n_seqs, int n_head, int hd, float scale, float *out, int64_t ldo) {
     for (int s = 0; s < n_seqs; s++) {
@@ -530,8 +639,7 @@ void ceo_attention(const float *q, const float *k, const float *v, int64_t ld, c
                 for (int j = 0; j < len; j++) {
                     const float *kj = k + (int64_t)(t0 + j) * ld + h * hd;
                     const float *vj = v + (int64_t)(t0 + j) * ld + h * hd;
-                    float sdot = 0.0f;
-                    for (int c = 0; c < hd; c++) sdot = fmaf(qi[c], kj[c], sdot);
+                    const float sdot = attn_dot(qi, kj, hd);
                     float sc = sdot * scale;
                     float ms = 1.0f, vs = 1.0f;
                     if (sc > M) {

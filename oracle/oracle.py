@@ -75,8 +75,12 @@ def lib():
         L.ceo_quant_act_q8_k.argtypes = [_fp, ctypes.c_int64, _up]
         L.ceo_dot_q8_0.argtypes = [ctypes.c_int64, _up, _up]
         L.ceo_dot_q8_0.restype = ctypes.c_float
+        L.ceo_dot_q8_0_scalar.argtypes = [ctypes.c_int64, _up, _up]
+        L.ceo_dot_q8_0_scalar.restype = ctypes.c_float
         L.ceo_dot_q4_k.argtypes = [ctypes.c_int64, _up, _up]
         L.ceo_dot_q4_k.restype = ctypes.c_float
+        L.ceo_dot_q4_k_scalar.argtypes = [ctypes.c_int64, _up, _up]
+        L.ceo_dot_q4_k_scalar.restype = ctypes.c_float
         L.ceo_matmul.argtypes = [ctypes.c_int, _up, ctypes.c_int64, ctypes.c_int64, _fp, ctypes.c_int64, _fp, _fp,
                                  ctypes.c_int]
         L.ceo_gelu_erf.argtypes = [_fp, ctypes.c_int64]

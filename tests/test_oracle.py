@@ -92,3 +92,48 @@ def test_pool_l2_epsilon(oracle):
     h = np.zeros((3, 8), np.float32)
     out = oracle.pool_l2(h, np.array([0, 3], np.int32))
     assert np.all(out == 0)
+
+
+def test_q8_0_dot_avx2_equals_scalar(oracle):
+    """The oracle's AVX2 Q8_0 dot (the host fast path) gives the scalar lane form's bits,
+    including blocks at the int8 limits, zero blocks and sign mixes."""
+    import ctypes
+    rng = np.random.default_rng(5)
+    L = oracle.lib()
+    up = ctypes.POINTER(ctypes.c_uint8)
+    for trial in range(200):
+        k = 32 * int(rng.integers(1, 97))
+        w = np.zeros((k // 32, 34), np.uint8)
+        a = np.zeros((k // 32, 34), np.uint8)
+        for blk in (w, a):
+            blk[:, :2] = (rng.uniform(1e-4, 2.0, k // 32).astype(np.float16)).view(np.uint8).reshape(-1, 2)
+            q = rng.integers(-127, 128, (k // 32, 32)).astype(np.int8)
+            if trial % 4 == 0:
+                q[0] = 127 * np.sign(rng.standard_normal(32)).astype(np.int8)  # the limits
+            if trial % 5 == 0:
+                q[-1] = 0
+            blk[:, 2:] = q.view(np.uint8)
+        wp, ap = np.ascontiguousarray(w.reshape(-1)), np.ascontiguousarray(a.reshape(-1))
+        fast = L.ceo_dot_q8_0(k, wp.ctypes.data_as(up), ap.ctypes.data_as(up))
+        slow = L.ceo_dot_q8_0_scalar(k, wp.ctypes.data_as(up), ap.ctypes.data_as(up))
+        assert np.float32(fast).tobytes() == np.float32(slow).tobytes(), trial
+
+
+def test_q4_k_dot_avx2_equals_scalar(oracle):
+    """The oracle's AVX2 Q4_K x Q8_K dot gives the scalar lane form's bits (random
+    super-blocks with every 4-bit value, the 6-bit scale extremes and full-range Q8_K)."""
+    import ctypes
+    rng = np.random.default_rng(6)
+    L = oracle.lib()
+    up = ctypes.POINTER(ctypes.c_uint8)
+    for trial in range(100):
+        k = 256 * int(rng.integers(1, 13))
+        w = rng.integers(0, 256, (k // 256, 144)).astype(np.uint8)
+        w[:, :4] = rng.uniform(1e-4, 1.0, (k // 256, 2)).astype(np.float16).view(np.uint8).reshape(-1, 4)
+        x = rng.standard_normal(k).astype(np.float32) * np.float32(rng.uniform(0.1, 10))
+        a = np.zeros(k // 256 * 292, np.uint8)
+        L.ceo_quant_act_q8_k(x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), k, a.ctypes.data_as(up))
+        wp = np.ascontiguousarray(w.reshape(-1))
+        fast = L.ceo_dot_q4_k(k, wp.ctypes.data_as(up), a.ctypes.data_as(up))
+        slow = L.ceo_dot_q4_k_scalar(k, wp.ctypes.data_as(up), a.ctypes.data_as(up))
+        assert np.float32(fast).tobytes() == np.float32(slow).tobytes(), trial
