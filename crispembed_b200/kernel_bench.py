@@ -7,6 +7,7 @@
     python -m crispembed_b200.kernel_bench pool --seqs 256
     python -m crispembed_b200.kernel_bench encode --seqs 256
     python -m crispembed_b200.kernel_bench cublas --m 70825 --n 3072 --k 768
+    torchrun --nproc-per-node N -m crispembed_b200.kernel_bench a2a --tokens 131072
 
 Used for the roofline numbers of single kernels and as the command that ncu
 captures (small cases: a few launches, a few GB at most).  Prints one JSON line.
@@ -263,6 +264,49 @@ def bench_cublas(a):
             "frac_of_peak": tf / pk["bf16_tflops"], "peak_source": src}
 
 
+def bench_a2a(a):
+    """NCCL all-to-all of one MoE block's exchange at the config-4 shape: every rank
+    holds `tokens` tokens x top_k fp16 rows of d values and sends an equal share to
+    every rank (itself included), dispatch then return, with all_to_all_single -- the
+    library collective the expert-parallel peer stores replace.  Rank 0 prints the
+    time per exchange (max over ranks) and the bytes each rank sends to other ranks
+    per second."""
+    import datetime
+    import os
+
+    import torch
+    import torch.distributed as dist
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
+    rows = a.tokens * a.topk // world * world
+    x = torch.randn((rows, a.d), device="cuda", dtype=torch.float16)
+    y = torch.empty_like(x)
+    z = torch.empty_like(x)
+    for _ in range(a.warmup):
+        dist.all_to_all_single(y, x)
+        dist.all_to_all_single(z, y)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        dist.all_to_all_single(y, x)  # dispatch
+        dist.all_to_all_single(z, y)  # return
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    off_rank = 2 * rows * a.d * 2 * (world - 1) / world  # bytes each rank sends to other ranks per exchange
+    r = {"kernel": "nccl_all_to_all", "world": world, "rows_per_rank": rows, "d": a.d,
+         "ms_per_exchange": float(ms.item()), "off_rank_bytes": off_rank,
+         "off_rank_gbs_per_rank": off_rank / (float(ms.item()) / 1e3) / 1e9}
+    dist.barrier()
+    dist.destroy_process_group()
+    return r if rank == 0 else None
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -321,7 +365,18 @@ def main(argv=None):
     c.add_argument("--k", type=int, default=768)
     c.add_argument("--iters", type=int, default=20)
     c.add_argument("--warmup", type=int, default=3)
+    n = sub.add_parser("a2a")
+    n.add_argument("--tokens", type=int, default=131072)
+    n.add_argument("--topk", type=int, default=2)
+    n.add_argument("--d", type=int, default=768)
+    n.add_argument("--iters", type=int, default=20)
+    n.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
+    if a.what == "a2a":
+        r = bench_a2a(a)
+        if r:
+            print(json.dumps(r), flush=True)
+        return 0
     r = {"gemm": bench_gemm, "moe": bench_moe, "route_ln": bench_route_ln, "attn": bench_attn, "pool": bench_pool,
          "encode": bench_encode, "cublas": bench_cublas}[a.what](a)
     print(json.dumps(r), flush=True)
