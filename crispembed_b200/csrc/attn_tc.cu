@@ -352,11 +352,7 @@ int ceb_attention_tc(const __half* qkv, int total_rows, const int32_t* cu, int n
                      __half* out, int* d_err, cudaStream_t st) {
     if (n_head <= 0 || (n_head % HPC) || d != n_head * HD || max_len > LMAX || max_len <= 0) return 1;
     if ((reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return 1;
-    static bool attr_set = false;
-    if (!attr_set) {
-        CEB_CUDA_OK(cudaFuncSetAttribute(attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LAUNCH));
-        attr_set = true;
-    }
+    if (int rc = ceb_func_smem(reinterpret_cast<const void*>(attn_pair_kernel), SMEM_LAUNCH)) return rc;
     CUtensorMap q_map, k_map, v_map;
     const uint64_t ld_bytes = (uint64_t)3 * d * 2;
     int rc = ceb_make_tmap_2d_sw(&q_map, qkv, 2, (uint64_t)3 * d, (uint64_t)total_rows, ld_bytes, HD, QT, 128);

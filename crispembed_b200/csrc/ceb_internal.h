@@ -108,7 +108,13 @@ void ceb_wplane_free(ceb_wplane* w);
 // dequantizer run once over every block); fp16 planes are left as they are.
 int ceb_wplane_expand_f16(ceb_wplane* w, cudaStream_t st);
 
-int ceb_num_sms();
+// Launch setup is per device: a process may drive several GPUs.
+constexpr int CEB_MAX_DEVICES = 64;
+int ceb_device_index();  // the current device (0 when it cannot be read)
+int ceb_num_sms();       // SMs of the current device
+// Raises the dynamic shared-memory limit of kernel `func` to `smem` bytes on the
+// current device, once per (device, kernel).
+int ceb_func_smem(const void* func, size_t smem);
 // device error word shared by the operator-level entry points (api.cpp)
 int* ceb_op_error_word();
 

@@ -516,12 +516,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 template <int FMT>
 int launch_fmt(const CUtensorMap& map, const CUtensorMap& omap, const ceb_wplane& w, const ceb_gemm_args& a, int grid,
                cudaStream_t st) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        CEB_CUDA_OK(cudaFuncSetAttribute(ceb_gemm_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)SMEM_BYTES));
-        attr_set = true;
-    }
+    if (int rc = ceb_func_smem(reinterpret_cast<const void*>(ceb_gemm_kernel<FMT>), SMEM_BYTES)) return rc;
     ceb_gemm_kernel<FMT><<<grid, NTHREADS, SMEM_BYTES, st>>>(map, omap, w, a);
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
@@ -1014,10 +1009,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 template <int FMT>
 int launch_pair(const CUtensorMap& xmap, const CUtensorMap& omap, const CUtensorMap& wmap, const ceb_wplane& w,
                 const ceb_gemm_args& a, int max_pairs, cudaStream_t st) {
-    static int pairs_resident = -1;
-    if (pairs_resident < 0) {
-        CEB_CUDA_OK(cudaFuncSetAttribute(ceb_gemm_pair_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)pair::LayOf<FMT>::SMEM));
+    static int resident_of[CEB_MAX_DEVICES] = {};  // co-resident pairs, per device
+    int& pairs_resident = resident_of[ceb_device_index()];
+    if (!pairs_resident) {
+        if (int rc = ceb_func_smem(reinterpret_cast<const void*>(ceb_gemm_pair_kernel<FMT>), pair::LayOf<FMT>::SMEM))
+            return rc;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * ceb_num_sms(), 1, 1);
         cfg.blockDim = dim3(NTHREADS, 1, 1);

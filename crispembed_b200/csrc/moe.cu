@@ -751,15 +751,17 @@ int launch_route_rows_t(const Rows& rows, int T, int E, int K, const uint8_t* rw
                         float* logits_out, cudaStream_t st) {
     auto kern = route_rows_kernel<NV, Q8, Rows>;
     const size_t smem = route_smem_bytes(NV * 128, E);
-    static int occ = 0;
-    static size_t occ_smem = 0;
-    if (!occ || occ_smem != smem) {
-        CEB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    static int occ_of[CEB_MAX_DEVICES] = {};  // resident CTAs per SM, per device
+    static size_t smem_of[CEB_MAX_DEVICES] = {};
+    const int dev = ceb_device_index();
+    if (!occ_of[dev] || smem_of[dev] != smem) {
+        if (int rc = ceb_func_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
         int n = 0;
         CEB_CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, RT_WARPS * 32, smem));
-        occ = std::max(n, 1);
-        occ_smem = smem;
+        occ_of[dev] = std::max(n, 1);
+        smem_of[dev] = smem;
     }
+    const int occ = occ_of[dev];
     const int nblk = (T + CHUNK - 1) / CHUNK;
     const int grid = std::min(nblk, occ * ceb_num_sms());
     CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,

@@ -37,15 +37,44 @@ int ceb_set_cuda_error(cudaError_t e, const char* what, const char* file, int li
 
 const char* ceb_last_error_message() { return g_last_error.c_str(); }
 
+int ceb_device_index() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= CEB_MAX_DEVICES) dev = 0;
+    return dev;
+}
+
 int ceb_num_sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
+    static int n_of[CEB_MAX_DEVICES] = {};
+    const int dev = ceb_device_index();
+    if (!n_of[dev]) {
+        int n = 0;
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
+        n_of[dev] = n > 0 ? n : 148;
     }
-    return n;
+    return n_of[dev];
+}
+
+namespace {
+// (device, kernel, dynamic shared memory) triples whose limit has been raised:
+// cudaFuncSetAttribute acts on the current device only.
+struct FuncSmem {
+    int dev;
+    const void* func;
+    size_t smem;
+};
+std::mutex g_func_mu;
+std::vector<FuncSmem> g_func_smem;
+}  // namespace
+
+int ceb_func_smem(const void* func, size_t smem) {
+    const int dev = ceb_device_index();
+    std::lock_guard<std::mutex> lk(g_func_mu);
+    for (const FuncSmem& f : g_func_smem)
+        if (f.dev == dev && f.func == func && f.smem >= smem) return 0;
+    cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return ceb_set_cuda_error(e, "cudaFuncSetAttribute", __FILE__, __LINE__);
+    g_func_smem.push_back({dev, func, smem});
+    return 0;
 }
 
 // ------------------------------------------------------------------ TMA maps

@@ -112,6 +112,24 @@ def test_moe_repeat_bit_identical(cuda):
         assert np.array_equal(a, b)
 
 
+def test_moe_on_two_devices_of_one_process():
+    """Launch setup (shared-memory limits, occupancy) is per device: the operator built
+    and run on GPU 1 after GPU 0 in the same process gives the same bits on both."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = []
+    for T, ffn in ((700, 3072), (40, 384)):  # fc1 of 384 features runs the single-CTA GEMM
+        inp = synth.make_moe_op_inputs(T, d=768, n_experts=8, top_k=2, ffn=ffn, wtype=GGML_Q8_0,
+                                       router_wtype=GGML_Q8_0, zipf_s=1.2, seed=6, with_bias=True)
+        per_dev = []
+        for dev in (0, 1):
+            with torch.cuda.device(dev):
+                per_dev.append(_run(f"cuda:{dev}", inp)[0])
+        for a, b in zip(*per_dev):
+            assert np.array_equal(a, b)
+
+
 @pytest.mark.parametrize("dtype", ["f32", "f16"])
 def test_moe_input_dtypes(cuda, oracle, dtype):
     inp = synth.make_moe_op_inputs(96, d=256, n_experts=4, top_k=2, ffn=512, wtype=GGML_Q8_0,
