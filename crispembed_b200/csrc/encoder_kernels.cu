@@ -391,6 +391,216 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
     }
 }
 
+// Rows of one tile (ROWS x 64 fp16, rows beyond n_valid zero-filled) by NT threads.
+template <int NT, int ROWS>
+CEB_DEV void load_rows(__half* s, const __half* g, size_t g_ld, int n_valid, int tid) {
+    static_assert((ROWS * 8) % NT == 0, "16-byte chunks per thread");
+#pragma unroll
+    for (int i = 0; i < ROWS * 8 / NT; ++i) {
+        const int chunk = tid + i * NT;
+        const int row = chunk >> 3, col = (chunk & 7) * 8;
+        const bool ok = row < n_valid;
+        const __half* src = g + (size_t)(ok ? row : 0) * g_ld + col;
+        cp_async16(smem_u32(s + row * AT_LD + col), src, ok ? 16 : 0);
+    }
+}
+
+// One CTA = 32*NW queries of one (sequence, head); each warp owns 32 query rows as
+// two m16 tiles, so every K / V fragment read from shared memory feeds two MMAs.
+// Keys in 64-key tiles (cp.async, double-buffered), processed in 32-key steps; a
+// step wholly past the sequence's end is skipped.  Q is staged in the second
+// buffer's space and moved to registers before the first prefetch lands there.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, 12 / NW) attention_rows32_kernel(const __half* __restrict__ qkv,
+                                                                   const int32_t* __restrict__ cu, int d,
+                                                                   float scale_log2, __half* __restrict__ out,
+                                                                   int total_rows, int max_len, int* __restrict__ err) {
+    constexpr int NT = NW * 32, QT = NW * 32, TILE = AT_K * AT_LD;
+    static_assert(QT <= 2 * AT_K, "Q staging uses the second K and V buffers");
+    __shared__ __align__(128) __half sm[4 * TILE];  // K0, V0, K1, V1
+    const int seq = blockIdx.z, head = blockIdx.y;
+    const int start = cu[seq], len = cu[seq + 1] - start;
+    if (start < 0 || len < 0 || len > total_rows - start || len > max_len) {
+        if (blockIdx.x == 0 && head == 0 && threadIdx.x == 0 && err) atomicCAS(err, 0, (int)CEB_DEVERR_BAD_INDEX);
+        return;
+    }
+    const int q0 = blockIdx.x * QT;
+    if (q0 >= len) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t ld = (size_t)3 * d;
+    const __half* Qg = qkv + (size_t)(start + q0) * ld + head * AT_HD;
+    const __half* Kg = qkv + (size_t)start * ld + d + head * AT_HD;
+    const __half* Vg = qkv + (size_t)start * ld + 2 * d + head * AT_HD;
+    const int nq = min(QT, len - q0);
+    const int n_kt = (len + AT_K - 1) / AT_K;
+    const bool active = warp * 32 < nq;  // warp-uniform: this warp holds a valid query row
+    __half* const sQ = sm + 2 * TILE;
+
+    load_rows<NT, QT>(sQ, Qg, ld, nq, tid);
+    load_rows<NT, AT_K>(sm, Kg, ld, min(AT_K, len), tid);
+    load_rows<NT, AT_K>(sm + TILE, Vg, ld, min(AT_K, len), tid);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    uint32_t qf[2][4][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            const int row = warp * 32 + m * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+            const int col = ks * 16 + 8 * (lane >> 4);
+            ldsm_x4(smem_u32(sQ + row * AT_LD + col), qf[m][ks][0], qf[m][ks][1], qf[m][ks][2], qf[m][ks][3]);
+        }
+    __syncthreads();  // the second buffer is free for the first prefetch
+
+    float o[2][8][4];
+    float o_sum[2][4];
+    float m_r[2][2];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[m][i][0] = o[m][i][1] = o[m][i][2] = o[m][i][3] = 0.0f;
+        o_sum[m][0] = o_sum[m][1] = o_sum[m][2] = o_sum[m][3] = 0.0f;
+        m_r[m][0] = m_r[m][1] = -INFINITY;
+    }
+    const int tq = lane & 3;
+
+    for (int kt = 0; kt < n_kt; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < n_kt) {
+            const int k0n = (kt + 1) * AT_K;
+            load_rows<NT, AT_K>(sm + (2 * (buf ^ 1)) * TILE, Kg + (size_t)k0n * ld, ld, min(AT_K, len - k0n), tid);
+            load_rows<NT, AT_K>(sm + (2 * (buf ^ 1) + 1) * TILE, Vg + (size_t)k0n * ld, ld, min(AT_K, len - k0n), tid);
+        }
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        const __half* sK = sm + (2 * buf) * TILE;
+        const __half* sV = sm + (2 * buf + 1) * TILE;
+        if (active) {
+            for (int h = 0; h < 2; ++h) {
+                const int kbase = kt * AT_K + 32 * h;
+                if (kbase >= len) break;
+                // S = Q K^T for 32 keys: 4 n-tiles of 8 keys, both m-tiles per K fragment
+                float s[2][4][4];
+#pragma unroll
+                for (int m = 0; m < 2; ++m)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) s[m][j][0] = s[m][j][1] = s[m][j][2] = s[m][j][3] = 0.0f;
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+                    for (int jp = 0; jp < 2; ++jp) {
+                        const int key = 32 * h + jp * 16 + (lane & 7) + 8 * (lane >> 4);
+                        const int col = ks * 16 + 8 * ((lane >> 3) & 1);
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4(smem_u32(sK + key * AT_LD + col), b0, b1, b2, b3);
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {
+                            mma16816(s[m][2 * jp], qf[m][ks], b0, b1);
+                            mma16816(s[m][2 * jp + 1], qf[m][ks], b2, b3);
+                        }
+                    }
+                }
+                if (kbase + 32 > len) {
+#pragma unroll
+                    for (int m = 0; m < 2; ++m)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                if (kbase + j * 8 + 2 * tq + (e & 1) >= len) s[m][j][e] = -INFINITY;
+                }
+                uint32_t pf[2][2][4];
+                float corr[2][2];
+#pragma unroll
+                for (int m = 0; m < 2; ++m) {
+                    float mx[2] = {m_r[m][0], m_r[m][1]};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        mx[0] = fmaxf(mx[0], fmaxf(s[m][j][0], s[m][j][1]));
+                        mx[1] = fmaxf(mx[1], fmaxf(s[m][j][2], s[m][j][3]));
+                    }
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+                        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+                    }
+                    float nm[2];
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        nm[r] = -mx[r] * scale_log2;
+                        corr[m][r] = ex2_approx(fmaf(m_r[m][r], scale_log2, nm[r]));
+                        m_r[m][r] = mx[r];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int kk = j >> 1, hi = j & 1;
+                        pf[m][kk][hi * 2 + 0] =
+                            ex2_h2(fmaf(s[m][j][0], scale_log2, nm[0]), fmaf(s[m][j][1], scale_log2, nm[0]));
+                        pf[m][kk][hi * 2 + 1] =
+                            ex2_h2(fmaf(s[m][j][2], scale_log2, nm[1]), fmaf(s[m][j][3], scale_log2, nm[1]));
+                    }
+                }
+                if (__any_sync(0xffffffffu, corr[0][0] != 1.0f || corr[0][1] != 1.0f || corr[1][0] != 1.0f ||
+                                                corr[1][1] != 1.0f)) {
+#pragma unroll
+                    for (int m = 0; m < 2; ++m) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            o[m][i][0] *= corr[m][0];
+                            o[m][i][1] *= corr[m][0];
+                            o[m][i][2] *= corr[m][1];
+                            o[m][i][3] *= corr[m][1];
+                        }
+                        o_sum[m][0] *= corr[m][0];
+                        o_sum[m][1] *= corr[m][0];
+                        o_sum[m][2] *= corr[m][1];
+                        o_sum[m][3] *= corr[m][1];
+                    }
+                }
+                // O += P V over the 32 keys, both m-tiles per V fragment; row sums from P x ones
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+                    for (int m = 0; m < 2; ++m) mma16816(o_sum[m], pf[m][kk], 0x3C003C00u, 0x3C003C00u);
+#pragma unroll
+                    for (int np = 0; np < 4; ++np) {
+                        const int key = 32 * h + kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                        const int col = np * 16 + 8 * (lane >> 4);
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4_t(smem_u32(sV + key * AT_LD + col), b0, b1, b2, b3);
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {
+                            mma16816(o[m][2 * np], pf[m][kk], b0, b1);
+                            mma16816(o[m][2 * np + 1], pf[m][kk], b2, b3);
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (!active) return;
+    const int g = lane >> 2;
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int q = q0 + warp * 32 + m * 16 + g + 8 * r;
+            if (q >= len) continue;
+            const float l = o_sum[m][2 * r];
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            __half* dst = out + (size_t)(start + q) * d + head * AT_HD;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int col = i * 8 + 2 * tq;
+                *reinterpret_cast<__half2*>(dst + col) =
+                    __floats2half2_rn(o[m][i][2 * r] * inv, o[m][i][2 * r + 1] * inv);
+            }
+        }
+}
+
 // ------------------------------------------------------------------ pooling
 // One CTA per sequence: mean over rows (row-parallel partial sums reduced in a
 // fixed order, so results are identical run to run), then L2 over out_dim.
@@ -574,6 +784,18 @@ int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_se
         if (rc != 1) return rc;  // launched (0) or failed
     }
     const float scale_log2 = (1.0f / sqrtf((float)AT_HD)) * 1.4426950408889634f;
+    const char* v2 = getenv("CEB_ATTN_R32");
+    if (v2 && (v2[0] == '2' || v2[0] == '4')) {
+        if (v2[0] == '2') {
+            dim3 g2((max_len + 63) / 64, n_head, n_seqs);
+            CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_rows32_kernel<2><<<g2, 64, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len, d_err));
+        } else {
+            dim3 g4((max_len + 127) / 128, n_head, n_seqs);
+            CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_rows32_kernel<4><<<g4, 128, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len, d_err));
+        }
+        CEB_CUDA_OK(cudaGetLastError());
+        return 0;
+    }
     dim3 grid((max_len + AT_Q - 1) / AT_Q, n_head, n_seqs);
     CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_kernel<<<grid, 128, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len,
                                                                              d_err));
