@@ -180,10 +180,10 @@ __global__ void rope_neox_kernel(__half* __restrict__ qkv, const int32_t* __rest
 }
 
 // ------------------------------------------------------------------ attention
-// One CTA = 64 queries of one (sequence, head); 4 warps x 16 query rows.
 // S = Q K^T and O = P V on mma.sync m16n8k16 (fp16 in, fp32 accumulate) with a
-// one-pass online softmax over 64-key tiles; keys beyond the sequence are masked.
-constexpr int AT_Q = 64, AT_K = 64, AT_HD = 64, AT_LD = 72;  // padded smem row (halfs)
+// one-pass online softmax over the keys; keys beyond the sequence are masked.
+constexpr int AT_NW = 4;                                    // warps per CTA, 32 query rows each
+constexpr int AT_Q = 32 * AT_NW, AT_K = 64, AT_HD = 64, AT_LD = 72;  // padded smem row (halfs)
 
 CEB_DEV float ex2_approx(float x) {  // MUFU 2^x (ex2(-inf) = 0)
     float r;
@@ -224,173 +224,6 @@ CEB_DEV void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// load a 64-row x 64-col fp16 tile (rows beyond n_valid zero-filled)
-CEB_DEV void load_tile(__half* s, const __half* g, size_t g_ld, int n_valid, int tid) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int chunk = tid + i * 128;  // 512 chunks of 16 B
-        const int row = chunk >> 3, col = (chunk & 7) * 8;
-        const bool ok = row < n_valid;
-        const __half* src = g + (size_t)(ok ? row : 0) * g_ld + col;
-        cp_async16(smem_u32(s + row * AT_LD + col), src, ok ? 16 : 0);
-    }
-}
-
-__global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ cu,
-                                                        int d, float scale_log2, __half* __restrict__ out,
-                                                        int total_rows, int max_len, int* __restrict__ err) {
-    __shared__ __align__(128) __half sQ[AT_Q * AT_LD];
-    __shared__ __align__(128) __half sK[2][AT_K * AT_LD];
-    __shared__ __align__(128) __half sV[2][AT_K * AT_LD];
-    const int seq = blockIdx.z, head = blockIdx.y;
-    const int start = cu[seq], len = cu[seq + 1] - start;
-    // row offsets that leave the rows or disagree with max_len: report, touch nothing
-    if (start < 0 || len < 0 || len > total_rows - start || len > max_len) {
-        if (blockIdx.x == 0 && head == 0 && threadIdx.x == 0 && err) atomicCAS(err, 0, (int)CEB_DEVERR_BAD_INDEX);
-        return;
-    }
-    const int q0 = blockIdx.x * AT_Q;
-    if (q0 >= len) return;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const size_t ld = (size_t)3 * d;
-    const __half* Qg = qkv + (size_t)(start + q0) * ld + head * AT_HD;
-    const __half* Kg = qkv + (size_t)start * ld + d + head * AT_HD;
-    const __half* Vg = qkv + (size_t)start * ld + 2 * d + head * AT_HD;
-    const int nq = min(AT_Q, len - q0);
-    const int n_kt = (len + AT_K - 1) / AT_K;
-
-    load_tile(sQ, Qg, ld, nq, tid);
-    load_tile(sK[0], Kg, ld, min(AT_K, len), tid);
-    load_tile(sV[0], Vg, ld, min(AT_K, len), tid);
-    cp_async_commit();
-
-    uint32_t qf[4][4];
-    float o[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-    float m_r[2] = {-INFINITY, -INFINITY};
-    float o_sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row sums of P, from the MMA: c0 row g, c2 row g + 8
-    const int g = lane >> 2, tq = lane & 3;
-
-    for (int kt = 0; kt < n_kt; ++kt) {
-        const int buf = kt & 1;
-        if (kt + 1 < n_kt) {
-            const int k0n = (kt + 1) * AT_K;
-            load_tile(sK[buf ^ 1], Kg + (size_t)k0n * ld, ld, min(AT_K, len - k0n), tid);
-            load_tile(sV[buf ^ 1], Vg + (size_t)k0n * ld, ld, min(AT_K, len - k0n), tid);
-        }
-        cp_async_commit();
-        cp_async_wait<1>();
-        __syncthreads();
-        if (kt == 0) {
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                const int row = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-                const int col = ks * 16 + 8 * (lane >> 4);
-                ldsm_x4(smem_u32(sQ + row * AT_LD + col), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-            }
-        }
-        // S = Q K^T for 64 keys: 8 n-tiles of 8 keys
-        float s[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-            for (int jp = 0; jp < 4; ++jp) {  // pairs of n-tiles
-                const int key = jp * 16 + (lane & 7) + 8 * (lane >> 4);
-                const int col = ks * 16 + 8 * ((lane >> 3) & 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(smem_u32(sK[buf] + key * AT_LD + col), b0, b1, b2, b3);
-                mma16816(s[2 * jp], qf[ks], b0, b1);
-                mma16816(s[2 * jp + 1], qf[ks], b2, b3);
-            }
-        }
-        // online softmax (rows g and g+8 of this warp).  Only the sequence's last key
-        // tile holds keys past its end; the max is taken on raw scores and the
-        // softmax scale folds into one FMA ahead of the exp2.
-        const int kbase = kt * AT_K;
-        if (kbase + AT_K > len) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    if (kbase + j * 8 + 2 * tq + (e & 1) >= len) s[j][e] = -INFINITY;
-        }
-        float mx[2] = {m_r[0], m_r[1]};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            mx[0] = fmaxf(mx[0], fmaxf(s[j][0], s[j][1]));
-            mx[1] = fmaxf(mx[1], fmaxf(s[j][2], s[j][3]));
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-        }
-        float corr[2], nm[2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            nm[r] = -mx[r] * scale_log2;
-            corr[r] = ex2_approx(fmaf(m_r[r], scale_log2, nm[r]));
-        }
-        uint32_t pf[4][4];
-        // P in fp16 pairs straight from the exponent unit; the row sums come from the
-        // P V product against an all-ones column tile (o_sum), so no float adds here
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int kk = j >> 1, hi = j & 1;
-            pf[kk][hi * 2 + 0] = ex2_h2(fmaf(s[j][0], scale_log2, nm[0]), fmaf(s[j][1], scale_log2, nm[0]));
-            pf[kk][hi * 2 + 1] = ex2_h2(fmaf(s[j][2], scale_log2, nm[1]), fmaf(s[j][3], scale_log2, nm[1]));
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) m_r[r] = mx[r];
-        if (__any_sync(0xffffffffu, corr[0] != 1.0f || corr[1] != 1.0f)) {  // the running max moved
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                o[i][0] *= corr[0];
-                o[i][1] *= corr[0];
-                o[i][2] *= corr[1];
-                o[i][3] *= corr[1];
-            }
-            o_sum[0] *= corr[0];
-            o_sum[1] *= corr[0];
-            o_sum[2] *= corr[1];
-            o_sum[3] *= corr[1];
-        }
-        // O += P V : k = 64 keys (4 steps of 16), n = 64 dims (8 tiles of 8)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
-            mma16816(o_sum, a, 0x3C003C00u, 0x3C003C00u);  // P times a tile of fp16 ones: row sums
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                const int key = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-                const int col = np * 16 + 8 * (lane >> 4);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(smem_u32(sV[buf] + key * AT_LD + col), b0, b1, b2, b3);
-                mma16816(o[2 * np], a, b0, b1);
-                mma16816(o[2 * np + 1], a, b2, b3);
-            }
-        }
-        __syncthreads();
-    }
-    // normalise and store fp16
-    const float l_r[2] = {o_sum[0], o_sum[2]};
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const int q = q0 + warp * 16 + g + 8 * r;
-        if (q >= len) continue;
-        const float inv = l_r[r] > 0.0f ? 1.0f / l_r[r] : 0.0f;
-        __half* dst = out + (size_t)(start + q) * d + head * AT_HD;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int col = i * 8 + 2 * tq;
-            *reinterpret_cast<__half2*>(dst + col) = __floats2half2_rn(o[i][2 * r] * inv, o[i][2 * r + 1] * inv);
-        }
-    }
-}
-
 // Rows of one tile (ROWS x 64 fp16, rows beyond n_valid zero-filled) by NT threads.
 template <int NT, int ROWS>
 CEB_DEV void load_rows(__half* s, const __half* g, size_t g_ld, int n_valid, int tid) {
@@ -405,17 +238,17 @@ CEB_DEV void load_rows(__half* s, const __half* g, size_t g_ld, int n_valid, int
     }
 }
 
-// One CTA = 32*NW queries of one (sequence, head); each warp owns 32 query rows as
-// two m16 tiles, so every K / V fragment read from shared memory feeds two MMAs.
-// Keys in 64-key tiles (cp.async, double-buffered), processed in 32-key steps; a
-// step wholly past the sequence's end is skipped.  Q is staged in the second
-// buffer's space and moved to registers before the first prefetch lands there.
-template <int NW>
-__global__ void __launch_bounds__(NW * 32, 12 / NW) attention_rows32_kernel(const __half* __restrict__ qkv,
-                                                                   const int32_t* __restrict__ cu, int d,
-                                                                   float scale_log2, __half* __restrict__ out,
-                                                                   int total_rows, int max_len, int* __restrict__ err) {
-    constexpr int NT = NW * 32, QT = NW * 32, TILE = AT_K * AT_LD;
+// One CTA = AT_Q queries of one (sequence, head); each warp owns 32 query rows as
+// two m16 tiles, so every K / V fragment read from shared memory feeds two MMAs
+// (two independent MMA chains per warp).  Keys in 64-key tiles (cp.async,
+// double-buffered), processed in 32-key steps; a step wholly past the sequence's
+// end is skipped.  Q is staged in the second buffer's space and moved to registers
+// before the first prefetch lands there.  168 registers: 3 CTAs per SM.
+__global__ void __launch_bounds__(AT_NW * 32, 3) attention_kernel(const __half* __restrict__ qkv,
+                                                                  const int32_t* __restrict__ cu, int d,
+                                                                  float scale_log2, __half* __restrict__ out,
+                                                                  int total_rows, int max_len, int* __restrict__ err) {
+    constexpr int NT = AT_NW * 32, QT = AT_Q, TILE = AT_K * AT_LD;
     static_assert(QT <= 2 * AT_K, "Q staging uses the second K and V buffers");
     __shared__ __align__(128) __half sm[4 * TILE];  // K0, V0, K1, V1
     const int seq = blockIdx.z, head = blockIdx.y;
@@ -777,27 +610,16 @@ int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_se
     if (n_seqs <= 0 || max_len <= 0) return 0;
     // The tcgen05 CTA-pair kernel (attn_tc.cu) is opt-in: CEB_ATTN_TC=1 in the environment.
     // On the benchmark batch (256 sequences, 32..512 tokens, 12 heads) it measures
-    // 0.386 ms per layer against 0.346 ms for the mma.sync kernel below.
+    // 0.408 ms per layer against 0.360 ms for the mma.sync kernel below (0.249 against
+    // 0.272 ms on 96 sequences of 384..512 tokens).
     const char* tc = getenv("CEB_ATTN_TC");
     if (tc && tc[0] == '1') {
         const int rc = ceb_attention_tc(qkv, total_rows, cu, n_seqs, max_len, d, n_head, out, d_err, st);
         if (rc != 1) return rc;  // launched (0) or failed
     }
     const float scale_log2 = (1.0f / sqrtf((float)AT_HD)) * 1.4426950408889634f;
-    const char* v2 = getenv("CEB_ATTN_R32");
-    if (v2 && (v2[0] == '2' || v2[0] == '4')) {
-        if (v2[0] == '2') {
-            dim3 g2((max_len + 63) / 64, n_head, n_seqs);
-            CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_rows32_kernel<2><<<g2, 64, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len, d_err));
-        } else {
-            dim3 g4((max_len + 127) / 128, n_head, n_seqs);
-            CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_rows32_kernel<4><<<g4, 128, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len, d_err));
-        }
-        CEB_CUDA_OK(cudaGetLastError());
-        return 0;
-    }
     dim3 grid((max_len + AT_Q - 1) / AT_Q, n_head, n_seqs);
-    CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_kernel<<<grid, 128, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len,
+    CEB_LAUNCH(CEB_PROF_ATTN, st, 0.0, 0.0, attention_kernel<<<grid, AT_NW * 32, 0, st>>>(qkv, cu, d, scale_log2, out, total_rows, max_len,
                                                                              d_err));
     CEB_CUDA_OK(cudaGetLastError());
     return 0;
