@@ -15,18 +15,21 @@
 //               in one of two TMEM buffers per head, so S of chunk c+1 is ready
 //               while the softmax of chunk c runs.
 //   softmax     one thread per query row, online over the chunks: the row max of
-//               the chunk from TMEM, exp2 on the MUFU, P as fp16 pairs written
-//               over the chunk's S columns (the S that reuses that buffer is
-//               issued after the P V that reads P, by the same thread, and
-//               tcgen05 MMAs run in issue order).  The max used for the exponentials is raised -- and O
-//               rescaled in TMEM, after the previous P V -- only when the true
-//               max exceeds it by more than 2^8: P <= 256 fits fp16 and O, the
-//               row sum stay fp32.
+//               the chunk from TMEM, exponentials as fp16 pairs on the MUFU
+//               (ex2.approx.f16x2), P written over the chunk's S columns (the S
+//               that reuses that buffer is issued after the P V that reads P, and
+//               tcgen05 MMAs run in issue order), the row sum as fp16 pair sums
+//               widened per chunk.  The max used for the exponentials is raised --
+//               and O rescaled in TMEM, after the previous P V -- only when the true
+//               max exceeds it by more than 2^2, so exponents stay <= 2 and P <= 4.
+//               Without a rescale P is published at once, ahead of the wait for
+//               the previous chunk's P V (per-buffer barriers keep that wait from
+//               ever running two phases behind).
 //   O = P V     TS form: A = P from TMEM, B = V MN-major (64-byte swizzle), each
 //               CTA holding 32 of the 64 dims for all keys; O (fp32) in TMEM,
 //               divided by the row sum at the end and stored fp16.
 // TMEM per CTA: head A  S/P buffers 0..63 and 64..127, O 128..191; head B +256.
-// Barriers that a waiter could otherwise find two phases ahead (S, P) exist once
+// Barriers that a waiter could otherwise find two phases ahead (S, P, P V) exist once
 // per buffer.
 // Rank 1's "P written" is relayed to the leader's barrier by a 16-byte
 // cp.async.bulk (asynchronous; a blocking cluster-scope release arrive costs
@@ -54,9 +57,11 @@ constexpr int HEAD_BYTES = Q_BYTES + K_BYTES + V_BYTES;  // 80 KB per head
 constexpr uint32_t BUF_STRIDE = 64;                    // S/P buffer b at columns 64 b
 constexpr uint32_t O_COL = 128, HEAD_COLS = 256;
 #ifndef CEB_ATTN_RESCALE_LOG2
-#define CEB_ATTN_RESCALE_LOG2 8.0f
+#define CEB_ATTN_RESCALE_LOG2 2.0f
 #endif
-constexpr float RESCALE_LOG2 = CEB_ATTN_RESCALE_LOG2;  // raise the exponent's max when exceeded by more than 2^8
+// raise the exponent's max when exceeded by more than 2^2: exponents stay <= 2, so their
+// fp16 rounding (the exponentials are taken in fp16 pairs) costs at most 2^-11 relative
+constexpr float RESCALE_LOG2 = CEB_ATTN_RESCALE_LOG2;
 constexpr int SBUF = 2;                                // S/P buffers per head
 #ifndef CEB_ATTN_HPC
 #define CEB_ATTN_HPC 1
@@ -65,7 +70,7 @@ constexpr int HPC = CEB_ATTN_HPC;  // heads per CTA pair (interleaved through on
 constexpr int NTHR = 128 + 128 * HPC;  // warps 0 TMA, 1 TMEM+MMA, 2..3 relays, 4.. softmax (4 per head)
 constexpr int SM_WARP0 = 4;
 // barriers, per head h: +h*PER; S, P and PLOCAL once per S/P buffer (+b)
-enum { B_LDQK, B_LDV, B_S, B_S1, B_P, B_P1, B_PV, B_PLOCAL, B_PLOCAL1, PER };
+enum { B_LDQK, B_LDV, B_S, B_S1, B_P, B_P1, B_PV, B_PV1, B_PLOCAL, B_PLOCAL1, PER };
 constexpr int B_DRAIN = HPC * PER, NBAR = HPC * PER + 1;
 // two heads: ~161 KB, one CTA per SM (512 TMEM columns); one head: ~81 KB, at most two CTAs
 // per SM (256 columns each), so TMEM allocations never wait on one another
@@ -73,12 +78,18 @@ constexpr size_t SMEM_LAUNCH = 1024 + HPC * HEAD_BYTES + 256;
 constexpr uint32_t TMEM_ALLOC = 256 * HPC;
 static_assert(HPC == 1 || HPC == 2, "heads per CTA");
 static_assert(HPC == 2 || 3 * SMEM_LAUNCH > 228 * 1024, "at most two one-head CTAs per SM");
-static_assert(NBAR * 8 <= 160, "barrier area");
+static_assert(NBAR * 8 <= 192, "barrier area");
 static_assert(SMEM_LAUNCH <= 227 * 1024, "attention shared memory");
 
 CEB_DEV float ex2f(float x) {
     float r;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+// 2^t0, 2^t1 as the packed fp16 pair P is stored in: one conversion, one MUFU op
+CEB_DEV uint32_t ex2_h2(float t0, float t1) {
+    uint32_t in = h2_as_u32(__floats2half2_rn(t0, t1)), r;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(in));
     return r;
 }
 
@@ -103,10 +114,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
     auto sK = [&](int h) { return base + h * HEAD_BYTES + Q_BYTES; };
     auto sV = [&](int h) { return base + h * HEAD_BYTES + Q_BYTES + K_BYTES; };
     uint8_t* misc = base + HPC * HEAD_BYTES;               // 1024-byte aligned
-    uint64_t* bars = reinterpret_cast<uint64_t*>(misc);    // <= 160 bytes
-    uint8_t* sig = misc + 160;                             // 2 x 16 bytes: sinks (leader) / sources (rank 1)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 192);
-    int* abort_flag = reinterpret_cast<int*>(misc + 196);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(misc);    // <= 192 bytes
+    uint8_t* sig = misc + 192;                             // 2 x 16 bytes: sinks (leader) / sources (rank 1)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 224);
+    int* abort_flag = reinterpret_cast<int*>(misc + 228);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -208,8 +219,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
                         mma_pair_f16_ts(tmem + h * HEAD_COLS + O_COL,
                                         tmem + h * HEAD_COLS + BUF_STRIDE * (uint32_t)b + (uint32_t)(8 * j), vdesc + (uint64_t)(64 * j),
                                         pv_idesc, (c | j) != 0);
-                    mma_pair_commit(bar(h * PER + B_PV));
-                    mma_pair_commit(mapa_shared(bar(h * PER + B_PV), 1));
+                    mma_pair_commit(bar(h * PER + B_PV + b));
+                    mma_pair_commit(mapa_shared(bar(h * PER + B_PV + b), 1));
                     if (c + SBUF < nch) issue_s(h, c + SBUF);  // reuses buffer b after the P V that reads it
                 }
             }
@@ -233,7 +244,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
         const int qd = warp & 3;                                // TMEM lane quadrant
         const uint32_t row_t = tmem + ((uint32_t)(32 * qd) << 16) + h * HEAD_COLS;
         const int q = q0 + QT * (int)rank + 32 * qd + lane;     // query index within the sequence
-        float m_use = -INFINITY, l_run = 0.0f;  // max used by the exponentials (log2 units), row sum
+        float m_use = -INFINITY;  // max used by the exponentials (log2 units)
+        float l_run = 0.0f;       // row sum of P (fp16 pair sums widened per chunk)
         bool ok = true;
         for (int c = 0; c < nch; ++c) {
             const int k0 = c * KC, nc = min(KC, lpad - k0), b = SBUF == 2 ? (c & 1) : 0;
@@ -246,15 +258,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
             tmem_ld32(buf, v[0]);
             if (nc > 32) tmem_ld32(buf + 32, v[1]);
             tmem_ld_wait();
-            float cmax = -INFINITY;
+            if (k0 + nc > len) {  // the sequence ends in this chunk (same for every thread): no weight past it
 #pragma unroll
-            for (int g = 0; g < 2; ++g)
-                if (32 * g < nc) {
+                for (int g = 0; g < 2; ++g)
 #pragma unroll
                     for (int t = 0; t < 32; ++t)
-                        if (k0 + 32 * g + t < len) cmax = fmaxf(cmax, __uint_as_float(v[g][t]));
-                }
-            const float cm = cmax * scale_log2;
+                        if (k0 + 32 * g + t >= len) v[g][t] = 0xff800000u;  // -inf
+            }
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int t = 0; t < 32; ++t) mx[t & 3] = fmaxf(mx[t & 3], __uint_as_float(v[0][t]));
+            if (nc > 32) {
+#pragma unroll
+                for (int t = 0; t < 32; ++t) mx[t & 3] = fmaxf(mx[t & 3], __uint_as_float(v[1][t]));
+            }
+            const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
             // raise the max used by the exponentials when the true max exceeds it by more than
             // 2^RESCALE_LOG2 (always on the first chunk: m_use = -inf); warp-uniform decision
             const bool raise = c > 0 && __any_sync(0xffffffffu, cm > m_use + RESCALE_LOG2);
@@ -266,28 +284,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
                 alpha = ex2f(m_use - m_new);
                 m_use = m_new;
             }
-            // exp2, row sum, fp16 P over the S columns just read
-            float sum = 0.0f;
+            // P = 2^(s*scale - m) as fp16 pairs over the S columns just read; the row sum adds
+            // the pairs in fp16 (a 16-pair tree per 32 keys, values <= 4) and widens per chunk
+            const float nm = -m_use;
+            float csum = 0.0f;
 #pragma unroll
             for (int g = 0; g < 2; ++g) {
                 if (32 * g < nc) {
                     uint32_t pk[16];
 #pragma unroll
-                    for (int t = 0; t < 32; t += 2) {
-                        const int kx = k0 + 32 * g + t;
-                        const float p0 = kx < len ? ex2f(fmaf(__uint_as_float(v[g][t]), scale_log2, -m_use)) : 0.0f;
-                        const float p1 = kx + 1 < len ? ex2f(fmaf(__uint_as_float(v[g][t + 1]), scale_log2, -m_use)) : 0.0f;
-                        sum += p0 + p1;
-                        pk[t >> 1] = h2_as_u32(__floats2half2_rn(p0, p1));
-                    }
+                    for (int t = 0; t < 32; t += 2)
+                        pk[t >> 1] = ex2_h2(fmaf(__uint_as_float(v[g][t]), scale_log2, nm),
+                                            fmaf(__uint_as_float(v[g][t + 1]), scale_log2, nm));
                     tmem_st16(buf + (uint32_t)(16 * g), pk);
+                    __half2 a[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) a[i] = __hadd2(u32_as_h2(pk[2 * i]), u32_as_h2(pk[2 * i + 1]));
+#pragma unroll
+                    for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+                        for (int i = 0; i < w; ++i) a[i] = __hadd2(a[i], a[i + w]);
+                    csum += __low2float(a[0]) + __high2float(a[0]);
                 }
             }
-            l_run = l_run * alpha + sum;
+            l_run = l_run * alpha + csum;
+            auto publish = [&]() {
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if (!leader)
+                        mbar_arrive(bar(h * PER + B_PLOCAL + b));
+                    else if (qd == 0)
+                        mbar_arrive_expect_tx(bar(h * PER + B_P + b), 16);  // + rank 1's relayed signal
+                    else
+                        mbar_arrive(bar(h * PER + B_P + b));
+                }
+            };
+            // Without a rescale P of chunk c is published at once (P V of chunk c runs after that
+            // of c-1 in issue order); a rescale of O waits for P V of chunk c-1 first.
+            const bool pub_now = !raise;
+            if (pub_now) publish();
             if (c > 0) {
-                // P V of chunk c-1 has finished before P of chunk c is published: O can be rescaled,
-                // and the barrier never runs more than one phase behind a later wait
-                ok = __all_sync(0xffffffffu, wait_at(h * PER + B_PV, (c - 1) & 1, CEB_DEVERR_TIMEOUT_EPI));
+                // per-parity barriers: the next phase of this one needs P of chunk c+1
+                const int cp = c - 1;
+                ok = __all_sync(0xffffffffu,
+                                wait_at(h * PER + B_PV + (cp & 1), (cp >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI));
                 if (!ok) break;
                 if (raise) {
                     tc_fence_after();
@@ -302,21 +344,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
                     }
                 }
             }
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if (!leader)
-                    mbar_arrive(bar(h * PER + B_PLOCAL + b));
-                else if (qd == 0)
-                    mbar_arrive_expect_tx(bar(h * PER + B_P + b), 16);  // + rank 1's relayed signal
-                else
-                    mbar_arrive(bar(h * PER + B_P + b));
-            }
+            if (!pub_now) publish();
         }
-        if (ok && __all_sync(0xffffffffu, wait_at(h * PER + B_PV, (nch - 1) & 1, CEB_DEVERR_TIMEOUT_EPI))) {
+        const int cl = nch - 1;
+        if (ok && __all_sync(0xffffffffu,
+                             wait_at(h * PER + B_PV + (cl & 1), (cl >> 1) & 1, CEB_DEVERR_TIMEOUT_EPI))) {
             tc_fence_after();
-            const float inv = 1.0f / l_run;
+            const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
             uint32_t pk[32];
 #pragma unroll
             for (int o0 = 0; o0 < HD; o0 += 32) {
@@ -344,6 +378,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHR, 1)
         tmem_dealloc_pair(tmem, TMEM_ALLOC);
     }
 }
+
 
 }  // namespace
 

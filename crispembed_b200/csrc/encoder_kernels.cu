@@ -610,8 +610,9 @@ int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_se
     if (n_seqs <= 0 || max_len <= 0) return 0;
     // The tcgen05 CTA-pair kernel (attn_tc.cu) is opt-in: CEB_ATTN_TC=1 in the environment.
     // On the benchmark batch (256 sequences, 32..512 tokens, 12 heads) it measures
-    // 0.408 ms per layer against 0.360 ms for the mma.sync kernel below (0.249 against
-    // 0.272 ms on 96 sequences of 384..512 tokens).
+    // 0.391-0.395 ms per layer against 0.360 ms for the mma.sync kernel below (0.244
+    // against 0.272 ms on 96 sequences of 384..512 tokens; a split of the batch between
+    // the two kernels by length, launched one after the other, measured 0.378 ms).
     const char* tc = getenv("CEB_ATTN_TC");
     if (tc && tc[0] == '1') {
         const int rc = ceb_attention_tc(qkv, total_rows, cu, n_seqs, max_len, d, n_head, out, d_err, st);

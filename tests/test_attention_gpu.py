@@ -17,6 +17,7 @@ LEN_SETS = [
     [17, 31, 32, 33],
     [128, 129, 255, 256, 257],
     [300, 511, 512, 7, 64],
+    [450, 200, 256, 30, 385, 193],
     [600, 40],  # longest > 512: the mma.sync kernel
 ]
 
