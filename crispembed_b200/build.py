@@ -21,7 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libcrispembed.so")
 
-SOURCES = ["gemm_tc.cu", "attn_tc.cu", "moe.cu", "moe_static.cu", "ep.cu", "encoder_kernels.cu", "ref_arith.cu", "runtime.cpp", "gguf_quants.cpp", "gguf.cpp", "tokenizer.cpp", "model.cpp", "api.cpp"]
+SOURCES = ["gemm_tc.cu", "attn_tc.cu", "attn_fa.cu", "moe.cu", "moe_static.cu", "ep.cu", "encoder_kernels.cu", "ref_arith.cu", "runtime.cpp", "gguf_quants.cpp", "gguf.cpp", "tokenizer.cpp", "model.cpp", "api.cpp"]
 HEADERS = ["common.cuh", "rowwise.cuh", "ceb_internal.h", "ceb_moe_internal.h", "ceb_ep_internal.h", "ceb_encoder_internal.h", "gguf.h", "tokenizer.h", "spm_norm_table.inc",
            "ceb_portable_math.h"]
 PUBLIC_HEADERS = [os.path.join(ROOT, "include", h) for h in ("crispembed.h", "ceb_ops.h")]

@@ -705,6 +705,8 @@ namespace {
 // the word of the device they run on, and ceb_sync_check reads the current
 // device's (a process may drive several GPUs).
 constexpr int OP_MAX_DEVICES = 64;
+// Each device's block holds the error word ([0]) and the attention entry's work-item
+// counter ([1], [2]).
 int* g_op_err[OP_MAX_DEVICES] = {};
 std::mutex g_op_mu;
 int* op_err_word() {
@@ -713,8 +715,8 @@ int* op_err_word() {
     std::lock_guard<std::mutex> lk(g_op_mu);
     if (!g_op_err[dev]) {
         int* p = nullptr;
-        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
-        if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
+        if (cudaMalloc(&p, 4 * sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, 4 * sizeof(int)) != cudaSuccess) {
             cudaFree(p);
             return nullptr;
         }
@@ -816,7 +818,7 @@ extern "C" int ceb_attention_forward(const void* d_qkv, int n_rows, const int32_
     int* err = op_err_word();
     if (!err) return ceb_set_error(3, "attention: device error word");
     return ceb_attention(static_cast<const __half*>(d_qkv), n_rows, d_cu_seqlens, n_seqs, max_len, d, n_head,
-                         static_cast<__half*>(d_out), err, static_cast<cudaStream_t>(stream));
+                         static_cast<__half*>(d_out), err, static_cast<cudaStream_t>(stream), err + 1);
 }
 
 struct ceb_linear {

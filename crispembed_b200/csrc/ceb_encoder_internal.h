@@ -21,12 +21,19 @@ int ceb_add_ln(const float* res, const __half* y, int M, int d, const float* gam
 int ceb_moe_combine_ln(const __half* down, const int32_t* slot_pos, const float* wts, int K, const float* moe_bias,
                        const float* cur, int M, int d, const float* gamma, const float* beta, float eps, float* out32,
                        __half* out16, cudaStream_t st);
+// sched: two device ints, zero before the first call, that the tcgen05 kernel uses to
+// hand out its work items (and returns to zero); calls sharing them must be ordered
+// on one stream.  nullptr: the mma.sync kernel.
 int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
-                  __half* out, int* d_err, cudaStream_t st);
+                  __half* out, int* d_err, cudaStream_t st, int* sched);
 // tcgen05 CTA-pair attention (attn_tc.cu); returns 1 without launching when the
 // shape is not handled there (head_dim != 64 or a sequence longer than 512)
 int ceb_attention_tc(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
                      __half* out, int* d_err, cudaStream_t st);
+// single-CTA tcgen05 attention (attn_fa.cu); returns 1 without launching when the shape
+// is not handled there (head_dim != 64, operands not 16-byte aligned)
+int ceb_attention_fa(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
+                     __half* out, int* d_err, cudaStream_t st, int* sched);
 // RoPE, NEOX pairing (dims i and i + 32 of each 64-dim head), on the Q and K thirds of
 // fused fp16 qkv rows in place; position = row - cu[seq] + pos_offset.
 int ceb_rope_neox(__half* qkv, int M, const int32_t* cu, int n_seqs, int d, int n_head, int pos_offset, float theta,
@@ -128,6 +135,7 @@ struct ceb_workspace {
     int32_t* ids = nullptr;    // [cap_tokens]
     int32_t* cu = nullptr;     // [cap_seqs + 1]
     float* out = nullptr;      // [cap_seqs x d]
+    int* attn_sched = nullptr;  // [2] attention work-item counter (zeroed at allocation)
 };
 
 int ceb_model_load(ceb_model* m, const std::string& path, std::string* err_out);

@@ -604,19 +604,25 @@ int ceb_moe_combine_ln(const __half* down, const int32_t* slot_pos, const float*
 }
 
 int ceb_attention(const __half* qkv, int total_rows, const int32_t* cu, int n_seqs, int max_len, int d, int n_head,
-                  __half* out, int* d_err, cudaStream_t st) {
+                  __half* out, int* d_err, cudaStream_t st, int* sched) {
     if (n_head <= 0 || d % n_head || d / n_head != AT_HD)
         return ceb_set_error(2, "attention: head_dim %d unsupported (64 only)", n_head > 0 ? d / n_head : -1);
     if (n_seqs <= 0 || max_len <= 0) return 0;
-    // The tcgen05 CTA-pair kernel (attn_tc.cu) is opt-in: CEB_ATTN_TC=1 in the environment.
-    // On the benchmark batch (256 sequences, 32..512 tokens, 12 heads) it measures
-    // 0.391-0.395 ms per layer against 0.360 ms for the mma.sync kernel below (0.244
-    // against 0.272 ms on 96 sequences of 384..512 tokens; a split of the batch between
-    // the two kernels by length, launched one after the other, measured 0.378 ms).
+    // Default: the single-CTA tcgen05 kernel (attn_fa.cu); on the benchmark batch (256
+    // sequences, 32..512 tokens, 12 heads) 0.253 ms per layer against 0.358 ms for the
+    // mma.sync kernel below, which remains for operands the tensor maps cannot take and
+    // for callers without a work-item counter.  CEB_ATTN_MMA=1 forces the mma.sync kernel;
+    // CEB_ATTN_TC=1 selects the CTA-pair tcgen05 kernel (attn_tc.cu, sequences of up to 512
+    // tokens; 0.391-0.395 ms on the same batch).
     const char* tc = getenv("CEB_ATTN_TC");
     if (tc && tc[0] == '1') {
         const int rc = ceb_attention_tc(qkv, total_rows, cu, n_seqs, max_len, d, n_head, out, d_err, st);
         if (rc != 1) return rc;  // launched (0) or failed
+    }
+    const char* mma = getenv("CEB_ATTN_MMA");
+    if (!(mma && mma[0] == '1') && sched) {
+        const int rc = ceb_attention_fa(qkv, total_rows, cu, n_seqs, max_len, d, n_head, out, d_err, st, sched);
+        if (rc != 1) return rc;
     }
     const float scale_log2 = (1.0f / sqrtf((float)AT_HD)) * 1.4426950408889634f;
     dim3 grid((max_len + AT_Q - 1) / AT_Q, n_head, n_seqs);

@@ -437,6 +437,7 @@ int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int
     const size_t moe_bytes = ceb_moe_ws_layout(T, d, E, K, Fm, nullptr, nullptr);
     const size_t o_moe = take(moe_bytes);
     const size_t o_ids = take((size_t)T * 4), o_cu = take((size_t)(S + 1) * 4), o_out = take((size_t)S * d * 4);
+    const size_t o_sched = take(2 * sizeof(int));
     // reference arithmetic: fp32 activations, Q8_0 copies of every matrix input, expert rows
     // padded to whole 32-row tiles per expert
     size_t r_qkv = 0, r_attn = 0, r_h = 0, r_xp = 0, r_down = 0, r_lg = 0, r_wts = 0, r_xq = 0, r_xd = 0, r_ids = 0,
@@ -483,6 +484,8 @@ int ceb_workspace_reserve(ceb_workspace* ws, const ceb_model& m, int tokens, int
     ws->ids = reinterpret_cast<int32_t*>(b + o_ids);
     ws->cu = reinterpret_cast<int32_t*>(b + o_cu);
     ws->out = reinterpret_cast<float*>(b + o_out);
+    ws->attn_sched = reinterpret_cast<int*>(b + o_sched);
+    if (cudaMemset(ws->attn_sched, 0, 2 * sizeof(int)) != cudaSuccess) return ceb_set_error(3, "workspace: clearing");
     if (m.ref_arith) {
         ceb_ref_ws& r = ws->ref;
         r.qkv = reinterpret_cast<float*>(b + r_qkv);
@@ -608,7 +611,7 @@ int ceb_encoder_forward(const ceb_model& m, ceb_workspace& ws, const int32_t* d_
         if (m.use_rope &&
             (rc = ceb_rope_neox(ws.qkv16, M, d_cu, n_seqs, d, hp.n_head, m.pos_offset, m.rope_theta, st)))
             return rc;
-        if ((rc = ceb_attention(ws.qkv16, M, d_cu, n_seqs, max_len, d, hp.n_head, ws.a16, d_err, st))) return rc;
+        if ((rc = ceb_attention(ws.qkv16, M, d_cu, n_seqs, max_len, d, hp.n_head, ws.a16, d_err, st, ws.attn_sched))) return rc;
         // output projection (+bias) -> fp16, residual + LN1
         a.out = ws.t16;
         a.ldo = d;

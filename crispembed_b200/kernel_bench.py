@@ -143,8 +143,12 @@ def bench_attn(a):
     import torch
 
     from . import binding
+    os.environ.pop("CEB_ATTN_TC", None)
+    os.environ.pop("CEB_ATTN_MMA", None)
     if a.impl == "tc":
         os.environ["CEB_ATTN_TC"] = "1"
+    elif a.impl == "mma":
+        os.environ["CEB_ATTN_MMA"] = "1"
     rng = np.random.default_rng(2)
     lens = rng.integers(a.lo, a.hi + 1, size=a.seqs).astype(np.int32)
     cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).cuda()
@@ -347,7 +351,8 @@ def main(argv=None):
     t.add_argument("--lo", type=int, default=32)
     t.add_argument("--hi", type=int, default=512)
     t.add_argument("--heads", type=int, default=12)
-    t.add_argument("--impl", choices=["mma", "tc"], default="mma")
+    t.add_argument("--impl", choices=["fa", "mma", "tc"], default="fa",
+                   help="fa: the default single-CTA tcgen05 kernel; mma: mma.sync; tc: the CTA-pair tcgen05 kernel")
     t.add_argument("--iters", type=int, default=20)
     t.add_argument("--warmup", type=int, default=3)
     p = sub.add_parser("pool")

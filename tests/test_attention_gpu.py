@@ -1,7 +1,8 @@
 """Varlen multi-head attention against the oracle's restatement of the encoder
 graph's attention (src/crispembed.cpp:1278-1297): softmax(Q K^T / 8) V per
-sequence and head.  Both kernels are checked: the mma.sync kernel (default) and
-the tcgen05 CTA-pair kernel (CEB_ATTN_TC=1; sequences of up to 512 tokens).
+sequence and head.  All three kernels are checked: the single-CTA tcgen05 kernel
+(default), the mma.sync kernel (CEB_ATTN_MMA=1) and the tcgen05 CTA-pair kernel
+(CEB_ATTN_TC=1; sequences of up to 512 tokens).
 
 Inputs are fp16 (as the QKV projection writes them); the oracle computes in fp32
 from the same fp16 values.  P is rounded to fp16 before the P V product on the
@@ -31,12 +32,16 @@ def _qkv(lens, n_head, seed):
     return qkv, cu, d
 
 
-@pytest.fixture(params=["mma_sync", "tcgen05"])
+@pytest.fixture(params=["tcgen05_cta", "mma_sync", "tcgen05_pair"])
 def attn_impl(request, monkeypatch):
-    if request.param == "tcgen05":
+    """tcgen05_cta: the default single-CTA tcgen05 kernel; mma_sync (CEB_ATTN_MMA=1) and
+    tcgen05_pair (CEB_ATTN_TC=1): the other two kernels."""
+    monkeypatch.delenv("CEB_ATTN_TC", raising=False)
+    monkeypatch.delenv("CEB_ATTN_MMA", raising=False)
+    if request.param == "tcgen05_pair":
         monkeypatch.setenv("CEB_ATTN_TC", "1")
-    else:
-        monkeypatch.delenv("CEB_ATTN_TC", raising=False)
+    elif request.param == "mma_sync":
+        monkeypatch.setenv("CEB_ATTN_MMA", "1")
     return request.param
 
 
