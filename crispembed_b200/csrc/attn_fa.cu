@@ -277,6 +277,9 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM)
             Item it;
             decode_item(idx, n_qt, n_head, cu, total_rows, max_len, nullptr, it);
             const int len = it.len, nch = (len + KC - 1) / KC;
+            // a warp whose 32 query rows all lie past the sequence keeps to the barrier protocol but
+            // computes no exponentials (its P rows stay stale; they only reach O rows never stored)
+            const bool dead = it.q0 + 32 * qd >= len;
             float m_use = -INFINITY, l_run = 0.0f;  // max used by the exponentials (log2 units), row sum
             for (int c = 0; c < nch; ++c, ++g) {
                 ok = __all_sync(0xffffffffu, wait_at(B_SFULL, g & 1, CEB_DEVERR_TIMEOUT_EPI));
@@ -284,6 +287,7 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM)
                 tc_fence_after();
                 const int k0 = c * KC;
                 const bool tail = k0 + KC > len;  // the sequence ends in this chunk: no weight past it
+                const int nv = tail ? (len - k0 + 31) / 32 : KC / 32;  // 32-key pieces holding a key
                 // the chunk's S row in registers with one wait; then S may be overwritten by the next chunk
                 uint32_t v[KC / 32][32];
 #pragma unroll
@@ -307,7 +311,7 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM)
                 const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
                 // raise the max used by the exponentials when the true max exceeds it by more than
                 // 2^RESCALE_LOG2 (always on the first chunk: m_use = -inf); warp-uniform decision
-                const bool raise = c > 0 && __any_sync(0xffffffffu, cm > m_use + RESCALE_LOG2);
+                const bool raise = c > 0 && !dead && __any_sync(0xffffffffu, cm > m_use + RESCALE_LOG2);
                 float alpha = 1.0f;
                 if (c == 0) {
                     m_use = cm;
@@ -321,10 +325,15 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM)
                 float csum = 0.0f;
 #pragma unroll
                 for (int pc = 0; pc < KC / 32; ++pc) {
+                    if (!dead && pc < nv) {  // no exponentials for keys past the sequence
 #pragma unroll
-                    for (int t = 0; t < 32; t += 2)
-                        pk[pc][t >> 1] = ex2_h2(fmaf(__uint_as_float(v[pc][t]), scale_log2, nm),
-                                                fmaf(__uint_as_float(v[pc][t + 1]), scale_log2, nm));
+                        for (int t = 0; t < 32; t += 2)
+                            pk[pc][t >> 1] = ex2_h2(fmaf(__uint_as_float(v[pc][t]), scale_log2, nm),
+                                                    fmaf(__uint_as_float(v[pc][t + 1]), scale_log2, nm));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) pk[pc][j] = 0u;
+                    }
                     __half2 a[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) a[j] = __hadd2(u32_as_h2(pk[pc][2 * j]), u32_as_h2(pk[pc][2 * j + 1]));
@@ -353,8 +362,10 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM)
                         }
                     }
                 }
+                if (!dead) {
 #pragma unroll
-                for (int pc = 0; pc < KC / 32; ++pc) tmem_st16(row_t + P_COL + (uint32_t)(16 * pc), pk[pc]);
+                    for (int pc = 0; pc < KC / 32; ++pc) tmem_st16(row_t + P_COL + (uint32_t)(16 * pc), pk[pc]);
+                }
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -363,6 +374,7 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM)
             // the item's last P V has finished: O / row sum -> fp16 rows of the sequence
             ok = ok && __all_sync(0xffffffffu, wait_at(B_PVDONE, (g - 1) & 1, CEB_DEVERR_TIMEOUT_EPI));
             if (!ok) break;
+            if (dead) continue;
             tc_fence_after();
             const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
             uint32_t pk[32];
