@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -705,8 +706,6 @@ namespace {
 // the word of the device they run on, and ceb_sync_check reads the current
 // device's (a process may drive several GPUs).
 constexpr int OP_MAX_DEVICES = 64;
-// Each device's block holds the error word ([0]) and the attention entry's work-item
-// counter ([1], [2]).
 int* g_op_err[OP_MAX_DEVICES] = {};
 std::mutex g_op_mu;
 int* op_err_word() {
@@ -715,8 +714,8 @@ int* op_err_word() {
     std::lock_guard<std::mutex> lk(g_op_mu);
     if (!g_op_err[dev]) {
         int* p = nullptr;
-        if (cudaMalloc(&p, 4 * sizeof(int)) != cudaSuccess) return nullptr;
-        if (cudaMemset(p, 0, 4 * sizeof(int)) != cudaSuccess) {
+        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
             cudaFree(p);
             return nullptr;
         }
@@ -727,6 +726,36 @@ int* op_err_word() {
 }  // namespace
 
 int* ceb_op_error_word() { return op_err_word(); }
+
+namespace {
+// Work-item counters of the operator-level attention entry, one pair per (device, stream):
+// launches on one stream run in order and share theirs, launches on different streams do
+// not (the kernel returns its counter to zero when it ends).
+struct SchedKey {
+    int dev;
+    cudaStream_t st;
+    bool operator<(const SchedKey& o) const { return dev != o.dev ? dev < o.dev : st < o.st; }
+};
+std::map<SchedKey, int*> g_attn_sched;
+int* attn_sched_words(cudaStream_t st) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_op_mu);
+    int*& p = g_attn_sched[SchedKey{dev, st}];
+    if (!p) {
+        if (cudaMalloc(&p, 2 * sizeof(int)) != cudaSuccess) {
+            p = nullptr;
+            return nullptr;
+        }
+        if (cudaMemset(p, 0, 2 * sizeof(int)) != cudaSuccess) {
+            cudaFree(p);
+            p = nullptr;
+            return nullptr;
+        }
+    }
+    return p;
+}
+}  // namespace
 
 extern "C" int ceb_moe_ffn(const ceb_moe_layer* L, const void* d_x, int x_dtype, int n_tokens, float* d_y,
                            int32_t* d_ids, float* d_weights, int32_t* d_expert_counts, float* d_logits,
@@ -817,8 +846,10 @@ extern "C" int ceb_attention_forward(const void* d_qkv, int n_rows, const int32_
         return ceb_set_error(1, "attention: qkv and out must be 16-byte aligned");
     int* err = op_err_word();
     if (!err) return ceb_set_error(3, "attention: device error word");
+    int* sched = attn_sched_words(static_cast<cudaStream_t>(stream));
+    if (!sched) return ceb_set_error(3, "attention: work-item counter");
     return ceb_attention(static_cast<const __half*>(d_qkv), n_rows, d_cu_seqlens, n_seqs, max_len, d, n_head,
-                         static_cast<__half*>(d_out), err, static_cast<cudaStream_t>(stream), err + 1);
+                         static_cast<__half*>(d_out), err, static_cast<cudaStream_t>(stream), sched);
 }
 
 struct ceb_linear {

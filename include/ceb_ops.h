@@ -261,9 +261,12 @@ CEB_API void ceb_tokenizer_free(ceb_text_tokenizer* tok);
  * beyond the sequence bounds.  d_qkv [n_rows x 3d] fp16 holds Q | K | V per row
  * (head h at columns h*64 .. h*64+63 of each third); d_out [n_rows x d] fp16.
  * head_dim must be 64; d_qkv and d_out 16-byte aligned (status 1 otherwise).
- * The default kernel is mma.sync with an online softmax; CEB_ATTN_TC=1 in the
- * environment selects the tcgen05 CTA-pair kernel for sequences of up to 512
- * tokens.  Asynchronous on `stream`; device-side failures surface through
+ * The default kernel runs single-CTA tcgen05 MMAs with an online softmax and
+ * takes its work items from a counter the library keeps per (device, stream), so
+ * calls on different streams may overlap; the first call on a stream allocates
+ * that counter (8 bytes).  CEB_ATTN_MMA=1 in the environment selects the mma.sync
+ * kernel, CEB_ATTN_TC=1 the tcgen05 CTA-pair kernel (sequences of up to 512
+ * tokens).  Asynchronous on `stream`; device-side failures surface through
  * ceb_sync_check.
  */
 CEB_API int ceb_attention_forward(const void* d_qkv, int n_rows, const int32_t* d_cu_seqlens, int n_seqs, int max_len,

@@ -126,3 +126,29 @@ def test_error_words_are_per_device(attn_impl):
         with pytest.raises(binding.CrispEmbedError, match=r"\(5\)"):
             binding.sync_check()
         binding.sync_check()
+
+
+def test_calls_on_two_streams_overlap(cuda):
+    """The operator entry keeps one work-item counter per (device, stream): launches on
+    two streams that overlap on the GPU give the bits the same calls give one at a time."""
+    import torch
+    from crispembed_b200 import binding
+    binding.load_library()
+    cases = []
+    for lens, seed in (([300, 511, 64, 200, 17], 11), ([128, 450, 33, 257], 12)):
+        qkv, cu, _ = _qkv(lens, 12, seed=seed)
+        cases.append((torch.from_numpy(qkv).to(cuda), torch.from_numpy(cu).to(cuda), max(lens)))
+    ref = [binding.attention(q, c, 12, max_len=m) for q, c, m in cases]
+    torch.cuda.synchronize()
+    binding.sync_check()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    got = [[], []]
+    for _ in range(4):
+        for k, ((q, c, m), s) in enumerate(zip(cases, streams)):
+            with torch.cuda.stream(s):
+                got[k].append(binding.attention(q, c, 12, max_len=m, stream=s.cuda_stream))
+    torch.cuda.synchronize()
+    binding.sync_check()
+    for k in range(2):
+        for o in got[k]:
+            assert torch.equal(o, ref[k])
