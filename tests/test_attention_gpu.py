@@ -19,7 +19,9 @@ LEN_SETS = [
     [128, 129, 255, 256, 257],
     [300, 511, 512, 7, 64],
     [450, 200, 256, 30, 385, 193],
-    [600, 40],  # longest > 512: the mma.sync kernel
+    [600, 40],  # longest > 512: the CTA-pair kernel falls back to mma.sync
+    [1500, 130],  # many 128-key chunks per item
+    [1] * 150 + [3, 129],  # many one-token sequences: mostly empty query tiles
 ]
 
 
