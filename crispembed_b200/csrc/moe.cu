@@ -420,6 +420,170 @@ __global__ void __launch_bounds__(RT_WARPS * 32, Q8 ? RT_MIN_BLOCKS : 2)
     }
 }
 
+// F32 router over activations in memory, for 8 < E <= 32 (E = 32,
+// d = 1024): the router product as a register-blocked SIMT GEMM.  A CTA of 8 warps keeps
+// the router rows in shared memory ([E][d + 4] fp32) and takes 512-token super-blocks (eight
+// histogram blocks); each warp owns 64 tokens, staged in k-chunks as fp32 in its shared
+// tile while the next chunk's loads are in flight.  Lane (tg, eg) = (lane / 4, lane % 4)
+// computes tokens tg + 8i (i < 8) x experts eg + 4j (j < 8): per 4 k, 8 + 8 sixteen-byte
+// shared reads (strided rows: no bank conflicts) feed 256 FMAs.  Each logit is summed in
+// k order.  Softmax, top-K and counts as in route_rows_kernel (group_route, 4 tokens per
+// pass from the logits transposed through shared memory).
+constexpr int RF_WARPS = 8, RF_TOK = 64, RF_XLD_PAD = 4, RF_LLD = 33;
+constexpr int RF_SUPER = RF_WARPS * RF_TOK;  // tokens per CTA pass: 8 histogram blocks
+static_assert(RF_SUPER % CHUNK == 0 && RF_TOK % CHUNK == 0, "warps and super-blocks hold whole histogram blocks");
+template <typename T>
+__host__ __device__ constexpr int rf_kc() { return sizeof(T) == 4 ? 16 : 32; }  // k per chunk: 8 sixteen-byte pieces per lane
+template <typename T>
+__host__ __device__ constexpr int rf_xld() { return rf_kc<T>() + RF_XLD_PAD; }
+template <typename T>
+inline size_t route_f32_smem_bytes(int d, int E) {
+    const size_t tile = (size_t)RF_TOK * (rf_xld<T>() > RF_LLD ? rf_xld<T>() : RF_LLD) * 4;
+    return (size_t)E * (d + 4) * 4 + (size_t)RF_WARPS * tile + (size_t)(RF_SUPER / CHUNK) * MAXE * 4;
+}
+
+template <typename T>
+CEB_DEV void rf_cvt8(uint4 raw, float (&f)[8]);
+template <>
+CEB_DEV void rf_cvt8<__nv_bfloat16>(uint4 raw, float (&f)[8]) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+template <>
+CEB_DEV void rf_cvt8<__half>(uint4 raw, float (&f)[8]) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+    }
+}
+
+// One warp's RF_TOK token rows x KC columns as raw 16-byte pieces: lane l holds pieces
+// l, l + 32, ... of the (row, piece) grid (rows past T are zero).
+template <typename T>
+struct RfStage {
+    static constexpr int KC = rf_kc<T>(), XLD = rf_xld<T>();
+    static constexpr int PIECE = 16 / (int)sizeof(T);  // elements per 16-byte piece
+    static constexpr int PER_ROW = KC / PIECE;         // pieces per row
+    static constexpr int N = RF_TOK * PER_ROW / 32;    // pieces per lane
+    uint4 raw[N];
+    CEB_DEV void load(const T* __restrict__ x, int d, int t0, int T_tokens, int k0, int lane) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int p = lane + 32 * i, r = p / PER_ROW, c = (p % PER_ROW) * PIECE;
+            raw[i] = t0 + r < T_tokens ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + r) * d + k0 + c))
+                                       : make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    CEB_DEV void store(float* xs, int lane) const {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int p = lane + 32 * i, r = p / PER_ROW, c = (p % PER_ROW) * PIECE;
+            float* dst = xs + r * XLD + c;
+            if constexpr (sizeof(T) == 4) {
+                *reinterpret_cast<uint4*>(dst) = raw[i];
+            } else {
+                float f[8];
+                rf_cvt8<T>(raw[i], f);
+                *reinterpret_cast<float4*>(dst) = make_float4(f[0], f[1], f[2], f[3]);
+                *reinterpret_cast<float4*>(dst + 4) = make_float4(f[4], f[5], f[6], f[7]);
+            }
+        }
+    }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(RF_WARPS * 32, 1)
+    route_f32_tile_kernel(const T* __restrict__ x, int T_tokens, int d, int nblk, int E, int K,
+                          const float* __restrict__ rw, int32_t* __restrict__ ids, float* __restrict__ wts,
+                          float* __restrict__ logits_out, int32_t* __restrict__ block_counts) {
+    constexpr int KC = rf_kc<T>(), XLD = rf_xld<T>();
+    constexpr int TILE = RF_TOK * (XLD > RF_LLD ? XLD : RF_LLD);
+    extern __shared__ __align__(16) uint8_t sm[];
+    float* wT = reinterpret_cast<float*>(sm);            // [E][d + 4]
+    float* xs_all = wT + (size_t)E * (d + 4);            // [warps][TILE]
+    int* cnt = reinterpret_cast<int*>(xs_all + RF_WARPS * TILE);  // [8][MAXE]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tg = lane >> 2, eg = lane & 3;
+    for (int i = threadIdx.x; i < E * d / 4; i += blockDim.x) {
+        const int e = (i * 4) / d, k = i * 4 - e * d;
+        *reinterpret_cast<float4*>(wT + (size_t)e * (d + 4) + k) = __ldg(reinterpret_cast<const float4*>(rw) + i);
+    }
+    float* xs = xs_all + warp * TILE;
+    const int nsb = RF_SUPER / CHUNK;
+    const int n_super = (nblk + nsb - 1) / nsb;
+    for (int sb = blockIdx.x; sb < n_super; sb += gridDim.x) {
+        for (int i = threadIdx.x; i < nsb * MAXE; i += blockDim.x) cnt[i] = 0;
+        __syncthreads();  // (also: the router rows are staged before the first pass)
+        const int t0 = sb * RF_SUPER + warp * RF_TOK;
+        if (t0 < T_tokens) {
+            float acc[8][8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+            RfStage<T> st;
+            st.load(x, d, t0, T_tokens, 0, lane);
+            for (int k0 = 0; k0 < d; k0 += KC) {
+                __syncwarp();
+                st.store(xs, lane);
+                __syncwarp();
+                if (k0 + KC < d) st.load(x, d, t0, T_tokens, k0 + KC, lane);
+#pragma unroll
+                for (int kk = 0; kk < KC; kk += 4) {
+                    float4 xv[8], wv[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(xs + (tg + 8 * i) * XLD + kk);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int e = eg + 4 * j < E ? eg + 4 * j : 0;
+                        wv[j] = *reinterpret_cast<const float4*>(wT + (size_t)e * (d + 4) + k0 + kk);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            acc[i][j] = fmaf(xv[i].x, wv[j].x, acc[i][j]);
+                            acc[i][j] = fmaf(xv[i].y, wv[j].y, acc[i][j]);
+                            acc[i][j] = fmaf(xv[i].z, wv[j].z, acc[i][j]);
+                            acc[i][j] = fmaf(xv[i].w, wv[j].w, acc[i][j]);
+                        }
+                }
+            }
+            // logits [token][expert] through the warp's tile, then 4 tokens per routing pass
+            __syncwarp();
+            float* lg = xs;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) lg[(tg + 8 * i) * RF_LLD + eg + 4 * j] = acc[i][j];
+            __syncwarp();
+            const int tt_l = lane >> 3, el = lane & 7;
+            for (int g = 0; g < RF_TOK; g += RT_GROUP) {
+                const int tl = g + tt_l;
+                float lgv[RT_MAXJ];
+#pragma unroll
+                for (int j = 0; j < RT_MAXJ; ++j) lgv[j] = el + 8 * j < E ? lg[tl * RF_LLD + el + 8 * j] : -INFINITY;
+                const int t = t0 + tl;
+                group_route(lgv, E, K, t < T_tokens, (size_t)t, el, ids, wts, logits_out,
+                            cnt + ((warp * RF_TOK + tl) / CHUNK) * MAXE);
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < nsb * E; i += blockDim.x) {
+            const int b = sb * nsb + i / E;
+            if (b < nblk) block_counts[(size_t)b * E + i % E] = cnt[(i / E) * MAXE + i % E];
+        }
+        __syncthreads();
+    }
+}
+
 // Expert offsets (exclusive scan of the totals) and, per histogram block, the
 // first output row of each expert.  Warp w owns a run of consecutive histogram
 // blocks and lane l the experts l, l + 32, ...: every load and store of a block's
@@ -771,10 +935,46 @@ int launch_route_rows_t(const Rows& rows, int T, int E, int K, const uint8_t* rw
     return 0;
 }
 
+template <class Rows>
+struct ActRowsType {
+    using type = void;
+};
+template <typename T, int NV>
+struct ActRowsType<ActRows<T, NV>> {
+    using type = T;
+};
+
+// The tiled F32 router (route_f32_tile_kernel) for activations in memory; 1 when the shape
+// is not its own (nothing launched).
+template <typename T>
+int launch_route_f32_tile(const T* x, int T_tokens, int d, int E, int K, const float* rw, const ceb_moe_ws& ws,
+                          float* logits_out, cudaStream_t st) {
+    const size_t smem = route_f32_smem_bytes<T>(d, E);
+    if (E <= 8 || E > 8 * RT_MAXJ || d % rf_kc<T>() || smem > 220 * 1024) return 1;
+    auto kern = route_f32_tile_kernel<T>;
+    if (int rc = ceb_func_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
+    const int nblk = (T_tokens + CHUNK - 1) / CHUNK;
+    const int n_super = (nblk + RF_SUPER / CHUNK - 1) / (RF_SUPER / CHUNK);
+    const int grid = std::min(n_super, ceb_num_sms());
+    CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
+               kern<<<grid, RF_WARPS * 32, smem, st>>>(x, T_tokens, d, nblk, E, K, rw, ws.ids, ws.wts, logits_out,
+                                                       ws.block_counts));
+    CEB_CUDA_OK(cudaGetLastError());
+    return 0;
+}
+
 template <int NV, class Rows>
 int launch_route_rows(const Rows& rows, int T, int E, int K, int rtype, const uint8_t* rw, const ceb_moe_ws& ws,
                       float* logits_out, cudaStream_t st) {
     if (rtype == CEB_GGML_Q8_0) return launch_route_rows_t<NV, true>(rows, T, E, K, rw, ws, logits_out, st);
+    using AT = typename ActRowsType<Rows>::type;
+    if constexpr (!std::is_void<AT>::value) {
+        if (T > 0) {
+            const int rc = launch_route_f32_tile<AT>(rows.x, T, NV * 128, E, K, reinterpret_cast<const float*>(rw), ws,
+                                                     logits_out, st);
+            if (rc != 1) return rc;
+        }
+    }
     return launch_route_rows_t<NV, false>(rows, T, E, K, rw, ws, logits_out, st);
 }
 

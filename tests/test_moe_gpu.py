@@ -130,6 +130,30 @@ def test_moe_on_two_devices_of_one_process():
             assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("E", [16, 32])
+def test_f32_router_tile_input_dtypes(cuda, oracle, E):
+    """F32 routers with 8 < E <= 32 over activations in memory run the tiled router kernel:
+    its logits are the same bits for fp32, fp16 and bf16 inputs holding the same values, and
+    match the oracle's F32 router."""
+    import dataclasses
+    inp = synth.make_moe_op_inputs(300, d=512, n_experts=E, top_k=4, ffn=256, wtype=GGML_Q8_0,
+                                   router_wtype=GGML_F32, zipf_s=None, seed=4, with_bias=False)
+    # values every input type holds exactly: bf16-representable and zero below fp16's normal range
+    x = inp.x.copy()
+    x[np.abs(x) < 2.0 ** -14] = 0.0
+    inp = dataclasses.replace(inp, x=x)
+    res = {dt: _run(cuda, inp, x_dtype=dt)[0] for dt in ("bf16", "f32", "f16")}
+    for dt in ("f32", "f16"):
+        assert np.array_equal(res[dt][4], res["bf16"][4])  # logits
+        assert np.array_equal(res[dt][1], res["bf16"][1])  # ids
+    _, rids, _, rlg = oracle.moe_ffn(inp.x, inp.n_experts, inp.top_k, inp.ffn, inp.router_wtype, inp.router_raw,
+                                     inp.wtype, inp.fc1_raw, inp.fc2_raw, inp.bias, oracle.GGML)
+    lg, ids = res["bf16"][4], res["bf16"][1]
+    assert np.allclose(lg, rlg, rtol=1e-5, atol=1e-5), np.abs(lg - rlg).max()
+    sure = _kth_gap(rlg, inp.top_k) > 1e-4
+    assert np.array_equal(ids[sure], rids[sure])
+
+
 @pytest.mark.parametrize("dtype", ["f32", "f16"])
 def test_moe_input_dtypes(cuda, oracle, dtype):
     inp = synth.make_moe_op_inputs(96, d=256, n_experts=4, top_k=2, ffn=512, wtype=GGML_Q8_0,
