@@ -4,11 +4,13 @@
 // of the reference: softmax(Q K^T / sqrt(head_dim)) V per head over the tokens of
 // one sequence, no causal mask) for head_dim 64 and any sequence length.
 //
-// Persistent CTAs (two per SM) loop over items = (sequence, head, 128-query tile),
-// longest sequences first;
-// the TMA warp loads the next item's Q (two Q buffers) and first K / V chunks while
-// the current item finishes, and every barrier phase follows one chunk counter that
-// runs across the items of a CTA.  Keys stream in chunks of 128:
+// Persistent CTAs (two per SM) take items = (sequence, head, 128-query tile) from a
+// device counter, so a CTA that drew short items draws more (the last CTA to finish
+// returns the counter to zero for the next launch); the TMA warp hands each item index
+// to the other roles through a small ring in shared memory, loads the next item's Q (two
+// Q buffers) and first K / V chunks while the current item finishes, and every barrier
+// phase follows one chunk counter that runs across the items of a CTA.  Keys stream in
+// chunks of 128:
 //   S = Q K^T   tcgen05.mma.cta_group::1, M = 128 queries, N = 128 keys, fp32 S in
 //               TMEM; Q and the K chunk by TMA (128-byte swizzle, K-major).
 //   softmax     one thread per query row (4 warps, one per TMEM lane quadrant):
@@ -19,7 +21,8 @@
 //               The max used for the exponentials is raised -- and O rescaled in
 //               TMEM -- only when the true max exceeds it by more than 2^2, so
 //               exponents stay <= 2 and P <= 4.  Row sums as fp16 pair sums
-//               widened to fp32 per chunk.
+//               widened to fp32 per chunk.  No exponentials for 32-key pieces past
+//               the sequence (P = 0 there) or for warps whose rows all lie past it.
 //   O = P V     TS form: A = P from TMEM, B = the V chunk MN-major (the same
 //               128-byte-swizzled TMA image as K), O (fp32) in TMEM; divided by
 //               the row sum at the end and stored fp16.
