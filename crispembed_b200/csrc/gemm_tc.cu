@@ -569,18 +569,21 @@ struct Smem {
 
 // Shared-memory plan and barrier indices for PS A+B stages and PR raw weight stages
 // (PR = 0: fp16 weights loaded by TMA, no raw stage).
-template <int PS_, int PR_, int NSLOT_>
+template <int PS_, int PR_, int NSLOT_, int KS_ = 1>
 struct Lay {
     static constexpr int PS = PS_, PR = PR_;
+    static constexpr int KS = KS_;                              // 64-wide K atoms per A+B stage
+    static constexpr int STAGE_T = KS * STAGE;
     static constexpr int NSLOT = NSLOT_;                        // staging slots per epilogue warp
     static constexpr int STAGING = 4 * EPI_WG * NSLOT * SLOT;
     static constexpr int NB = 2 * PS + 4 + 1 + 2 * PR + PS + 2;
     static constexpr int SIG_BYTES = (PS + 2 + 1) * SIG;  // sinks for FULL[s], ACC_EMPTY[b] + one source
-    static constexpr size_t SMEM = 1024 + (size_t)PS * STAGE + (size_t)PR * RAW_STAGE + STAGING + SIG_BYTES +
+    static constexpr size_t SMEM = 1024 + (size_t)PS * STAGE_T + (size_t)PR * RAW_STAGE + STAGING + SIG_BYTES +
                                    NB * 8 + 16 + 3 * (MAXG + 1) * 4;
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static_assert(PR % DEQ_WG == 0, "raw stages must map to one dequant warpgroup each");
-    static_assert((PS * STAGE + PR * RAW_STAGE) % 1024 == 0, "staging slots must stay 1024-byte aligned");
+    static_assert((PS * STAGE_T + PR * RAW_STAGE) % 1024 == 0, "staging slots must stay 1024-byte aligned");
+    static_assert(KS == 1 || PR == 0, "several K atoms per stage only with fp16 planes");
 
     static CEB_DEV int B_FULL(int s) { return s; }
     static CEB_DEV int B_EMPTY(int s) { return PS + s; }
@@ -596,7 +599,7 @@ struct Lay {
         Smem s;
         uintptr_t p = (reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023);
         s.stages = reinterpret_cast<uint8_t*>(p);
-        p += (size_t)PS * STAGE;
+        p += (size_t)PS * STAGE_T;
         s.raw = reinterpret_cast<uint8_t*>(p);
         p += (size_t)PR * RAW_STAGE;
         s.staging = reinterpret_cast<uint8_t*>(p);
@@ -614,15 +617,24 @@ struct Lay {
         return s;
     }
 };
+// fp16 planes: stages of two 64-wide K atoms (64 KB: one barrier round trip per 128 K),
+// three of them, one staging slot per epilogue warp.  Measured at M = 70,825 against five
+// one-atom stages with two slots: qkv 1151 -> 1232, attention-out 1046 -> 1108, fc1 + GELU
+// 1044 -> 1057, fc2 1242 -> 1314 TFLOP/s; two two-atom stages with two slots lose on all
+// but fc1.
 #ifndef CEB_PAIR_PS_F16
-#define CEB_PAIR_PS_F16 5
+#define CEB_PAIR_PS_F16 3
 #endif
 #ifndef CEB_PAIR_SLOTS_F16
-#define CEB_PAIR_SLOTS_F16 2
+#define CEB_PAIR_SLOTS_F16 1
+#endif
+#ifndef CEB_PAIR_KS_F16
+#define CEB_PAIR_KS_F16 2
 #endif
 // quantized weights: 4 A+B stages + 4 raw stages; fp16 weights: the raw bytes become more A+B stages
 template <int FMT>
-using LayOf = Lay<FMT == CEB_W_F16 ? CEB_PAIR_PS_F16 : 4, FMT == CEB_W_F16 ? 0 : 4, FMT == CEB_W_F16 ? CEB_PAIR_SLOTS_F16 : 1>;
+using LayOf = Lay<FMT == CEB_W_F16 ? CEB_PAIR_PS_F16 : 4, FMT == CEB_W_F16 ? 0 : 4, FMT == CEB_W_F16 ? CEB_PAIR_SLOTS_F16 : 1,
+                  FMT == CEB_W_F16 ? CEB_PAIR_KS_F16 : 1>;
 
 struct Tile {
     int g, fp, row0, rows;  // group, feature-pair tile, first token of the pair tile, tokens in it (<= 256)
@@ -748,8 +760,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairWarps<FMT>::THRE
     auto wait_cl = [&](int i, uint32_t parity, int code) {
         return mbar_wait_cluster(bar(i), parity, abort, a.err, code | ((i + 1) << 16));
     };
-    auto x_stage = [&](int s) { return SH.stages + (size_t)s * STAGE; };
-    auto w_stage = [&](int s) { return SH.stages + (size_t)s * STAGE + X_BYTES; };
+    constexpr int KS = L::KS;  // 64-wide K atoms per stage: stage s holds KS activation atoms, then KS weight atoms
+    const int nst = nkb / KS;  // stages per tile
+    auto x_stage = [&](int s) { return SH.stages + (size_t)s * L::STAGE_T; };
+    auto w_stage = [&](int s) { return SH.stages + (size_t)s * L::STAGE_T + KS * X_BYTES; };
     auto wblock = [&](const Tile& ti, int kb) {
         const int ft = 2 * ti.fp + (int)rank;  // this CTA's 128-feature weight tile
         return w.q + (((size_t)ti.g * n_ftiles + ft) * nkb + kb) * (size_t)w.blk_bytes;
@@ -762,15 +776,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairWarps<FMT>::THRE
             bool ok = true;
             for (int t = pair_id; t < total && ok; t += n_pairs) {
                 const Tile ti = pair::decode(SH, G, n_fp, t);
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                for (int ks = 0; ks < nst; ++ks, ++it) {
                     const int s = it % PS;
                     if (!wait_at(L::B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(bar(L::B_FULL(s)), kTmaW ? 2 * (X_BYTES + W_BYTES) : 2 * X_BYTES + SIG);
-                    tma_load_2d_pair(smem_u32(x_stage(s)), &xmap, lead_bar(L::B_FULL(s)), kb * BK,
-                                     ti.row0 + TOK * (int)rank);
+                    if (leader)
+                        mbar_arrive_expect_tx(bar(L::B_FULL(s)), kTmaW ? 2 * KS * (X_BYTES + W_BYTES) : 2 * X_BYTES + SIG);
+#pragma unroll
+                    for (int a = 0; a < KS; ++a)
+                        tma_load_2d_pair(smem_u32(x_stage(s) + a * X_BYTES), &xmap, lead_bar(L::B_FULL(s)),
+                                         (ks * KS + a) * BK, ti.row0 + TOK * (int)rank);
                 }
             }
             if (!ok && leader) {  // let issued copies land before the CTA can exit
@@ -813,19 +830,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairWarps<FMT>::THRE
                 if (!wait_cl(L::B_ACC_EMPTY(ab), ((lt >> 1) & 1) ^ 1, CEB_DEVERR_TIMEOUT_MMA)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + (uint32_t)(ab * FEAT);
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                for (int ks = 0; ks < nst; ++ks, ++it) {
                     const int s = it % PS;
                     if (!wait_cl(L::B_FULL(s), (it / PS) & 1, CEB_DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw128(smem_u32(x_stage(s)));
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(w_stage(s)));
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        mma_pair_f16_ss(d_tmem, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
-                                        (kb | kk) != 0);
+                    for (int a = 0; a < KS; ++a) {
+                        const uint64_t adesc = smem_desc_sw128(smem_u32(x_stage(s) + a * X_BYTES));
+                        const uint64_t bdesc = smem_desc_sw128(smem_u32(w_stage(s) + a * W_BYTES));
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            mma_pair_f16_ss(d_tmem, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
+                                            (ks | a | kk) != 0);
+                    }
                     mma_pair_commit(bar(L::B_EMPTY(s)));
                     mma_pair_commit(mapa_shared(bar(L::B_EMPTY(s)), 1));
                 }
@@ -849,15 +869,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairWarps<FMT>::THRE
                 const Tile ti = pair::decode(SH, G, n_fp, t);
                 const int ft = 2 * ti.fp + (int)rank;
                 bool ok = true;
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                for (int ks = 0; ks < nst; ++ks, ++it) {
                     const int s = it % PS;
                     if (!wait_at(L::B_EMPTY(s), ((it / PS) & 1) ^ 1, CEB_DEVERR_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
                     // block (g, ft, kb) is rows [128 * index, +128) of the [blocks * 128, 64] fp16 view
-                    tma_load_2d_pair(smem_u32(w_stage(s)), &wmap, lead_bar(L::B_FULL(s)), 0,
-                                     (int)((((size_t)ti.g * n_ftiles + ft) * nkb + kb) * 128));
+#pragma unroll
+                    for (int a = 0; a < KS; ++a)
+                        tma_load_2d_pair(smem_u32(w_stage(s) + a * W_BYTES), &wmap, lead_bar(L::B_FULL(s)), 0,
+                                         (int)((((size_t)ti.g * n_ftiles + ft) * nkb + ks * KS + a) * 128));
                 }
                 if (!ok) break;
             }
@@ -1101,6 +1123,7 @@ static bool ceb_gemm_use_pairs(const ceb_wplane& w, const ceb_gemm_args& a) {
     }();
     if (forced_single) return false;
     if (w.n_out % pair::FEAT) return false;
+    if (w.format == CEB_W_F16 && (w.k / BK) % CEB_PAIR_KS_F16) return false;  // whole stages of K atoms
     if ((a.epi & CEB_EPI_BIAS) &&
         ((reinterpret_cast<uintptr_t>(a.bias) & 15) || (a.offsets && (a.bias_group_stride & 3))))
         return false;
