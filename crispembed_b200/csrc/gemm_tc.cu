@@ -964,44 +964,78 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairWarps<FMT>::THRE
                 // slots are used in turn; the store that last used this one has finished reading it
                 uint8_t* slot = SH.staging + (size_t)(ew * NSLOT + (int)(nstore % NSLOT)) * SLOT;
                 const uint32_t slot_u32 = smem_u32(slot);
-                if (full && nstore >= NSLOT) {
-                    if (lane == 0) bulk_wait_read<NSLOT - 1>();
-                    __syncwarp();
-                }
-                for (int h = 0; h < chunk_cols; h += 32) {
-                    uint32_t v[32];
-                    tmem_ld32(tmem + lane_addr + col0 + (uint32_t)(c0 + h), v);
-                    tmem_ld_wait();
-                    epi_math(v, bias ? bias + f_base + c0 + h : nullptr, gelu);
-                    const float* x = reinterpret_cast<const float*>(v);
-                    if (f16) {
-                        uint32_t p[16];
+                if (kTmaW && gelu && f16) {
+                    // fc1 + GELU: the chunk's TMEM loads and GELU run before the wait for the store
+                    // that last used this slot, so that store's read of shared memory hides behind
+                    // the math (+4.5 % at M = 70,825). Without GELU the math is short and the
+                    // branch below, which writes each 32-column half as soon as it is ready,
+                    // measured ~1 % faster.
+                    uint32_t p[32];  // the chunk's 64 columns as 32 packed fp16 pairs
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) p[j] = h2_as_u32(__floats2half2_rn(x[2 * j], x[2 * j + 1]));
-                        if (full) {  // 64 B = chunks 4*(h/32) .. +3 of the 128-B swizzled row
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t v[32];
+                        tmem_ld32(tmem + lane_addr + col0 + (uint32_t)(c0 + 32 * h), v);
+                        tmem_ld_wait();
+                        epi_math(v, bias ? bias + f_base + c0 + 32 * h : nullptr, true);
+                        const float* x = reinterpret_cast<const float*>(v);
 #pragma unroll
-                            for (int c = 0; c < 4; ++c) {
-                                const int cc = c + (h >> 3);
-                                *reinterpret_cast<uint4*>(slot + lane * 128 + ((cc ^ (lane & 7)) << 4)) =
-                                    make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
-                            }
-                        } else if (lane < lim) {
-                            uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) +
-                                                                (size_t)(row + lane) * a.ldo + f_base + c0 + h);
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) o[c] = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+                        for (int j = 0; j < 16; ++j) p[16 * h + j] = h2_as_u32(__floats2half2_rn(x[2 * j], x[2 * j + 1]));
+                    }
+                    if (full) {
+                        if (nstore >= NSLOT) {
+                            if (lane == 0) bulk_wait_read<NSLOT - 1>();
+                            __syncwarp();
                         }
-                    } else {
-                        if (full) {
 #pragma unroll
-                            for (int c = 0; c < 8; ++c)
-                                *reinterpret_cast<float4*>(slot + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-                                    make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
-                        } else if (lane < lim) {
-                            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) +
-                                                                  (size_t)(row + lane) * a.ldo + f_base + c0 + h);
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<uint4*>(slot + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                                make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+                    } else if (lane < lim) {
+                        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) +
+                                                            (size_t)(row + lane) * a.ldo + f_base + c0);
 #pragma unroll
-                            for (int c = 0; c < 8; ++c) o[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+                        for (int c = 0; c < 8; ++c) o[c] = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+                    }
+                } else {
+                    if (full && nstore >= NSLOT) {
+                        if (lane == 0) bulk_wait_read<NSLOT - 1>();
+                        __syncwarp();
+                    }
+                    for (int h = 0; h < chunk_cols; h += 32) {
+                        uint32_t v[32];
+                        tmem_ld32(tmem + lane_addr + col0 + (uint32_t)(c0 + h), v);
+                        tmem_ld_wait();
+                        epi_math(v, bias ? bias + f_base + c0 + h : nullptr, gelu);
+                        const float* x = reinterpret_cast<const float*>(v);
+                        if (f16) {
+                            uint32_t p[16];
+    #pragma unroll
+                            for (int j = 0; j < 16; ++j) p[j] = h2_as_u32(__floats2half2_rn(x[2 * j], x[2 * j + 1]));
+                            if (full) {  // 64 B = chunks 4*(h/32) .. +3 of the 128-B swizzled row
+    #pragma unroll
+                                for (int c = 0; c < 4; ++c) {
+                                    const int cc = c + (h >> 3);
+                                    *reinterpret_cast<uint4*>(slot + lane * 128 + ((cc ^ (lane & 7)) << 4)) =
+                                        make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+                                }
+                            } else if (lane < lim) {
+                                uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) +
+                                                                    (size_t)(row + lane) * a.ldo + f_base + c0 + h);
+    #pragma unroll
+                                for (int c = 0; c < 4; ++c) o[c] = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+                            }
+                        } else {
+                            if (full) {
+    #pragma unroll
+                                for (int c = 0; c < 8; ++c)
+                                    *reinterpret_cast<float4*>(slot + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                                        make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+                            } else if (lane < lim) {
+                                float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) +
+                                                                      (size_t)(row + lane) * a.ldo + f_base + c0 + h);
+    #pragma unroll
+                                for (int c = 0; c < 8; ++c) o[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+                            }
                         }
                     }
                 }
