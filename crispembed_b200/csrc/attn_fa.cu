@@ -330,9 +330,13 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM)
                 for (int pc = 0; pc < KC / 32; ++pc) {
                     if (!dead && pc < nv) {  // no exponentials for keys past the sequence
 #pragma unroll
-                        for (int t = 0; t < 32; t += 2)
-                            pk[pc][t >> 1] = ex2_h2(fmaf(__uint_as_float(v[pc][t]), scale_log2, nm),
-                                                    fmaf(__uint_as_float(v[pc][t + 1]), scale_log2, nm));
+                        for (int t = 0; t < 32; t += 2) {  // s * scale - max for two keys in one packed FMA
+                            float e0, e1;
+                            f2_unpack(f2_fma(f2_pack(__uint_as_float(v[pc][t]), __uint_as_float(v[pc][t + 1])),
+                                             f2_splat(scale_log2), f2_splat(nm)),
+                                      e0, e1);
+                            pk[pc][t >> 1] = ex2_h2(e0, e1);
+                        }
                     } else {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) pk[pc][j] = 0u;

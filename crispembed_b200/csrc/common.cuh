@@ -346,6 +346,34 @@ CEB_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 CEB_DEV uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 CEB_DEV __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one instruction, two round-to-nearest
+// results, each equal to the scalar operation's (no flush to zero, as the scalar code).
+struct f32x2 {
+    uint64_t v;
+};
+CEB_DEV f32x2 f2_pack(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
+    return r;
+}
+CEB_DEV f32x2 f2_splat(float a) { return f2_pack(a, a); }
+CEB_DEV void f2_unpack(f32x2 a, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(a.v)); }
+CEB_DEV f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+    return d;
+}
+CEB_DEV f32x2 f2_mul(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
+    return d;
+}
+CEB_DEV f32x2 f2_add(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
+    return d;
+}
+
 // Four int8 values -> two half2 holding d*q (each product rounded once to fp16).
 // q+128 is placed in the low mantissa byte of fp16 1024 (0x64xx), then 1152 is
 // subtracted exactly, leaving q as an fp16 integer.

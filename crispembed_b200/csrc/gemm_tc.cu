@@ -255,6 +255,35 @@ CEB_DEV float gelu_as(float x) {
     const float h = 0.5f * x;
     return fmaf(fabsf(h), erf_abs, h);                      // 0.5x + 0.5|x| erf(|x|/sqrt2)
 }
+// gelu_as on two values with packed fp32 arithmetic: the same operations in the same
+// order, so both results equal gelu_as's bit for bit. The polynomial is evaluated with
+// negated coefficients (Horner with round-to-nearest is odd in them), which yields
+// -p t without a separate negation; (x kE)^2 = (|x| kE)^2 exactly.
+CEB_DEV f32x2 gelu_as2(f32x2 x) {
+    constexpr float kZ = 0.70710678118654752f;
+    constexpr float kE = 0.84932180028801904f;
+    float x0, x1;
+    f2_unpack(x, x0, x1);
+    const f32x2 ax = f2_pack(fabsf(x0), fabsf(x1));
+    f32x2 t = f2_fma(f2_splat(0.3275911f * kZ), ax, f2_splat(1.0f));
+    {
+        float t0, t1;
+        f2_unpack(t, t0, t1);
+        t = f2_pack(rcp_approx(t0), rcp_approx(t1));
+    }
+    f32x2 p = f2_fma(f2_splat(-1.061405429f), t, f2_splat(1.453152027f));
+    p = f2_fma(p, t, f2_splat(-1.421413741f));
+    p = f2_fma(p, t, f2_splat(0.284496736f));
+    p = f2_fma(p, t, f2_splat(-0.254829592f));  // -p of gelu_as
+    const f32x2 u = f2_mul(x, f2_splat(kE));
+    const f32x2 s = f2_mul(u, u);
+    float s0, s1;
+    f2_unpack(s, s0, s1);
+    const f32x2 e = f2_pack(ex2_approx(-s0), ex2_approx(-s1));
+    const f32x2 erf_abs = f2_fma(f2_mul(p, t), e, f2_splat(1.0f));
+    const f32x2 h = f2_mul(x, f2_splat(0.5f));
+    return f2_fma(f2_mul(ax, f2_splat(0.5f)), erf_abs, h);
+}
 
 template <int FMT>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -655,17 +684,35 @@ CEB_DEV Tile decode(const Smem& S_, int G, int n_fp, int t) {
 
 // one 32-row x 32-column fp32 accumulator block -> bias (+GELU), in place: the
 // accumulator bits become the float results (no second 32-register array)
+// PACKED: fp32 pairs, half the instructions of the scalar form and the same results
+// (the fp16-plane kernel; the quantized-plane kernels, capped at 96 registers a thread,
+// keep the scalar form, which needs fewer live registers)
+template <bool PACKED>
 CEB_DEV void epi_math(uint32_t (&v)[32], const float* bias, bool gelu) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
         float4 b = bias ? __ldg(reinterpret_cast<const float4*>(bias + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        float x0 = __uint_as_float(v[j]) + b.x, x1 = __uint_as_float(v[j + 1]) + b.y;
-        float x2 = __uint_as_float(v[j + 2]) + b.z, x3 = __uint_as_float(v[j + 3]) + b.w;
-        if (gelu) {
-            x0 = gelu_as(x0);
-            x1 = gelu_as(x1);
-            x2 = gelu_as(x2);
-            x3 = gelu_as(x3);
+        float x0, x1, x2, x3;
+        if constexpr (PACKED) {
+            f32x2 xa = f2_add(f2_pack(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), f2_pack(b.x, b.y));
+            f32x2 xb = f2_add(f2_pack(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])), f2_pack(b.z, b.w));
+            if (gelu) {
+                xa = gelu_as2(xa);
+                xb = gelu_as2(xb);
+            }
+            f2_unpack(xa, x0, x1);
+            f2_unpack(xb, x2, x3);
+        } else {
+            x0 = __uint_as_float(v[j]) + b.x;
+            x1 = __uint_as_float(v[j + 1]) + b.y;
+            x2 = __uint_as_float(v[j + 2]) + b.z;
+            x3 = __uint_as_float(v[j + 3]) + b.w;
+            if (gelu) {
+                x0 = gelu_as(x0);
+                x1 = gelu_as(x1);
+                x2 = gelu_as(x2);
+                x3 = gelu_as(x3);
+            }
         }
         v[j] = __float_as_uint(x0);
         v[j + 1] = __float_as_uint(x1);
@@ -976,7 +1023,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairWarps<FMT>::THRE
                         uint32_t v[32];
                         tmem_ld32(tmem + lane_addr + col0 + (uint32_t)(c0 + 32 * h), v);
                         tmem_ld_wait();
-                        epi_math(v, bias ? bias + f_base + c0 + 32 * h : nullptr, true);
+                        epi_math<true>(v, bias ? bias + f_base + c0 + 32 * h : nullptr, true);
                         const float* x = reinterpret_cast<const float*>(v);
 #pragma unroll
                         for (int j = 0; j < 16; ++j) p[16 * h + j] = h2_as_u32(__floats2half2_rn(x[2 * j], x[2 * j + 1]));
@@ -1005,7 +1052,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairWarps<FMT>::THRE
                         uint32_t v[32];
                         tmem_ld32(tmem + lane_addr + col0 + (uint32_t)(c0 + h), v);
                         tmem_ld_wait();
-                        epi_math(v, bias ? bias + f_base + c0 + h : nullptr, gelu);
+                        epi_math<kTmaW>(v, bias ? bias + f_base + c0 + h : nullptr, gelu);
                         const float* x = reinterpret_cast<const float*>(v);
                         if (f16) {
                             uint32_t p[16];
