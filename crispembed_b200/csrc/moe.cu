@@ -420,18 +420,17 @@ __global__ void __launch_bounds__(RT_WARPS * 32, Q8 ? RT_MIN_BLOCKS : 2)
     }
 }
 
-// F32 router over activations in memory, for 8 < E <= 32 (E = 32,
+// F32 router over activations in memory, for 8 < E <= 32 (the wide-routing shape E = 32,
 // d = 1024): the router product as a register-blocked SIMT GEMM.  A CTA of 8 warps keeps
-// the router rows in shared memory ([E][d + 4] fp32) and takes 512-token super-blocks (eight
-// histogram blocks); each warp owns 64 tokens, staged in k-chunks as fp32 in its shared
+// the router rows in shared memory ([E][d + 4] fp32); each warp takes 64-token histogram
+// blocks in turn (one block = one warp's tile), staged in k-chunks as fp32 in its shared
 // tile while the next chunk's loads are in flight.  Lane (tg, eg) = (lane / 4, lane % 4)
 // computes tokens tg + 8i (i < 8) x experts eg + 4j (j < 8): per 4 k, 8 + 8 sixteen-byte
 // shared reads (strided rows: no bank conflicts) feed 256 FMAs.  Each logit is summed in
 // k order.  Softmax, top-K and counts as in route_rows_kernel (group_route, 4 tokens per
 // pass from the logits transposed through shared memory).
 constexpr int RF_WARPS = 8, RF_TOK = 64, RF_XLD_PAD = 4, RF_LLD = 33;
-constexpr int RF_SUPER = RF_WARPS * RF_TOK;  // tokens per CTA pass: 8 histogram blocks
-static_assert(RF_SUPER % CHUNK == 0 && RF_TOK % CHUNK == 0, "warps and super-blocks hold whole histogram blocks");
+static_assert(RF_TOK == CHUNK, "one warp's token tile is one histogram block");
 template <typename T>
 __host__ __device__ constexpr int rf_kc() { return sizeof(T) == 4 ? 16 : 32; }  // k per chunk: 8 sixteen-byte pieces per lane
 template <typename T>
@@ -439,7 +438,7 @@ __host__ __device__ constexpr int rf_xld() { return rf_kc<T>() + RF_XLD_PAD; }
 template <typename T>
 inline size_t route_f32_smem_bytes(int d, int E) {
     const size_t tile = (size_t)RF_TOK * (rf_xld<T>() > RF_LLD ? rf_xld<T>() : RF_LLD) * 4;
-    return (size_t)E * (d + 4) * 4 + (size_t)RF_WARPS * tile + (size_t)(RF_SUPER / CHUNK) * MAXE * 4;
+    return (size_t)E * (d + 4) * 4 + (size_t)RF_WARPS * tile + (size_t)RF_WARPS * MAXE * 4;
 }
 
 template <typename T>
@@ -516,13 +515,16 @@ __global__ void __launch_bounds__(RF_WARPS * 32, 1)
         *reinterpret_cast<float4*>(wT + (size_t)e * (d + 4) + k) = __ldg(reinterpret_cast<const float4*>(rw) + i);
     }
     float* xs = xs_all + warp * TILE;
-    const int nsb = RF_SUPER / CHUNK;
-    const int n_super = (nblk + nsb - 1) / nsb;
-    for (int sb = blockIdx.x; sb < n_super; sb += gridDim.x) {
-        for (int i = threadIdx.x; i < nsb * MAXE; i += blockDim.x) cnt[i] = 0;
-        __syncthreads();  // (also: the router rows are staged before the first pass)
-        const int t0 = sb * RF_SUPER + warp * RF_TOK;
-        if (t0 < T_tokens) {
+    int* wcnt = cnt + warp * MAXE;  // this warp's histogram block
+    __syncthreads();                // the router rows are staged
+    // Warp-major order: histogram block b goes to warp b / gridDim.x % RF_WARPS of CTA
+    // b % gridDim.x, so a partial last round spreads over every SM (each gets its share
+    // of blocks to within one) instead of leaving whole CTAs idle.
+    for (int b = warp * gridDim.x + blockIdx.x; b < nblk; b += gridDim.x * RF_WARPS) {
+        for (int i = lane; i < MAXE; i += 32) wcnt[i] = 0;
+        __syncwarp();
+        const int t0 = b * RF_TOK;
+        {
             float acc[8][8];
 #pragma unroll
             for (int i = 0; i < 8; ++i)
@@ -571,16 +573,12 @@ __global__ void __launch_bounds__(RF_WARPS * 32, 1)
 #pragma unroll
                 for (int j = 0; j < RT_MAXJ; ++j) lgv[j] = el + 8 * j < E ? lg[tl * RF_LLD + el + 8 * j] : -INFINITY;
                 const int t = t0 + tl;
-                group_route(lgv, E, K, t < T_tokens, (size_t)t, el, ids, wts, logits_out,
-                            cnt + ((warp * RF_TOK + tl) / CHUNK) * MAXE);
+                group_route(lgv, E, K, t < T_tokens, (size_t)t, el, ids, wts, logits_out, wcnt);
             }
         }
-        __syncthreads();
-        for (int i = threadIdx.x; i < nsb * E; i += blockDim.x) {
-            const int b = sb * nsb + i / E;
-            if (b < nblk) block_counts[(size_t)b * E + i % E] = cnt[(i / E) * MAXE + i % E];
-        }
-        __syncthreads();
+        __syncwarp();
+        for (int e = lane; e < E; e += 32) block_counts[(size_t)b * E + e] = wcnt[e];
+        __syncwarp();  // read before the next block clears it
     }
 }
 
@@ -954,8 +952,7 @@ int launch_route_f32_tile(const T* x, int T_tokens, int d, int E, int K, const f
     auto kern = route_f32_tile_kernel<T>;
     if (int rc = ceb_func_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
     const int nblk = (T_tokens + CHUNK - 1) / CHUNK;
-    const int n_super = (nblk + RF_SUPER / CHUNK - 1) / (RF_SUPER / CHUNK);
-    const int grid = std::min(n_super, ceb_num_sms());
+    const int grid = std::min((nblk + RF_WARPS - 1) / RF_WARPS, ceb_num_sms());
     CEB_LAUNCH(CEB_PROF_ROUTE, st, 0.0, 0.0,
                kern<<<grid, RF_WARPS * 32, smem, st>>>(x, T_tokens, d, nblk, E, K, rw, ws.ids, ws.wts, logits_out,
                                                        ws.block_counts));

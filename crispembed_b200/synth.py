@@ -263,7 +263,6 @@ def _write_llama_naming(path: str, spec: ModelSpec, tokenizer=None) -> List[str]
 
 
 # ---------------------------------------------------------------------------
-# token-id batches (2, 4)# ---------------------------------------------------------------------------
 # token-id batches (2, 4)
 # ---------------------------------------------------------------------------
 
