@@ -119,6 +119,31 @@ def test_q8_0_dot_avx2_equals_scalar(oracle):
         assert np.float32(fast).tobytes() == np.float32(slow).tobytes(), trial
 
 
+def test_q8_0_matmul_blocked_equals_per_dot(oracle):
+    """The ggml-mode Q8_0 matmul (four dots at a time over two weight and two activation
+    rows) gives every output the bits of its own ceo_dot_q8_0 (+ bias), for odd and even
+    row counts and tile edges."""
+    import ctypes
+    from crispembed_b200.gguf_io import GGML_Q8_0
+    rng = np.random.default_rng(11)
+    L = oracle.lib()
+    up = ctypes.POINTER(ctypes.c_uint8)
+    for m_rows, n_out, k in ((1, 1, 32), (3, 5, 64), (33, 31, 96), (64, 66, 768), (37, 70, 256)):
+        w = quant.quantize_q8_0((rng.standard_normal((n_out, k)) * 0.05).astype(np.float32))
+        x = rng.standard_normal((m_rows, k)).astype(np.float32)
+        bias = rng.standard_normal(n_out).astype(np.float32)
+        got = oracle.matmul(GGML_Q8_0, w, n_out, k, x, oracle.GGML, bias)
+        wrows = np.ascontiguousarray(w).reshape(n_out, -1)
+        want = np.empty_like(got)
+        for m in range(m_rows):
+            a = np.ascontiguousarray(oracle.quant_act_q8_0(x[m]))
+            for n in range(n_out):
+                wr = np.ascontiguousarray(wrows[n])
+                s = np.float32(L.ceo_dot_q8_0(k, wr.ctypes.data_as(up), a.ctypes.data_as(up)))
+                want[m, n] = s + bias[n]
+        assert got.tobytes() == want.tobytes(), (m_rows, n_out, k)
+
+
 def test_q4_k_dot_avx2_equals_scalar(oracle):
     """The oracle's AVX2 Q4_K x Q8_K dot gives the scalar lane form's bits (random
     super-blocks with every 4-bit value, the 6-bit scale extremes and full-range Q8_K)."""
