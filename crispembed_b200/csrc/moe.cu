@@ -524,57 +524,55 @@ __global__ void __launch_bounds__(RF_WARPS * 32, 1)
         for (int i = lane; i < MAXE; i += 32) wcnt[i] = 0;
         __syncwarp();
         const int t0 = b * RF_TOK;
-        {
-            float acc[8][8];
+        float acc[8][8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-            RfStage<T> st;
-            st.load(x, d, t0, T_tokens, 0, lane);
-            for (int k0 = 0; k0 < d; k0 += KC) {
-                __syncwarp();
-                st.store(xs, lane);
-                __syncwarp();
-                if (k0 + KC < d) st.load(x, d, t0, T_tokens, k0 + KC, lane);
+            for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+        RfStage<T> st;
+        st.load(x, d, t0, T_tokens, 0, lane);
+        for (int k0 = 0; k0 < d; k0 += KC) {
+            __syncwarp();
+            st.store(xs, lane);
+            __syncwarp();
+            if (k0 + KC < d) st.load(x, d, t0, T_tokens, k0 + KC, lane);
 #pragma unroll
-                for (int kk = 0; kk < KC; kk += 4) {
-                    float4 xv[8], wv[8];
+            for (int kk = 0; kk < KC; kk += 4) {
+                float4 xv[8], wv[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(xs + (tg + 8 * i) * XLD + kk);
+                for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(xs + (tg + 8 * i) * XLD + kk);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int e = eg + 4 * j < E ? eg + 4 * j : 0;
+                    wv[j] = *reinterpret_cast<const float4*>(wT + (size_t)e * (d + 4) + k0 + kk);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        const int e = eg + 4 * j < E ? eg + 4 * j : 0;
-                        wv[j] = *reinterpret_cast<const float4*>(wT + (size_t)e * (d + 4) + k0 + kk);
+                        acc[i][j] = fmaf(xv[i].x, wv[j].x, acc[i][j]);
+                        acc[i][j] = fmaf(xv[i].y, wv[j].y, acc[i][j]);
+                        acc[i][j] = fmaf(xv[i].z, wv[j].z, acc[i][j]);
+                        acc[i][j] = fmaf(xv[i].w, wv[j].w, acc[i][j]);
                     }
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            acc[i][j] = fmaf(xv[i].x, wv[j].x, acc[i][j]);
-                            acc[i][j] = fmaf(xv[i].y, wv[j].y, acc[i][j]);
-                            acc[i][j] = fmaf(xv[i].z, wv[j].z, acc[i][j]);
-                            acc[i][j] = fmaf(xv[i].w, wv[j].w, acc[i][j]);
-                        }
-                }
             }
-            // logits [token][expert] through the warp's tile, then 4 tokens per routing pass
-            __syncwarp();
-            float* lg = xs;
+        }
+        // logits [token][expert] through the warp's tile, then 4 tokens per routing pass
+        __syncwarp();
+        float* lg = xs;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) lg[(tg + 8 * i) * RF_LLD + eg + 4 * j] = acc[i][j];
-            __syncwarp();
-            const int tt_l = lane >> 3, el = lane & 7;
-            for (int g = 0; g < RF_TOK; g += RT_GROUP) {
-                const int tl = g + tt_l;
-                float lgv[RT_MAXJ];
+            for (int j = 0; j < 8; ++j) lg[(tg + 8 * i) * RF_LLD + eg + 4 * j] = acc[i][j];
+        __syncwarp();
+        const int tt_l = lane >> 3, el = lane & 7;
+        for (int g = 0; g < RF_TOK; g += RT_GROUP) {
+            const int tl = g + tt_l;
+            float lgv[RT_MAXJ];
 #pragma unroll
-                for (int j = 0; j < RT_MAXJ; ++j) lgv[j] = el + 8 * j < E ? lg[tl * RF_LLD + el + 8 * j] : -INFINITY;
-                const int t = t0 + tl;
-                group_route(lgv, E, K, t < T_tokens, (size_t)t, el, ids, wts, logits_out, wcnt);
-            }
+            for (int j = 0; j < RT_MAXJ; ++j) lgv[j] = el + 8 * j < E ? lg[tl * RF_LLD + el + 8 * j] : -INFINITY;
+            const int t = t0 + tl;
+            group_route(lgv, E, K, t < T_tokens, (size_t)t, el, ids, wts, logits_out, wcnt);
         }
         __syncwarp();
         for (int e = lane; e < E; e += 32) block_counts[(size_t)b * E + e] = wcnt[e];
