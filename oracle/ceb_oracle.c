@@ -502,6 +502,62 @@ static float dot_q4_k(int64_t k, const uint8_t *w, const uint8_t *a, int use_sim
     return sumf;
 }
 
+#if defined(__AVX2__)
+/* Four Q4_K x Q8_K dots of one weight row against activation rows a[0..3]: per super-block
+ * the weight's scales, mins and 4-bit values are unpacked once and reused; each dot keeps
+ * exactly dot_q4_k's integer lanes and float operations in the same order. */
+static void dot_q4_k_1x4_avx2(int64_t nsb, const uint8_t *w, const uint8_t *const a[4], float out[4]) {
+    float sums[4][8] = {{0}}, sumf[4] = {0, 0, 0, 0};
+    const __m128i m4 = _mm_set1_epi8(0x0F);
+    for (int64_t b = 0; b < nsb; b++) {
+        const uint8_t *wb = w + b * Q4_K_BYTES, *sc = wb + 4, *qs = wb + 16;
+        int scs[8], mns[8];
+        for (int j = 0; j < 8; j++) q4k_scale_min(j, sc, &scs[j], &mns[j]);
+        __m256i acc[4] = {_mm256_setzero_si256(), _mm256_setzero_si256(), _mm256_setzero_si256(),
+                          _mm256_setzero_si256()};
+        for (int j = 0; j < 8; j++) {
+            const uint8_t *src = qs + 32 * (j >> 1);
+            __m128i b0 = _mm_loadu_si128((const __m128i *)src), b1 = _mm_loadu_si128((const __m128i *)(src + 16));
+            if (j & 1) {
+                b0 = _mm_srli_epi16(b0, 4);
+                b1 = _mm_srli_epi16(b1, 4);
+            }
+            const __m256i w0 = _mm256_cvtepu8_epi16(_mm_and_si128(b0, m4));
+            const __m256i w1 = _mm256_cvtepu8_epi16(_mm_and_si128(b1, m4));
+            const __m256i scj = _mm256_set1_epi32(scs[j]);
+            for (int r = 0; r < 4; r++) {
+                const int8_t *q8 = (const int8_t *)(a[r] + b * Q8_K_BYTES + 4);
+                const __m256i a0 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(q8 + 32 * j)));
+                const __m256i a1 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(q8 + 32 * j + 16)));
+                const __m256i t = _mm256_add_epi16(_mm256_mullo_epi16(w0, a0), _mm256_mullo_epi16(w1, a1));
+                const __m128i u = _mm_add_epi16(_mm256_castsi256_si128(t), _mm256_extracti128_si256(t, 1));
+                acc[r] = _mm256_add_epi32(acc[r], _mm256_mullo_epi32(_mm256_cvtepi16_epi32(u), scj));
+            }
+        }
+        const float dw = ceo_f16_to_f32(rd_u16(wb)), dminw = ceo_f16_to_f32(rd_u16(wb + 2));
+        for (int r = 0; r < 4; r++) {
+            const uint8_t *ab = a[r] + b * Q8_K_BYTES;
+            float ad;
+            memcpy(&ad, ab, 4);
+            int16_t bs[16];
+            memcpy(bs, ab + 4 + QK_K, sizeof bs);
+            int sumi = 0;
+            for (int j = 0; j < 16; j++) sumi += bs[j] * mns[j / 2];
+            int32_t aux32[8];
+            _mm256_storeu_si256((__m256i *)aux32, acc[r]);
+            const float d = dw * ad;
+            for (int l = 0; l < 8; l++) sums[r][l] += d * (float)aux32[l];
+            const float dmin = dminw * ad;
+            sumf[r] -= dmin * (float)sumi;
+        }
+    }
+    for (int r = 0; r < 4; r++) {
+        for (int l = 0; l < 8; l++) sumf[r] += sums[r][l];
+        out[r] = sumf[r];
+    }
+}
+#endif
+
 /* ---------------------------------------------------------- matrix product */
 /* out[m, n] = sum_k W[n, k] * x[m, k] (+ bias[n]).  W is N rows of `type`. */
 void ceo_matmul(int type, const uint8_t *w, int64_t n_out, int64_t k, const float *x, int64_t m_rows,
@@ -558,6 +614,34 @@ void ceo_matmul(int type, const uint8_t *w, int64_t n_out, int64_t k, const floa
                 }
             free(wd);
             free(ad);
+            free(xq);
+            return;
+        }
+#endif
+#if defined(__AVX2__)
+        if (type == T_Q4_K) {
+            /* Q4_K: one weight row against four activation rows per pass (dot_q4_k_1x4_avx2,
+             * the same value for every dot as ceo_dot_q4_k) */
+#pragma omp parallel for schedule(static) collapse(2)
+            for (int64_t bm = 0; bm < mt; bm++)
+                for (int64_t bn = 0; bn < nt; bn++) {
+                    const int64_t m1 = m_rows < (bm + 1) * TM ? m_rows : (bm + 1) * TM;
+                    const int64_t n1 = n_out < (bn + 1) * TN ? n_out : (bn + 1) * TN;
+                    int64_t m = bm * TM;
+                    for (; m + 4 <= m1; m += 4)
+                        for (int64_t n = bn * TN; n < n1; n++) {
+                            const uint8_t *a4[4] = {xq + m * qb, xq + (m + 1) * qb, xq + (m + 2) * qb,
+                                                    xq + (m + 3) * qb};
+                            float r[4];
+                            dot_q4_k_1x4_avx2(k / QK_K, w + n * rb, a4, r);
+                            for (int i = 0; i < 4; i++) out[(m + i) * n_out + n] = bias ? r[i] + bias[n] : r[i];
+                        }
+                    for (; m < m1; m++)
+                        for (int64_t n = bn * TN; n < n1; n++) {
+                            const float s = ceo_dot_q4_k(k, w + n * rb, xq + m * qb);
+                            out[m * n_out + n] = bias ? s + bias[n] : s;
+                        }
+                }
             free(xq);
             return;
         }

@@ -119,29 +119,41 @@ def test_q8_0_dot_avx2_equals_scalar(oracle):
         assert np.float32(fast).tobytes() == np.float32(slow).tobytes(), trial
 
 
-def test_q8_0_matmul_blocked_equals_per_dot(oracle):
-    """The ggml-mode Q8_0 matmul (four dots at a time over two weight and two activation
-    rows) gives every output the bits of its own ceo_dot_q8_0 (+ bias), for odd and even
-    row counts and tile edges."""
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_k"])
+def test_matmul_blocked_equals_per_dot(oracle, fmt):
+    """The ggml-mode matmul forms several dots per pass (Q8_0: two weight x two activation
+    rows; Q4_K: one weight row x four activation rows) and gives every output the bits of
+    its own ceo_dot_q8_0 / ceo_dot_q4_k (+ bias), for odd row counts and tile edges."""
     import ctypes
-    from crispembed_b200.gguf_io import GGML_Q8_0
+    from crispembed_b200.gguf_io import GGML_Q4_K, GGML_Q8_0
     rng = np.random.default_rng(11)
     L = oracle.lib()
     up = ctypes.POINTER(ctypes.c_uint8)
-    for m_rows, n_out, k in ((1, 1, 32), (3, 5, 64), (33, 31, 96), (64, 66, 768), (37, 70, 256)):
-        w = quant.quantize_q8_0((rng.standard_normal((n_out, k)) * 0.05).astype(np.float32))
+    if fmt == "q8_0":
+        t, qz, dot, act = GGML_Q8_0, quant.quantize_q8_0, L.ceo_dot_q8_0, oracle.quant_act_q8_0
+        shapes = ((1, 1, 32), (3, 5, 64), (33, 31, 96), (64, 66, 768), (37, 70, 256))
+    else:
+        def act(v):
+            out = np.zeros(v.size // 256 * 292, np.uint8)
+            vv = np.ascontiguousarray(v, dtype=np.float32)
+            L.ceo_quant_act_q8_k(vv.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), v.size, out.ctypes.data_as(up))
+            return out
+        t, qz, dot = GGML_Q4_K, quant.quantize_q4_k, L.ceo_dot_q4_k
+        shapes = ((1, 1, 256), (3, 5, 512), (34, 31, 256), (67, 40, 768))
+    for m_rows, n_out, k in shapes:
+        w = qz((rng.standard_normal((n_out, k)) * 0.05).astype(np.float32))
         x = rng.standard_normal((m_rows, k)).astype(np.float32)
         bias = rng.standard_normal(n_out).astype(np.float32)
-        got = oracle.matmul(GGML_Q8_0, w, n_out, k, x, oracle.GGML, bias)
+        got = oracle.matmul(t, w, n_out, k, x, oracle.GGML, bias)
         wrows = np.ascontiguousarray(w).reshape(n_out, -1)
         want = np.empty_like(got)
         for m in range(m_rows):
-            a = np.ascontiguousarray(oracle.quant_act_q8_0(x[m]))
+            a = np.ascontiguousarray(act(x[m]))
             for n in range(n_out):
                 wr = np.ascontiguousarray(wrows[n])
-                s = np.float32(L.ceo_dot_q8_0(k, wr.ctypes.data_as(up), a.ctypes.data_as(up)))
+                s = np.float32(dot(k, wr.ctypes.data_as(up), a.ctypes.data_as(up)))
                 want[m, n] = s + bias[n]
-        assert got.tobytes() == want.tobytes(), (m_rows, n_out, k)
+        assert got.tobytes() == want.tobytes(), (fmt, m_rows, n_out, k)
 
 
 def test_q4_k_dot_avx2_equals_scalar(oracle):
