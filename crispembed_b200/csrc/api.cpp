@@ -146,8 +146,10 @@ int forward_maybe_graph(crispembed_context* ctx, const int32_t* d_ids, int n_seq
         drop_graphs(ctx);
         ctx->graph_ws_base = ctx->ws.base;
     }
-    const char* tc = getenv("CEB_ATTN_TC");  // the attention kernel is chosen per call
-    const int variant = (tc && tc[0] == '1') ? 1 : 0;
+    // the attention kernel is chosen per call: a graph records the one of its capture
+    const char* tc = getenv("CEB_ATTN_TC");
+    const char* mma = getenv("CEB_ATTN_MMA");
+    const int variant = ((tc && tc[0] == '1') ? 1 : 0) | ((mma && mma[0] == '1') ? 2 : 0);
     auto same = [&](const crispembed_context::Graph& g) {
         return g.M == M && g.n_seqs == n_seqs && g.max_len == max_len && g.out_dim == out_dim && g.d_ids == d_ids &&
                g.d_out == d_out && g.st == st && g.variant == variant;
